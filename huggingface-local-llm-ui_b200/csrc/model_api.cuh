@@ -1,0 +1,405 @@
+// model_api.cuh -- C ABI of the whole-model forward (b2q_model_*), included
+// by b2q_api.cu after model_impl.cuh.
+#pragma once
+
+#include "model_impl.cuh"
+
+using namespace b2q;
+
+extern "C" {
+
+b2q_status b2q_tp_unique_id(unsigned char out[128]) {
+  if (!out) return set_error(B2Q_EINVAL, "b2q_tp_unique_id: out is NULL");
+  return tp_unique_id(out);
+}
+
+b2q_status b2q_model_create(b2q_engine* e, const b2q_model_config* cfg, const unsigned char* tp_id,
+                            b2q_model** out) {
+  if (!e || !cfg || !out) return set_error(B2Q_EINVAL, "b2q_model_create: NULL argument");
+  *out = nullptr;
+  const b2q_model_config& c = *cfg;
+  if (c.n_layers <= 0 || c.n_embd <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_ff <= 0 ||
+      c.n_vocab <= 0 || c.max_seq <= 0)
+    return set_error(B2Q_EINVAL, "b2q_model_create: all sizes must be positive");
+  if (c.head_dim != kHeadDim)
+    return set_error(B2Q_EUNSUP, "b2q_model_create: head_dim %d (only %d is built)", c.head_dim, kHeadDim);
+  if (c.n_heads % c.n_kv_heads != 0)
+    return set_error(B2Q_EINVAL, "b2q_model_create: n_heads %% n_kv_heads != 0");
+  const int G = c.n_heads / c.n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return set_error(B2Q_EUNSUP, "b2q_model_create: GQA ratio %d not built (1, 2, 4, 8)", G);
+  const int P = c.tp_size < 1 ? 1 : c.tp_size;
+  if (c.tp_rank < 0 || c.tp_rank >= P) return set_error(B2Q_EINVAL, "b2q_model_create: bad tp_rank");
+  if (c.n_kv_heads % P || c.n_embd % P || c.n_ff % P || c.n_vocab % P)
+    return set_error(B2Q_EINVAL,
+                     "b2q_model_create: tp_size %d must divide n_kv_heads, n_embd, n_ff and n_vocab", P);
+  if (c.n_embd % 256 || c.n_ff % 256 || (c.n_heads * c.head_dim) % 256)
+    return set_error(B2Q_EUNSUP, "b2q_model_create: n_embd, n_ff and n_heads*head_dim must be multiples of 256");
+  std::lock_guard<std::mutex> lk(e->mu);
+  cudaSetDevice(e->device);
+  b2q_model* M = new b2q_model();
+  M->eng = e;
+  M->c = c;
+  M->c.tp_size = P;
+  M->L.resize(c.n_layers);
+  M->H_loc = c.n_heads / P;
+  M->KV_loc = c.n_kv_heads / P;
+  M->F_loc = c.n_ff / P;
+  M->V_loc = c.n_vocab / P;
+  cudaError_t err = cudaStreamCreateWithFlags(&M->st, cudaStreamNonBlocking);
+  if (err != cudaSuccess) {
+    delete M;
+    return cuda_error(err, "model stream");
+  }
+  if (P > 1) {
+    const size_t stage = (size_t)P * M->mmax * std::max({c.n_embd, c.n_ff, c.n_heads * c.head_dim}) +
+                         (size_t)c.n_vocab;
+    b2q_status s = tp_init(M->tp, tp_id, c.tp_rank, P, stage);
+    if (s != B2Q_OK) {
+      tp_destroy(M->tp);
+      cudaStreamDestroy(M->st);
+      delete M;
+      return s;
+    }
+  }
+  *out = M;
+  return B2Q_OK;
+}
+
+b2q_status b2q_model_shard_rows(b2q_model* M, const char* name, int64_t n, int64_t* b, int64_t* e) {
+  if (!M || !name || !b || !e) return set_error(B2Q_EINVAL, "b2q_model_shard_rows: NULL argument");
+  int layer = -1;
+  std::string role = role_of(name, &layer);
+  if (role == "token_embd" || role == "output_norm" || role == "attn_norm" || role == "ffn_norm") {
+    *b = 0;
+    *e = n;
+    return B2Q_OK;
+  }
+  shard_range(M, role, n, b, e);
+  return B2Q_OK;
+}
+
+static b2q_status set_tensor_impl(b2q_model* M, const char* name, int dtype, const int64_t* dims,
+                                  int nd, int64_t rb, int64_t re, const void* bytes, size_t len) {
+  if (!M || !name || !dims || nd < 1 || !bytes)
+    return set_error(B2Q_EINVAL, "b2q_model_set_tensor: NULL argument");
+  if (M->finalized) return set_error(B2Q_EINVAL, "b2q_model_set_tensor: model already finalized");
+  int layer = -1;
+  const std::string role = role_of(name, &layer);
+  const b2q_model_config& c = M->c;
+  if (layer >= c.n_layers) return set_error(B2Q_EINVAL, "tensor %s: layer out of range", name);
+  const int64_t k = dims[nd - 1];
+  const int64_t n = nd > 1 ? dims[0] : 1;
+  for (int i = 1; i < nd - 1; ++i)
+    if (dims[i] != 1) return set_error(B2Q_EUNSUP, "tensor %s: more than 2 non-trivial dims", name);
+  const int bs = dtype_block(dtype), ts = dtype_size(dtype);
+  if (bs == 0) return set_error(B2Q_EUNSUP, "tensor %s: GGML type %d not supported", name, dtype);
+  if (k % bs) return set_error(B2Q_EINVAL, "tensor %s: inner dim %lld not a multiple of %d", name, (long long)k, bs);
+  const int64_t row_bytes = k / bs * ts;
+  if (rb < 0 || re > n || rb >= re) return set_error(B2Q_EINVAL, "tensor %s: bad row range", name);
+  if ((int64_t)len != (re - rb) * row_bytes)
+    return set_error(B2Q_EINVAL, "tensor %s: %zu bytes for %lld rows of %lld bytes", name, len,
+                     (long long)(re - rb), (long long)row_bytes);
+  std::lock_guard<std::mutex> lk(M->eng->mu);
+  cudaSetDevice(M->eng->device);
+  const uint8_t* src = static_cast<const uint8_t*>(bytes);
+
+  // 1-D f32 tensors (norms, biases): dequantised on the host side by the
+  // reference too (tensor_f32_1d, inference.rs:494-500); here only F32 is taken
+  auto take_vec = [&](float** dst, int64_t want_b, int64_t want_e) -> b2q_status {
+    if (dtype != kF32) return set_error(B2Q_EUNSUP, "tensor %s: 1-D tensors must be F32", name);
+    if (rb > want_b || re < want_e) return set_error(B2Q_EINVAL, "tensor %s: shard rows missing", name);
+    const float* f = reinterpret_cast<const float*>(src) + (want_b - rb) * k;
+    M->have[name] = true;
+    return upload_f32(f, (size_t)(want_e - want_b) * k, dst);
+  };
+  auto take_weight = [&](b2q_weight** dst) -> b2q_status {
+    int64_t sb, se;
+    shard_range(M, role, n, &sb, &se);
+    if (rb > sb || re < se)
+      return set_error(B2Q_EINVAL, "tensor %s: rows [%lld, %lld) of this rank were not supplied", name,
+                       (long long)sb, (long long)se);
+    if (!gemv_supported(dtype))
+      return set_error(B2Q_EUNSUP, "tensor %s: GGML type %d has no GEMV kernel", name, dtype);
+    M->eng->mu.unlock();
+    b2q_status s = b2q_upload_weight(M->eng, src + (sb - rb) * row_bytes, (size_t)((se - sb) * row_bytes),
+                                     dtype, se - sb, k, dst);
+    M->eng->mu.lock();
+    if (s == B2Q_OK) {
+      M->weight_bytes += (*dst)->gguf_bytes;
+      M->have[name] = true;
+    }
+    return s;
+  };
+
+  if (role == "token_embd") {
+    if (n != c.n_vocab || k != c.n_embd) return set_error(B2Q_EINVAL, "token_embd: wrong shape");
+    if (rb != 0 || re != n) return set_error(B2Q_EINVAL, "token_embd: every rank needs all rows");
+    cudaError_t err = cudaMalloc(&M->tok_raw, len);
+    if (err == cudaSuccess) err = cudaMemcpy(M->tok_raw, src, len, cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) return cuda_error(err, "token_embd upload");
+    M->tok_dtype = dtype;
+    M->tok_row_bytes = row_bytes;
+    M->weight_bytes += len;
+    M->have[name] = true;
+    // tied output head (inference.rs:2560-2562) unless output.weight comes
+    if (!M->output && dtype_block(dtype) > 1 && gemv_supported(dtype)) {
+      int64_t sb, se;
+      shard_range(M, "output", n, &sb, &se);
+      M->eng->mu.unlock();
+      b2q_status s = b2q_upload_weight(M->eng, src + sb * row_bytes, (size_t)((se - sb) * row_bytes),
+                                       dtype, se - sb, k, &M->output);
+      M->eng->mu.lock();
+      if (s != B2Q_OK) return s;
+      M->have["output.tied"] = true;
+    }
+    return B2Q_OK;
+  }
+  if (role == "output") {
+    if (n != c.n_vocab || k != c.n_embd) return set_error(B2Q_EINVAL, "output: wrong shape");
+    if (M->output) {
+      b2q_weight_free(M->output);
+      M->output = nullptr;
+    }
+    M->have.erase("output.tied");
+    return take_weight(&M->output);
+  }
+  if (role == "output_norm") return take_vec(&M->output_norm, 0, 1);
+  if (layer < 0) return set_error(B2Q_EINVAL, "tensor %s: unknown name", name);
+  LayerW& Lw = M->L[layer];
+  const int hd = c.head_dim;
+  if (role == "attn_norm") return take_vec(&Lw.attn_norm, 0, 1);
+  if (role == "ffn_norm") return take_vec(&Lw.ffn_norm, 0, 1);
+  if (role == "attn_q.bias" || role == "attn_k.bias" || role == "attn_v.bias") {
+    // 1-D [n] biases: dims = [n]; shard by heads
+    const int64_t nn = k;
+    int64_t sb, se;
+    shard_range(M, role, nn, &sb, &se);
+    if (dtype != kF32) return set_error(B2Q_EUNSUP, "tensor %s: biases must be F32", name);
+    float** dst = role == "attn_q.bias" ? &Lw.q_bias : role == "attn_k.bias" ? &Lw.k_bias : &Lw.v_bias;
+    M->have[name] = true;
+    return upload_f32(reinterpret_cast<const float*>(src) + sb, (size_t)(se - sb), dst);
+  }
+  struct { const char* r; b2q_weight** w; int64_t n, k; } tab[] = {
+      {"attn_q", &Lw.q, (int64_t)c.n_heads * hd, c.n_embd},
+      {"attn_k", &Lw.k, (int64_t)c.n_kv_heads * hd, c.n_embd},
+      {"attn_v", &Lw.v, (int64_t)c.n_kv_heads * hd, c.n_embd},
+      {"attn_output", &Lw.o, c.n_embd, (int64_t)c.n_heads * hd},
+      {"ffn_gate", &Lw.gate, c.n_ff, c.n_embd},
+      {"ffn_up", &Lw.up, c.n_ff, c.n_embd},
+      {"ffn_down", &Lw.down, c.n_embd, c.n_ff},
+  };
+  for (auto& t : tab) {
+    if (role == t.r) {
+      if (n != t.n || k != t.k)
+        return set_error(B2Q_EINVAL, "tensor %s: shape [%lld, %lld], expected [%lld, %lld]", name,
+                         (long long)n, (long long)k, (long long)t.n, (long long)t.k);
+      if (*t.w) {
+        b2q_weight_free(*t.w);
+        *t.w = nullptr;
+      }
+      return take_weight(t.w);
+    }
+  }
+  return set_error(B2Q_EINVAL, "tensor %s: unknown name", name);
+}
+
+b2q_status b2q_model_set_tensor(b2q_model* M, const char* name, int dtype, const int64_t* dims, int nd,
+                                const void* bytes, size_t len) {
+  if (!dims || nd < 1) return set_error(B2Q_EINVAL, "b2q_model_set_tensor: no dims");
+  const int64_t n = nd > 1 ? dims[0] : 1;
+  return set_tensor_impl(M, name, dtype, dims, nd, 0, n, bytes, len);
+}
+
+b2q_status b2q_model_set_tensor_rows(b2q_model* M, const char* name, int dtype, const int64_t* dims,
+                                     int nd, int64_t rb, int64_t re, const void* bytes, size_t len) {
+  return set_tensor_impl(M, name, dtype, dims, nd, rb, re, bytes, len);
+}
+
+b2q_status b2q_model_finalize(b2q_model* M) {
+  if (!M) return set_error(B2Q_EINVAL, "b2q_model_finalize: NULL model");
+  if (M->finalized) return B2Q_OK;
+  const b2q_model_config& c = M->c;
+  if (!M->tok_raw) return set_error(B2Q_EINVAL, "missing tensor token_embd.weight");
+  if (!M->output) return set_error(B2Q_EINVAL, "missing tensor output.weight");
+  if (!M->output_norm) return set_error(B2Q_EINVAL, "missing tensor output_norm.weight");
+  for (int l = 0; l < c.n_layers; ++l) {
+    const LayerW& w = M->L[l];
+    const char* miss = !w.attn_norm ? "attn_norm" : !w.ffn_norm ? "ffn_norm" : !w.q ? "attn_q"
+                     : !w.k ? "attn_k" : !w.v ? "attn_v" : !w.o ? "attn_output" : !w.gate ? "ffn_gate"
+                     : !w.up ? "ffn_up" : !w.down ? "ffn_down" : nullptr;
+    if (miss) return set_error(B2Q_EINVAL, "missing tensor blk.%d.%s.weight", l, miss);
+    if (w.gate->dtype != w.up->dtype)
+      return set_error(B2Q_EUNSUP, "blk.%d: ffn_gate and ffn_up must share a GGML type", l);
+  }
+  std::lock_guard<std::mutex> lk(M->eng->mu);
+  cudaSetDevice(M->eng->device);
+  const int E = c.n_embd, hd = c.head_dim, H = c.n_heads;
+  const int mm = M->mmax;
+  M->nsplit = (c.max_seq + kAttnTile - 1) / kAttnTile;
+  cudaError_t err = cudaSuccess;
+  const size_t kv = (size_t)M->KV_loc * c.max_seq * hd;
+  for (int l = 0; l < c.n_layers && err == cudaSuccess; ++l) {
+    err = dalloc(&M->L[l].kc, kv);
+    if (err == cudaSuccess) err = dalloc(&M->L[l].vc, kv);
+  }
+  if (err == cudaSuccess) err = dalloc(&M->x, (size_t)mm * E);
+  if (err == cudaSuccess) err = dalloc(&M->qkv, (size_t)mm * (M->H_loc + 2 * M->KV_loc) * hd);
+  if (err == cudaSuccess) err = dalloc(&M->attn, (size_t)mm * H * hd);
+  if (err == cudaSuccess) err = dalloc(&M->attn_loc, (size_t)mm * M->H_loc * hd);
+  if (err == cudaSuccess) err = dalloc(&M->hbuf, (size_t)mm * c.n_ff);
+  if (err == cudaSuccess) err = dalloc(&M->h_loc, (size_t)mm * M->F_loc);
+  if (err == cudaSuccess) err = dalloc(&M->y_loc, (size_t)mm * E);
+  if (err == cudaSuccess) err = dalloc(&M->logits, (size_t)c.n_vocab);
+  if (err == cudaSuccess) err = dalloc(&M->logits_loc, (size_t)M->V_loc);
+  if (err == cudaSuccess) err = dalloc(&M->part, (size_t)mm * M->H_loc * M->nsplit * (hd + 2));
+  if (err == cudaSuccess) err = dalloc(&M->tokens, (size_t)2 * mm);  // ids + host staging
+  if (err == cudaSuccess) err = dalloc(&M->argmax, 1);
+  if (err == cudaSuccess) err = dalloc(&M->pos, 1);
+  if (err == cudaSuccess) err = xq_alloc(&M->xq_e, mm, E);
+  if (err == cudaSuccess) err = xq_alloc(&M->xq_a, mm, H * hd);
+  if (err == cudaSuccess) err = xq_alloc(&M->xq_f, mm, c.n_ff);
+  if (err == cudaSuccess) err = cudaMallocHost(&M->h_tok, sizeof(uint32_t) * mm);
+  if (err != cudaSuccess) return cuda_error(err, "b2q_model_finalize: allocation");
+  // RoPE tables: freq = 1/theta^(2j/hd) in f32 powf, angle in f32, f32 cos/sin
+  // (inference.rs:2538-2549), for positions 0..8191
+  {
+    const int half = hd / 2, NP = 8192;
+    std::vector<float> cs((size_t)NP * half), sn((size_t)NP * half);
+    for (int p = 0; p < NP; ++p)
+      for (int j = 0; j < half; ++j) {
+        const float freq = 1.0f / powf(c.rope_theta, (float)(2 * j) / (float)hd);
+        const float angle = (float)p * freq;
+        cs[(size_t)p * half + j] = cosf(angle);
+        sn[(size_t)p * half + j] = sinf(angle);
+      }
+    b2q_status s = upload_f32(cs.data(), cs.size(), &M->rope_cos);
+    if (s == B2Q_OK) s = upload_f32(sn.data(), sn.size(), &M->rope_sin);
+    if (s != B2Q_OK) return s;
+  }
+  err = cudaDeviceSynchronize();
+  if (err != cudaSuccess) return cuda_error(err, "b2q_model_finalize: sync");
+  if (!c.no_graph) {
+    err = build_decode_graph(M);
+    if (err != cudaSuccess) return cuda_error(err, "b2q_model_finalize: decode graph capture");
+  }
+  M->finalized = true;
+  return B2Q_OK;
+}
+
+static b2q_status forward_impl(b2q_model* M, const uint32_t* tokens, bool tok_on_dev, int n, int start,
+                               cudaStream_t st) {
+  const b2q_model_config& c = M->c;
+  if (n <= 0) return set_error(B2Q_EINVAL, "forward: no tokens");
+  if (start < 0 || start + n > c.max_seq)
+    return set_error(B2Q_EINVAL, "forward: positions [%d, %d) exceed the KV capacity %d", start,
+                     start + n, c.max_seq);
+  if (!tok_on_dev)
+    for (int i = 0; i < n; ++i)
+      if (tokens[i] >= (uint32_t)c.n_vocab)
+        return set_error(B2Q_EINVAL, "forward: token id %u >= vocab %d", tokens[i], c.n_vocab);
+  cudaError_t err = cudaSuccess;
+  for (int off = 0; off < n && err == cudaSuccess; off += M->mmax) {
+    const int m = std::min(M->mmax, n - off);
+    const uint32_t* src = tokens + off;
+    if (!tok_on_dev) {
+      // host tokens: stage through the pinned buffer (synchronous callers only)
+      memcpy(M->h_tok, tokens + off, sizeof(uint32_t) * m);
+      err = cudaMemcpyAsync(M->tokens + M->mmax, M->h_tok, sizeof(uint32_t) * m, cudaMemcpyHostToDevice, st);
+      if (err != cudaSuccess) break;
+      src = M->tokens + M->mmax;
+    }
+    launch_counted(M->eng, 1);
+    set_step_kernel<<<1, 64, 0, st>>>(M->pos, start + off, M->tokens, src, m, c.n_vocab);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) break;
+    if (m == 1 && M->graph) {
+      err = cudaGraphLaunch(M->graph, st);
+      M->eng->launches.fetch_add(M->graph_kernels);
+    } else {
+      err = forward_pass(M, m, false, st);
+    }
+    // the pinned staging is reused by the next chunk: wait for its copy
+    if (err == cudaSuccess && !tok_on_dev && off + m < n) err = cudaStreamSynchronize(st);
+  }
+  if (err != cudaSuccess) return cuda_error(err, "forward");
+  return B2Q_OK;
+}
+
+b2q_status b2q_forward_dev(b2q_model* M, const uint32_t* tokens_dev, int n, int start, float* logits_dev,
+                           uint32_t* argmax_dev, void* stream) {
+  if (!M || !tokens_dev) return set_error(B2Q_EINVAL, "b2q_forward_dev: NULL argument");
+  if (!M->finalized) return set_error(B2Q_EINVAL, "b2q_forward_dev: model not finalized");
+  std::lock_guard<std::mutex> lk(M->eng->mu);
+  cudaSetDevice(M->eng->device);
+  cudaStream_t st = stream ? (cudaStream_t)stream : M->st;
+  b2q_status s = forward_impl(M, tokens_dev, true, n, start, st);
+  if (s != B2Q_OK) return s;
+  cudaError_t err = cudaSuccess;
+  if (logits_dev)
+    err = cudaMemcpyAsync(logits_dev, M->logits, sizeof(float) * M->c.n_vocab, cudaMemcpyDeviceToDevice, st);
+  if (err == cudaSuccess && argmax_dev)
+    err = cudaMemcpyAsync(argmax_dev, M->argmax, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st);
+  if (err != cudaSuccess) return cuda_error(err, "b2q_forward_dev: copy out");
+  return B2Q_OK;
+}
+
+b2q_status b2q_forward(b2q_model* M, const uint32_t* tokens, int n, int start, float* logits,
+                       uint32_t* argmax) {
+  if (!M || !tokens) return set_error(B2Q_EINVAL, "b2q_forward: NULL argument");
+  if (!M->finalized) return set_error(B2Q_EINVAL, "b2q_forward: model not finalized");
+  std::lock_guard<std::mutex> lk(M->eng->mu);
+  cudaSetDevice(M->eng->device);
+  b2q_status s = forward_impl(M, tokens, false, n, start, M->st);
+  if (s != B2Q_OK) return s;
+  cudaError_t err = cudaSuccess;
+  if (logits)
+    err = cudaMemcpyAsync(logits, M->logits, sizeof(float) * M->c.n_vocab, cudaMemcpyDeviceToHost, M->st);
+  if (err == cudaSuccess && argmax)
+    err = cudaMemcpyAsync(argmax, M->argmax, sizeof(uint32_t), cudaMemcpyDeviceToHost, M->st);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
+  if (err != cudaSuccess) return cuda_error(err, "b2q_forward");
+  return B2Q_OK;
+}
+
+b2q_status b2q_clear_state(b2q_model* M) {
+  // The KV cache is indexed by absolute position, so clearing only resets
+  // what the caller considers the current position; entries past it are
+  // never read (attention reads keys t < start + s + 1).
+  if (!M) return set_error(B2Q_EINVAL, "b2q_clear_state: NULL model");
+  return B2Q_OK;
+}
+
+size_t b2q_model_weight_bytes(const b2q_model* M) { return M ? M->weight_bytes : 0; }
+
+b2q_status b2q_model_destroy(b2q_model* M) {
+  if (!M) return B2Q_OK;
+  cudaSetDevice(M->eng->device);
+  cudaStreamSynchronize(M->st);
+  if (M->graph) cudaGraphExecDestroy(M->graph);
+  tp_destroy(M->tp);
+  for (auto& l : M->L) {
+    b2q_weight* ws[7] = {l.q, l.k, l.v, l.o, l.gate, l.up, l.down};
+    for (auto* w : ws) b2q_weight_free(w);
+    float* fs[5] = {l.attn_norm, l.ffn_norm, l.q_bias, l.k_bias, l.v_bias};
+    for (auto* f : fs)
+      if (f) cudaFree(f);
+    if (l.kc) cudaFree(l.kc);
+    if (l.vc) cudaFree(l.vc);
+  }
+  b2q_weight_free(M->output);
+  void* ps[] = {M->tok_raw, M->output_norm, M->x, M->qkv, M->attn, M->attn_loc, M->hbuf, M->h_loc,
+                M->y_loc, M->logits, M->logits_loc, M->part, M->tokens, M->argmax, M->pos,
+                M->rope_cos, M->rope_sin};
+  for (void* p : ps)
+    if (p) cudaFree(p);
+  xq_free(&M->xq_e);
+  xq_free(&M->xq_a);
+  xq_free(&M->xq_f);
+  if (M->h_tok) cudaFreeHost(M->h_tok);
+  cudaStreamDestroy(M->st);
+  delete M;
+  return B2Q_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,142 @@
+"""Python mirror of the reference's Llama engine (src/inference.rs:2406-2905).
+
+``StandardNativeEngine`` keeps the reference's entry points -- construction
+from GGUF-named tensors, ``forward(tokens, start_pos)`` returning the logits
+of the last position, ``clear_state()`` -- over the C ABI of libb2q, which
+keeps the weights, activations and the f16 KV cache on the device.
+``generate_greedy`` is the decode loop of LocalLlm at temperature 0
+(inference.rs:3190-3231 prefill, :3354 decode, :1620-1630 greedy sampling).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import ggml
+from ._lib import ModelConfig, check, lib
+from .engine import CudaEngine
+
+LLAMA3_8B = dict(n_layers=32, n_embd=4096, n_heads=32, n_kv_heads=8, head_dim=128, n_ff=14336,
+                 n_vocab=128256, rms_eps=1e-5, rope_theta=500000.0)
+LLAMA3_70B = dict(n_layers=80, n_embd=8192, n_heads=64, n_kv_heads=8, head_dim=128, n_ff=28672,
+                  n_vocab=128256, rms_eps=1e-5, rope_theta=500000.0)
+
+
+def tp_unique_id() -> bytes:
+    buf = (C.c_ubyte * 128)()
+    check(lib().b2q_tp_unique_id(buf))
+    return bytes(buf)
+
+
+class StandardNativeEngine:
+    """Llama-family decoder on one device, or one tensor-parallel rank."""
+
+    def __init__(self, engine: CudaEngine, cfg: dict, max_seq: int = 8192, tp_rank: int = 0,
+                 tp_size: int = 1, tp_id: bytes | None = None, use_graph: bool = True):
+        self.engine = engine
+        self.cfg = dict(cfg)
+        self.max_seq = max_seq
+        c = ModelConfig(cfg["n_layers"], cfg["n_embd"], cfg["n_heads"], cfg["n_kv_heads"],
+                        cfg["head_dim"], cfg["n_ff"], cfg["n_vocab"], cfg["rms_eps"],
+                        cfg["rope_theta"], max_seq, tp_rank, tp_size, 0 if use_graph else 1)
+        h = C.c_void_p()
+        idbuf = (C.c_ubyte * 128).from_buffer_copy(tp_id) if tp_id else None
+        check(lib().b2q_model_create(engine.handle, C.byref(c), idbuf, C.byref(h)))
+        self._h = h
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        self.current_pos = 0
+
+    # -- loading (from_gguf, inference.rs:2513-2620) -----------------------
+    def shard_rows(self, name: str, n: int) -> tuple[int, int]:
+        b, e = C.c_int64(), C.c_int64()
+        check(lib().b2q_model_shard_rows(self._h, name.encode(), n, C.byref(b), C.byref(e)))
+        return b.value, e.value
+
+    def set_tensor(self, name: str, dtype: int, dims, data: np.ndarray, row_begin: int | None = None,
+                   row_end: int | None = None) -> None:
+        arr = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+        d = (C.c_int64 * len(dims))(*[int(v) for v in dims])
+        if row_begin is None:
+            check(lib().b2q_model_set_tensor(self._h, name.encode(), dtype, d, len(dims),
+                                             arr.ctypes.data, arr.size))
+        else:
+            check(lib().b2q_model_set_tensor_rows(self._h, name.encode(), dtype, d, len(dims),
+                                                  row_begin, row_end, arr.ctypes.data, arr.size))
+
+    def finalize(self) -> None:
+        check(lib().b2q_model_finalize(self._h))
+
+    @classmethod
+    def from_tensors(cls, engine: CudaEngine, cfg: dict, tensors: dict, max_seq: int = 8192,
+                     **tp) -> "StandardNativeEngine":
+        """`tensors`: GGUF name -> (ggml type, dims [outer.., inner], array)."""
+        m = cls(engine, cfg, max_seq=max_seq, **tp)
+        for name, (dtype, dims, arr) in tensors.items():
+            m.set_tensor(name, dtype, dims, arr)
+        m.finalize()
+        return m
+
+    @property
+    def weight_bytes(self) -> int:
+        return int(lib().b2q_model_weight_bytes(self._h))
+
+    # -- inference --------------------------------------------------------
+    def forward(self, tokens, start_pos: int) -> np.ndarray:
+        """Logits [n_vocab] of the last position (inference.rs:2695-2860)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        logits = np.empty(self.cfg["n_vocab"], dtype=np.float32)
+        check(lib().b2q_forward(self._h, t.ctypes.data_as(C.POINTER(C.c_uint32)), t.size, start_pos,
+                                logits.ctypes.data_as(C.POINTER(C.c_float)), None))
+        return logits
+
+    def forward_argmax(self, tokens, start_pos: int) -> int:
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = C.c_uint32()
+        check(lib().b2q_forward(self._h, t.ctypes.data_as(C.POINTER(C.c_uint32)), t.size, start_pos,
+                                None, C.byref(out)))
+        return int(out.value)
+
+    def forward_dev(self, tokens_ptr: int, n: int, start_pos: int, logits_ptr: int = 0,
+                    argmax_ptr: int = 0, stream: int = 0) -> None:
+        check(lib().b2q_forward_dev(self._h, tokens_ptr, n, start_pos, logits_ptr or None,
+                                    argmax_ptr or None, stream or None))
+
+    def clear_state(self) -> None:
+        check(lib().b2q_clear_state(self._h))
+        self.current_pos = 0
+
+    def generate_greedy(self, prompt, max_tokens: int, prefill_chunk: int = 64) -> list[int]:
+        """Chunked prefill, then greedy decode of `max_tokens` tokens."""
+        prompt = list(prompt)
+        if not prompt:
+            raise ValueError("no tokens to prefill")
+        nxt = None
+        for off in range(0, len(prompt), prefill_chunk):
+            chunk = prompt[off:off + prefill_chunk]
+            nxt = self.forward_argmax(chunk, self.current_pos)
+            self.current_pos += len(chunk)
+        out = []
+        for _ in range(max_tokens):
+            out.append(nxt)
+            nxt = self.forward_argmax([nxt], self.current_pos)
+            self.current_pos += 1
+        return out
+
+    def close(self) -> None:
+        if self._h:
+            lib().b2q_model_destroy(self._h)
+            self._h = C.c_void_p(None)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def q4_k_m_types() -> dict:
+    """GGML types per tensor role of the Llama Q4_K_M layout used here."""
+    return {"token_embd": ggml.Q4_K, "output": ggml.Q6_K, "attn_q": ggml.Q4_K, "attn_k": ggml.Q4_K,
+            "attn_v": ggml.Q6_K, "attn_output": ggml.Q4_K, "ffn_gate": ggml.Q4_K,
+            "ffn_up": ggml.Q4_K, "ffn_down": ggml.Q6_K}

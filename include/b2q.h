@@ -1,0 +1,220 @@
+/*
+ * b2q.h -- C ABI of the B200 GGUF dequant-GEMV decode library (libb2q.so).
+ *
+ * Drop-in boundary for the reference engine's GPU accelerator
+ * (roblar658/huggingface-Local-LLM-UI, src/gpu.rs `CudaEngine`) and for its
+ * model forward (src/inference.rs `StandardNativeEngine`).  Plain pointers,
+ * sizes and status codes only; no C++ or framework types cross the ABI.
+ *
+ * Conventions
+ *  - Every call returns a b2q_status; B2Q_OK is 0.  On failure
+ *    b2q_last_error() returns a thread-local description.  There is no CPU
+ *    fallback: the reference returned None and silently ran on the CPU
+ *    (inference.rs:600-606); a caller of this ABI maps a non-OK status to
+ *    its own error.
+ *  - GGUF tensors are passed as their raw on-disk block bytes, `n` rows of
+ *    `k` elements ([n][k] row-major, the order the reference's parser
+ *    produces after reversing GGML's dims, inference.rs:403).  The library
+ *    may repack blocks at upload; dequantised values stay bit-exact.
+ *  - Activations are f32.  Entry points without a suffix take HOST pointers
+ *    and return after the result is on the host, as the reference's
+ *    synchronous memcpy path did.  `_dev` entry points take DEVICE pointers
+ *    and a cudaStream_t (passed as void*) and are asynchronous.
+ *  - One engine per CUDA device; handles are internally locked.
+ */
+#ifndef B2Q_H
+#define B2Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  B2Q_OK = 0,
+  B2Q_EINVAL = 1,   /* bad dtype, shape, pointer or argument */
+  B2Q_ENOMEM = 2,   /* device allocation failed */
+  B2Q_ECUDA = 3,    /* CUDA runtime / kernel error */
+  B2Q_ENCCL = 4,    /* NCCL error */
+  B2Q_ETIMEOUT = 5, /* a bounded device-side wait gave up */
+  B2Q_EUNSUP = 6    /* dtype or feature not supported */
+} b2q_status;
+
+/* GGML type ids (GgmlDType::from_u32, inference.rs:136-155). */
+enum {
+  B2Q_F32 = 0, B2Q_F16 = 1, B2Q_Q4_0 = 2, B2Q_Q8_0 = 8,
+  B2Q_Q4_K = 12, B2Q_Q5_K = 13, B2Q_Q6_K = 14, B2Q_BF16 = 30
+};
+
+typedef struct b2q_engine b2q_engine; /* CudaEngine (gpu.rs:183-207) */
+typedef struct b2q_weight b2q_weight; /* CudaWeightBuffer (gpu.rs:212-238) */
+typedef struct b2q_model b2q_model;   /* StandardNativeEngine (inference.rs:2498-2510) */
+
+/* Thread-local text of the last failure on this thread. */
+const char* b2q_last_error(void);
+
+/* Library version string. */
+const char* b2q_version(void);
+
+/* ---- engine ---------------------------------------------------------- */
+
+/* Replaces CudaEngine::global / init_internal (gpu.rs:238-385): bind the
+ * device, create the stream and workspace.  Kernels are compiled into the
+ * library for sm_100a; nothing is JIT-loaded. */
+b2q_status b2q_init(int device, b2q_engine** out);
+b2q_status b2q_engine_destroy(b2q_engine* eng);
+
+/* Device name and memory (the reference's device_name / cuMemGetInfo). */
+b2q_status b2q_device_info(b2q_engine* eng, char* name, size_t name_len,
+                           size_t* free_bytes, size_t* total_bytes);
+
+/* Replaces CudaEngine::can_safely_alloc (gpu.rs:403-437): true (1) if
+ * `bytes` more can be allocated while keeping `reserve_bytes` free. */
+int b2q_can_alloc(b2q_engine* eng, size_t bytes, size_t reserve_bytes);
+
+/* ---- weights --------------------------------------------------------- */
+
+/* Replaces CudaEngine::try_upload_weight (gpu.rs:468-507): copy the raw GGUF
+ * bytes of an [n][k] tensor (`len` must equal n * row_bytes) to the device,
+ * repacked into the GEMV layout.  `bytes` may be a host or device pointer. */
+b2q_status b2q_upload_weight(b2q_engine* eng, const void* bytes, size_t len,
+                             int ggml_type, int64_t n, int64_t k, b2q_weight** out);
+
+/* Drop for CudaWeightBuffer (gpu.rs:222-238). */
+b2q_status b2q_weight_free(b2q_weight* w);
+
+/* Device bytes held by a weight (equals the GGUF byte length). */
+size_t b2q_weight_bytes(const b2q_weight* w);
+
+/* ---- matvec entry points --------------------------------------------- */
+
+/* Replaces CudaEngine::matmul_batched (gpu.rs:557-589) and the kernels
+ * matmul_{q4k,q6k,q8_0,...} it launched (gpu.rs:510-555):
+ * y[t][r] = sum_c dequant(W)[r][c] * x[t][c], x [m][k], y [m][n], f32. */
+b2q_status b2q_matmul(b2q_engine* eng, const b2q_weight* w, const float* x, float* y,
+                      int m, int n, int k);
+b2q_status b2q_matmul_dev(b2q_engine* eng, const b2q_weight* w, const float* x_dev,
+                          float* y_dev, int m, int n, int k, void* stream);
+
+/* Replaces CudaEngine::matmul_group_same_input (gpu.rs:593-650): `count`
+ * weights sharing the input x [m][k]; outputs are concatenated in order,
+ * each as its own [m][n_i] block, into y_flat (gpu.rs:617-646). */
+b2q_status b2q_matmul_group(b2q_engine* eng, const b2q_weight* const* ws, const int* ns,
+                            int count, const float* x, int m, int k, float* y_flat);
+b2q_status b2q_matmul_group_dev(b2q_engine* eng, const b2q_weight* const* ws, const int* ns,
+                                int count, const float* x_dev, int m, int k, float* y_flat_dev,
+                                void* stream);
+
+/* Replaces CudaEngine::ffn_swiglu_fused (gpu.rs:657-734) and the swiglu_f32
+ * kernel: y = W_down * (silu(W_gate * x) .* (W_up * x)); x [m][n_embd],
+ * y [m][n_embd]. */
+b2q_status b2q_ffn_swiglu(b2q_engine* eng, const b2q_weight* gate, const b2q_weight* up,
+                          const b2q_weight* down, const float* x, int m, int n_embd,
+                          int ffn_inter, float* y);
+b2q_status b2q_ffn_swiglu_dev(b2q_engine* eng, const b2q_weight* gate, const b2q_weight* up,
+                              const b2q_weight* down, const float* x_dev, int m, int n_embd,
+                              int ffn_inter, float* y_dev, void* stream);
+
+/* Replaces dequantize_slice (inference.rs:1347-1474) on the device: raw GGUF
+ * bytes (device pointer) of `n_elems` elements to f32, bit-exact. */
+b2q_status b2q_dequantize_dev(b2q_engine* eng, const void* raw_dev, int ggml_type,
+                              int64_t n_elems, float* out_dev, void* stream);
+
+/* ---- whole model (keeps activations and the KV cache on the device) ---- */
+
+typedef struct {
+  int n_layers;      /* {arch}.block_count */
+  int n_embd;        /* {arch}.embedding_length */
+  int n_heads;       /* {arch}.attention.head_count */
+  int n_kv_heads;    /* {arch}.attention.head_count_kv */
+  int head_dim;      /* {arch}.attention.key_length */
+  int n_ff;          /* rows of ffn_gate */
+  int n_vocab;       /* rows of output / token_embd */
+  float rms_eps;     /* {arch}.attention.layer_norm_rms_epsilon, default 1e-5 */
+  float rope_theta;  /* {arch}.rope.freq_base, default 1e4 */
+  int max_seq;       /* KV capacity in tokens; positions clamp at 8191 for RoPE */
+  int tp_rank;       /* tensor-parallel rank of this process (0 for 1 GPU) */
+  int tp_size;       /* tensor-parallel world size (1 for 1 GPU) */
+  int no_graph;      /* 1: run single-token steps eagerly instead of replaying
+                        the captured CUDA graph (0, the default, uses it) */
+} b2q_model_config;
+
+/* Unique id for NCCL communicator setup (ncclGetUniqueId); rank 0 creates
+ * it and the caller broadcasts the 128 bytes to the other ranks. */
+b2q_status b2q_tp_unique_id(unsigned char out[128]);
+
+/* Replaces StandardNativeEngine::from_gguf (inference.rs:2513-2620):
+ * create an empty model; tensors are then added by GGUF name. */
+b2q_status b2q_model_create(b2q_engine* eng, const b2q_model_config* cfg,
+                            const unsigned char* tp_unique_id, b2q_model** out);
+
+/* Add one tensor by its GGUF name ("token_embd.weight", "output_norm.weight",
+ * "output.weight", "blk.{i}.attn_norm.weight", "blk.{i}.attn_q.weight",
+ * ".attn_k", ".attn_v", ".attn_output", ".ffn_norm", ".ffn_gate", ".ffn_up",
+ * ".ffn_down", optional ".attn_{q,k,v}.bias").  dims are [outer.., inner]
+ * as the reference stores them (inference.rs:403).  Under tensor
+ * parallelism each rank passes the FULL tensor; the library keeps its
+ * shard.  `bytes` is a host pointer. */
+b2q_status b2q_model_set_tensor(b2q_model* m, const char* name, int ggml_type,
+                                const int64_t* dims, int n_dims, const void* bytes, size_t len);
+
+/* Same, but the caller passes only rows [row_begin, row_end) of an [n][k]
+ * tensor (its own shard, for sharded loading of large models). */
+b2q_status b2q_model_set_tensor_rows(b2q_model* m, const char* name, int ggml_type,
+                                     const int64_t* dims, int n_dims, int64_t row_begin,
+                                     int64_t row_end, const void* bytes, size_t len);
+
+/* Row range of an [n][...] tensor this rank must supply for `name`. */
+b2q_status b2q_model_shard_rows(b2q_model* m, const char* name, int64_t n,
+                                int64_t* row_begin, int64_t* row_end);
+
+/* Validate that every tensor is present, allocate the KV cache and build
+ * the decode graphs. */
+b2q_status b2q_model_finalize(b2q_model* m);
+
+/* Replaces StandardNativeEngine::forward (inference.rs:2695-2860): run
+ * `n_tokens` tokens starting at `start_pos`, appending to the KV cache, and
+ * write the logits of the LAST position ([n_vocab] f32) to `logits` (host
+ * pointer, may be NULL).  If `argmax` is non-NULL the greedy next token
+ * (SelfMadeSampler at temperature <= 1e-5, inference.rs:1620-1630) is
+ * written there too. */
+b2q_status b2q_forward(b2q_model* m, const uint32_t* tokens, int n_tokens, int start_pos,
+                       float* logits, uint32_t* argmax);
+
+/* Device-pointer form: tokens_dev / logits_dev / argmax_dev are device
+ * pointers (any may be NULL except tokens_dev); asynchronous on `stream`
+ * (NULL: the model's own stream). */
+b2q_status b2q_forward_dev(b2q_model* m, const uint32_t* tokens_dev, int n_tokens,
+                           int start_pos, float* logits_dev, uint32_t* argmax_dev, void* stream);
+
+/* Replaces StandardNativeEngine::clear_state (inference.rs:2688-2693). */
+b2q_status b2q_clear_state(b2q_model* m);
+
+/* Device bytes held by the model's weights on this rank. */
+size_t b2q_model_weight_bytes(const b2q_model* m);
+
+b2q_status b2q_model_destroy(b2q_model* m);
+
+/* Kernel timing for benchmarks: quantise x (device, [k] f32) once, then
+ * launch the GEMV of each of the `count` weights (same k) `reps` times in
+ * turn on `stream`, writing y to scratch, and return the average device
+ * time of one GEMV launch in *avg_ms (CUDA events on `stream`).  Rotating
+ * through weights that together exceed the L2 cache times HBM streaming. */
+b2q_status b2q_time_gemv(b2q_engine* eng, const b2q_weight* const* ws, int count,
+                         const float* x_dev, int k, int reps, void* stream, float* avg_ms);
+
+/* Launch statistics: number of library kernels launched so far on this
+ * engine (graph replays count every kernel node). */
+uint64_t b2q_kernel_launch_count(b2q_engine* eng);
+
+/* Read and clear the device-side error word (B2Q_ETIMEOUT when a bounded
+ * wait gave up); synchronises the engine's stream. */
+b2q_status b2q_check_device_error(b2q_engine* eng);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2Q_H */

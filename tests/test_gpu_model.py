@@ -1,0 +1,127 @@
+"""Whole-model forward on the device against the fp64 oracle forward.
+
+The oracle runs the reference's Llama block loop (inference.rs:2695-2860) in
+double precision over the bit-exact dequantised weights, with the KV cache
+rounded to f16 as the device cache is.  Logits of every forward must be
+within rel-L2 <= 1e-3.  Models use the unit-variance synthetic distribution
+(see synth.py: the benchmark distribution is numerically chaotic).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+TOY = dict(n_layers=2, n_embd=512, n_heads=8, n_kv_heads=2, head_dim=128, n_ff=1536,
+           n_vocab=1000, rms_eps=1e-5, rope_theta=500000.0)
+
+
+def _pair(engine, orc, pkg, cfg, seed=1, max_seq=256):
+    from hf_llm_b200 import model, synth
+    t = synth.llama_tensors(cfg, model.q4_k_m_types(), seed, dist="unit")
+    dev = model.StandardNativeEngine.from_tensors(engine, cfg, t, max_seq=max_seq)
+    ref = orc.Model(cfg, t, kv_capacity=max_seq)
+    return dev, ref
+
+
+def test_prefill_then_decode_matches_fp64(engine, orc, pkg):
+    dev, ref = _pair(engine, orc, pkg, TOY)
+    toks = [1, 5, 900, 33, 2, 7, 400]
+    a = dev.forward(toks, 0)
+    b = ref.forward_f64(toks, 0, kv_f16=True)
+    assert rel_l2(a, b) <= TOL
+    pos = len(toks)
+    for step in range(4):  # single-token steps replay the captured decode graph
+        tok = [int(np.argmax(b))]
+        a = dev.forward(tok, pos)
+        b = ref.forward_f64(tok, pos, kv_f16=True)
+        assert rel_l2(a, b) <= TOL, f"decode step {step}: {rel_l2(a, b)}"
+        pos += 1
+
+
+@pytest.mark.parametrize("gqa", [1, 2, 4, 8])
+def test_gqa_ratios(engine, orc, pkg, gqa):
+    cfg = dict(TOY, n_heads=8, n_kv_heads=8 // gqa)
+    dev, ref = _pair(engine, orc, pkg, cfg, seed=gqa)
+    toks = [3, 14, 15, 92, 65]
+    assert rel_l2(dev.forward(toks, 0), ref.forward_f64(toks, 0, kv_f16=True)) <= TOL
+    assert rel_l2(dev.forward([35], 5), ref.forward_f64([35], 5, kv_f16=True)) <= TOL
+
+
+def test_long_prompt_chunks_and_splits(engine, orc, pkg):
+    """A prompt longer than one forward chunk (64) and than one attention
+    split (128 keys) exercises the chunked prefill and the split merge."""
+    dev, ref = _pair(engine, orc, pkg, dict(TOY, n_layers=1), seed=7, max_seq=512)
+    rng = np.random.default_rng(0)
+    toks = rng.integers(0, TOY["n_vocab"], 300).tolist()
+    a = dev.forward(toks, 0)
+    b = ref.forward_f64(toks, 0, kv_f16=True)
+    assert rel_l2(a, b) <= TOL
+    assert rel_l2(dev.forward([11], 300), ref.forward_f64([11], 300, kv_f16=True)) <= TOL
+
+
+def test_llama3_8b_geometry_two_layers(engine, orc, pkg):
+    """Full Llama-3-8B widths (hidden 4096, 32/8 heads, FFN 14336, vocab
+    128256) with 2 layers."""
+    from hf_llm_b200 import model
+    cfg = dict(model.LLAMA3_8B, n_layers=2)
+    dev, ref = _pair(engine, orc, pkg, cfg, seed=11, max_seq=64)
+    toks = [128000, 9906, 1917, 11]
+    assert rel_l2(dev.forward(toks, 0), ref.forward_f64(toks, 0, kv_f16=True)) <= TOL
+    assert rel_l2(dev.forward([13], 4), ref.forward_f64([13], 4, kv_f16=True)) <= TOL
+
+
+def test_graph_decode_equals_eager(engine, orc, pkg):
+    """The captured single-token graph and the eager path give identical
+    logits (same kernels, same order)."""
+    import torch
+    from hf_llm_b200 import model, synth
+    t = synth.llama_tensors(TOY, model.q4_k_m_types(), 5, dist="unit")
+    a_m = model.StandardNativeEngine(engine, TOY, max_seq=64)
+    b_m = model.StandardNativeEngine(engine, TOY, max_seq=64, use_graph=False)
+    for mm in (a_m, b_m):
+        for name, (dt, dims, arr) in t.items():
+            mm.set_tensor(name, dt, dims, arr)
+        mm.finalize()
+        mm.forward([1, 2, 3], 0)
+    la = a_m.forward([4], 3)  # graph replay
+    tok = torch.tensor([4], dtype=torch.int32, device="cuda")
+    lb = torch.empty(TOY["n_vocab"], dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+    b_m.forward_dev(tok.data_ptr(), 1, 3, lb.data_ptr(), 0, s.cuda_stream)  # eager, other stream
+    s.synchronize()
+    assert np.array_equal(la, lb.cpu().numpy())
+
+
+def test_greedy_generation_follows_fp64_argmax(engine, orc, pkg):
+    dev, ref = _pair(engine, orc, pkg, TOY, seed=3)
+    out = dev.generate_greedy([5, 6, 7], 6)
+    pos, tok = 3, None
+    logits = ref.forward_f64([5, 6, 7], 0, kv_f16=True)
+    for t in out:
+        srt = np.sort(logits)
+        if srt[-1] - srt[-2] > 1e-3 * np.abs(srt[-1]):  # no near-tie
+            assert t == int(np.argmax(logits))
+        logits = ref.forward_f64([t], pos, kv_f16=True)
+        pos += 1
+
+
+def test_model_error_paths(engine, pkg):
+    from hf_llm_b200 import model, synth
+    from hf_llm_b200._lib import B2QError, EINVAL
+    t = synth.llama_tensors(TOY, model.q4_k_m_types(), 2, dist="unit")
+    m = model.StandardNativeEngine.from_tensors(engine, TOY, t, max_seq=16)
+    with pytest.raises(B2QError) as e:
+        m.forward([TOY["n_vocab"]], 0)  # token id out of range
+    assert e.value.status == EINVAL
+    with pytest.raises(B2QError) as e:
+        m.forward([1, 2], 15)  # beyond the KV capacity
+    assert e.value.status == EINVAL
+    incomplete = model.StandardNativeEngine(engine, TOY, max_seq=16)
+    with pytest.raises(B2QError):
+        incomplete.finalize()  # tensors missing
+    engine.check_device_error()
