@@ -184,6 +184,53 @@ def cpu_decode_rate(orc, cfg, host, steps: int, warmup: int, threads: int) -> di
                       f"{threads} threads (OpenMP), quantised-x AVX2/FMA matvecs"}
 
 
+GEMV_SHAPES = {  # key: (ggml type, n, k, copies rotated to exceed L2)
+    "q4k_14336x4096": (12, 14336, 4096, 24), "q4k_4096x14336": (12, 4096, 14336, 24),
+    "q4k_4096x4096": (12, 4096, 4096, 48), "q4k_1024x4096": (12, 1024, 4096, 96),
+    "q6k_128256x4096": (14, 128256, 4096, 2), "q6k_4096x14336": (14, 4096, 14336, 16),
+    "q8_0_4096x4096": (8, 4096, 4096, 48),
+}
+
+
+def time_gemv_shape(engine, synth, key, seed, dev, sp, copies=None, reps=None):
+    import torch
+    t, n, k, cp = GEMV_SHAPES[key]
+    copies = copies or cp
+    raw = synth.tensor_rows(t, n, k, seed, 900)
+    bufs = [engine.try_upload_weight(raw, t, n, k) for _ in range(copies)]
+    x = torch.randn(k, device=dev)
+    engine.time_gemv(bufs, x.data_ptr(), k, 2, sp)  # warm-up
+    reps = reps or max(2, 400 // copies)
+    ms_l = engine.time_gemv(bufs, x.data_ptr(), k, reps, sp)
+    alg = n * raw.shape[1] + 4 * k + 4 * n
+    for b in bufs:
+        b.free()
+    return ms_l, alg
+
+
+def run_gemv_only(args):
+    """One GEMV shape, its weights rotated over `--copies` copies: the
+    workload of the kernel profiles (ncu) under profiles/."""
+    import torch
+    load_pkg()
+    from hf_llm_b200 import build as bld
+    bld.build()
+    from hf_llm_b200 import synth
+    from hf_llm_b200.engine import CudaEngine
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    engine = CudaEngine(0)
+    stream = torch.cuda.Stream(device=dev)
+    ms_l, alg = time_gemv_shape(engine, synth, args.gemv_only, args.seed, dev, stream.cuda_stream,
+                                args.copies, args.reps)
+    peak, kind = measured_peaks()
+    gbs = alg / (ms_l * 1e-3) / 1e9
+    print(json.dumps({"gemv": args.gemv_only, "us_per_launch": round(ms_l * 1000, 3),
+                      "algorithmic_bytes": alg, "GBps": round(gbs, 1), "frac": round(gbs / peak, 4),
+                      "peak": peak, "peak_kind": kind, "copies": args.copies, "reps": args.reps}))
+    return 0
+
+
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -220,11 +267,18 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--no-gemv-shapes", action="store_true", help="skip the per-shape GEMV timings")
+    ap.add_argument("--gemv-only", default=None,
+                    help="time one GEMV shape only (e.g. q4k_14336x4096), for kernel profiling")
+    ap.add_argument("--copies", type=int, default=24, help="weight copies rotated by --gemv-only")
+    ap.add_argument("--reps", type=int, default=20, help="rotations timed by --gemv-only")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.gemv_only:
+        return run_gemv_only(args)
 
     import torch
     pkg = load_pkg()
@@ -286,12 +340,14 @@ def main():
     launches0 = engine.kernel_launches()
     with ClockSampler(local) as clk:
         torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_push("decode")
         ev0.record(stream)
         for _ in range(args.steps):
             step(pos)
             pos += 1
         ev1.record(stream)
         ev1.synchronize()
+        torch.cuda.nvtx.range_pop()
     launches = engine.kernel_launches() - launches0
     ms = ev0.elapsed_time(ev1)
     if dist:
@@ -325,30 +381,18 @@ def main():
     roof = None
     gemv_shapes = {}
     if rank == 0:
-        shapes = [("q4k_14336x4096", 12, 14336, 4096, 24), ("q4k_4096x14336", 12, 4096, 14336, 24),
-                  ("q4k_4096x4096", 12, 4096, 4096, 48), ("q4k_1024x4096", 12, 1024, 4096, 96),
-                  ("q6k_128256x4096", 14, 128256, 4096, 2), ("q8_0_4096x4096", 8, 4096, 4096, 48)]
-        for key, t, n, k, copies in shapes:
-            raw = synth.tensor_rows(t, n, k, args.seed, 900)
-            bufs = [engine.try_upload_weight(raw, t, n, k) for _ in range(copies)]
-            x = torch.randn(k, device=dev)
-            engine.time_gemv(bufs, x.data_ptr(), k, 2, sp)  # warm-up
-            reps = max(2, 400 // copies)
-            ms_l = engine.time_gemv(bufs, x.data_ptr(), k, reps, sp)
-            alg = n * raw.shape[1] + 4 * k + 4 * n
+        keys = ["q4k_14336x4096"] if args.no_gemv_shapes else list(GEMV_SHAPES)
+        for key in keys:
+            ms_l, alg = time_gemv_shape(engine, synth, key, args.seed, dev, sp)
             gemv_shapes[key] = {"us": round(ms_l * 1000, 3), "GBps": round(alg / (ms_l * 1e-3) / 1e9, 1),
                                 "bytes": alg}
             if key == "q4k_14336x4096":
                 ach = alg / (ms_l * 1e-3) / 1e9
-                traffic = profile_traffic()
                 roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                        "frac": round(ach / peak, 4), "traffic": traffic,
+                        "frac": round(ach / peak, 4), "traffic": profile_traffic(),
                         "kernel": "gemv_kernel (Q4_K, 14336x4096)",
                         "algorithmic_bytes_per_launch": alg, "peak_kind": peak_kind,
                         "launch_us": round(ms_l * 1000, 3)}
-            for b in bufs:
-                b.free()
-            del bufs
     # decode-step bandwidth: weights + KV read per token
     kv_bytes = cfg["n_layers"] * 2 * cfg["n_kv_heads"] * cfg["head_dim"] * 2 * (args.prefill + args.warmup +
                                                                                   args.steps // 2)

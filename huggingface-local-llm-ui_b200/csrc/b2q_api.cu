@@ -72,16 +72,19 @@ cudaError_t xq_alloc(XQBuf* b, int m, int k) {
   b->k = k;
   b->kpad = round_up_int(k, 256);
   const size_t nq = (size_t)m * b->kpad;
-  const size_t bq = align_up(nq * 2, 256), bs = align_up(nq / 32 * 4, 256),
+  const size_t bq = align_up(nq * 2, 256), bs = align_up(nq / 64 * 4, 256),
                b16 = align_up(nq / 16 * 4, 256);
-  cudaError_t err = cudaMalloc(&b->mem, bq + 2 * bs + b16);
+  cudaError_t err = cudaMalloc(&b->mem, bq + bs + b16);
   if (err != cudaSuccess) return err;
-  cudaMemset(b->mem, 0, bq + 2 * bs + b16);
+  err = cudaMemset(b->mem, 0, bq + bs + b16);
+  // the memset runs on the legacy stream, which does not order with the
+  // library's non-blocking streams: finish it before anyone uses the buffer
+  if (err == cudaSuccess) err = cudaDeviceSynchronize();
+  if (err != cudaSuccess) return err;
   uint8_t* p = static_cast<uint8_t*>(b->mem);
   b->x.q = reinterpret_cast<int16_t*>(p);
   b->x.scale = reinterpret_cast<float*>(p + bq);
-  b->x.fsum = reinterpret_cast<float*>(p + bq + bs);
-  b->x.s16 = reinterpret_cast<int32_t*>(p + bq + 2 * bs);
+  b->x.s16 = reinterpret_cast<int32_t*>(p + bq + bs);
   b->x.kpad = b->kpad;
   return cudaSuccess;
 }
@@ -94,29 +97,48 @@ void xq_free(XQBuf* b) {
 // ---------------------------------------------------------------------------
 // GEMV launch planning
 // ---------------------------------------------------------------------------
-template <int R, int WK, int MT, int EPI>
+constexpr int kStageMax = 40 * 1024;  // two tiles per stage when they fit
+
+template <int MT, int EPI>
 static cudaError_t launch_gemv_t(b2q_engine* e, GemvArgs& a, cudaStream_t st, bool pdl) {
-  constexpr int RO = (EPI == kEpiSwiglu) ? R / 2 : R;
-  constexpr int rows_per_cta = (8 / WK) * RO;
-  int tiles = 0;
+  constexpr bool kPair = EPI == kEpiSwiglu;
+  // bytes per segment -> share of the persistent grid (one CTA per SM)
+  double total = 0.0;
+  double bytes[kMaxSegs];
+  int slot = 0;
   for (int s = 0; s < a.nseg; ++s) {
-    a.seg[s].tile0 = tiles;
-    tiles += (a.seg[s].rows_out + rows_per_cta - 1) / rows_per_cta;
+    const TileLayout& L = a.seg[s].w.L;
+    const int tb = (int)tile_bytes(L);
+    a.seg[s].nr = (kPair || 2 * tb <= kStageMax) ? 2 : 1;
+    slot = std::max(slot, tb * a.seg[s].nr);
+    bytes[s] = (double)L.G * L.C * tb * (kPair ? 2 : 1);
+    total += bytes[s];
   }
-  a.tiles_total = tiles;
-  if (tiles == 0) return cudaSuccess;
-  const size_t smem = gemv_smem_bytes(a.kpad, MT);
-  auto kern = gemv_kernel<R, WK, MT, EPI>;
+  int cta = 0, rows_cap = 8;
+  for (int s = 0; s < a.nseg; ++s) {
+    GemvSeg& g = a.seg[s];
+    int n = (int)((double)e->num_sms * bytes[s] / total + 0.5);
+    n = std::max(1, std::min(n, g.w.L.G));
+    g.cta0 = cta;
+    g.ncta = n;
+    cta += n;
+    rows_cap = std::max(rows_cap, gemv_rows_cap(g.w.L.G, n));
+  }
+  if (cta == 0) return cudaSuccess;
+  a.rows_cap = rows_cap;
+  const size_t xb = gemv_x_bytes(a.kpad, MT);
+  const size_t rb = (size_t)2 * (kPair ? 2 : 1) * rows_cap * MT * sizeof(float);
+  if (xb + rb + 2 * (size_t)slot > kGemvSmemBudget) return cudaErrorInvalidConfiguration;
+  const int ns = (int)std::min<size_t>(kGemvMaxStages, (kGemvSmemBudget - xb - rb) / (size_t)slot);
+  a.ns = ns;
+  a.slot_bytes = slot;
+  const size_t smem = xb + (size_t)ns * slot + rb;
+  auto kern = gemv_kernel<MT, EPI>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
-  int occ = 0;
-  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, smem);
-  if (err != cudaSuccess) return err;
-  if (occ < 1) occ = 1;
-  const int grid = std::min(tiles, e->num_sms * occ);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(256);
+  cfg.gridDim = dim3(cta);
+  cfg.blockDim = dim3(kGemvThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -128,73 +150,19 @@ static cudaError_t launch_gemv_t(b2q_engine* e, GemvArgs& a, cudaStream_t st, bo
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-// Pick the split of the 8 warps of a CTA over rows (R rows per warp, WK
-// warps per row group) so that the persistent grid has enough tiles.
-static int pick_wk(b2q_engine* e, const GemvArgs& a, int R, int RO) {
-  int maxU = 1 << 30;
-  for (int s = 0; s < a.nseg; ++s) maxU = std::min(maxU, a.seg[s].w.U);
-  const int cand[4] = {1, 2, 4, 8};
-  int best = 1;
-  for (int i = 0; i < 4; ++i) {
-    const int wk = cand[i];
-    if (wk > 1 && maxU < 32 * wk) break;  // every warp keeps all 32 lanes busy
-    best = wk;
-    int tiles = 0;
-    const int rpc = (8 / wk) * RO;
-    for (int s = 0; s < a.nseg; ++s) tiles += (a.seg[s].rows_out + rpc - 1) / rpc;
-    if (tiles >= 2 * e->num_sms) break;
-  }
-  (void)R;
-  return best;
-}
-
 cudaError_t launch_gemv(b2q_engine* e, GemvArgs& a, int epi, int mt, cudaStream_t st, bool pdl) {
-  if (epi == kEpiSwiglu) {
-    const int wk = pick_wk(e, a, 2, 1);
-    switch (wk) {
-      case 1: return launch_gemv_t<2, 1, 1, kEpiSwiglu>(e, a, st, pdl);
-      case 2: return launch_gemv_t<2, 2, 1, kEpiSwiglu>(e, a, st, pdl);
-      case 4: return launch_gemv_t<2, 4, 1, kEpiSwiglu>(e, a, st, pdl);
-      default: return launch_gemv_t<2, 8, 1, kEpiSwiglu>(e, a, st, pdl);
-    }
-  }
-  if (mt == 1) {
-    const int wk = pick_wk(e, a, 2, 2);
-    if (epi == kEpiStore) {
-      switch (wk) {
-        case 1: return launch_gemv_t<2, 1, 1, kEpiStore>(e, a, st, pdl);
-        case 2: return launch_gemv_t<2, 2, 1, kEpiStore>(e, a, st, pdl);
-        case 4: return launch_gemv_t<2, 4, 1, kEpiStore>(e, a, st, pdl);
-        default: return launch_gemv_t<2, 8, 1, kEpiStore>(e, a, st, pdl);
-      }
-    } else {
-      switch (wk) {
-        case 1: return launch_gemv_t<2, 1, 1, kEpiAdd>(e, a, st, pdl);
-        case 2: return launch_gemv_t<2, 2, 1, kEpiAdd>(e, a, st, pdl);
-        case 4: return launch_gemv_t<2, 4, 1, kEpiAdd>(e, a, st, pdl);
-        default: return launch_gemv_t<2, 8, 1, kEpiAdd>(e, a, st, pdl);
-      }
-    }
-  }
-  // multi-token passes (prefill through the GEMV path)
-  if (epi == kEpiStore) {
-    if (mt == 2) return launch_gemv_t<2, 1, 2, kEpiStore>(e, a, st, pdl);
-    if (mt == 4) return launch_gemv_t<2, 1, 4, kEpiStore>(e, a, st, pdl);
-    return launch_gemv_t<2, 1, 8, kEpiStore>(e, a, st, pdl);
-  }
-  if (mt == 2) return launch_gemv_t<2, 1, 2, kEpiAdd>(e, a, st, pdl);
-  if (mt == 4) return launch_gemv_t<2, 1, 4, kEpiAdd>(e, a, st, pdl);
-  return launch_gemv_t<2, 1, 8, kEpiAdd>(e, a, st, pdl);
+  if (epi == kEpiSwiglu) return launch_gemv_t<1, kEpiSwiglu>(e, a, st, pdl);
+  if (epi == kEpiStore) return mt == 1 ? launch_gemv_t<1, kEpiStore>(e, a, st, pdl)
+                                       : launch_gemv_t<2, kEpiStore>(e, a, st, pdl);
+  return mt == 1 ? launch_gemv_t<1, kEpiAdd>(e, a, st, pdl) : launch_gemv_t<2, kEpiAdd>(e, a, st, pdl);
 }
 
-// Largest token count per GEMV pass whose staged activations fit in shared
-// memory next to the kernel's static buffers.
+// Largest token count per GEMV pass: each consumer lane keeps the
+// activations of every token of the pass in registers (32 per token), so
+// passes carry at most two tokens; larger prompts loop over passes.
 int gemv_max_mt(int kpad) {
-  const size_t budget = 200 * 1024;
-  if (gemv_smem_bytes(kpad, 8) <= budget) return 8;
-  if (gemv_smem_bytes(kpad, 4) <= budget) return 4;
-  if (gemv_smem_bytes(kpad, 2) <= budget) return 2;
-  return 1;
+  const size_t budget = kGemvSmemBudget - 4 * (size_t)(8 * 3360);
+  return gemv_x_bytes(kpad, 2) <= budget ? 2 : 1;
 }
 
 // Run y = W x for all m tokens of an XQ buffer, in passes of MT tokens.
@@ -204,11 +172,7 @@ cudaError_t run_gemv(b2q_engine* e, const GemvSeg* segs, int nseg, const XQBuf& 
   int t = 0;
   const int mtmax = (epi == kEpiSwiglu) ? 1 : gemv_max_mt(xq.kpad);
   while (t < m) {
-    int mt = 1;
-    const int left = m - t;
-    if (mtmax >= 8 && left >= 8) mt = 8;
-    else if (mtmax >= 4 && left >= 4) mt = 4;
-    else if (mtmax >= 2 && left >= 2) mt = 2;
+    const int mt = (mtmax >= 2 && m - t >= 2) ? 2 : 1;
     GemvArgs a;
     memset(&a, 0, sizeof a);
     a.nseg = nseg;
@@ -218,7 +182,6 @@ cudaError_t run_gemv(b2q_engine* e, const GemvSeg* segs, int nseg, const XQBuf& 
     }
     a.xq = xq.x.q;
     a.xscale = xq.x.scale;
-    a.xfsum = xq.x.fsum;
     a.xs16 = xq.x.s16;
     a.kpad = xq.kpad;
     a.t0 = t;
@@ -356,40 +319,17 @@ b2q_status b2q_upload_weight(b2q_engine* e, const void* bytes, size_t len, int d
   w->k = k;
   w->gguf_bytes = need;
   WeightDev& v = w->view;
-  v.dtype = dtype;
-  v.n = (int)n;
-  v.k = (int)k;
-  v.nb = (int)nb;
-  size_t sz_qs = 0, sz_aux = 0, sz_aux2 = 0;
-  if (dtype == kQ4_K) {
-    v.U = (int)(k / 64);
-    v.row_qs = (int64_t)v.U * 32;
-    sz_qs = (size_t)n * v.row_qs;
-    sz_aux = (size_t)n * v.U * 4;
-  } else if (dtype == kQ6_K) {
-    v.U = (int)(k / 64);
-    v.row_qs = (int64_t)v.U * 48;
-    sz_qs = (size_t)n * v.row_qs;
-    sz_aux = (size_t)n * v.U * 4;
-    sz_aux2 = (size_t)n * nb * 2;
-  } else {  // Q8_0
-    v.U = (int)nb;
-    v.row_qs = (int64_t)v.U * 32;
-    sz_qs = (size_t)n * v.row_qs;
-    sz_aux = (size_t)n * v.U * 2;
-  }
-  const size_t o_aux = align_up(sz_qs, 256), o_aux2 = o_aux + align_up(sz_aux, 256);
-  const size_t total = o_aux2 + align_up(std::max<size_t>(sz_aux2, 16), 256);
+  v.L = make_tile_layout(dtype, n, k);
+  const size_t total = (size_t)v.L.G * v.L.C * (size_t)tile_bytes(v.L);
   cudaError_t err = cudaMalloc(&w->mem, total);
   if (err != cudaSuccess) {
     delete w;
     return cuda_error(err, "b2q_upload_weight: cudaMalloc");
   }
+  cudaMemsetAsync(w->mem, 0, total, e->stream);  // padding units / rows stay zero
   w->mem_bytes = total;
   uint8_t* base = static_cast<uint8_t*>(w->mem);
-  v.qs = base;
-  v.aux = base + o_aux;
-  v.aux2 = base + o_aux2;
+  v.base = base;
   // stage the raw bytes on the device, then repack
   cudaPointerAttributes pa;
   const bool is_dev = cudaPointerGetAttributes(&pa, bytes) == cudaSuccess &&
@@ -408,19 +348,15 @@ b2q_status b2q_upload_weight(b2q_engine* e, const void* bytes, size_t len, int d
     err = cudaMemcpyAsync(raw, bytes, need, cudaMemcpyHostToDevice, e->stream);
   }
   if (err == cudaSuccess) {
-    const int64_t units = n * v.U;
+    const int64_t units = n * (int64_t)v.L.U;
     const int blocks = (int)std::min<int64_t>((units + 255) / 256, 65535);
     const uint8_t* r8 = static_cast<const uint8_t*>(raw);
     if (dtype == kQ4_K)
-      repack_q4k_kernel<<<blocks, 256, 0, e->stream>>>(r8, n, (int)nb, base,
-                                                       reinterpret_cast<uint32_t*>(base + o_aux));
+      repack_q4k_kernel<<<blocks, 256, 0, e->stream>>>(r8, v.L, base);
     else if (dtype == kQ6_K)
-      repack_q6k_kernel<<<blocks, 256, 0, e->stream>>>(r8, n, (int)nb, base,
-                                                       reinterpret_cast<uint32_t*>(base + o_aux),
-                                                       reinterpret_cast<uint16_t*>(base + o_aux2));
+      repack_q6k_kernel<<<blocks, 256, 0, e->stream>>>(r8, v.L, base);
     else
-      repack_q80_kernel<<<blocks, 256, 0, e->stream>>>(r8, n, (int)nb, base,
-                                                       reinterpret_cast<uint16_t*>(base + o_aux));
+      repack_q80_kernel<<<blocks, 256, 0, e->stream>>>(r8, v.L, base);
     launch_counted(e, 1);
     err = cudaGetLastError();
     if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
@@ -583,7 +519,6 @@ static b2q_status ffn_core(b2q_engine* e, const b2q_weight* gate, const b2q_weig
     a.seg[0] = sg;
     a.xq = e->ws_xq.x.q;
     a.xscale = e->ws_xq.x.scale;
-    a.xfsum = e->ws_xq.x.fsum;
     a.xs16 = e->ws_xq.x.s16;
     a.kpad = e->ws_xq.kpad;
     a.t0 = t;

@@ -3,22 +3,38 @@
 // y[t][r] = sum_c dequant(W)[r][c] * x[t][c] for t in [0, MT).
 //
 // Design (HBM-bound integer/byte work; no tensor cores):
-//  * Weights stream from HBM as 16-byte vector loads, coalesced across the
-//    warp: lane l of a warp reads unit u = l + 32*j of each of its R rows, and
-//    the repacked layout puts the 16-byte pieces of consecutive units next to
-//    each other.  A unit is 64 weights (Q4_K, Q6_K) or 32 (Q8_0).
-//  * The activation x arrives pre-quantised to int16 per 32-element block
-//    (quant.cuh) and is staged once per CTA into shared memory with a bulk
-//    async copy; all R rows of a lane reuse each shared-memory read.
+//  * Weights are stored tiled (quant.cuh): a tile is 8 rows x one k-chunk
+//    of <= 64 units and is one contiguous byte range.
+//  * One persistent CTA per SM owns a contiguous range of 8-row groups of
+//    one weight (segment).  A producer warp streams the CTA's tiles into a
+//    shared-memory ring with 1-D bulk async copies (the TMA engine), one copy
+//    per stage.  Weight copies are issued before the kernel waits for its
+//    predecessor (programmatic dependent launch): weights never depend on an
+//    earlier kernel, so the first stages stream while the previous kernel
+//    drains.
+//  * The CTA walks its tiles chunk-major: for each k-chunk c, every 8-row
+//    group it owns.  A stage holds NR = 2 tiles when they fit (two groups, or
+//    the gate and up tiles of the fused SwiGLU), else one.
+//  * Sixteen consumer warps, activation-stationary: warp 2p+h owns row p of
+//    every tile and unit half h (unit u = c*KC + 32h + lane) of the chunk, so
+//    a lane's 64 activations stay in registers for the whole chunk pass and
+//    the steady state reads only weights from shared memory.  Lane -> one
+//    unit of 64 (Q4_K, Q6_K) or 32 (Q8_0) weights.  After each stage every
+//    row partial is reduced across the warp and added into a per-CTA
+//    shared-memory accumulator (one writer per entry, fixed order:
+//    deterministic); the epilogue writes y once at the end.  There is no
+//    CTA-wide barrier in the steady state.
+//  * The activation arrives pre-quantised to int16 per 64-element block
+//    (quant.cuh) in a swizzled layout that makes every lane pattern below
+//    bank-conflict-free, and is staged once per CTA.
 //  * The inner product is integer: dp2a multiplies two int16 activations by
-//    two weight bytes and accumulates in int32.  Q4_K nibbles are masked in
+//    two weight bytes with int32 accumulation.  Q4_K nibbles are masked in
 //    place (low nibbles as 0..15, high nibbles as 16*q, shifted after the
-//    sum), Q6_K codes are rebuilt from ql/qh as unsigned 0..63 with the -32
-//    offset applied through the precomputed 16-element sums.  Per 32-block
-//    the int32 partial is scaled once in f32 by d * sub-scale * x-scale.
-//  * The grid is persistent (CTAs = SMs x occupancy) and walks row tiles of
-//    one or more segments (weights sharing the same x); a segment may pair
-//    two weights (gate/up) for a fused SwiGLU epilogue.
+//    sum); Q6_K codes are rebuilt from ql/qh as unsigned 0..63 and the -32
+//    offset is applied with the precomputed 16-element activation sums.  The
+//    sub-block scales and mins are applied in int32 too; each unit ends with
+//    one or two int->f32 conversions scaled by d (and dmin) and the
+//    activation block scale.
 #pragma once
 
 #include "quant.cuh"
@@ -27,13 +43,15 @@ namespace b2q {
 
 enum : int { kEpiStore = 0, kEpiAdd = 1, kEpiSwiglu = 2 };
 
+constexpr int kGemvConsumerWarps = 16;  // two per row of an 8-row tile
+constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
+constexpr int kGemvMaxStages = 10;
+constexpr int kGemvSmemBudget = 225 * 1024;
+
 // Device view of a repacked weight.
 struct WeightDev {
-  const uint8_t* qs;    // quant stream [n][S][U][16]
-  const uint8_t* aux;   // Q4_K hdr u32 [n][U]; Q6_K scale words u32 [n][U]; Q8_0 d u16 [n][U]
-  const uint8_t* aux2;  // Q6_K d u16 [n][nb]
-  int dtype, n, k, U, nb;
-  int64_t row_qs;       // bytes per row of the quant stream
+  const uint8_t* base;  // tiles, (group, chunk) major
+  TileLayout L;
 };
 
 struct GemvSeg {
@@ -41,20 +59,25 @@ struct GemvSeg {
   WeightDev w2;      // up (SwiGLU only)
   float* y;          // output: y[t * ldy + row]
   int ldy;
-  int tile0;         // first global tile of this segment
   int rows_out;      // output rows (n)
+  int cta0, ncta;    // CTAs [cta0, cta0 + ncta) own this segment
+  int nr;            // 8-row tiles per stage (1 or 2; SwiGLU: gate + up = 2)
 };
+
+// Most rows one CTA may own (sizes the shared-memory row accumulators).
+__host__ __device__ inline int gemv_rows_cap(int G, int ncta) { return ((G + ncta - 1) / ncta) * 8; }
 
 constexpr int kMaxSegs = 4;
 
 struct GemvArgs {
   GemvSeg seg[kMaxSegs];
   int nseg;
-  int tiles_total;
+  int ns;              // pipeline stages
+  int slot_bytes;      // bytes per stage slot
+  int rows_cap;        // max rows per CTA over the segments
   // quantised activations, tokens [t0, t0 + MT)
   const int16_t* xq;
   const float* xscale;
-  const float* xfsum;
   const int32_t* xs16;
   int kpad;
   int t0;
@@ -64,361 +87,402 @@ struct GemvArgs {
 struct SX {
   const int16_t* q;
   const float* scale;
-  const float* fsum;
   const int32_t* s16;
   int kpad;
 };
 
-__host__ __device__ inline size_t gemv_smem_bytes(int kpad, int mt) {
-  return (size_t)mt * kpad * 2 + (size_t)mt * (kpad / 32) * 8 + (size_t)mt * (kpad / 16) * 4;
+__host__ __device__ inline size_t gemv_x_bytes(int kpad, int mt) {
+  return (size_t)mt * kpad * 2 + (size_t)mt * (kpad / 64) * 4 + (size_t)mt * (kpad / 16) * 4;
+}
+
+__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// Per-lane activation swizzle phase.  A consumer lane processes units
+// u = c*KC + 32*h + lane with KC a multiple of 8 (16 for Q8_0), so the
+// low bits of every activation group it touches depend only on the lane:
+// the chunk permutation (xswz_f) is a per-lane constant, precomputed as the
+// byte-offset xor mask F = xswz_f(...) << 4.
+struct XPhase {
+  int f4;       // Q4_K: group u
+  int f6a, f6b; // Q6_K: group 4b+2h and 4b+2h+1
+  int f8;       // Q8_0: group u >> 1
+};
+
+__device__ __forceinline__ XPhase make_xphase(int lane) {
+  XPhase p;
+  p.f4 = xswz_f(lane & 7) << 4;
+  const int g6 = 4 * ((lane >> 2) & 1) + 2 * ((lane >> 1) & 1);
+  p.f6a = xswz_f(g6) << 4;
+  p.f6b = xswz_f(g6 + 1) << 4;
+  p.f8 = xswz_f((lane >> 1) & 7) << 4;
+  return p;
+}
+
+// 16-byte chunk c of the 64-element group at byte address `gb` (shared
+// memory), given the xor mask F of that group.
+__device__ __forceinline__ int4 xld(const uint8_t* gb, int c, int F) {
+  return *reinterpret_cast<const int4*>(gb + ((c << 4) ^ F));
 }
 
 // ---------------------------------------------------------------------------
-// Q4_K
+// Activations of one unit held in registers (x-stationary): the 64 int16
+// values of activation block `u` as 8 x 16 bytes, its scale and its
+// 16-element sums.
 // ---------------------------------------------------------------------------
-struct FmtQ4K {
-  struct Reg { uint4 a, b; uint32_t h; };
-  __device__ __forceinline__ static void zero(Reg& r) {
-    r.a = make_uint4(0, 0, 0, 0); r.b = r.a; r.h = 0;
-  }
-  __device__ __forceinline__ static void load(Reg& r, const WeightDev& w, int row, int u, uint64_t pol) {
-    const uint8_t* base = w.qs + (int64_t)row * w.row_qs;
-    r.a = ldg_stream128(base + (int64_t)u * 16, pol);
-    r.b = ldg_stream128(base + (int64_t)(w.U + u) * 16, pol);
-    r.h = ldg_stream32(w.aux + ((int64_t)row * w.U + u) * 4, pol);
-  }
+struct XUnit {
+  int4 v[8];
+  float xs;      // Q4_K / Q8_0: scale of the unit's block
+  float2 xs2;    // Q6_K: scales of its two blocks
+  int4 s16;      // Q4_K: sums of the 4 quarters; Q6_K: .x..w = sums of groups 0..3
+};
 
-#define B2Q_Q4K_WORD(W, XA, XB, YA, YB)                       \
-  {                                                           \
+// Q4_K unit u = activation block u: chunks 0..7 of group u.
+__device__ __forceinline__ void xload_q4k(XUnit& X, const SX& sx, int t, int u, int F) {
+  const uint8_t* gb = reinterpret_cast<const uint8_t*>(sx.q + (int64_t)t * sx.kpad) + u * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) X.v[c] = xld(gb, c, F);
+  X.xs = sx.scale[t * (sx.kpad >> 6) + u];
+  X.s16 = *reinterpret_cast<const int4*>(sx.s16 + t * (sx.kpad >> 4) + 4 * u);
+}
+
+// Q6_K unit u = 4b + 2h + s: group g = 16 elements of block grp0 + (g >> 1),
+// chunks 2s + 4(g & 1) and the next one.
+__device__ __forceinline__ void xload_q6k(XUnit& X, const SX& sx, int t, int u, int Fa, int Fb) {
+  const int s = u & 1;
+  const int grp0 = (u >> 2) * 4 + ((u >> 1) & 1) * 2;
+  const uint8_t* gb0 = reinterpret_cast<const uint8_t*>(sx.q + (int64_t)t * sx.kpad) + grp0 * 128;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint8_t* gb = gb0 + (g >> 1) * 128;
+    const int F = (g >> 1) ? Fb : Fa;
+    const int c0 = 2 * s + 4 * (g & 1);
+    X.v[2 * g] = xld(gb, c0, F);
+    X.v[2 * g + 1] = xld(gb, c0 + 1, F);
+  }
+  X.xs2 = *reinterpret_cast<const float2*>(sx.scale + t * (sx.kpad >> 6) + grp0);
+  const int32_t* q16 = sx.s16 + t * (sx.kpad >> 4) + 4 * grp0 + s;
+  X.s16 = make_int4(32 * q16[0], 32 * q16[2], 32 * q16[4], 32 * q16[6]);
+}
+
+// Q8_0 unit u = 32 elements: chunks (u & 1) * 4 .. +3 of group u >> 1.
+__device__ __forceinline__ void xload_q80(XUnit& X, const SX& sx, int t, int u, int F) {
+  const uint8_t* gb = reinterpret_cast<const uint8_t*>(sx.q + (int64_t)t * sx.kpad) + (u >> 1) * 128;
+  const int c0 = (u & 1) * 4;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) X.v[c] = xld(gb, c0 + c, F);
+  X.xs = sx.scale[t * (sx.kpad >> 6) + (u >> 1)];
+}
+
+// ---------------------------------------------------------------------------
+// Per-row unit kernels.  rc: row-chunk base of the row in shared memory;
+// ul: unit index within the chunk.  Return the row's contribution.
+// ---------------------------------------------------------------------------
+#define B2Q_Q4K_WORD(W, IA, IB, XA, XB, YA, YB)                  \
+  {                                                              \
     const uint32_t lo_ = (W)&0x0F0F0F0Fu, hi_ = (W)&0xF0F0F0F0u; \
-    ia = dp2a_lo_ss((XA), (int)lo_, ia);                      \
-    ia = dp2a_hi_ss((XB), (int)lo_, ia);                      \
-    ib = dp2a_lo_su((YA), hi_, ib);                           \
-    ib = dp2a_hi_su((YB), hi_, ib);                           \
+    IA = dp2a_lo_ss((XA), (int)lo_, IA);                         \
+    IA = dp2a_hi_ss((XB), (int)lo_, IA);                         \
+    IB = dp2a_lo_su((YA), hi_, IB);                              \
+    IB = dp2a_hi_su((YB), hi_, IB);                              \
   }
 
-  template <int R, int MT>
-  __device__ __forceinline__ static void compute(const Reg (&r)[R], int u, const SX& sx,
-                                                 float (&acc)[R][MT]) {
-    const int c = u & 3;
-    const int base = (u >> 2) * 256 + c * 64;
-    const int xb = base >> 5;
-    float d[R], dm[R], ma[R], mb[R];
-    int sca[R], scb[R];
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-      const uint32_t h = r[i].h;
-      sca[i] = (int)(h & 63u);
-      scb[i] = (int)((h >> 6) & 63u);
-      ma[i] = (float)((h >> 12) & 63u);
-      mb[i] = (float)((h >> 18) & 63u);
-      uint32_t dd = (h >> 24) << (8 * c);
-      dd |= __shfl_xor_sync(B2Q_FULL, dd, 1);
-      dd |= __shfl_xor_sync(B2Q_FULL, dd, 2);
-      d[i] = f16_bits_fast(dd & 0xffffu);
-      dm[i] = f16_bits_fast(dd >> 16);
-    }
-#pragma unroll
-    for (int t = 0; t < MT; ++t) {
-      const int4* xv = reinterpret_cast<const int4*>(sx.q + (int64_t)t * sx.kpad + base);
-      const int4 xl0 = xv[0], xl1 = xv[1], xl2 = xv[2], xl3 = xv[3];  // base + 0..31
-      const int4 xh0 = xv[4], xh1 = xv[5], xh2 = xv[6], xh3 = xv[7];  // base + 32..63
-      const int nb32 = sx.kpad >> 5;
-      const float xsa = sx.scale[t * nb32 + xb], xsb = sx.scale[t * nb32 + xb + 1];
-      const float fsa = sx.fsum[t * nb32 + xb], fsb = sx.fsum[t * nb32 + xb + 1];
-#pragma unroll
-      for (int i = 0; i < R; ++i) {
-        int ia = 0, ib = 0;
-        B2Q_Q4K_WORD(r[i].a.x, xl0.x, xl0.y, xh0.x, xh0.y)
-        B2Q_Q4K_WORD(r[i].a.y, xl0.z, xl0.w, xh0.z, xh0.w)
-        B2Q_Q4K_WORD(r[i].a.z, xl1.x, xl1.y, xh1.x, xh1.y)
-        B2Q_Q4K_WORD(r[i].a.w, xl1.z, xl1.w, xh1.z, xh1.w)
-        B2Q_Q4K_WORD(r[i].b.x, xl2.x, xl2.y, xh2.x, xh2.y)
-        B2Q_Q4K_WORD(r[i].b.y, xl2.z, xl2.w, xh2.z, xh2.w)
-        B2Q_Q4K_WORD(r[i].b.z, xl3.x, xl3.y, xh3.x, xh3.y)
-        B2Q_Q4K_WORD(r[i].b.w, xl3.z, xl3.w, xh3.z, xh3.w)
-        const float t1 = xsa * (float)(sca[i] * ia) + xsb * (float)(scb[i] * (ib >> 4));
-        const float t2 = ma[i] * fsa + mb[i] * fsb;
-        acc[i][t] += d[i] * t1 - dm[i] * t2;
-      }
-    }
-  }
+// Q4_K: qs bytes 32c..32c+31 of block b (u = 4b + c); its two 32-element
+// sub-blocks share activation block u.  `csel` = u & 3.
+__device__ __forceinline__ float row_q4k(const uint8_t* rc, int KC, int o_aux, int ul, int csel,
+                                         const XUnit& X) {
+  const uint4 a = lds128(rc + ul * 16);
+  const uint4 b = lds128(rc + (KC + ul) * 16);
+  const uint4 hb = lds128(rc + o_aux + (ul >> 2) * 16);  // the 4 header words of this block
+  const uint32_t h = (csel & 2) ? ((csel & 1) ? hb.w : hb.z) : ((csel & 1) ? hb.y : hb.x);
+  // d | dmin << 16 from the top bytes of the 4 words
+  const uint32_t dd = __byte_perm(__byte_perm(hb.x, hb.y, 0x0073), __byte_perm(hb.z, hb.w, 0x0073), 0x5410);
+  const float d = f16_bits_fast(dd & 0xffffu), dm = f16_bits_fast(dd >> 16);
+  int ia0 = 0, ia1 = 0, ib0 = 0, ib1 = 0;
+  B2Q_Q4K_WORD(a.x, ia0, ib0, X.v[0].x, X.v[0].y, X.v[4].x, X.v[4].y)
+  B2Q_Q4K_WORD(a.y, ia1, ib1, X.v[0].z, X.v[0].w, X.v[4].z, X.v[4].w)
+  B2Q_Q4K_WORD(a.z, ia0, ib0, X.v[1].x, X.v[1].y, X.v[5].x, X.v[5].y)
+  B2Q_Q4K_WORD(a.w, ia1, ib1, X.v[1].z, X.v[1].w, X.v[5].z, X.v[5].w)
+  B2Q_Q4K_WORD(b.x, ia0, ib0, X.v[2].x, X.v[2].y, X.v[6].x, X.v[6].y)
+  B2Q_Q4K_WORD(b.y, ia1, ib1, X.v[2].z, X.v[2].w, X.v[6].z, X.v[6].w)
+  B2Q_Q4K_WORD(b.z, ia0, ib0, X.v[3].x, X.v[3].y, X.v[7].x, X.v[7].y)
+  B2Q_Q4K_WORD(b.w, ia1, ib1, X.v[3].z, X.v[3].w, X.v[7].z, X.v[7].w)
+  // sum_l (d sc q_l - dmin m) x_l over both sub-blocks, in units of xs
+  const int isum = (int)(h & 63u) * (ia0 + ia1) + (int)((h >> 6) & 63u) * ((ib0 + ib1) >> 4);
+  const int msum = (int)((h >> 12) & 63u) * (X.s16.x + X.s16.y) + (int)((h >> 18) & 63u) * (X.s16.z + X.s16.w);
+  return X.xs * (d * (float)isum - dm * (float)msum);
+}
 #undef B2Q_Q4K_WORD
-};
+
+// Q6_K: u = 4b + 2h + s covers l = 16s..16s+15 of half h for all four
+// groups g (weights 128h + 32g + l); groups 0,1 lie in activation block
+// 4b+2h, groups 2,3 in the next one.
+__device__ __forceinline__ float row_q6k(const uint8_t* rc, int KC, int o_aux, int o_aux2, int ul,
+                                         const XUnit& X) {
+  const uint4 va = lds128(rc + ul * 16);
+  const uint4 vb = lds128(rc + (KC + ul) * 16);
+  const uint4 vh = lds128(rc + (2 * KC + ul) * 16);
+  const uint32_t sw = *reinterpret_cast<const uint32_t*>(rc + o_aux + ul * 4);
+  const float d = f16_bits_fast(*reinterpret_cast<const uint16_t*>(rc + o_aux2 + (ul >> 2) * 2));
+  const uint32_t qa[4] = {va.x, va.y, va.z, va.w};
+  const uint32_t qb[4] = {vb.x, vb.y, vb.z, vb.w};
+  const uint32_t qh[4] = {vh.x, vh.y, vh.z, vh.w};
+  int s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t q1 = (qa[j] & 0x0F0F0F0Fu) | ((qh[j] << 4) & 0x30303030u);
+    const uint32_t q2 = (qb[j] & 0x0F0F0F0Fu) | ((qh[j] << 2) & 0x30303030u);
+    const uint32_t q3 = ((qa[j] >> 4) & 0x0F0F0F0Fu) | (qh[j] & 0x30303030u);
+    const uint32_t q4 = ((qb[j] >> 4) & 0x0F0F0F0Fu) | ((qh[j] >> 2) & 0x30303030u);
+    // word j covers elements 4j..4j+3 of each group: chunk j/2 of the pair
+    const int4& x1 = X.v[0 + (j >> 1)];
+    const int4& x2 = X.v[2 + (j >> 1)];
+    const int4& x3 = X.v[4 + (j >> 1)];
+    const int4& x4 = X.v[6 + (j >> 1)];
+    const bool up = (j & 1) != 0;
+    s0[0] = dp2a_lo_ss(up ? x1.z : x1.x, (int)q1, s0[0]);
+    s1[0] = dp2a_hi_ss(up ? x1.w : x1.y, (int)q1, s1[0]);
+    s0[1] = dp2a_lo_ss(up ? x2.z : x2.x, (int)q2, s0[1]);
+    s1[1] = dp2a_hi_ss(up ? x2.w : x2.y, (int)q2, s1[1]);
+    s0[2] = dp2a_lo_ss(up ? x3.z : x3.x, (int)q3, s0[2]);
+    s1[2] = dp2a_hi_ss(up ? x3.w : x3.y, (int)q3, s1[2]);
+    s0[3] = dp2a_lo_ss(up ? x4.z : x4.x, (int)q4, s0[3]);
+    s1[3] = dp2a_hi_ss(up ? x4.w : x4.y, (int)q4, s1[3]);
+  }
+  const int sc0 = (int)(int8_t)(sw & 0xffu), sc1 = (int)(int8_t)((sw >> 8) & 0xffu);
+  const int sc2 = (int)(int8_t)((sw >> 16) & 0xffu), sc3 = (int)(int8_t)(sw >> 24);
+  const int i01 = sc0 * (s0[0] + s1[0] - X.s16.x) + sc1 * (s0[1] + s1[1] - X.s16.y);
+  const int i23 = sc2 * (s0[2] + s1[2] - X.s16.z) + sc3 * (s0[3] + s1[3] - X.s16.w);
+  return d * (X.xs2.x * (float)i01 + X.xs2.y * (float)i23);
+}
+
+// Q8_0: one block (32 weights).
+__device__ __forceinline__ float row_q80(const uint8_t* rc, int KC, int o_aux, int ul, const XUnit& X) {
+  const uint4 a = lds128(rc + ul * 16);
+  const uint4 b = lds128(rc + (KC + ul) * 16);
+  const float d = f16_bits_fast(*reinterpret_cast<const uint16_t*>(rc + o_aux + ul * 2));
+  int s0 = 0, s1 = 0;
+  s0 = dp2a_lo_ss(X.v[0].x, (int)a.x, s0); s1 = dp2a_hi_ss(X.v[0].y, (int)a.x, s1);
+  s0 = dp2a_lo_ss(X.v[0].z, (int)a.y, s0); s1 = dp2a_hi_ss(X.v[0].w, (int)a.y, s1);
+  s0 = dp2a_lo_ss(X.v[1].x, (int)a.z, s0); s1 = dp2a_hi_ss(X.v[1].y, (int)a.z, s1);
+  s0 = dp2a_lo_ss(X.v[1].z, (int)a.w, s0); s1 = dp2a_hi_ss(X.v[1].w, (int)a.w, s1);
+  s0 = dp2a_lo_ss(X.v[2].x, (int)b.x, s0); s1 = dp2a_hi_ss(X.v[2].y, (int)b.x, s1);
+  s0 = dp2a_lo_ss(X.v[2].z, (int)b.y, s0); s1 = dp2a_hi_ss(X.v[2].w, (int)b.y, s1);
+  s0 = dp2a_lo_ss(X.v[3].x, (int)b.z, s0); s1 = dp2a_hi_ss(X.v[3].y, (int)b.z, s1);
+  s0 = dp2a_lo_ss(X.v[3].z, (int)b.w, s0); s1 = dp2a_hi_ss(X.v[3].w, (int)b.w, s1);
+  return d * (X.xs * (float)(s0 + s1));
+}
 
 // ---------------------------------------------------------------------------
-// Q6_K
-// ---------------------------------------------------------------------------
-struct FmtQ6K {
-  struct Reg { uint4 a, b, c; uint32_t s; uint32_t d; };
-  __device__ __forceinline__ static void zero(Reg& r) {
-    r.a = make_uint4(0, 0, 0, 0); r.b = r.a; r.c = r.a; r.s = 0; r.d = 0;
-  }
-  __device__ __forceinline__ static void load(Reg& r, const WeightDev& w, int row, int u, uint64_t pol) {
-    const uint8_t* base = w.qs + (int64_t)row * w.row_qs;
-    r.a = ldg_stream128(base + (int64_t)u * 16, pol);
-    r.b = ldg_stream128(base + (int64_t)(w.U + u) * 16, pol);
-    r.c = ldg_stream128(base + (int64_t)(2 * w.U + u) * 16, pol);
-    r.s = ldg_stream32(w.aux + ((int64_t)row * w.U + u) * 4, pol);
-    r.d = ldg_stream16(w.aux2 + ((int64_t)row * w.nb + (u >> 2)) * 2, pol);
-  }
-
-  template <int R, int MT>
-  __device__ __forceinline__ static void compute(const Reg (&r)[R], int u, const SX& sx,
-                                                 float (&acc)[R][MT]) {
-    const int base0 = (u >> 2) * 256 + ((u >> 1) & 1) * 128 + (u & 1) * 16;
-    float d[R];
-    int sc[R][4];
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-      d[i] = f16_bits_fast(r[i].d);
-#pragma unroll
-      for (int g = 0; g < 4; ++g) sc[i][g] = (int)(int8_t)((r[i].s >> (8 * g)) & 0xffu);
-    }
-#pragma unroll
-    for (int t = 0; t < MT; ++t) {
-      const int16_t* xt = sx.q + (int64_t)t * sx.kpad;
-      int4 X[4][2];
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const int4* xv = reinterpret_cast<const int4*>(xt + base0 + 32 * g);
-        X[g][0] = xv[0];
-        X[g][1] = xv[1];
-      }
-      const int nb32 = sx.kpad >> 5, nb16 = sx.kpad >> 4;
-      float xs[4];
-      int s16[4];
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        xs[g] = sx.scale[t * nb32 + ((base0 + 32 * g) >> 5)];
-        s16[g] = sx.s16[t * nb16 + ((base0 + 32 * g) >> 4)];
-      }
-#pragma unroll
-      for (int i = 0; i < R; ++i) {
-        int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
-        const uint32_t qa[4] = {r[i].a.x, r[i].a.y, r[i].a.z, r[i].a.w};
-        const uint32_t qb[4] = {r[i].b.x, r[i].b.y, r[i].b.z, r[i].b.w};
-        const uint32_t qh[4] = {r[i].c.x, r[i].c.y, r[i].c.z, r[i].c.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t q1 = (qa[j] & 0x0F0F0F0Fu) | ((qh[j] << 4) & 0x30303030u);
-          const uint32_t q2 = (qb[j] & 0x0F0F0F0Fu) | ((qh[j] << 2) & 0x30303030u);
-          const uint32_t q3 = ((qa[j] >> 4) & 0x0F0F0F0Fu) | (qh[j] & 0x30303030u);
-          const uint32_t q4 = ((qb[j] >> 4) & 0x0F0F0F0Fu) | ((qh[j] >> 2) & 0x30303030u);
-          const int4& x0 = X[0][j >> 1];
-          const int4& x1 = X[1][j >> 1];
-          const int4& x2 = X[2][j >> 1];
-          const int4& x3 = X[3][j >> 1];
-          const bool up = (j & 1) != 0;
-          a0 = dp2a_lo_ss(up ? x0.z : x0.x, (int)q1, a0);
-          a0 = dp2a_hi_ss(up ? x0.w : x0.y, (int)q1, a0);
-          a1 = dp2a_lo_ss(up ? x1.z : x1.x, (int)q2, a1);
-          a1 = dp2a_hi_ss(up ? x1.w : x1.y, (int)q2, a1);
-          a2 = dp2a_lo_ss(up ? x2.z : x2.x, (int)q3, a2);
-          a2 = dp2a_hi_ss(up ? x2.w : x2.y, (int)q3, a2);
-          a3 = dp2a_lo_ss(up ? x3.z : x3.x, (int)q4, a3);
-          a3 = dp2a_hi_ss(up ? x3.w : x3.y, (int)q4, a3);
-        }
-        float f = xs[0] * (float)(sc[i][0] * (a0 - 32 * s16[0]));
-        f += xs[1] * (float)(sc[i][1] * (a1 - 32 * s16[1]));
-        f += xs[2] * (float)(sc[i][2] * (a2 - 32 * s16[2]));
-        f += xs[3] * (float)(sc[i][3] * (a3 - 32 * s16[3]));
-        acc[i][t] += d[i] * f;
-      }
-    }
-  }
-};
-
-// ---------------------------------------------------------------------------
-// Q8_0
-// ---------------------------------------------------------------------------
-struct FmtQ80 {
-  struct Reg { uint4 a, b; uint32_t d; };
-  __device__ __forceinline__ static void zero(Reg& r) {
-    r.a = make_uint4(0, 0, 0, 0); r.b = r.a; r.d = 0;
-  }
-  __device__ __forceinline__ static void load(Reg& r, const WeightDev& w, int row, int u, uint64_t pol) {
-    const uint8_t* base = w.qs + (int64_t)row * w.row_qs;
-    r.a = ldg_stream128(base + (int64_t)u * 16, pol);
-    r.b = ldg_stream128(base + (int64_t)(w.U + u) * 16, pol);
-    r.d = ldg_stream16(w.aux + ((int64_t)row * w.U + u) * 2, pol);
-  }
-  template <int R, int MT>
-  __device__ __forceinline__ static void compute(const Reg (&r)[R], int u, const SX& sx,
-                                                 float (&acc)[R][MT]) {
-    float d[R];
-#pragma unroll
-    for (int i = 0; i < R; ++i) d[i] = f16_bits_fast(r[i].d);
-#pragma unroll
-    for (int t = 0; t < MT; ++t) {
-      const int4* xv = reinterpret_cast<const int4*>(sx.q + (int64_t)t * sx.kpad + u * 32);
-      const int4 x0 = xv[0], x1 = xv[1], x2 = xv[2], x3 = xv[3];
-      const float xs = sx.scale[t * (sx.kpad >> 5) + u];
-#pragma unroll
-      for (int i = 0; i < R; ++i) {
-        int s = 0;
-        s = dp2a_lo_ss(x0.x, (int)r[i].a.x, s); s = dp2a_hi_ss(x0.y, (int)r[i].a.x, s);
-        s = dp2a_lo_ss(x0.z, (int)r[i].a.y, s); s = dp2a_hi_ss(x0.w, (int)r[i].a.y, s);
-        s = dp2a_lo_ss(x1.x, (int)r[i].a.z, s); s = dp2a_hi_ss(x1.y, (int)r[i].a.z, s);
-        s = dp2a_lo_ss(x1.z, (int)r[i].a.w, s); s = dp2a_hi_ss(x1.w, (int)r[i].a.w, s);
-        s = dp2a_lo_ss(x2.x, (int)r[i].b.x, s); s = dp2a_hi_ss(x2.y, (int)r[i].b.x, s);
-        s = dp2a_lo_ss(x2.z, (int)r[i].b.y, s); s = dp2a_hi_ss(x2.w, (int)r[i].b.y, s);
-        s = dp2a_lo_ss(x3.x, (int)r[i].b.z, s); s = dp2a_hi_ss(x3.y, (int)r[i].b.z, s);
-        s = dp2a_lo_ss(x3.z, (int)r[i].b.w, s); s = dp2a_hi_ss(x3.w, (int)r[i].b.w, s);
-        acc[i][t] += d[i] * (xs * (float)s);
-      }
-    }
-  }
-};
-
-// ---------------------------------------------------------------------------
-// Tile driver
+// Kernel
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
-template <class F, int R, int WK, int MT, int EPI>
-__device__ __forceinline__ void gemv_tile(const GemvSeg& sg, int local_tile, int warp, int lane,
-                                          const SX& sx, uint64_t pol, float* red) {
-  constexpr int RG = 8 / WK;                        // row groups per CTA
-  constexpr int RO = (EPI == kEpiSwiglu) ? R / 2 : R;  // output rows per warp
-  const int rg = warp / WK, wk = warp % WK;
-  const int r0 = (local_tile * RG + rg) * RO;
-  const int n = sg.rows_out;
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
-  // row slot -> (weight, row)
-  int rows[R];
-  bool rv[R];
-#pragma unroll
-  for (int i = 0; i < R; ++i) {
-    const int rr = r0 + (i % RO);
-    rows[i] = rr;
-    rv[i] = rr < n;
-  }
-  const WeightDev& wa = sg.w;
-  const WeightDev& wb = (EPI == kEpiSwiglu) ? sg.w2 : sg.w;
-  const int U = wa.U;
-  const int step = 32 * WK;
-  const int nj = (U + step - 1) / step;
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
-  float acc[R][MT];
-#pragma unroll
-  for (int i = 0; i < R; ++i)
-#pragma unroll
-    for (int t = 0; t < MT; ++t) acc[i][t] = 0.0f;
-
-  typename F::Reg cur[R], nxt[R];
-  {
-    const int u = lane + 32 * wk;
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-      if (u < U && rv[i]) F::load(cur[i], (i < RO) ? wa : wb, rows[i], u, pol);
-      else F::zero(cur[i]);
+// The CTA's stages, chunk-major: for chunk c = 0..C-1, the 8-row groups
+// [gb, ge) taken NR at a time (SwiGLU: one group, gate tile + up tile).
+// Iterated with counters only (no division in the loop).
+template <int NR, bool PAIR>
+struct StageIter {
+  int gb, ge, C, NS;
+  int c = 0, g = 0, slot = 0, phase = 0;
+  __device__ __forceinline__ StageIter(int gb_, int ge_, int C_, int NS_) : gb(gb_), ge(ge_), C(C_), NS(NS_) { g = gb; }
+  __device__ __forceinline__ bool done() const { return c >= C || gb >= ge; }
+  __device__ __forceinline__ int ntiles() const { return PAIR ? 2 : ((NR == 2 && g + 1 < ge) ? 2 : 1); }
+  __device__ __forceinline__ void next() {
+    g += (PAIR || NR == 1) ? 1 : 2;
+    if (g >= ge) {
+      g = gb;
+      ++c;
+    }
+    if (++slot == NS) {
+      slot = 0;
+      phase ^= 1;
     }
   }
-  for (int j = 0; j < nj; ++j) {
-    const int u = lane + 32 * wk + step * j;
-    const int un = u + step;
-    if (j + 1 < nj) {
-#pragma unroll
-      for (int i = 0; i < R; ++i) {
-        if (un < U && rv[i]) F::load(nxt[i], (i < RO) ? wa : wb, rows[i], un, pol);
-        else F::zero(nxt[i]);
-      }
-    }
-    F::template compute<R, MT>(cur, u < U ? u : 0, sx, acc);
-    if (j + 1 < nj) {
-#pragma unroll
-      for (int i = 0; i < R; ++i) cur[i] = nxt[i];
-    }
-  }
+};
 
-  // reduce over the warp, then over the WK warps sharing the rows
-#pragma unroll
-  for (int i = 0; i < R; ++i)
-#pragma unroll
-    for (int t = 0; t < MT; ++t) acc[i][t] = warp_sum(acc[i][t]);
-  if (WK > 1) {
-    if (lane == 0) {
-#pragma unroll
-      for (int i = 0; i < R; ++i)
-#pragma unroll
-        for (int t = 0; t < MT; ++t) red[(warp * R + i) * MT + t] = acc[i][t];
-    }
-    __syncthreads();
-    if (wk == 0 && lane == 0) {
-#pragma unroll
-      for (int i = 0; i < R; ++i)
+template <int NR, bool PAIR>
+__device__ __forceinline__ void gemv_producer(const GemvArgs& a, const GemvSeg& sg, int gb, int ge,
+                                              uint8_t* stages, uint64_t* full_bar, uint64_t* empty_bar) {
+  const TileLayout& L = sg.w.L;
+  const uint32_t tb = (uint32_t)tile_bytes(L);
+  int used = 0;
+  for (StageIter<NR, PAIR> it(gb, ge, L.C, a.ns); !it.done(); it.next(), ++used) {
+    if (used >= a.ns && !mbar_wait_bounded(&empty_bar[it.slot], it.phase ^ 1)) break;
+    const int nt = it.ntiles();
+    mbar_arrive_expect_tx(&full_bar[it.slot], tb * nt);
+    uint8_t* sl = stages + (size_t)it.slot * a.slot_bytes;
+    const int64_t t0 = (int64_t)it.g * L.C + it.c;
+    bulk_g2s(sl, sg.w.base + t0 * tb, tb, &full_bar[it.slot]);
+    if (PAIR) bulk_g2s(sl + tb, sg.w2.base + t0 * tb, tb, &full_bar[it.slot]);
+    else if (nt == 2) bulk_g2s(sl + tb, sg.w.base + (t0 + L.C) * tb, tb, &full_bar[it.slot]);
+  }
+}
+
+// Row accumulators in shared memory: racc[h][tile i][row][t], h = unit half.
+template <int MT, int NR, bool PAIR, int EPI>
+__device__ __forceinline__ void gemv_consumer(const GemvArgs& a, const GemvSeg& sg, int gb, int ge,
+                                              uint8_t* stages, uint64_t* full_bar, uint64_t* empty_bar,
+                                              const SX& sx, bool ok, float* racc) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const TileLayout& L = sg.w.L;
+  const uint32_t tb = (uint32_t)tile_bytes(L);
+  const int p = warp >> 1, hf = warp & 1;  // row p of every tile; unit half hf
+  const int rows_cap = a.rows_cap;
+  const int nrows = (ge - gb) * 8;
+  // racc layout: [2 halves][PAIR ? 2 : 1][rows_cap][MT]
+  constexpr int NW = PAIR ? 2 : 1;
+  for (int i = threadIdx.x; i < 2 * NW * rows_cap * MT; i += kGemvConsumerWarps * 32) racc[i] = 0.0f;
+  consumer_sync();
+
+  const XPhase xp = make_xphase(lane);
+  const int lane0 = lane + 32 * hf;
+  const int csel = lane & 3;  // u & 3 for every unit of this lane (KC % 8 == 0)
+  XUnit X[MT];
+  int cur_c = -1;
+  bool uok = false;
+  int ul = 0;
+  for (StageIter<NR, PAIR> it(gb, ge, L.C, a.ns); !it.done(); it.next()) {
+    if (it.c != cur_c) {  // new chunk pass: this lane's activations
+      cur_c = it.c;
+      ul = lane0;
+      const int u = it.c * L.KC + ul;
+      uok = ul < L.KC && u < L.U;
+      if (uok && ok) {
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
-          float v = 0.0f;
-          for (int w2 = 0; w2 < WK; ++w2) v += red[((warp + w2) * R + i) * MT + t];
-          acc[i][t] = v;
+          if (L.dtype == kQ4_K) xload_q4k(X[t], sx, t, u, xp.f4);
+          else if (L.dtype == kQ6_K) xload_q6k(X[t], sx, t, u, xp.f6a, xp.f6b);
+          else xload_q80(X[t], sx, t, u, xp.f8);
         }
-    }
-    __syncthreads();
-  }
-  if (wk == 0 && lane == 0) {
-#pragma unroll
-    for (int i = 0; i < RO; ++i) {
-      if (!rv[i]) continue;
-#pragma unroll
-      for (int t = 0; t < MT; ++t) {
-        float* yp = sg.y + (int64_t)t * sg.ldy + rows[i];
-        if (EPI == kEpiStore) *yp = acc[i][t];
-        else if (EPI == kEpiAdd) *yp += acc[i][t];
-        else *yp = silu_f(acc[i][t]) * acc[i + RO][t];
       }
+    }
+    if (ok) ok = mbar_wait_bounded(&full_bar[it.slot], it.phase);
+    const int nt = it.ntiles();
+    float part[NR][MT];
+#pragma unroll
+    for (int i = 0; i < NR; ++i)
+#pragma unroll
+      for (int t = 0; t < MT; ++t) part[i][t] = 0.0f;
+    if (ok && uok) {
+      const uint8_t* sl = stages + (size_t)it.slot * a.slot_bytes + p * L.rc;
+#pragma unroll
+      for (int i = 0; i < NR; ++i) {
+        if (i >= nt) break;
+        const uint8_t* rc = sl + i * tb;
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+          if (L.dtype == kQ4_K) part[i][t] = row_q4k(rc, L.KC, L.o_aux, ul, csel, X[t]);
+          else if (L.dtype == kQ6_K) part[i][t] = row_q6k(rc, L.KC, L.o_aux, L.o_aux2, ul, X[t]);
+          else part[i][t] = row_q80(rc, L.KC, L.o_aux, ul, X[t]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[it.slot]);  // the stage may be refilled
+#pragma unroll
+    for (int i = 0; i < NR; ++i)
+#pragma unroll
+      for (int t = 0; t < MT; ++t) part[i][t] = warp_sum(part[i][t]);
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < NR; ++i) {
+        if (i >= nt) break;
+        // PAIR: tile 0 = gate, tile 1 = up, same row; else tile i = group g + i
+        const int wsel = PAIR ? i : 0;
+        const int r = (PAIR ? (it.g - gb) : (it.g + i - gb)) * 8 + p;
+        float* dst = racc + ((hf * NW + wsel) * rows_cap + r) * MT;
+#pragma unroll
+        for (int t = 0; t < MT; ++t) dst[t] += part[i][t];
+      }
+    }
+  }
+  consumer_sync();
+  // epilogue: y for every (row, token) of this CTA
+  const int row0 = gb * 8;
+  for (int idx = threadIdx.x; idx < nrows * MT; idx += kGemvConsumerWarps * 32) {
+    const int r = idx / MT, t = idx % MT;
+    const int row = row0 + r;
+    if (row >= L.n) continue;
+    const float v = racc[(0 * NW * rows_cap + r) * MT + t] + racc[(1 * NW * rows_cap + r) * MT + t];
+    float* yp = sg.y + (int64_t)t * sg.ldy + row;
+    if (PAIR) {
+      const float uv = racc[((0 * NW + 1) * rows_cap + r) * MT + t] + racc[((1 * NW + 1) * rows_cap + r) * MT + t];
+      if (ok) *yp = silu_f(v) * uv;
+    } else if (ok) {
+      if (EPI == kEpiAdd) *yp += v;
+      else *yp = v;
     }
   }
 }
 
-template <int R, int WK, int MT, int EPI>
-__global__ void __launch_bounds__(256, 2) gemv_kernel(const __grid_constant__ GemvArgs a) {
+template <int MT, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bar;
-  __shared__ float red[8 * R * MT];
+  __shared__ uint64_t full_bar[kGemvMaxStages], empty_bar[kGemvMaxStages], x_bar;
+  constexpr bool kPair = EPI == kEpiSwiglu;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // segment of this CTA and its contiguous range of 8-row groups
+  int s = 0;
+#pragma unroll
+  for (int q = 1; q < kMaxSegs; ++q)
+    if (q < a.nseg && (int)blockIdx.x >= a.seg[q].cta0) s = q;
+  const GemvSeg& sg = a.seg[s];
+  const TileLayout& L = sg.w.L;
+  const int ci = blockIdx.x - sg.cta0;
+  const int gb = (int)((int64_t)L.G * ci / sg.ncta);
+  const int ge = (int)((int64_t)L.G * (ci + 1) / sg.ncta);
+  const int NS = a.ns;
+
   const int kp = a.kpad;
+  uint8_t* stages = smem + gemv_x_bytes(kp, MT);
+  float* racc = reinterpret_cast<float*>(stages + (size_t)NS * a.slot_bytes);
   SX sx;
   sx.q = reinterpret_cast<const int16_t*>(smem);
   sx.scale = reinterpret_cast<const float*>(smem + (size_t)MT * kp * 2);
-  sx.fsum = sx.scale + MT * (kp / 32);
-  sx.s16 = reinterpret_cast<const int32_t*>(sx.fsum + MT * (kp / 32));
+  sx.s16 = reinterpret_cast<const int32_t*>(sx.scale + MT * (kp / 64));
   sx.kpad = kp;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], kGemvConsumerWarps);
+    }
+    mbar_init(&x_bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  pdl_wait();  // the activations come from the previous kernel
-  if (threadIdx.x == 0) {
-    const uint32_t bq = (uint32_t)(MT * kp * 2), bs = (uint32_t)(MT * (kp / 32) * 4),
-                   b16 = (uint32_t)(MT * (kp / 16) * 4);
-    mbar_arrive_expect_tx(&bar, bq + 2 * bs + b16);
-    bulk_g2s((void*)sx.q, a.xq + (int64_t)a.t0 * kp, bq, &bar);
-    bulk_g2s((void*)sx.scale, a.xscale + (int64_t)a.t0 * (kp / 32), bs, &bar);
-    bulk_g2s((void*)sx.fsum, a.xfsum + (int64_t)a.t0 * (kp / 32), bs, &bar);
-    bulk_g2s((void*)sx.s16, a.xs16 + (int64_t)a.t0 * (kp / 16), b16, &bar);
-  }
-  const bool ok = mbar_wait_bounded(&bar, 0);
-  if (__syncthreads_or(!ok)) return;
-  pdl_launch_dependents();
 
-  const uint64_t pol = make_evict_first_policy();
-  for (int tile = blockIdx.x; tile < a.tiles_total; tile += gridDim.x) {
-    int s = 0;
-#pragma unroll
-    for (int q = 1; q < kMaxSegs; ++q)
-      if (q < a.nseg && tile >= a.seg[q].tile0) s = q;
-    const GemvSeg& sg = a.seg[s];
-    const int lt = tile - sg.tile0;
-    switch (sg.w.dtype) {
-      case kQ4_K: gemv_tile<FmtQ4K, R, WK, MT, EPI>(sg, lt, warp, lane, sx, pol, red); break;
-      case kQ6_K: gemv_tile<FmtQ6K, R, WK, MT, EPI>(sg, lt, warp, lane, sx, pol, red); break;
-      default: gemv_tile<FmtQ80, R, WK, MT, EPI>(sg, lt, warp, lane, sx, pol, red); break;
+  if (warp == kGemvConsumerWarps) {
+    // producer: weights never depend on the previous kernel
+    if (lane == 0) {
+      if (kPair) gemv_producer<2, true>(a, sg, gb, ge, stages, full_bar, empty_bar);
+      else if (sg.nr == 2) gemv_producer<2, false>(a, sg, gb, ge, stages, full_bar, empty_bar);
+      else gemv_producer<1, false>(a, sg, gb, ge, stages, full_bar, empty_bar);
     }
+    return;
   }
+
+  if (threadIdx.x == 0) {
+    pdl_wait();  // the activations come from the previous kernel
+    const uint32_t bq = (uint32_t)(MT * kp * 2), bs = (uint32_t)(MT * (kp / 64) * 4),
+                   b16 = (uint32_t)(MT * (kp / 16) * 4);
+    mbar_arrive_expect_tx(&x_bar, bq + bs + b16);
+    bulk_g2s((void*)sx.q, a.xq + (int64_t)a.t0 * kp, bq, &x_bar);
+    bulk_g2s((void*)sx.scale, a.xscale + (int64_t)a.t0 * (kp / 64), bs, &x_bar);
+    bulk_g2s((void*)sx.s16, a.xs16 + (int64_t)a.t0 * (kp / 16), b16, &x_bar);
+  }
+  const bool ok = mbar_wait_bounded(&x_bar, 0);
+  if (kPair) gemv_consumer<MT, 2, true, EPI>(a, sg, gb, ge, stages, full_bar, empty_bar, sx, ok, racc);
+  else if (sg.nr == 2) gemv_consumer<MT, 2, false, EPI>(a, sg, gb, ge, stages, full_bar, empty_bar, sx, ok, racc);
+  else gemv_consumer<MT, 1, false, EPI>(a, sg, gb, ge, stages, full_bar, empty_bar, sx, ok, racc);
+  if (threadIdx.x == 0) pdl_launch_dependents();
 }
 
 }  // namespace b2q

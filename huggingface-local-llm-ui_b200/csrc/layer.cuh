@@ -12,8 +12,8 @@ constexpr int kHeadDim = 128;
 
 // RMSNorm of each row (rms_norm_rows, inference.rs:1501-1512) fused with the
 // int16 quantisation the next GEMV consumes.  One CTA of 1024 threads per
-// row; thread i owns elements i, i+1024, ... so every warp holds whole
-// 32-element blocks.  `y` (optional) receives the f32 normalised row.
+// row; each warp normalises and quantises whole 64-element blocks (lane i:
+// elements 64j + i and 64j + 32 + i).  `y` (optional) receives the f32 row.
 __global__ void __launch_bounds__(1024) rmsnorm_quant_kernel(
     const float* __restrict__ x, int row_stride, int row0, const float* __restrict__ w, int dim,
     float eps, XQ xq, float* __restrict__ y) {
@@ -34,34 +34,17 @@ __global__ void __launch_bounds__(1024) rmsnorm_quant_kernel(
   }
   __syncthreads();
   const float inv = 1.0f / sqrtf(part[0] / (float)dim + eps);
-  for (int e0 = warp * 32; e0 < xq.kpad; e0 += blockDim.x) {
-    const int e = e0 + lane;
+  const int nw = blockDim.x >> 5;
+  for (int e0 = warp * 64; e0 < xq.kpad; e0 += nw * 64) {
+    const int ea = e0 + lane, eb = e0 + 32 + lane;
     // (x * inv) * w, two separate roundings as the reference computes it
-    const float v = e < dim ? __fmul_rn(__fmul_rn(xr[e], inv), w[e]) : 0.0f;
-    if (y != nullptr && e < dim) y[(int64_t)t * dim + e] = v;
-    // quantise this warp's 32-block from registers
-    float amax = fabsf(v);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(B2Q_FULL, amax, o));
-    int q = 0;
-    float scale = 0.0f;
-    if (amax > 0.0f && amax <= 3.0e38f) {
-      scale = amax / (float)kXMax;
-      q = max(-kXMax, min(kXMax, __float2int_rn(v * ((float)kXMax / amax))));
+    const float va = ea < dim ? __fmul_rn(__fmul_rn(xr[ea], inv), w[ea]) : 0.0f;
+    const float vb = eb < dim ? __fmul_rn(__fmul_rn(xr[eb], inv), w[eb]) : 0.0f;
+    if (y != nullptr) {
+      if (ea < dim) y[(int64_t)t * dim + ea] = va;
+      if (eb < dim) y[(int64_t)t * dim + eb] = vb;
     }
-    const int kp = xq.kpad, j = e0 >> 5;
-    xq.q[(int64_t)t * kp + e] = (int16_t)q;
-    int s = q;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(B2Q_FULL, s, o);
-    const int s_other = __shfl_xor_sync(B2Q_FULL, s, 16);
-    if (lane == 0) {
-      xq.s16[(int64_t)t * (kp / 16) + 2 * j] = s;
-      xq.scale[(int64_t)t * (kp / 32) + j] = scale;
-      xq.fsum[(int64_t)t * (kp / 32) + j] = scale * (float)(s + s_other);
-    } else if (lane == 16) {
-      xq.s16[(int64_t)t * (kp / 16) + 2 * j + 1] = s;
-    }
+    xq_store_block(va, vb, lane, t, e0 >> 6, xq);
   }
   pdl_launch_dependents();
 }
@@ -238,6 +221,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int m, int H
                                     float* __restrict__ out, XQ xq) {
   pdl_wait();
   constexpr int HD = kHeadDim;
+  __shared__ float vals[8 * HD];
   const int g = blockIdx.x, s = blockIdx.y;
   const int h = g * G + threadIdx.x / HD, d = threadIdx.x % HD;
   const int start = *pos_dev;
@@ -254,32 +238,14 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int m, int H
     O += f * pp[z * (HD + 2) + 2 + d];
   }
   const float v = O * (1.0f / fmaxf(L, 1e-12f));
-  const int col = h * HD + d;
-  out[(int64_t)s * H * HD + col] = v;
-  // quantise: every warp holds one 32-block of this row
-  const int lane = threadIdx.x & 31;
-  float amax = fabsf(v);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(B2Q_FULL, amax, o));
-  int q = 0;
-  float sc = 0.0f;
-  if (amax > 0.0f && amax <= 3.0e38f) {
-    sc = amax / (float)kXMax;
-    q = max(-kXMax, min(kXMax, __float2int_rn(v * ((float)kXMax / amax))));
-  }
-  const int kp = xq.kpad, j = col >> 5;
-  xq.q[(int64_t)s * kp + col] = (int16_t)q;
-  int sm = q;
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) sm += __shfl_xor_sync(B2Q_FULL, sm, o);
-  const int s_other = __shfl_xor_sync(B2Q_FULL, sm, 16);
-  if (lane == 0) {
-    xq.s16[(int64_t)s * (kp / 16) + 2 * j] = sm;
-    xq.scale[(int64_t)s * (kp / 32) + j] = sc;
-    xq.fsum[(int64_t)s * (kp / 32) + j] = sc * (float)(sm + s_other);
-  } else if (lane == 16) {
-    xq.s16[(int64_t)s * (kp / 16) + 2 * j + 1] = sm;
-  }
+  const int col0 = g * G * HD;
+  out[(int64_t)s * H * HD + col0 + threadIdx.x] = v;
+  vals[threadIdx.x] = v;
+  __syncthreads();
+  // quantise: warp w < 2G takes the 64-element block w of this KV group
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < 2 * G)
+    xq_store_block(vals[64 * warp + lane], vals[64 * warp + 32 + lane], lane, s, (col0 >> 6) + warp, xq);
   pdl_launch_dependents();
 }
 

@@ -73,10 +73,13 @@ namespace b2q {
 
 static b2q_status model_cuda(cudaError_t e, const char* what) { return cuda_error(e, what); }
 
+// Zeroed device allocation.  The memset is synchronous (legacy stream, then
+// a device sync) so no later work on a non-blocking stream can overtake it.
 template <class T>
 static cudaError_t dalloc(T** p, size_t count) {
   cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(count, 1) * sizeof(T));
-  if (e == cudaSuccess) cudaMemset(*p, 0, std::max<size_t>(count, 1) * sizeof(T));
+  if (e == cudaSuccess) e = cudaMemset(*p, 0, std::max<size_t>(count, 1) * sizeof(T));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
   return e;
 }
 
@@ -276,7 +279,6 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
         a.seg[0].rows_out = Fl;
         a.xq = M->xq_e.x.q;
         a.xscale = M->xq_e.x.scale;
-        a.xfsum = M->xq_e.x.fsum;
         a.xs16 = M->xq_e.x.s16;
         a.kpad = M->xq_e.kpad;
         a.t0 = t;
@@ -346,7 +348,7 @@ static cudaError_t build_decode_graph(b2q_model* M) {
   }
   const uint64_t before = M->eng->launches.load();
   cudaGraph_t g = nullptr;
-  cudaError_t err = cudaStreamBeginCapture(M->st, cudaStreamCaptureModeThreadLocal);
+  cudaError_t err = cudaStreamBeginCapture(M->st, cudaStreamCaptureModeRelaxed);
   if (err != cudaSuccess) return err;
   cudaError_t ferr = forward_pass(M, 1, /*pdl=*/true, M->st);
   err = cudaStreamEndCapture(M->st, &g);

@@ -11,66 +11,83 @@ enum : int {
 };
 
 // Activation format consumed by the GEMV kernels.  Each f32 vector of k
-// values is cut into 32-element blocks; block j is stored as 16-bit integers
-// q in [-16383, 16383] with x ~= q * scale[j] (scale = max|x| / 16383), plus
-// per-block sums used by the formats with an offset or a min term:
-//   s16[2j], s16[2j+1] = sum of q over the two 16-element halves,
-//   fsum[j]            = scale[j] * (s16[2j] + s16[2j+1]).
-// Rows are padded to kpad (a multiple of 256) with zeros.  The int16 range is
-// limited to +-16383 so that every integer partial sum the GEMV forms stays
-// inside int32 (Q6_K: 4 groups x 16 x 32 x 16383 x 64 < 2^31).
+// values is cut into 64-element blocks; block j is stored as 16-bit integers
+// q in [-16383, 16383] with x ~= q * scale[j] (scale = max|x| / 16383; the q
+// row is stored in the bank-swizzled order of xswz below), plus the sums of
+// q over each 16-element quarter, s16[4j .. 4j+3], used by the formats with
+// an offset (Q6_K) or a min term (Q4_K).  Rows are padded to kpad (a
+// multiple of 256) with zeros.  The int16 range is limited to +-16383 so that
+// every integer partial sum the GEMV forms stays inside int32 (the largest,
+// Q6_K: 2 groups x 16 x 32 x 16383 x 64 < 2^31).
 constexpr int kXMax = 16383;
+constexpr int kXBlock = 64;
 
 struct XQ {
-  int16_t* q;    // [m][kpad]
-  float* scale;  // [m][kpad/32]
-  float* fsum;   // [m][kpad/32]
-  int32_t* s16;  // [m][kpad/16]
+  int16_t* q;     // [m][kpad]
+  float* scale;   // [m][kpad/64]
+  int32_t* s16;   // [m][kpad/16]
   int kpad;
 };
 
 __host__ __device__ inline int round_up_int(int a, int b) { return (a + b - 1) / b * b; }
 
-// One warp per 32-element block.  x [m][ldx] f32 (first k columns used).
-__device__ __forceinline__ void quantize_block_warp(const float* x, int k, int t, int j, int lane,
-                                                    const XQ& xq) {
-  const int pos = j * 32 + lane;
-  const float v = pos < k ? x[pos] : 0.0f;
-  float amax = fabsf(v);
+// Shared-memory bank swizzle of the int16 activation rows.  A row is cut into
+// 64-element groups (128 bytes = all 32 banks); 16-byte chunk c of group g is
+// stored at chunk position c ^ f(g), f(g) = g's low three bits with bits 0
+// and 1 exchanged.  Every GEMV lane pattern (Q4_K: 8 lanes read chunk c of 8
+// consecutive groups; Q6_K / Q8_0: pairs of lanes share a group and read
+// chunks 2 or 4 apart) then hits 8 distinct chunk positions per 8-lane phase.
+__host__ __device__ inline int xswz_f(int g) { return ((g >> 1) & 1) | ((g & 1) << 1) | (g & 4); }
+__host__ __device__ inline int xswz_chunk(int g, int c) { return (g << 6) | ((c ^ xswz_f(g)) << 3); }
+__host__ __device__ inline int xswz(int pos) { return xswz_chunk(pos >> 6, (pos >> 3) & 7) | (pos & 7); }
+
+// Quantise one 64-element block held two values per lane (lane i holds
+// elements 64*j + i and 64*j + 32 + i of row t) and store it into `xq`.
+// All 32 lanes call it.
+__device__ __forceinline__ void xq_store_block(float v0, float v1, int lane, int t, int j, const XQ& xq) {
+  float amax = fmaxf(fabsf(v0), fabsf(v1));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(B2Q_FULL, amax, o));
-  int q = 0;
+  int q0 = 0, q1 = 0;
   float scale = 0.0f;
   if (amax > 0.0f && amax <= 3.0e38f) {
     scale = amax / (float)kXMax;
     const float inv = (float)kXMax / amax;
-    q = __float2int_rn(v * inv);
-    q = max(-kXMax, min(kXMax, q));
+    q0 = max(-kXMax, min(kXMax, __float2int_rn(v0 * inv)));
+    q1 = max(-kXMax, min(kXMax, __float2int_rn(v1 * inv)));
   }
   const int kp = xq.kpad;
-  xq.q[(size_t)t * kp + pos] = (int16_t)q;
-  int s = q;
+  int16_t* qr = xq.q + (int64_t)t * kp;
+  qr[xswz(j * 64 + lane)] = (int16_t)q0;
+  qr[xswz(j * 64 + 32 + lane)] = (int16_t)q1;
+  int s0 = q0, s1 = q1;
 #pragma unroll
-  for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(B2Q_FULL, s, o);  // within 16-lane halves
-  const int s_other = __shfl_xor_sync(B2Q_FULL, s, 16);
+  for (int o = 8; o > 0; o >>= 1) {  // sums within 16-lane halves
+    s0 += __shfl_xor_sync(B2Q_FULL, s0, o);
+    s1 += __shfl_xor_sync(B2Q_FULL, s1, o);
+  }
+  int32_t* sr = xq.s16 + (int64_t)t * (kp / 16) + 4 * j;
   if (lane == 0) {
-    xq.s16[(size_t)t * (kp / 16) + 2 * j] = s;
-    xq.scale[(size_t)t * (kp / 32) + j] = scale;
-    xq.fsum[(size_t)t * (kp / 32) + j] = scale * (float)(s + s_other);
+    sr[0] = s0;
+    sr[2] = s1;
+    xq.scale[(int64_t)t * (kp / 64) + j] = scale;
   } else if (lane == 16) {
-    xq.s16[(size_t)t * (kp / 16) + 2 * j + 1] = s;
+    sr[1] = s0;
+    sr[3] = s1;
   }
 }
 
-// x [m][k] f32 -> XQ (all kpad/32 blocks of every row, zero tail).
+// x [m][k] f32 -> XQ (all kpad/64 blocks of every row, zero tail).
 __global__ void quantize_x_kernel(const float* __restrict__ x, int m, int k, XQ xq) {
   pdl_wait();
   const int lane = threadIdx.x & 31;
-  const int nblk = xq.kpad / 32;
+  const int nblk = xq.kpad / 64;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int idx = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; idx < m * nblk; idx += warps) {
     const int t = idx / nblk, j = idx % nblk;
-    quantize_block_warp(x + (size_t)t * k, k, t, j, lane, xq);
+    const int p0 = j * 64 + lane, p1 = p0 + 32;
+    const float* xr = x + (size_t)t * k;
+    xq_store_block(p0 < k ? xr[p0] : 0.0f, p1 < k ? xr[p1] : 0.0f, lane, t, j, xq);
   }
   pdl_launch_dependents();
 }
@@ -214,39 +231,89 @@ __global__ void embed_rows_kernel(const uint8_t* __restrict__ raw, int dtype, in
 }
 
 // ---------------------------------------------------------------------------
-// Load-time repack into the GEMV stream layout.  All byte values are moved,
+// Load-time repack into the tiled GEMV layout.  All byte values are moved,
 // never recomputed, so the dequantised values stay bit-exact.
 //
-//   Q4_K (U = k/64 units of 64 weights per row; unit u = 4*block + chunk):
-//     qs  [n][2][U][16]  half 0: qs bytes 32c..32c+15, half 1: 32c+16..32c+31
-//     hdr [n][U] u32     sc(2c) | sc(2c+1)<<6 | m(2c)<<12 | m(2c+1)<<18 |
-//                        byte c of (d | dmin<<16) << 24
-//   Q6_K (U = k/64; unit u = 4*block + 2*half + sub, sub covers l = 16*sub..):
-//     qs  [n][3][U][16]  ql[64h+16s..], ql[64h+32+16s..], qh[32h+16s..]
-//     scw [n][U] u32     int8 scales sc[8h+s+2i], i = 0..3, byte i
-//     d   [n][nb] u16
-//   Q8_0 (U = k/32; unit = block):
-//     qs  [n][2][U][16]  codes 0..15 / 16..31
-//     d   [n][U] u16
-// Every stream row is 16-byte aligned when k is a multiple of 32.
+// A row of k weights is U units (Q4_K, Q6_K: 64 weights; Q8_0: 32), cut into
+// C k-chunks of KC <= 64 units (C = ceil(U / 64); KC a multiple of 8, of 16
+// for Q8_0, so that a GEMV lane always sees the same activation-swizzle
+// phase, see gemv.cuh).  Rows are
+// grouped by 8.  Tile (g, c) = rows 8g..8g+7, chunk c, stored as 8
+// consecutive row-chunks of rc bytes; tiles are ordered (g, c) row-group
+// major, so one pipeline stage of the GEMV is one contiguous bulk copy.
+// Row-chunk content (ul = unit index within the chunk):
+//   Q4_K  [16 B x KC: qs bytes 32c'..32c'+15 of unit ul = 4*block + c']
+//         [16 B x KC: qs bytes 32c'+16..32c'+31]
+//         [ 4 B x KC: sc(2c') | sc(2c'+1)<<6 | m(2c')<<12 | m(2c'+1)<<18 |
+//                     byte c' of (d | dmin<<16) << 24]
+//   Q6_K  (unit ul = 4*block + 2*half + s covers l = 16s..16s+15 of a half)
+//         [16 B x KC: ql[64h+16s..]] [16 B x KC: ql[64h+32+16s..]]
+//         [16 B x KC: qh[32h+16s..]] [4 B x KC: int8 sc[8h+s+2i], i=0..3]
+//         [2 B x KC/4: d per block, padded to 16 B]
+//   Q8_0  [16 B x KC: codes 0..15] [16 B x KC: codes 16..31]
+//         [2 B x KC: d, padded to 16 B]
+// Padding units (u >= U) and rows (>= n) are zero and never read.
 // ---------------------------------------------------------------------------
-__global__ void repack_q4k_kernel(const uint8_t* __restrict__ raw, int64_t n, int nb,
-                                  uint8_t* __restrict__ qs, uint32_t* __restrict__ hdr) {
-  const int U = nb * 4;
-  const int64_t total = n * U;
+struct TileLayout {
+  int dtype, n, k;
+  int U, nb;    // units per row, GGUF blocks per row
+  int KC, C;    // units per chunk, chunks per row
+  int G;        // groups of 8 rows
+  int rc;       // bytes per row-chunk
+  int o_aux;    // offset of the per-unit scale words / d in a row-chunk
+  int o_aux2;   // Q6_K: offset of the per-block d
+};
+
+__host__ __device__ inline int64_t tile_bytes(const TileLayout& L) { return 8LL * L.rc; }
+
+__host__ inline TileLayout make_tile_layout(int dtype, int64_t n, int64_t k) {
+  TileLayout L;
+  L.dtype = dtype;
+  L.n = (int)n;
+  L.k = (int)k;
+  const int qk = dtype == kQ8_0 ? 32 : 256;
+  L.nb = (int)(k / qk);
+  L.U = dtype == kQ8_0 ? L.nb : (int)(k / 64);
+  L.C = (L.U + 63) / 64;
+  L.KC = round_up_int((L.U + L.C - 1) / L.C, dtype == kQ8_0 ? 16 : 8);
+  L.G = (int)((n + 7) / 8);
+  const int kc = L.KC;
+  if (dtype == kQ4_K) {
+    L.o_aux = 32 * kc;
+    L.o_aux2 = 0;
+    L.rc = 36 * kc;
+  } else if (dtype == kQ6_K) {
+    L.o_aux = 48 * kc;
+    L.o_aux2 = 52 * kc;
+    L.rc = 52 * kc + round_up_int(kc / 2, 16);
+  } else {
+    L.o_aux = 32 * kc;
+    L.o_aux2 = 0;
+    L.rc = 32 * kc + round_up_int(2 * kc, 16);
+  }
+  return L;
+}
+
+__device__ __forceinline__ uint8_t* tile_row_chunk(uint8_t* base, const TileLayout& L, int64_t row, int c) {
+  const int64_t g = row >> 3;
+  return base + ((g * L.C + c) * 8 + (row & 7)) * (int64_t)L.rc;
+}
+
+__global__ void repack_q4k_kernel(const uint8_t* __restrict__ raw, TileLayout L, uint8_t* __restrict__ out) {
+  const int64_t total = (int64_t)L.n * L.U;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = idx / U;
-    const int u = (int)(idx % U);
-    const int blk = u >> 2, c = u & 3;
-    const uint8_t* b = raw + (row * nb + blk) * 144;
-    const uint4* src = reinterpret_cast<const uint4*>(b + 16 + 32 * c);
-    uint4* dst0 = reinterpret_cast<uint4*>(qs + row * (int64_t)U * 32 + (int64_t)u * 16);
-    uint4* dst1 = reinterpret_cast<uint4*>(qs + row * (int64_t)U * 32 + (int64_t)(U + u) * 16);
-    *dst0 = src[0];
-    *dst1 = src[1];
+    const int64_t row = idx / L.U;
+    const int u = (int)(idx % L.U);
+    const int c = u / L.KC, ul = u % L.KC;
+    const int blk = u >> 2, cc = u & 3;
+    const uint8_t* b = raw + (row * L.nb + blk) * 144;
+    uint8_t* rcp = tile_row_chunk(out, L, row, c);
+    const uint4* src = reinterpret_cast<const uint4*>(b + 16 + 32 * cc);
+    *reinterpret_cast<uint4*>(rcp + 16 * ul) = src[0];
+    *reinterpret_cast<uint4*>(rcp + 16 * (L.KC + ul)) = src[1];
     const uint8_t* s = b + 4;
-    const int j0 = 2 * c, j1 = 2 * c + 1;
+    const int j0 = 2 * cc, j1 = 2 * cc + 1;
     uint32_t sc0, m0, sc1, m1;
     if (j0 < 4) {
       sc0 = s[j0] & 63; m0 = s[j0 + 4] & 63; sc1 = s[j1] & 63; m1 = s[j1 + 4] & 63;
@@ -257,53 +324,51 @@ __global__ void repack_q4k_kernel(const uint8_t* __restrict__ raw, int64_t n, in
       m1 = (s[j1 + 4] >> 4) | ((s[j1] >> 6) << 4);
     }
     const uint32_t dd = rd16(b) | (rd16(b + 2) << 16);
-    hdr[row * U + u] = sc0 | (sc1 << 6) | (m0 << 12) | (m1 << 18) | (((dd >> (8 * c)) & 0xffu) << 24);
+    *reinterpret_cast<uint32_t*>(rcp + L.o_aux + 4 * ul) =
+        sc0 | (sc1 << 6) | (m0 << 12) | (m1 << 18) | (((dd >> (8 * cc)) & 0xffu) << 24);
   }
 }
 
-__global__ void repack_q6k_kernel(const uint8_t* __restrict__ raw, int64_t n, int nb,
-                                  uint8_t* __restrict__ qs, uint32_t* __restrict__ scw,
-                                  uint16_t* __restrict__ dd) {
-  const int U = nb * 4;
-  const int64_t total = n * U;
+__global__ void repack_q6k_kernel(const uint8_t* __restrict__ raw, TileLayout L, uint8_t* __restrict__ out) {
+  const int64_t total = (int64_t)L.n * L.U;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = idx / U;
-    const int u = (int)(idx % U);
+    const int64_t row = idx / L.U;
+    const int u = (int)(idx % L.U);
+    const int c = u / L.KC, ul = u % L.KC;
     const int blk = u >> 2, h = (u >> 1) & 1, s = u & 1;
-    const uint8_t* b = raw + (row * nb + blk) * 210;
-    uint8_t* base = qs + row * (int64_t)U * 48;
+    const uint8_t* b = raw + (row * L.nb + blk) * 210;
+    uint8_t* rcp = tile_row_chunk(out, L, row, c);
     // raw Q6_K blocks are only 2-byte aligned: copy bytewise
     const uint8_t* src0 = b + 64 * h + 16 * s;
     const uint8_t* src1 = b + 64 * h + 32 + 16 * s;
     const uint8_t* src2 = b + 128 + 32 * h + 16 * s;
-    uint8_t* d0 = base + (int64_t)u * 16;
-    uint8_t* d1 = base + (int64_t)(U + u) * 16;
-    uint8_t* d2 = base + (int64_t)(2 * U + u) * 16;
+    uint8_t* d0 = rcp + 16 * ul;
+    uint8_t* d1 = rcp + 16 * (L.KC + ul);
+    uint8_t* d2 = rcp + 16 * (2 * L.KC + ul);
 #pragma unroll
     for (int i = 0; i < 16; i++) { d0[i] = src0[i]; d1[i] = src1[i]; d2[i] = src2[i]; }
     const uint8_t* sc = b + 192 + 8 * h + s;
-    scw[row * U + u] = (uint32_t)sc[0] | ((uint32_t)sc[2] << 8) | ((uint32_t)sc[4] << 16) |
-                       ((uint32_t)sc[6] << 24);
-    if ((u & 3) == 0) dd[row * nb + blk] = (uint16_t)rd16(b + 208);
+    *reinterpret_cast<uint32_t*>(rcp + L.o_aux + 4 * ul) =
+        (uint32_t)sc[0] | ((uint32_t)sc[2] << 8) | ((uint32_t)sc[4] << 16) | ((uint32_t)sc[6] << 24);
+    if ((ul & 3) == 0) *reinterpret_cast<uint16_t*>(rcp + L.o_aux2 + 2 * (ul >> 2)) = (uint16_t)rd16(b + 208);
   }
 }
 
-__global__ void repack_q80_kernel(const uint8_t* __restrict__ raw, int64_t n, int nb,
-                                  uint8_t* __restrict__ qs, uint16_t* __restrict__ dd) {
-  const int U = nb;
-  const int64_t total = n * U;
+__global__ void repack_q80_kernel(const uint8_t* __restrict__ raw, TileLayout L, uint8_t* __restrict__ out) {
+  const int64_t total = (int64_t)L.n * L.U;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = idx / U;
-    const int u = (int)(idx % U);
-    const uint8_t* b = raw + (row * nb + u) * 34;
-    uint8_t* base = qs + row * (int64_t)U * 32;
-    uint8_t* d0 = base + (int64_t)u * 16;
-    uint8_t* d1 = base + (int64_t)(U + u) * 16;
+    const int64_t row = idx / L.U;
+    const int u = (int)(idx % L.U);
+    const int c = u / L.KC, ul = u % L.KC;
+    const uint8_t* b = raw + (row * L.nb + u) * 34;
+    uint8_t* rcp = tile_row_chunk(out, L, row, c);
+    uint8_t* d0 = rcp + 16 * ul;
+    uint8_t* d1 = rcp + 16 * (L.KC + ul);
 #pragma unroll
     for (int i = 0; i < 16; i++) { d0[i] = b[2 + i]; d1[i] = b[18 + i]; }
-    dd[row * U + u] = (uint16_t)rd16(b);
+    *reinterpret_cast<uint16_t*>(rcp + L.o_aux + 2 * ul) = (uint16_t)rd16(b);
   }
 }
 
