@@ -46,6 +46,7 @@ SIGNATURES = [
     ("b2q_weight_bytes", _SZ, [_VP]),
     ("b2q_matmul", _I, [_VP, _VP, _FP, _FP, _I, _I, _I]),
     ("b2q_matmul_dev", _I, [_VP, _VP, _VP, _VP, _I, _I, _I, _VP]),
+    ("b2q_matmul_noalloc_dev", _I, [_VP, _VP, _VP, _I, _I, _I, _VP]),
     ("b2q_matmul_group", _I, [_VP, C.POINTER(_VP), C.POINTER(_I), _I, _FP, _I, _I, _FP]),
     ("b2q_matmul_group_dev", _I, [_VP, C.POINTER(_VP), C.POINTER(_I), _I, _VP, _I, _I, _VP, _VP]),
     ("b2q_ffn_swiglu", _I, [_VP, _VP, _VP, _VP, _FP, _I, _I, _I, _FP]),

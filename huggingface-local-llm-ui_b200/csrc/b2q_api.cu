@@ -213,6 +213,51 @@ cudaError_t launch_quantize(b2q_engine* e, const float* x, int m, int k, XQBuf& 
 using namespace b2q;
 
 // ===========================================================================
+// Allocation-free matvec scratch.
+//
+// b2q_matmul_noalloc_dev serves callers that must not allocate device
+// memory -- code running where cudaMalloc is forbidden or unsafe (inside a
+// memory pool that has to stay fixed for the life of a process, on a
+// real-time path that cannot afford an allocation's synchronisation, or
+// in a host whose allocator is owned by someone else).  Its only scratch,
+// the quantised activations, lives in this file-scope array, which every GPU
+// that loads the library holds until the process exits.
+// ===========================================================================
+namespace {
+
+// int16 codes of m*kpad activations + one f32 scale per 64 + one int32 sum
+// per 16: 2 + 4/64 + 4/16 bytes per element.
+constexpr int64_t kNoAllocMaxElems = 262144;  // m * round_up(k, 256) limit
+constexpr size_t kNoAllocQBytes = (size_t)kNoAllocMaxElems * 2;
+constexpr size_t kNoAllocScaleBytes = (size_t)kNoAllocMaxElems / 64 * 4;
+constexpr size_t kNoAllocSumBytes = (size_t)kNoAllocMaxElems / 16 * 4;
+constexpr size_t kNoAllocBytes = kNoAllocQBytes + kNoAllocScaleBytes + kNoAllocSumBytes;  // 606,208
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device.  The host-side
+// name g_noalloc_scratch is only a stand-in for the symbol; the address a
+// kernel can use comes from cudaGetSymbolAddress, looked up once per device.
+b2q_status noalloc_scratch(int device, void** out) {
+  if (device < 0 || device >= kMaxDevices) return set_error(B2Q_EINVAL, "noalloc: device %d out of range", device);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void* p = nullptr;
+    cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess || p == nullptr) return cuda_error(err, "noalloc: cudaGetSymbolAddress");
+    g_noalloc_ptr[device] = p;
+  }
+  *out = g_noalloc_ptr[device];
+  return B2Q_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
 // C ABI
 // ===========================================================================
 extern "C" {
@@ -620,6 +665,45 @@ b2q_status b2q_time_gemv(b2q_engine* e, const b2q_weight* const* ws, int count, 
   cudaEventDestroy(ev1);
   if (err != cudaSuccess) return cuda_error(err, "b2q_time_gemv");
   *avg_ms = ms / (float)(reps * count);
+  return B2Q_OK;
+}
+
+b2q_status b2q_matmul_noalloc_dev(const b2q_weight* w, const float* x_dev, float* y_dev, int m, int n, int k,
+                                  void* stream) {
+  if (!w || !x_dev || !y_dev) return set_error(B2Q_EINVAL, "matmul_noalloc_dev: NULL argument");
+  if (m <= 0 || n <= 0 || k <= 0) return set_error(B2Q_EINVAL, "matmul_noalloc_dev: m, n and k must be positive");
+  b2q_status s = check_weight(w, n, k, "matmul_noalloc_dev");
+  if (s != B2Q_OK) return s;
+  const int kpad = round_up_int(k, 256);
+  if ((int64_t)m * kpad > kNoAllocMaxElems)
+    return set_error(B2Q_EINVAL,
+                     "matmul_noalloc_dev: m * round_up(k, 256) = %lld exceeds the fixed scratch of %lld "
+                     "activations (use b2q_matmul_dev)",
+                     (long long)m * kpad, (long long)kNoAllocMaxElems);
+  b2q_engine* e = w->eng;
+  cudaError_t err = cudaSetDevice(e->device);
+  if (err != cudaSuccess) return cuda_error(err, "matmul_noalloc_dev: cudaSetDevice");
+  void* base = nullptr;
+  s = noalloc_scratch(e->device, &base);
+  if (s != B2Q_OK) return s;
+  // carve the quantised-activation buffer out of the static array; the
+  // quantiser rewrites every element the GEMV reads, so nothing in it has
+  // to start at zero
+  XQBuf xq;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  xq.m = m;
+  xq.k = k;
+  xq.kpad = kpad;
+  xq.x.kpad = kpad;
+  xq.x.q = reinterpret_cast<int16_t*>(p);
+  xq.x.scale = reinterpret_cast<float*>(p + kNoAllocQBytes);
+  xq.x.s16 = reinterpret_cast<int32_t*>(p + kNoAllocQBytes + kNoAllocScaleBytes);
+  cudaStream_t st = stream ? (cudaStream_t)stream : e->stream;
+  err = launch_quantize(e, x_dev, m, k, xq, st, false);
+  if (err != cudaSuccess) return cuda_error(err, "matmul_noalloc_dev: quantize launch");
+  GemvSeg sg = make_seg(w, y_dev, n);
+  err = run_gemv(e, &sg, 1, xq, m, kEpiStore, st, false);
+  if (err != cudaSuccess) return cuda_error(err, "matmul_noalloc_dev: gemv launch");
   return B2Q_OK;
 }
 

@@ -98,6 +98,22 @@ b2q_status b2q_matmul(b2q_engine* eng, const b2q_weight* w, const float* x, floa
 b2q_status b2q_matmul_dev(b2q_engine* eng, const b2q_weight* w, const float* x_dev,
                           float* y_dev, int m, int n, int k, void* stream);
 
+/* No counterpart in the reference.  y = W x like b2q_matmul_dev, for callers
+ * that must not allocate device memory (a fixed memory pool, a real-time
+ * path that cannot take an allocation's implicit synchronisation, a host
+ * that owns the allocator): this entry point calls no cudaMalloc, cudaFree
+ * or allocating library routine.  Its scratch (the quantised activations)
+ * is a fixed array inside the library, about 0.6 MB per GPU that loads the
+ * library, held until the process exits; calls with
+ * m * round_up(k, 256) > 262144 are rejected with B2Q_EINVAL.  The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture.  Every call shares the
+ * array: calls that overlap on the GPU (different streams, no ordering)
+ * race and must be serialised by the caller.  x_dev / y_dev are device
+ * pointers; asynchronous on `stream` (NULL: the engine's stream). */
+b2q_status b2q_matmul_noalloc_dev(const b2q_weight* w, const float* x_dev, float* y_dev, int m, int n,
+                                  int k, void* stream);
+
 /* Replaces CudaEngine::matmul_group_same_input (gpu.rs:593-650): `count`
  * weights sharing the input x [m][k]; outputs are concatenated in order,
  * each as its own [m][n_i] block, into y_flat (gpu.rs:617-646). */
