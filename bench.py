@@ -142,9 +142,10 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def build_model(pkg, engine, cfg, seed, rank, size, tp_id, max_seq, dist="bench"):
+def build_model(pkg, engine, cfg, seed, rank, size, tp_id, max_seq, dist="bench", decode="graph"):
     from hf_llm_b200 import model, synth
-    m = model.StandardNativeEngine(engine, cfg, max_seq=max_seq, tp_rank=rank, tp_size=size, tp_id=tp_id)
+    m = model.StandardNativeEngine(engine, cfg, max_seq=max_seq, tp_rank=rank, tp_size=size, tp_id=tp_id,
+                                   decode=decode)
     host = {}
     for spec in synth.llama_specs(cfg, model.q4_k_m_types()):
         name, t, dims, _ = spec
@@ -267,6 +268,8 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--decode", default="graph", choices=["graph", "persistent", "eager"],
+                    help="single-token step: captured kernel graph, one persistent kernel, or eager")
     ap.add_argument("--no-gemv-shapes", action="store_true", help="skip the per-shape GEMV timings")
     ap.add_argument("--gemv-only", default=None,
                     help="time one GEMV shape only (e.g. q4k_14336x4096), for kernel profiling")
@@ -313,7 +316,7 @@ def main():
     cfg = dict(model.LLAMA3_8B)
     max_seq = args.prefill + args.warmup + args.steps + args.e2e_steps + 8
     t_load = time.perf_counter()
-    m, host = build_model(pkg, engine, cfg, args.seed, rank, world, tp_id, max_seq)
+    m, host = build_model(pkg, engine, cfg, args.seed, rank, world, tp_id, max_seq, decode=args.decode)
     t_load = time.perf_counter() - t_load
 
     stream = torch.cuda.Stream(device=dev)
@@ -415,7 +418,7 @@ def main():
                 "dtype": "int16xint8 dp2a, f32 accum", "data": "synthetic",
                 "config": {"workload": "llama3-8b-q4_k_m-decode", "layers": 32, "hidden": 4096,
                            "heads": "32/8", "ffn": 14336, "vocab": 128256, "prefill": args.prefill,
-                           "batch": 1, "kv_cache": "f16", "tp": world,
+                           "batch": 1, "kv_cache": "f16", "tp": world, "decode": m.decode_mode,
                            "l2": "inputs larger than L2 (4.9 GB weights per step)"},
                 "decode_step": {"bytes_per_step_rank0": int(step_bytes),
                                 "GBps_rank0": round(step_bytes / (ms_step * 1e-3) / 1e9, 1)},

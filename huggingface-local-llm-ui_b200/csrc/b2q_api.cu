@@ -709,6 +709,16 @@ b2q_status b2q_matmul_noalloc_dev(const b2q_weight* w, const float* x_dev, float
 
 uint64_t b2q_kernel_launch_count(b2q_engine* e) { return e ? e->launches.load() : 0; }
 
+#ifdef B2Q_DECODE_TRACE
+// Developer build only: copy the persistent decode kernel's timeline out.
+int b2q_debug_decode_trace(void* host, size_t bytes) {
+  return cudaMemcpyFromSymbol(host, b2q::g_dec_trace, std::min(bytes, sizeof(b2q::g_dec_trace))) == cudaSuccess ? 0 : 1;
+}
+int b2q_debug_decode_dbg(void* host, size_t bytes) {
+  return cudaMemcpyFromSymbol(host, b2q::g_dec_dbg, std::min(bytes, sizeof(b2q::g_dec_dbg))) == cudaSuccess ? 0 : 1;
+}
+#endif
+
 b2q_status b2q_check_device_error(b2q_engine* e) {
   if (!e) return set_error(B2Q_EINVAL, "engine is NULL");
   cudaSetDevice(e->device);

@@ -283,14 +283,36 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
-// The CTA's stages, chunk-major: for chunk c = 0..C-1, the 8-row groups
-// [gb, ge) taken NR at a time (SwiGLU: one group, gate tile + up tile).
-// Iterated with counters only (no division in the loop).
+// Shared-memory ring of weight stages: `ns` slots of `slot_bytes`, one full
+// and one empty mbarrier per slot.  The producer and the consumers each keep
+// their own copy of the (slot, phase) position and advance it once per stage;
+// a ring may carry the stages of several GEMVs back to back.
+struct Ring {
+  uint8_t* base;
+  uint64_t* full;
+  uint64_t* empty;
+  int ns, slot_bytes;
+  int slot = 0;
+  uint32_t phase = 0;
+  int used = 0;  // stages issued so far, saturating at ns (producer only)
+  __device__ __forceinline__ uint8_t* slot_ptr() const { return base + (size_t)slot * slot_bytes; }
+  __device__ __forceinline__ void advance() {
+    if (used < ns) ++used;
+    if (++slot == ns) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+// The CTA's stages of one GEMV, chunk-major: for chunk c = 0..C-1, the 8-row
+// groups [gb, ge) taken NR at a time (SwiGLU: one group, gate tile + up
+// tile).  Iterated with counters only (no division in the loop).
 template <int NR, bool PAIR>
 struct StageIter {
-  int gb, ge, C, NS;
-  int c = 0, g = 0, slot = 0, phase = 0;
-  __device__ __forceinline__ StageIter(int gb_, int ge_, int C_, int NS_) : gb(gb_), ge(ge_), C(C_), NS(NS_) { g = gb; }
+  int gb, ge, C;
+  int c = 0, g = 0;
+  __device__ __forceinline__ StageIter(int gb_, int ge_, int C_) : gb(gb_), ge(ge_), C(C_) { g = gb; }
   __device__ __forceinline__ bool done() const { return c >= C || gb >= ge; }
   __device__ __forceinline__ int ntiles() const { return PAIR ? 2 : ((NR == 2 && g + 1 < ge) ? 2 : 1); }
   __device__ __forceinline__ void next() {
@@ -299,44 +321,46 @@ struct StageIter {
       g = gb;
       ++c;
     }
-    if (++slot == NS) {
-      slot = 0;
-      phase ^= 1;
-    }
   }
 };
 
+// Producer (one thread): bulk-copy the CTA's tiles of groups [gb, ge) of
+// `w` (and `w2`, SwiGLU) into the ring.  Returns false if a wait for a free
+// slot gave up (the consumers stopped); the caller then stops producing.
 template <int NR, bool PAIR>
-__device__ __forceinline__ void gemv_producer(const GemvArgs& a, const GemvSeg& sg, int gb, int ge,
-                                              uint8_t* stages, uint64_t* full_bar, uint64_t* empty_bar) {
-  const TileLayout& L = sg.w.L;
+__device__ __forceinline__ bool produce_gemv(Ring& rg, const WeightDev& w, const WeightDev& w2, int gb,
+                                             int ge) {
+  const TileLayout& L = w.L;
   const uint32_t tb = (uint32_t)tile_bytes(L);
-  int used = 0;
-  for (StageIter<NR, PAIR> it(gb, ge, L.C, a.ns); !it.done(); it.next(), ++used) {
-    if (used >= a.ns && !mbar_wait_bounded(&empty_bar[it.slot], it.phase ^ 1)) break;
+  for (StageIter<NR, PAIR> it(gb, ge, L.C); !it.done(); it.next()) {
+    if (rg.used >= rg.ns && !mbar_wait_bounded(&rg.empty[rg.slot], rg.phase ^ 1u)) return false;
     const int nt = it.ntiles();
-    mbar_arrive_expect_tx(&full_bar[it.slot], tb * nt);
-    uint8_t* sl = stages + (size_t)it.slot * a.slot_bytes;
+    uint64_t* fb = &rg.full[rg.slot];
+    mbar_arrive_expect_tx(fb, tb * nt);
+    uint8_t* sl = rg.slot_ptr();
     const int64_t t0 = (int64_t)it.g * L.C + it.c;
-    bulk_g2s(sl, sg.w.base + t0 * tb, tb, &full_bar[it.slot]);
-    if (PAIR) bulk_g2s(sl + tb, sg.w2.base + t0 * tb, tb, &full_bar[it.slot]);
-    else if (nt == 2) bulk_g2s(sl + tb, sg.w.base + (t0 + L.C) * tb, tb, &full_bar[it.slot]);
+    bulk_g2s(sl, w.base + t0 * tb, tb, fb);
+    if (PAIR) bulk_g2s(sl + tb, w2.base + t0 * tb, tb, fb);
+    else if (nt == 2) bulk_g2s(sl + tb, w.base + (t0 + L.C) * tb, tb, fb);
+    rg.advance();
   }
+  return true;
 }
 
-// Row accumulators in shared memory: racc[h][tile i][row][t], h = unit half.
-template <int MT, int NR, bool PAIR, int EPI>
-__device__ __forceinline__ void gemv_consumer(const GemvArgs& a, const GemvSeg& sg, int gb, int ge,
-                                              uint8_t* stages, uint64_t* full_bar, uint64_t* empty_bar,
-                                              const SX& sx, bool ok, float* racc) {
+// Consumers (warps 0..15): the row partials of the CTA's stages of one
+// GEMV, accumulated into the shared-memory row accumulators
+// racc[h][tile i][row][t] (h = unit half; i = gate/up for SwiGLU).  The
+// accumulators are zeroed here; the caller runs the epilogue after the
+// trailing consumer_sync.  `ok` turns false if a wait gave up.  DT: the GGML
+// type when known at compile time, or -1 to dispatch on L.dtype.
+template <int MT, int NR, bool PAIR, int DT = -1>
+__device__ __forceinline__ void consume_gemv(Ring& rg, const TileLayout& L, int gb, int ge, int rows_cap,
+                                             const SX& sx, bool& ok, float* racc) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const TileLayout& L = sg.w.L;
   const uint32_t tb = (uint32_t)tile_bytes(L);
   const int p = warp >> 1, hf = warp & 1;  // row p of every tile; unit half hf
-  const int rows_cap = a.rows_cap;
-  const int nrows = (ge - gb) * 8;
-  // racc layout: [2 halves][PAIR ? 2 : 1][rows_cap][MT]
   constexpr int NW = PAIR ? 2 : 1;
+  const int dt = DT >= 0 ? DT : L.dtype;
   for (int i = threadIdx.x; i < 2 * NW * rows_cap * MT; i += kGemvConsumerWarps * 32) racc[i] = 0.0f;
   consumer_sync();
 
@@ -347,7 +371,7 @@ __device__ __forceinline__ void gemv_consumer(const GemvArgs& a, const GemvSeg& 
   int cur_c = -1;
   bool uok = false;
   int ul = 0;
-  for (StageIter<NR, PAIR> it(gb, ge, L.C, a.ns); !it.done(); it.next()) {
+  for (StageIter<NR, PAIR> it(gb, ge, L.C); !it.done(); it.next()) {
     if (it.c != cur_c) {  // new chunk pass: this lane's activations
       cur_c = it.c;
       ul = lane0;
@@ -356,13 +380,13 @@ __device__ __forceinline__ void gemv_consumer(const GemvArgs& a, const GemvSeg& 
       if (uok && ok) {
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
-          if (L.dtype == kQ4_K) xload_q4k(X[t], sx, t, u, xp.f4);
-          else if (L.dtype == kQ6_K) xload_q6k(X[t], sx, t, u, xp.f6a, xp.f6b);
+          if (dt == kQ4_K) xload_q4k(X[t], sx, t, u, xp.f4);
+          else if (dt == kQ6_K) xload_q6k(X[t], sx, t, u, xp.f6a, xp.f6b);
           else xload_q80(X[t], sx, t, u, xp.f8);
         }
       }
     }
-    if (ok) ok = mbar_wait_bounded(&full_bar[it.slot], it.phase);
+    if (ok) ok = mbar_wait_bounded(&rg.full[rg.slot], rg.phase);
     const int nt = it.ntiles();
     float part[NR][MT];
 #pragma unroll
@@ -370,21 +394,22 @@ __device__ __forceinline__ void gemv_consumer(const GemvArgs& a, const GemvSeg& 
 #pragma unroll
       for (int t = 0; t < MT; ++t) part[i][t] = 0.0f;
     if (ok && uok) {
-      const uint8_t* sl = stages + (size_t)it.slot * a.slot_bytes + p * L.rc;
+      const uint8_t* sl = rg.slot_ptr() + p * L.rc;
 #pragma unroll
       for (int i = 0; i < NR; ++i) {
         if (i >= nt) break;
         const uint8_t* rc = sl + i * tb;
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
-          if (L.dtype == kQ4_K) part[i][t] = row_q4k(rc, L.KC, L.o_aux, ul, csel, X[t]);
-          else if (L.dtype == kQ6_K) part[i][t] = row_q6k(rc, L.KC, L.o_aux, L.o_aux2, ul, X[t]);
+          if (dt == kQ4_K) part[i][t] = row_q4k(rc, L.KC, L.o_aux, ul, csel, X[t]);
+          else if (dt == kQ6_K) part[i][t] = row_q6k(rc, L.KC, L.o_aux, L.o_aux2, ul, X[t]);
           else part[i][t] = row_q80(rc, L.KC, L.o_aux, ul, X[t]);
         }
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[it.slot]);  // the stage may be refilled
+    if (lane == 0) mbar_arrive(&rg.empty[rg.slot]);  // the stage may be refilled
+    rg.advance();
 #pragma unroll
     for (int i = 0; i < NR; ++i)
 #pragma unroll
@@ -403,21 +428,32 @@ __device__ __forceinline__ void gemv_consumer(const GemvArgs& a, const GemvSeg& 
     }
   }
   consumer_sync();
-  // epilogue: y for every (row, token) of this CTA
+}
+
+// Final value of local row r, token t, weight wsel (SwiGLU: 0 gate, 1 up).
+template <int MT, bool PAIR>
+__device__ __forceinline__ float racc_value(const float* racc, int rows_cap, int r, int t, int wsel) {
+  constexpr int NW = PAIR ? 2 : 1;
+  return racc[((0 * NW + wsel) * rows_cap + r) * MT + t] + racc[((1 * NW + wsel) * rows_cap + r) * MT + t];
+}
+
+// Epilogue: y for every (row, token) of rows [8 gb, 8 ge) (rows >= n skipped).
+template <int MT, int EPI>
+__device__ __forceinline__ void gemv_epilogue(const float* racc, int rows_cap, int gb, int ge, int n, float* y,
+                                              int ldy, bool ok) {
+  constexpr bool kPair = EPI == kEpiSwiglu;
+  if (!ok) return;
   const int row0 = gb * 8;
+  const int nrows = (ge - gb) * 8;
   for (int idx = threadIdx.x; idx < nrows * MT; idx += kGemvConsumerWarps * 32) {
     const int r = idx / MT, t = idx % MT;
     const int row = row0 + r;
-    if (row >= L.n) continue;
-    const float v = racc[(0 * NW * rows_cap + r) * MT + t] + racc[(1 * NW * rows_cap + r) * MT + t];
-    float* yp = sg.y + (int64_t)t * sg.ldy + row;
-    if (PAIR) {
-      const float uv = racc[((0 * NW + 1) * rows_cap + r) * MT + t] + racc[((1 * NW + 1) * rows_cap + r) * MT + t];
-      if (ok) *yp = silu_f(v) * uv;
-    } else if (ok) {
-      if (EPI == kEpiAdd) *yp += v;
-      else *yp = v;
-    }
+    if (row >= n) continue;
+    const float v = racc_value<MT, kPair>(racc, rows_cap, r, t, 0);
+    float* yp = y + (int64_t)t * ldy + row;
+    if (kPair) *yp = silu_f(v) * racc_value<MT, kPair>(racc, rows_cap, r, t, 1);
+    else if (EPI == kEpiAdd) *yp = __ldcg(yp) + v;  // y may be written by other CTAs
+    else *yp = v;
   }
 }
 
@@ -458,13 +494,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     fence_mbar_init();
   }
   __syncthreads();
+  Ring rg;
+  rg.base = stages;
+  rg.full = full_bar;
+  rg.empty = empty_bar;
+  rg.ns = NS;
+  rg.slot_bytes = a.slot_bytes;
 
   if (warp == kGemvConsumerWarps) {
     // producer: weights never depend on the previous kernel
     if (lane == 0) {
-      if (kPair) gemv_producer<2, true>(a, sg, gb, ge, stages, full_bar, empty_bar);
-      else if (sg.nr == 2) gemv_producer<2, false>(a, sg, gb, ge, stages, full_bar, empty_bar);
-      else gemv_producer<1, false>(a, sg, gb, ge, stages, full_bar, empty_bar);
+      if (kPair) produce_gemv<2, true>(rg, sg.w, sg.w2, gb, ge);
+      else if (sg.nr == 2) produce_gemv<2, false>(rg, sg.w, sg.w2, gb, ge);
+      else produce_gemv<1, false>(rg, sg.w, sg.w2, gb, ge);
     }
     return;
   }
@@ -478,10 +520,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     bulk_g2s((void*)sx.scale, a.xscale + (int64_t)a.t0 * (kp / 64), bs, &x_bar);
     bulk_g2s((void*)sx.s16, a.xs16 + (int64_t)a.t0 * (kp / 16), b16, &x_bar);
   }
-  const bool ok = mbar_wait_bounded(&x_bar, 0);
-  if (kPair) gemv_consumer<MT, 2, true, EPI>(a, sg, gb, ge, stages, full_bar, empty_bar, sx, ok, racc);
-  else if (sg.nr == 2) gemv_consumer<MT, 2, false, EPI>(a, sg, gb, ge, stages, full_bar, empty_bar, sx, ok, racc);
-  else gemv_consumer<MT, 1, false, EPI>(a, sg, gb, ge, stages, full_bar, empty_bar, sx, ok, racc);
+  bool ok = mbar_wait_bounded(&x_bar, 0);
+  if (kPair) consume_gemv<MT, 2, true>(rg, L, gb, ge, a.rows_cap, sx, ok, racc);
+  else if (sg.nr == 2) consume_gemv<MT, 2, false>(rg, L, gb, ge, a.rows_cap, sx, ok, racc);
+  else consume_gemv<MT, 1, false>(rg, L, gb, ge, a.rows_cap, sx, ok, racc);
+  gemv_epilogue<MT, EPI>(racc, a.rows_cap, gb, ge, L.n, sg.y, sg.ldy, ok);
   if (threadIdx.x == 0) pdl_launch_dependents();
 }
 

@@ -10,6 +10,7 @@
 #include "../../include/b2q.h"
 #include "gemv.cuh"
 #include "layer.cuh"
+#include "decode.cuh"
 
 namespace b2q {
 

@@ -7,7 +7,7 @@
 
 namespace b2q {
 
-constexpr int kAttnTile = 128;  // tokens per attention split (4 warps x 32)
+constexpr int kAttnTile = 64;  // key tokens per attention split
 constexpr int kHeadDim = 128;
 
 // RMSNorm of each row (rms_norm_rows, inference.rs:1501-1512) fused with the
@@ -22,7 +22,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_quant_kernel(
   const int t = blockIdx.x;
   const float* xr = x + (int64_t)(row0 + t) * row_stride;
   float ss = 0.0f;
-  for (int e = threadIdx.x; e < dim; e += blockDim.x) ss += xr[e] * xr[e];
+  for (int e = threadIdx.x; e < dim; e += blockDim.x) ss = fmaf(xr[e], xr[e], ss);
   ss = warp_sum(ss);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) part[warp] = ss;
@@ -99,117 +99,160 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int m, int H, int KV, in
   pdl_launch_dependents();
 }
 
-// Split-T GQA attention for queries at positions start+s (causal: keys
-// t < start+s+1).  grid (KV, m, nsplit), 128 threads.  One lane per key
-// token for the scores, one lane per 4 head dims for P*V, an online softmax
-// per warp, merged across the CTA's 4 warps; the split partials
-// (max, sum, out[hd]) go to `part` and are merged by attn_combine_kernel.
+// ---------------------------------------------------------------------------
+// Split GQA attention over the f16 KV cache (inference.rs:2782-2820).  The
+// cached keys of a query are cut into splits of kAttnTile tokens; one item =
+// (KV head g, split z) on 128 threads computes, for the G query heads of g,
+// the split's softmax partial (max, sum, unnormalised P*V).  The K and V rows
+// of the split are brought into shared memory with two bulk async copies (one
+// round trip to HBM), then everything runs from shared memory.  The same
+// item code serves the per-kernel path (attn_split_kernel) and the persistent
+// decode kernel, so both give the same bits.
+// ---------------------------------------------------------------------------
+template <int G>
+struct AttnTile {
+  __half k[kAttnTile * kHeadDim];  // rows t_begin.. of the split (reused for the P*V halves)
+  __half v[kAttnTile * kHeadDim];
+  float q[G][kHeadDim];            // rotated queries
+  float sp[2][G][kAttnTile];       // score halves; sp[0] then holds the probabilities
+  float m[G], l[G];                // softmax max and sum per head
+};
+
+// Issue the bulk copies of K/V rows [t0, t0 + rows) of KV head g into the
+// tile (one thread); completes on `bar` (expect_tx included).
+template <int G>
+__device__ __forceinline__ void attn_tile_load(AttnTile<G>& T, const __half* kc, const __half* vc, int g, int cap,
+                                               int t0, int rows, uint64_t* bar) {
+  const uint32_t bytes = (uint32_t)rows * kHeadDim * 2;
+  mbar_arrive_expect_tx(bar, 2 * bytes);
+  bulk_g2s(T.k, kc + ((int64_t)g * cap + t0) * kHeadDim, bytes, bar);
+  bulk_g2s(T.v, vc + ((int64_t)g * cap + t0) * kHeadDim, bytes, bar);
+}
+
+// The split partial of one item; T.q and the first `nv` rows of T.k / T.v
+// are in place.  `sync` is the 128-thread barrier of the item.  Writes
+// part[(h * nsplit + z) * 130] = {max, sum, O[128]} for the G heads of
+// head group g (h = g*G + i).
+template <int G, class Sync>
+__device__ __forceinline__ void attn_tile_compute(AttnTile<G>& T, int nv, float scale, float* part, int g, int z,
+                                                  int nsplit, Sync sync) {
+  constexpr int HD = kHeadDim;
+  const int tid = threadIdx.x & 127, lane = threadIdx.x & 31, w = tid >> 5;
+  // scores: thread = (token t, half dh of the dims); 16-byte chunks read in
+  // a per-token rotated order (conflict-free shared-memory phases)
+  {
+    const int t = tid & (kAttnTile - 1), dh = tid >> 6;
+    float acc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) acc[h] = 0.0f;
+    if (t < nv) {
+      const __half* kr = T.k + t * HD + dh * 64;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int cc = (c + t) & 7;
+        const uint4 pk = *reinterpret_cast<const uint4*>(kr + cc * 8);
+        const __half2* h2 = reinterpret_cast<const __half2*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 kf = __half22float2(h2[e]);
+          const int d = dh * 64 + cc * 8 + 2 * e;
+#pragma unroll
+          for (int h = 0; h < G; ++h) {
+            acc[h] = fmaf(T.q[h][d], kf.x, acc[h]);
+            acc[h] = fmaf(T.q[h][d + 1], kf.y, acc[h]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) T.sp[dh][h][t] = acc[h];
+  }
+  sync();
+  // softmax per head: warp w takes heads w, w + 4; lane holds tokens lane, lane + 32
+  for (int h = w; h < G; h += 4) {
+    const int t0 = lane, t1 = lane + 32;
+    const float s0 = t0 < nv ? (T.sp[0][h][t0] + T.sp[1][h][t0]) * scale : -INFINITY;
+    const float s1 = t1 < nv ? (T.sp[0][h][t1] + T.sp[1][h][t1]) * scale : -INFINITY;
+    const float mx = warp_max(fmaxf(s0, s1));
+    const float p0 = t0 < nv ? expf(s0 - mx) : 0.0f;
+    const float p1 = t1 < nv ? expf(s1 - mx) : 0.0f;
+    const float sum = warp_sum(p0 + p1);
+    T.sp[0][h][t0] = p0;
+    T.sp[0][h][t1] = p1;
+    if (lane == 0) { T.m[h] = mx; T.l[h] = sum; }
+  }
+  sync();
+  // P * V: thread = (dims 2dp, 2dp+1; token half th); halves summed after
+  {
+    const int dp = tid & 63, th = tid >> 6;
+    float o[G][2];
+#pragma unroll
+    for (int h = 0; h < G; ++h) o[h][0] = o[h][1] = 0.0f;
+    for (int j = 0; j < kAttnTile / 2; ++j) {
+      const int t = th * (kAttnTile / 2) + j;
+      if (t >= nv) break;
+      const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(T.v + t * HD + 2 * dp));
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float ph = T.sp[0][h][t];
+        o[h][0] = fmaf(ph, vf.x, o[h][0]);
+        o[h][1] = fmaf(ph, vf.y, o[h][1]);
+      }
+    }
+    float* o2 = reinterpret_cast<float*>(T.k);  // [2][G][HD], K is no longer read
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      o2[(th * G + h) * HD + 2 * dp] = o[h][0];
+      o2[(th * G + h) * HD + 2 * dp + 1] = o[h][1];
+    }
+  }
+  sync();
+  const float* o2 = reinterpret_cast<const float*>(T.k);
+  for (int i = tid; i < G * HD; i += 128) {
+    const int h = i / HD, d = i % HD;
+    float* pp = part + ((int64_t)(g * G + h) * nsplit + z) * (HD + 2);
+    if (d == 0) { pp[0] = T.m[h]; pp[1] = T.l[h]; }
+    pp[2 + d] = o2[h * HD + d] + o2[(G + h) * HD + d];
+  }
+}
+
+// Per-kernel path: grid (KV, m, nsplit), 128 threads, sizeof(AttnTile<G>)
+// bytes of dynamic shared memory.  Query s sits at position start+s and sees
+// keys t < start+s+1 (causal); q was rotated in place by rope_kv_kernel.
 template <int G>
 __global__ void __launch_bounds__(128) attn_split_kernel(
     const float* __restrict__ qkv, int m, int H, int KV, const int* __restrict__ pos_dev, int cap,
     const __half* __restrict__ kc, const __half* __restrict__ vc, float scale, int nsplit,
     float* __restrict__ part) {
+  extern __shared__ __align__(128) uint8_t attn_smem[];
+  __shared__ uint64_t bar;
+  AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(attn_smem);
   pdl_wait();
   constexpr int HD = kHeadDim;
-  __shared__ float qs[G][HD];
-  __shared__ float wm[4][G], wl[4][G];
-  __shared__ float wo[4][G][HD];
   const int g = blockIdx.x, s = blockIdx.y, z = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int start = *pos_dev;
   const int valid = min(start + s + 1, cap);
   const int t_begin = z * kAttnTile;
-  const int width = (H + 2 * KV) * HD;
-  float* pm = part + (((int64_t)s * H + g * G) * nsplit + z) * (HD + 2);
+  float* ps = part + (int64_t)s * H * nsplit * (HD + 2);
   if (t_begin >= valid) {
     if (threadIdx.x < G) {
-      float* p = part + (((int64_t)s * H + g * G + threadIdx.x) * nsplit + z) * (HD + 2);
+      float* p = ps + ((int64_t)(g * G + threadIdx.x) * nsplit + z) * (HD + 2);
       p[0] = -INFINITY;
       p[1] = 0.0f;
     }
     return;
   }
-  for (int i = threadIdx.x; i < G * HD; i += blockDim.x)
-    qs[i / HD][i % HD] = qkv[(int64_t)s * width + (g * G) * HD + i];
+  const int nv = min(kAttnTile, valid - t_begin);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    attn_tile_load(T, kc, vc, g, cap, t_begin, nv, &bar);
+  }
+  const int width = (H + 2 * KV) * HD;
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) T.q[i / HD][i % HD] = qkv[(int64_t)s * width + g * G * HD + i];
   __syncthreads();
-
-  const int t = t_begin + warp * 32 + lane;
-  const bool tv = t < valid;
-  float sc[G];
-#pragma unroll
-  for (int h = 0; h < G; ++h) sc[h] = 0.0f;
-  if (tv) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kc + ((int64_t)g * cap + t) * HD);
-#pragma unroll 4
-    for (int c = 0; c < HD / 8; ++c) {
-      const uint4 pk = kr[c];
-      const __half2* h2 = reinterpret_cast<const __half2*>(&pk);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 kf = __half22float2(h2[e]);
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          sc[h] = fmaf(qs[h][c * 8 + 2 * e], kf.x, sc[h]);
-          sc[h] = fmaf(qs[h][c * 8 + 2 * e + 1], kf.y, sc[h]);
-        }
-      }
-    }
-  }
-  float mx[G], l[G], p[G];
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    const float sv = tv ? sc[h] * scale : -INFINITY;
-    mx[h] = warp_max(sv);
-    p[h] = tv ? expf(sv - mx[h]) : 0.0f;
-    l[h] = warp_sum(p[h]);
-  }
-  // P * V over this warp's 32 tokens; lane owns dims 4*lane .. 4*lane+3
-  float o[G][4];
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[h][e] = 0.0f;
-  const int nt = min(32, valid - (t_begin + warp * 32));
-  for (int src = 0; src < nt; ++src) {
-    const int ts = t_begin + warp * 32 + src;
-    const uint2 pv = *reinterpret_cast<const uint2*>(vc + ((int64_t)g * cap + ts) * HD + 4 * lane);
-    const __half2* v2 = reinterpret_cast<const __half2*>(&pv);
-    const float2 va = __half22float2(v2[0]), vb = __half22float2(v2[1]);
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float ph = __shfl_sync(B2Q_FULL, p[h], src);
-      o[h][0] = fmaf(ph, va.x, o[h][0]);
-      o[h][1] = fmaf(ph, va.y, o[h][1]);
-      o[h][2] = fmaf(ph, vb.x, o[h][2]);
-      o[h][3] = fmaf(ph, vb.y, o[h][3]);
-    }
-  }
-  if (lane == 0) {
-#pragma unroll
-    for (int h = 0; h < G; ++h) { wm[warp][h] = mx[h]; wl[warp][h] = l[h]; }
-  }
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) wo[warp][h][4 * lane + e] = o[h][e];
-  __syncthreads();
-  // merge the 4 warps: thread handles (h, d) pairs
-  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-    const int h = i / HD, d = i % HD;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w2 = 0; w2 < 4; ++w2) M = fmaxf(M, wm[w2][h]);
-    float L = 0.0f, O = 0.0f;
-#pragma unroll
-    for (int w2 = 0; w2 < 4; ++w2) {
-      const float f = wm[w2][h] == -INFINITY ? 0.0f : expf(wm[w2][h] - M);
-      L += f * wl[w2][h];
-      O += f * wo[w2][h][d];
-    }
-    float* pp = pm + (int64_t)h * nsplit * (HD + 2);
-    if (d == 0) { pp[0] = M; pp[1] = L; }
-    pp[2 + d] = O;
-  }
+  mbar_wait_bounded(&bar, 0);  // a timeout is recorded in the device error word
+  attn_tile_compute<G>(T, nv, scale, ps, g, z, nsplit, [] { __syncthreads(); });
   pdl_launch_dependents();
 }
 
@@ -234,8 +277,8 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int m, int H
   for (int z = 0; z < ns; ++z) {
     const float mz = pp[z * (HD + 2)];
     const float f = mz == -INFINITY ? 0.0f : expf(mz - M);
-    L += f * pp[z * (HD + 2) + 1];
-    O += f * pp[z * (HD + 2) + 2 + d];
+    L = fmaf(f, pp[z * (HD + 2) + 1], L);
+    O = fmaf(f, pp[z * (HD + 2) + 2 + d], O);
   }
   const float v = O * (1.0f / fmaxf(L, 1e-12f));
   const int col0 = g * G * HD;

@@ -279,7 +279,11 @@ b2q_status b2q_model_finalize(b2q_model* M) {
   }
   err = cudaDeviceSynchronize();
   if (err != cudaSuccess) return cuda_error(err, "b2q_model_finalize: sync");
-  if (!c.no_graph) {
+  if (c.no_graph == 2) {
+    err = setup_decode(M);
+    if (err != cudaSuccess) return cuda_error(err, "b2q_model_finalize: persistent decode set-up");
+  }
+  if (c.no_graph == 0 || (c.no_graph == 2 && !M->dec_on)) {
     err = build_decode_graph(M);
     if (err != cudaSuccess) return cuda_error(err, "b2q_model_finalize: decode graph capture");
   }
@@ -287,8 +291,11 @@ b2q_status b2q_model_finalize(b2q_model* M) {
   return B2Q_OK;
 }
 
+// `argmax_dev` (optional): a device word that a single-token step on the
+// persistent kernel writes directly; *argmax_done tells the caller so.
 static b2q_status forward_impl(b2q_model* M, const uint32_t* tokens, bool tok_on_dev, int n, int start,
-                               cudaStream_t st) {
+                               cudaStream_t st, uint32_t* argmax_dev = nullptr, bool* argmax_done = nullptr) {
+  if (argmax_done) *argmax_done = false;
   const b2q_model_config& c = M->c;
   if (n <= 0) return set_error(B2Q_EINVAL, "forward: no tokens");
   if (start < 0 || start + n > c.max_seq)
@@ -308,6 +315,13 @@ static b2q_status forward_impl(b2q_model* M, const uint32_t* tokens, bool tok_on
       err = cudaMemcpyAsync(M->tokens + M->mmax, M->h_tok, sizeof(uint32_t) * m, cudaMemcpyHostToDevice, st);
       if (err != cudaSuccess) break;
       src = M->tokens + M->mmax;
+    }
+    if (m == 1 && M->dec_on) {
+      // one persistent kernel for the whole step (validates the id itself)
+      err = launch_decode(M, src, start + off, argmax_dev, st);
+      if (err == cudaSuccess && argmax_done) *argmax_done = argmax_dev != nullptr;
+      if (err == cudaSuccess && !tok_on_dev && off + m < n) err = cudaStreamSynchronize(st);
+      continue;
     }
     launch_counted(M->eng, 1);
     set_step_kernel<<<1, 64, 0, st>>>(M->pos, start + off, M->tokens, src, m, c.n_vocab);
@@ -333,12 +347,13 @@ b2q_status b2q_forward_dev(b2q_model* M, const uint32_t* tokens_dev, int n, int 
   std::lock_guard<std::mutex> lk(M->eng->mu);
   cudaSetDevice(M->eng->device);
   cudaStream_t st = stream ? (cudaStream_t)stream : M->st;
-  b2q_status s = forward_impl(M, tokens_dev, true, n, start, st);
+  bool argmax_done = false;
+  b2q_status s = forward_impl(M, tokens_dev, true, n, start, st, argmax_dev, &argmax_done);
   if (s != B2Q_OK) return s;
   cudaError_t err = cudaSuccess;
   if (logits_dev)
     err = cudaMemcpyAsync(logits_dev, M->logits, sizeof(float) * M->c.n_vocab, cudaMemcpyDeviceToDevice, st);
-  if (err == cudaSuccess && argmax_dev)
+  if (err == cudaSuccess && argmax_dev && !argmax_done)
     err = cudaMemcpyAsync(argmax_dev, M->argmax, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st);
   if (err != cudaSuccess) return cuda_error(err, "b2q_forward_dev: copy out");
   return B2Q_OK;
@@ -367,6 +382,15 @@ b2q_status b2q_clear_state(b2q_model* M) {
   // what the caller considers the current position; entries past it are
   // never read (attention reads keys t < start + s + 1).
   if (!M) return set_error(B2Q_EINVAL, "b2q_clear_state: NULL model");
+  if (M->dec_sync) {
+    // re-arm the persistent kernel's barrier words (a step that gave up on
+    // a wait can leave them inconsistent)
+    std::lock_guard<std::mutex> lk(M->eng->mu);
+    cudaSetDevice(M->eng->device);
+    cudaError_t err = cudaMemsetAsync(M->dec_sync, 0, sizeof(b2q::DecSync), M->st);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
+    if (err != cudaSuccess) return cuda_error(err, "b2q_clear_state");
+  }
   return B2Q_OK;
 }
 
@@ -390,7 +414,7 @@ b2q_status b2q_model_destroy(b2q_model* M) {
   b2q_weight_free(M->output);
   void* ps[] = {M->tok_raw, M->output_norm, M->x, M->qkv, M->attn, M->attn_loc, M->hbuf, M->h_loc,
                 M->y_loc, M->logits, M->logits_loc, M->part, M->tokens, M->argmax, M->pos,
-                M->rope_cos, M->rope_sin};
+                M->rope_cos, M->rope_sin, M->dec_layers, M->dec_tab, M->dec_sync, M->dec_cand};
   for (void* p : ps)
     if (p) cudaFree(p);
   xq_free(&M->xq_e);

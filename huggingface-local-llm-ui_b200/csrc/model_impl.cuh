@@ -65,6 +65,15 @@ struct b2q_model {
   // decode graph (m = 1)
   cudaGraphExec_t graph = nullptr;
   uint64_t graph_kernels = 0;
+  // persistent decode kernel (m = 1, one GPU)
+  b2q::DecLayer* dec_layers = nullptr;
+  b2q::CtaPhase* dec_tab = nullptr;
+  b2q::DecSync* dec_sync = nullptr;
+  int2* dec_cand = nullptr;
+  b2q::DecodeArgs dec{};
+  size_t dec_smem = 0;
+  int dec_G = 0;
+  bool dec_on = false;
   bool finalized = false;
   std::map<std::string, bool> have;
 };
@@ -207,7 +216,9 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
     // attention (split over the cached tokens) + combine/quantise
     {
       float* aout = P > 1 ? M->attn_loc : M->attn;
-      cudaLaunchConfig_t cfg = lcfg(dim3(KVl, m, M->nsplit), dim3(128), 0, st, attr, pdl);
+      const size_t tile = G == 4 ? sizeof(AttnTile<4>) : G == 8 ? sizeof(AttnTile<8>)
+                        : G == 2 ? sizeof(AttnTile<2>) : sizeof(AttnTile<1>);
+      cudaLaunchConfig_t cfg = lcfg(dim3(KVl, m, M->nsplit), dim3(128), tile, st, attr, pdl);
       launch_counted(e, 1);
       if (G == 4)
         err = cudaLaunchKernelEx(&cfg, attn_split_kernel<4>, (const float*)M->qkv, m, Hl, KVl,
@@ -363,6 +374,247 @@ static cudaError_t build_decode_graph(b2q_model* M) {
   // capture does not launch anything
   M->eng->launches.fetch_sub(M->graph_kernels);
   return err;
+}
+
+// ---------------------------------------------------------------------------
+// persistent decode kernel (decode.cuh): plan and launch
+// ---------------------------------------------------------------------------
+
+// One phase of the persistent kernel: the grid (one CTA per SM) is split
+// over the phase's weights in proportion to their bytes, as launch_gemv_t
+// splits its grid, but never beyond the grid.
+constexpr int kDecStageMax = 56 * 1024;  // two tiles per stage when they fit
+
+static void plan_dec_phase(DecPhase* ph, b2q_weight* const* ws, const b2q_weight* w2, int nw, const int* ycol,
+                           bool pair, int grid, int* stage_max) {
+  memset(ph, 0, sizeof *ph);
+  ph->nseg = nw;
+  ph->pair = pair ? 1 : 0;
+  double bytes[kDecSegs], total = 0.0;
+  for (int s = 0; s < nw; ++s) {
+    const TileLayout& L = ws[s]->view.L;
+    const int tb = (int)tile_bytes(L);
+    DecSeg& sg = ph->seg[s];
+    sg.w = ws[s]->view;
+    sg.w2 = pair ? w2->view : ws[s]->view;
+    sg.nr = (pair || 2 * tb <= kDecStageMax) ? 2 : 1;
+    sg.ycol = ycol[s];
+    *stage_max = std::max(*stage_max, tb * sg.nr);
+    bytes[s] = (double)L.G * L.C * tb * (pair ? 2 : 1);
+    total += bytes[s];
+  }
+  int n[kDecSegs], sum = 0;
+  for (int s = 0; s < nw; ++s) {
+    n[s] = (int)((double)grid * bytes[s] / total + 0.5);
+    n[s] = std::max(1, std::min(n[s], ph->seg[s].w.L.G));
+    sum += n[s];
+  }
+  while (sum > grid) {
+    int big = 0;
+    for (int s = 1; s < nw; ++s)
+      if (n[s] > n[big]) big = s;
+    if (n[big] <= 1) break;
+    --n[big];
+    --sum;
+  }
+  int cta = 0;
+  for (int s = 0; s < nw; ++s) {
+    ph->seg[s].cta0 = cta;
+    ph->seg[s].ncta = n[s];
+    cta += n[s];
+  }
+}
+
+// The consumers' view of a phase for CTA b (cta_range in decode.cuh).
+static CtaPhase cta_phase(const DecPhase& ph, int b) {
+  CtaPhase r;
+  memset(&r, 0, sizeof r);
+  for (int s = 0; s < ph.nseg; ++s) {
+    const DecSeg& sg = ph.seg[s];
+    if (b < sg.cta0 || b >= sg.cta0 + sg.ncta) continue;
+    const TileLayout& L = sg.w.L;
+    const int ci = b - sg.cta0;
+    r.gb = (int)((int64_t)L.G * ci / sg.ncta);
+    r.ge = (int)((int64_t)L.G * (ci + 1) / sg.ncta);
+    r.dtype_nr = L.dtype | ((ph.pair ? 2 : sg.nr) << 8);
+    r.KC = L.KC;
+    r.C = L.C;
+    r.U = L.U;
+    r.n = L.n;
+    r.ycol = sg.ycol;
+    break;
+  }
+  return r;
+}
+
+template <int G>
+static void* decode_kernel_for() { return reinterpret_cast<void*>(decode_kernel<G>); }
+
+static void* decode_kernel_ptr(int G, size_t* attn_smem) {
+  switch (G) {
+    case 1: *attn_smem = sizeof(AttnTile<1>); return decode_kernel_for<1>();
+    case 2: *attn_smem = sizeof(AttnTile<2>); return decode_kernel_for<2>();
+    case 4: *attn_smem = sizeof(AttnTile<4>); return decode_kernel_for<4>();
+    case 8: *attn_smem = sizeof(AttnTile<8>); return decode_kernel_for<8>();
+    default: return nullptr;
+  }
+}
+
+static size_t round128(size_t v) { return (v + 127) / 128 * 128; }
+
+// Builds the persistent decode plan.  Leaves dec_on false (single-token
+// steps then use the captured graph) when the model does not fit it:
+// tensor parallelism, an unsupported head grouping, or too little shared
+// memory for two pipeline stages.
+static cudaError_t setup_decode(b2q_model* M) {
+  const b2q_model_config& c = M->c;
+  b2q_engine* e = M->eng;
+  M->dec_on = false;
+  if (c.tp_size != 1 || c.n_kv_heads > 64) return cudaSuccess;
+  const int H = c.n_heads, KV = c.n_kv_heads, G = H / KV, hd = c.head_dim;
+  size_t attn_one = 0;
+  void* kern = decode_kernel_ptr(G, &attn_one);
+  if (!kern) return cudaSuccess;
+  // the split merge stages {max, sum} of every split of a head group in one tile
+  if (2 * G * M->nsplit > kAttnTile * kHeadDim / 2) return cudaSuccess;
+  const int grid = e->num_sms;
+  int stage_max = 0;
+  std::vector<DecLayer> host((size_t)c.n_layers);
+  std::vector<const DecPhase*> phases;
+  const int y0[1] = {0};
+  for (int l = 0; l < c.n_layers; ++l) {
+    LayerW& w = M->L[l];
+    DecLayer& d = host[(size_t)l];
+    memset(&d, 0, sizeof d);
+    b2q_weight* qkv[3] = {w.q, w.k, w.v};
+    const int yc[3] = {0, H * hd, (H + KV) * hd};
+    plan_dec_phase(&d.ph[kPhQKV], qkv, nullptr, 3, yc, false, grid, &stage_max);
+    b2q_weight* o[1] = {w.o};
+    plan_dec_phase(&d.ph[kPhO], o, nullptr, 1, y0, false, grid, &stage_max);
+    b2q_weight* gt[1] = {w.gate};
+    plan_dec_phase(&d.ph[kPhGU], gt, w.up, 1, y0, true, grid, &stage_max);
+    b2q_weight* dn[1] = {w.down};
+    plan_dec_phase(&d.ph[kPhDown], dn, nullptr, 1, y0, false, grid, &stage_max);
+    d.attn_norm = w.attn_norm;
+    d.ffn_norm = w.ffn_norm;
+    d.qb = w.q_bias;
+    d.kb = w.k_bias;
+    d.vb = w.v_bias;
+    d.kc = w.kc;
+    d.vc = w.vc;
+  }
+  DecodeArgs& a = M->dec;
+  memset(&a, 0, sizeof a);
+  b2q_weight* hw[1] = {M->output};
+  plan_dec_phase(&a.head, hw, nullptr, 1, y0, false, grid, &stage_max);
+  for (auto& d : host)
+    for (int p = 0; p < kDecPhases; ++p) phases.push_back(&d.ph[p]);
+  phases.push_back(&a.head);
+  const int nph = (int)phases.size();
+  // per-CTA phase tables and the accumulator size
+  std::vector<CtaPhase> tab((size_t)grid * nph);
+  size_t racc = 128;
+  for (int b = 0; b < grid; ++b)
+    for (int p = 0; p < nph; ++p) {
+      const CtaPhase r = cta_phase(*phases[(size_t)p], b);
+      tab[(size_t)b * nph + p] = r;
+      racc = std::max(racc, (size_t)2 * (phases[(size_t)p]->pair ? 2 : 1) * (r.ge - r.gb) * 8 * sizeof(float));
+    }
+  racc = round128(racc);
+  // shared memory: [ring][staging][accumulators][phase table]; attention
+  // tiles overlay staging + accumulators (idle during attention)
+  const int kp_e = round_up_int(c.n_embd, 256);
+  const int kpmax = std::max({kp_e, round_up_int(H * hd, 256), round_up_int(c.n_ff, 256)});
+  const size_t tile = round128(attn_one);
+  size_t stage = std::max(xq_smem_bytes(kpmax), xq_smem_bytes(kp_e) + (size_t)4 * c.n_embd);
+  if (stage + racc < tile) stage = tile - racc;
+  stage = round128(stage);
+  const int ngrp = (int)std::min<size_t>(4, (stage + racc) / tile);
+  const size_t tabb = round128((size_t)nph * sizeof(CtaPhase));
+  cudaFuncAttributes fa;
+  cudaError_t err = cudaFuncGetAttributes(&fa, kern);
+  if (err != cudaSuccess) return err;
+  const size_t budget = (size_t)232448 - fa.sharedSizeBytes;
+  if (stage + racc + tabb + 2 * (size_t)stage_max > budget) return cudaSuccess;
+  const size_t cap = (budget - stage - racc - tabb) / 128 * 128;
+  const size_t smem = cap + stage + racc + tabb;
+  err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return err;
+  int per_sm = 0;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGemvThreads, smem);
+  if (err != cudaSuccess) return err;
+  if (per_sm < 1) return cudaSuccess;
+  err = dalloc(&M->dec_layers, host.size());
+  if (err == cudaSuccess)
+    err = cudaMemcpy(M->dec_layers, host.data(), host.size() * sizeof(DecLayer), cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = dalloc(&M->dec_tab, tab.size());
+  if (err == cudaSuccess)
+    err = cudaMemcpy(M->dec_tab, tab.data(), tab.size() * sizeof(CtaPhase), cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = dalloc(&M->dec_sync, 1);
+  if (err == cudaSuccess) err = dalloc(&M->dec_cand, (size_t)grid);
+  if (err != cudaSuccess) return err;
+  a.layers = M->dec_layers;
+  a.ctab = M->dec_tab;
+  a.nph = nph;
+  a.n_layers = c.n_layers;
+  a.E = c.n_embd;
+  a.H = H;
+  a.KV = KV;
+  a.F = c.n_ff;
+  a.V = c.n_vocab;
+  a.eps = c.rms_eps;
+  a.scale = 1.0f / sqrtf((float)hd);
+  a.max_seq = c.max_seq;
+  a.out_norm = M->output_norm;
+  a.tok_raw = static_cast<const uint8_t*>(M->tok_raw);
+  a.tok_dtype = M->tok_dtype;
+  a.tok_row_bytes = M->tok_row_bytes;
+  a.rope_cos = M->rope_cos;
+  a.rope_sin = M->rope_sin;
+  a.x = M->x;
+  a.qkv = M->qkv;
+  a.attn = M->attn;
+  a.h = M->hbuf;
+  a.logits = M->logits;
+  a.part = M->part;
+  a.nsplit = M->nsplit;
+  a.sync = M->dec_sync;
+  a.cand = M->dec_cand;
+  a.argmax = M->argmax;
+  a.cap = (int)cap;
+  a.stage_bytes = (int)stage;
+  a.racc_bytes = (int)racc;
+  a.tile_bytes = (int)tile;
+  a.ngrp = ngrp;
+  M->dec_smem = smem;
+  M->dec_G = G;
+  M->dec_on = true;
+  return cudaSuccess;
+}
+
+// One single-token step: token id at `tok` (device), position `pos`.
+static cudaError_t launch_decode(b2q_model* M, const uint32_t* tok, int pos, uint32_t* argmax2, cudaStream_t st) {
+  DecodeArgs a = M->dec;
+  a.token = tok;
+  a.pos = pos;
+  a.argmax2 = argmax2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M->eng->num_sms);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = M->dec_smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  launch_counted(M->eng, 1);
+  switch (M->dec_G) {
+    case 1: return cudaLaunchKernelEx(&cfg, decode_kernel<1>, a);
+    case 2: return cudaLaunchKernelEx(&cfg, decode_kernel<2>, a);
+    case 4: return cudaLaunchKernelEx(&cfg, decode_kernel<4>, a);
+    default: return cudaLaunchKernelEx(&cfg, decode_kernel<8>, a);
+  }
 }
 
 }  // namespace b2q

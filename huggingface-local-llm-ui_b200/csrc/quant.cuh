@@ -77,6 +77,62 @@ __device__ __forceinline__ void xq_store_block(float v0, float v1, int lane, int
   }
 }
 
+// The same for N blocks at once (block i = j0 + i * jstride, skipped when
+// >= nb), with the reductions of the N blocks interleaved so that their
+// shuffle chains overlap instead of running one after another.  Values are
+// those of xq_store_block.
+template <int N>
+__device__ __forceinline__ void xq_store_blocks(const float (&v0)[N], const float (&v1)[N], int lane, int t, int j0,
+                                                int jstride, int nb, const XQ& xq) {
+  float amax[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) amax[i] = fmaxf(fabsf(v0[i]), fabsf(v1[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < N; ++i) amax[i] = fmaxf(amax[i], __shfl_xor_sync(B2Q_FULL, amax[i], o));
+  int s0[N], s1[N];
+  const int kp = xq.kpad;
+  int16_t* qr = xq.q + (int64_t)t * kp;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    int q0 = 0, q1 = 0;
+    if (amax[i] > 0.0f && amax[i] <= 3.0e38f) {
+      const float inv = (float)kXMax / amax[i];
+      q0 = max(-kXMax, min(kXMax, __float2int_rn(v0[i] * inv)));
+      q1 = max(-kXMax, min(kXMax, __float2int_rn(v1[i] * inv)));
+    }
+    const int j = j0 + i * jstride;
+    if (j < nb) {
+      qr[xswz(j * 64 + lane)] = (int16_t)q0;
+      qr[xswz(j * 64 + 32 + lane)] = (int16_t)q1;
+    }
+    s0[i] = q0;
+    s1[i] = q1;
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      s0[i] += __shfl_xor_sync(B2Q_FULL, s0[i], o);
+      s1[i] += __shfl_xor_sync(B2Q_FULL, s1[i], o);
+    }
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const int j = j0 + i * jstride;
+    if (j >= nb) continue;
+    int32_t* sr = xq.s16 + (int64_t)t * (kp / 16) + 4 * j;
+    if (lane == 0) {
+      sr[0] = s0[i];
+      sr[2] = s1[i];
+      xq.scale[(int64_t)t * (kp / 64) + j] = (amax[i] > 0.0f && amax[i] <= 3.0e38f) ? amax[i] / (float)kXMax : 0.0f;
+    } else if (lane == 16) {
+      sr[1] = s0[i];
+      sr[3] = s1[i];
+    }
+  }
+}
+
 // x [m][k] f32 -> XQ (all kpad/64 blocks of every row, zero tail).
 __global__ void quantize_x_kernel(const float* __restrict__ x, int m, int k, XQ xq) {
   pdl_wait();

@@ -32,14 +32,27 @@ def tp_unique_id() -> bytes:
 class StandardNativeEngine:
     """Llama-family decoder on one device, or one tensor-parallel rank."""
 
+    # single-token step modes (b2q_model_config.no_graph)
+    DECODE_MODES = {"graph": 0, "eager": 1, "persistent": 2}
+
     def __init__(self, engine: CudaEngine, cfg: dict, max_seq: int = 8192, tp_rank: int = 0,
-                 tp_size: int = 1, tp_id: bytes | None = None, use_graph: bool = True):
+                 tp_size: int = 1, tp_id: bytes | None = None, use_graph: bool = True,
+                 decode: str | None = None):
+        """`decode` picks how single-token steps run: "graph" (default: the
+        captured graph of the per-layer kernels), "eager" (the same kernels
+        launched one by one; also use_graph=False) or "persistent" (one
+        persistent kernel per token on one GPU; the graph under tensor
+        parallelism).  All three give the same logits bit for bit."""
         self.engine = engine
         self.cfg = dict(cfg)
         self.max_seq = max_seq
+        mode = decode or ("graph" if use_graph else "eager")
+        if mode not in self.DECODE_MODES:
+            raise ValueError(f"decode must be one of {sorted(self.DECODE_MODES)}")
+        self.decode_mode = mode
         c = ModelConfig(cfg["n_layers"], cfg["n_embd"], cfg["n_heads"], cfg["n_kv_heads"],
                         cfg["head_dim"], cfg["n_ff"], cfg["n_vocab"], cfg["rms_eps"],
-                        cfg["rope_theta"], max_seq, tp_rank, tp_size, 0 if use_graph else 1)
+                        cfg["rope_theta"], max_seq, tp_rank, tp_size, self.DECODE_MODES[mode])
         h = C.c_void_p()
         idbuf = (C.c_ubyte * 128).from_buffer_copy(tp_id) if tp_id else None
         check(lib().b2q_model_create(engine.handle, C.byref(c), idbuf, C.byref(h)))

@@ -77,11 +77,11 @@ def test_llama3_8b_geometry_two_layers(engine, orc, pkg):
 
 def test_graph_decode_equals_eager(engine, orc, pkg):
     """The captured single-token graph and the eager path give identical
-    logits (same kernels, same order)."""
+    logits (same kernels, same order), the eager step on a foreign stream."""
     import torch
     from hf_llm_b200 import model, synth
     t = synth.llama_tensors(TOY, model.q4_k_m_types(), 5, dist="unit")
-    a_m = model.StandardNativeEngine(engine, TOY, max_seq=64)
+    a_m = model.StandardNativeEngine(engine, TOY, max_seq=64, decode="graph")
     b_m = model.StandardNativeEngine(engine, TOY, max_seq=64, use_graph=False)
     for mm in (a_m, b_m):
         for name, (dt, dims, arr) in t.items():
@@ -95,6 +95,66 @@ def test_graph_decode_equals_eager(engine, orc, pkg):
     b_m.forward_dev(tok.data_ptr(), 1, 3, lb.data_ptr(), 0, s.cuda_stream)  # eager, other stream
     s.synchronize()
     assert np.array_equal(la, lb.cpu().numpy())
+
+
+@pytest.mark.parametrize("gqa", [1, 2, 4, 8])
+def test_persistent_decode_bit_identical(engine, orc, pkg, gqa):
+    """The persistent decode kernel computes every value with the operations
+    and order of the per-kernel path: logits and argmax agree bit for bit
+    with the eager and graph steps, step after step, across the 128-key
+    attention split boundary, and stay within the fp64 tolerance."""
+    from hf_llm_b200 import model, synth
+    cfg = dict(TOY, n_heads=8, n_kv_heads=8 // gqa)
+    t = synth.llama_tensors(cfg, model.q4_k_m_types(), 20 + gqa, dist="unit")
+    modes = ("persistent", "graph", "eager")
+    ms = {md: model.StandardNativeEngine.from_tensors(engine, cfg, t, max_seq=320, decode=md) for md in modes}
+    ref = orc.Model(cfg, t, kv_capacity=320)
+    rng = np.random.default_rng(gqa)
+    prompt = rng.integers(0, cfg["n_vocab"], 125).tolist()
+    first = {md: m.forward(prompt, 0) for md, m in ms.items()}
+    b = ref.forward_f64(prompt, 0, kv_f16=True)
+    tok = int(np.argmax(first["eager"]))
+    for step in range(6):  # positions 125..130: the step at 128 opens a second split
+        pos = 125 + step
+        outs = {md: m.forward([tok], pos) for md, m in ms.items()}
+        b = ref.forward_f64([tok], pos, kv_f16=True)
+        for md in ("persistent", "graph"):
+            assert np.array_equal(outs[md].view(np.uint32), outs["eager"].view(np.uint32)), (md, pos)
+        assert rel_l2(outs["persistent"], b) <= TOL, f"pos {pos}: {rel_l2(outs['persistent'], b)}"
+        # argmax written by the kernel itself == first index of the maximum
+        am = {md: m.forward_argmax([tok], pos) for md, m in ms.items()}
+        assert am["persistent"] == am["eager"] == am["graph"] == int(np.argmax(outs["eager"]))
+        tok = am["eager"]
+
+
+def test_persistent_decode_llama3_8b_geometry(engine, orc, pkg):
+    """Llama-3-8B widths (4096 / 32:8 heads / 14336 / vocab 128256), the
+    benchmark's weight distributions, one layer: the persistent step equals
+    the eager step bit for bit, including the 128256-row output head split
+    over the grid and the grid-wide argmax, through the device-pointer API
+    on a foreign stream."""
+    import torch
+    from hf_llm_b200 import model, synth
+    cfg = dict(model.LLAMA3_8B, n_layers=1)
+    t = synth.llama_tensors(cfg, model.q4_k_m_types(), 17, dist="bench")
+    pm = model.StandardNativeEngine.from_tensors(engine, cfg, t, max_seq=64, decode="persistent")
+    em = model.StandardNativeEngine.from_tensors(engine, cfg, t, max_seq=64, decode="eager")
+    assert pm.decode_mode == "persistent"
+    toks = [128000, 791, 4062, 14198, 39935]
+    for m in (pm, em):
+        m.forward(toks, 0)
+    s = torch.cuda.Stream()
+    tok = torch.tensor([1234], dtype=torch.int32, device="cuda")
+    res = {}
+    for name, m in (("p", pm), ("e", em)):
+        lg = torch.empty(cfg["n_vocab"], dtype=torch.float32, device="cuda")
+        am = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+        m.forward_dev(tok.data_ptr(), 1, 5, lg.data_ptr(), am.data_ptr(), s.cuda_stream)
+        s.synchronize()
+        res[name] = (lg.cpu().numpy(), int(am.item()))
+    assert np.array_equal(res["p"][0].view(np.uint32), res["e"][0].view(np.uint32))
+    assert res["p"][1] == res["e"][1] == int(np.argmax(res["e"][0]))
+    engine.check_device_error()
 
 
 def test_greedy_generation_follows_fp64_argmax(engine, orc, pkg):
