@@ -142,7 +142,7 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def build_model(pkg, engine, cfg, seed, rank, size, tp_id, max_seq, dist="bench", decode="graph"):
+def build_model(pkg, engine, cfg, seed, rank, size, tp_id, max_seq, dist="bench", decode="persistent"):
     from hf_llm_b200 import model, synth
     m = model.StandardNativeEngine(engine, cfg, max_seq=max_seq, tp_rank=rank, tp_size=size, tp_id=tp_id,
                                    decode=decode)
@@ -268,7 +268,7 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--e2e-steps", type=int, default=64)
-    ap.add_argument("--decode", default="graph", choices=["graph", "persistent", "eager"],
+    ap.add_argument("--decode", default="persistent", choices=["persistent", "graph", "eager"],
                     help="single-token step: captured kernel graph, one persistent kernel, or eager")
     ap.add_argument("--no-gemv-shapes", action="store_true", help="skip the per-shape GEMV timings")
     ap.add_argument("--gemv-only", default=None,

@@ -714,6 +714,12 @@ uint64_t b2q_kernel_launch_count(b2q_engine* e) { return e ? e->launches.load() 
 int b2q_debug_decode_trace(void* host, size_t bytes) {
   return cudaMemcpyFromSymbol(host, b2q::g_dec_trace, std::min(bytes, sizeof(b2q::g_dec_trace))) == cudaSuccess ? 0 : 1;
 }
+int b2q_debug_decode_wait(void* host, size_t bytes) {
+  return cudaMemcpyFromSymbol(host, b2q::g_dec_wait, std::min(bytes, sizeof(b2q::g_dec_wait))) == cudaSuccess ? 0 : 1;
+}
+int b2q_debug_decode_fine(void* host, size_t bytes) {
+  return cudaMemcpyFromSymbol(host, b2q::g_dec_fine, std::min(bytes, sizeof(b2q::g_dec_fine))) == cudaSuccess ? 0 : 1;
+}
 int b2q_debug_decode_dbg(void* host, size_t bytes) {
   return cudaMemcpyFromSymbol(host, b2q::g_dec_dbg, std::min(bytes, sizeof(b2q::g_dec_dbg))) == cudaSuccess ? 0 : 1;
 }

@@ -80,9 +80,8 @@ struct CtaPhase {
   int ycol;       // first output column
 };
 
-// Synchronisation words (zeroed at set-up; every complete launch leaves
-// them consistent: the barrier count stays a multiple of the grid size and
-// the arrival counters return to zero).
+// Synchronisation words (zeroed at set-up; every complete launch returns
+// them to zero).
 struct DecSync {
   unsigned long long bar;  // grid barrier arrivals (monotonic)
   unsigned int head_cnt;   // CTAs done with their argmax candidate
@@ -121,8 +120,6 @@ struct DecodeArgs {
   int cap;
   int stage_bytes;
   int racc_bytes;
-  int tile_bytes;         // one attention tile (AttnTile<G>), 128-byte multiple
-  int ngrp;               // attention items processed at once per CTA (<= 4)
 };
 
 // Row-chunk bytes and aux offsets of a tile layout (make_tile_layout).
@@ -155,6 +152,19 @@ __device__ __forceinline__ void dec_trace(int slot, bool producer) {
 #define B2Q_TRACE(slot) do { if (threadIdx.x == 0) dec_trace((slot), false); } while (0)
 #define B2Q_PTRACE(slot) dec_trace((slot), true)
 __device__ int g_dec_dbg[2 * 160 * 160 * 4];
+// fine stamps of one layer: [cta][32]
+__device__ unsigned long long g_dec_fine[160 * 32];
+__device__ int g_dec_fine_layer = 1;
+// per CTA per phase: cycles warp 0 spent waiting for full stages, cycles of the whole consume
+__device__ long long g_dec_wait[160 * 160 * 2];
+#define B2Q_FTRACE(layer, i)                                                                  \
+  do {                                                                                        \
+    if (threadIdx.x % 128 == 0 && (layer) == g_dec_fine_layer && blockIdx.x < 160) {          \
+      unsigned long long t_;                                                                  \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                  \
+      g_dec_fine[blockIdx.x * 32 + (i)] = t_;                                                 \
+    }                                                                                         \
+  } while (0)
 #define B2Q_DBG(prod, ph, v0, v1, v2, v3)                                                   \
   do {                                                                                     \
     if (blockIdx.x < 160 && (ph) < 160) {                                                 \
@@ -164,6 +174,7 @@ __device__ int g_dec_dbg[2 * 160 * 160 * 4];
   } while (0)
 #else
 #define B2Q_DBG(prod, ph, v0, v1, v2, v3) do { } while (0)
+#define B2Q_FTRACE(layer, i) do { } while (0)
 #define B2Q_TRACE(slot) do { } while (0)
 #define B2Q_PTRACE(slot) do { } while (0)
 #endif
@@ -177,15 +188,16 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
   return v;
 }
 
-// Barrier over the consumer warps of every CTA.  `s_ok` (shared) turns 0
-// when this CTA's wait gave up; later barriers are then skipped.
-__device__ __forceinline__ void grid_sync(unsigned long long* bar, volatile int* s_ok) {
+// Barrier over the consumer warps of every CTA.  The counter starts every
+// launch at 0 (the last CTA to finish resets it), so barrier number k
+// completes at (k + 1) * gridDim.x arrivals: the arrival is a release
+// reduction that does not wait for a reply.  `s_ok` (shared) turns 0 when
+// this CTA's wait gave up; later barriers are then skipped.
+__device__ __forceinline__ void grid_sync(unsigned long long* bar, int& k, volatile int* s_ok) {
   consumer_sync();
   if (threadIdx.x == 0 && *s_ok) {
-    __threadfence();
-    const unsigned long long n = gridDim.x;
-    const unsigned long long old = atomicAdd(bar, 1ull);
-    const unsigned long long target = (old / n + 1ull) * n;
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
+    const unsigned long long target = (unsigned long long)(k + 1) * gridDim.x;
     const long long t0 = clock64();
     while (ld_acquire_u64(bar) < target) {
       if (clock64() - t0 > kSpinLimitCycles) {
@@ -194,8 +206,8 @@ __device__ __forceinline__ void grid_sync(unsigned long long* bar, volatile int*
         break;
       }
     }
-    __threadfence();
   }
+  ++k;
   consumer_sync();
 }
 
@@ -210,7 +222,7 @@ __device__ __forceinline__ void group_sync(int g) {
 // issued in batches ahead of their use; the quantisation reductions of a
 // batch are interleaved (xq_store_blocks).
 // ---------------------------------------------------------------------------
-constexpr int kStageBatch = 8;  // 64-element blocks per warp per batch
+constexpr int kStageBatch = 4;  // x elements per thread per load batch / 1024
 
 __device__ __forceinline__ XQ smem_xq(uint8_t* xs, int kpad) {
   XQ q;
@@ -233,12 +245,16 @@ __device__ __forceinline__ SX smem_sx(const XQ& q) {
 __host__ __device__ __forceinline__ size_t xq_smem_bytes(int kpad) { return (gemv_x_bytes(kpad, 1) + 127) / 128 * 128; }
 
 // RMSNorm of x [dim] times w, quantised.  x is read once (into shared memory
-// after the quantised row, `xs`).  The sum of squares follows the reduction
-// order of rmsnorm_quant_kernel's 1024-thread CTA exactly (consumer thread i
-// plays threads i and i + 512), so the values are the same bits.
+// after the quantised row, `xs`); the norm weights are loaded together with
+// x, so the staging costs one round trip per 4096 elements.  The sum of
+// squares follows the reduction order of rmsnorm_quant_kernel's 1024-thread
+// CTA exactly (consumer thread i plays threads i and i + 512), so the values
+// are the same bits.  Quantisation: 8 lanes per block (xq_store_chunk8),
+// warp w takes blocks 4w..4w+3, then 4w+64.. .
 __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, int dim, float eps, const XQ& q,
-                                              float* xs, float* red) {
+                                              float* xs, float* red, int tl = -1, int tb = 0) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nb = q.kpad >> 6;
   float sa = 0.0f, sb = 0.0f;
   for (int e0 = 0; e0 < dim; e0 += 1024 * kStageBatch) {
     float va[kStageBatch], vb[kStageBatch];
@@ -247,6 +263,10 @@ __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, in
       const int ea = e0 + 1024 * i + tid, eb = ea + 512;
       va[i] = ea < dim ? __ldcg(x + ea) : 0.0f;
       vb[i] = eb < dim ? __ldcg(x + eb) : 0.0f;
+    }
+    if (e0 == 0) {  // norm weights towards L1 while x is in flight (one 128-byte line per thread)
+      const int e = tid * 32;
+      if (e < dim) asm volatile("prefetch.global.L1 [%0];" ::"l"(w + e));
     }
 #pragma unroll
     for (int i = 0; i < kStageBatch; ++i) {
@@ -257,25 +277,31 @@ __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, in
   }
   sa = warp_sum(sa);
   sb = warp_sum(sb);
+  B2Q_FTRACE(tl, tb + 0);
   if (lane == 0) {
     red[warp] = sa;
     red[warp + 16] = sb;
   }
   consumer_sync();
+  B2Q_FTRACE(tl, tb + 1);
   const float tot = warp_sum(red[lane]);
   const float inv = 1.0f / sqrtf(tot / (float)dim + eps);
-  const int nb = q.kpad >> 6;
-  for (int j0 = warp; j0 < nb; j0 += kGemvConsumerWarps * kStageBatch) {
-    float va[kStageBatch], vb[kStageBatch];
+  B2Q_FTRACE(tl, tb + 2);
+  for (int jq = 4 * warp; jq < nb; jq += 4 * kGemvConsumerWarps) {
+    const int j = jq + (lane >> 3), e = j * 64 + (lane & 7) * 8;
+    const bool in = e < dim;
+    const float4 x0 = *reinterpret_cast<const float4*>(xs + e), x1 = *reinterpret_cast<const float4*>(xs + e + 4);
+    const float4 w0 = in ? *reinterpret_cast<const float4*>(w + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 w1 = in ? *reinterpret_cast<const float4*>(w + e + 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    const float wvv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    float v[8];
 #pragma unroll
-    for (int i = 0; i < kStageBatch; ++i) {
-      const int ea = (j0 + kGemvConsumerWarps * i) * 64 + lane, eb = ea + 32;
-      // (x * inv) * w, two separate roundings as the reference computes it
-      va[i] = ea < dim ? __fmul_rn(__fmul_rn(xs[ea], inv), w[ea]) : 0.0f;
-      vb[i] = eb < dim ? __fmul_rn(__fmul_rn(xs[eb], inv), w[eb]) : 0.0f;
-    }
-    xq_store_blocks<kStageBatch>(va, vb, lane, 0, j0, kGemvConsumerWarps, nb, q);
+    for (int i = 0; i < 8; ++i)  // (x * inv) * w, two separate roundings as the reference computes it
+      v[i] = e + i < dim ? __fmul_rn(__fmul_rn(xv[i], inv), wvv[i]) : 0.0f;
+    xq_store_chunk8(v, lane, 0, j, j < nb, q);
   }
+  B2Q_FTRACE(tl, tb + 3);
   consumer_sync();
 }
 
@@ -283,15 +309,27 @@ __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, in
 __device__ __forceinline__ void stage_plain(const float* src, int dim, const XQ& q) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = q.kpad >> 6;
-  for (int j0 = warp; j0 < nb; j0 += kGemvConsumerWarps * kStageBatch) {
-    float xa[kStageBatch], xb[kStageBatch];
+  constexpr int kQ = 2;  // block quads per warp per batch
+  for (int j0 = 4 * warp; j0 < nb; j0 += 4 * kGemvConsumerWarps * kQ) {
+    float4 xv[kQ][2];
 #pragma unroll
-    for (int i = 0; i < kStageBatch; ++i) {
-      const int ea = (j0 + kGemvConsumerWarps * i) * 64 + lane, eb = ea + 32;
-      xa[i] = ea < dim ? __ldcg(src + ea) : 0.0f;
-      xb[i] = eb < dim ? __ldcg(src + eb) : 0.0f;
+    for (int it = 0; it < kQ; ++it) {
+      const int j = j0 + 4 * kGemvConsumerWarps * it + (lane >> 3), e = j * 64 + (lane & 7) * 8;
+      const bool in = j < nb && e < dim;
+      xv[it][0] = in ? __ldcg(reinterpret_cast<const float4*>(src + e)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      xv[it][1] = in ? __ldcg(reinterpret_cast<const float4*>(src + e + 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    xq_store_blocks<kStageBatch>(xa, xb, lane, 0, j0, kGemvConsumerWarps, nb, q);
+#pragma unroll
+    for (int it = 0; it < kQ; ++it) {
+      const int jq = j0 + 4 * kGemvConsumerWarps * it;
+      if (jq >= nb) break;
+      const int j = jq + (lane >> 3), e = j * 64 + (lane & 7) * 8;
+      float v[8] = {xv[it][0].x, xv[it][0].y, xv[it][0].z, xv[it][0].w, xv[it][1].x, xv[it][1].y, xv[it][1].z, xv[it][1].w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (e + i >= dim) v[i] = 0.0f;
+      xq_store_chunk8(v, lane, 0, j, j < nb, q);
+    }
   }
   consumer_sync();
 }
@@ -443,7 +481,11 @@ struct Consumer {
 };
 
 __device__ __forceinline__ void consume_phase(Consumer& cs, const CtaPhase& ph, bool pair, const SX& sx, bool& ok,
-                                              float* racc) {
+                                              float* racc, int tph = -1) {
+#ifdef B2Q_DECODE_TRACE
+  long long wsum = 0;
+  const long long tc0 = clock64();
+#endif
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int p = warp >> 1, hf = warp & 1;  // row p of every tile; unit half hf
   const int gb = ph.gb, ge = ph.ge;
@@ -479,19 +521,28 @@ __device__ __forceinline__ void consume_phase(Consumer& cs, const CtaPhase& ph, 
     if (off + size > cs.R.cap) off = 0;
     cs.ro = off + size;
     const int slot = cs.j & (kRingSlots - 1);
+#ifdef B2Q_DECODE_TRACE
+    const long long tw0 = clock64();
+#endif
     if (ok) ok = mbar_wait_bounded(&cs.R.full[slot], (uint32_t)((cs.j / kRingSlots) & 1));
+#ifdef B2Q_DECODE_TRACE
+    wsum += clock64() - tw0;
+#endif
     float p0 = 0.0f, p1 = 0.0f;
     if (ok && uok) {
+      // both rows unconditionally (the second re-reads the first tile when
+      // the stage has one), so their instruction streams interleave
       const uint8_t* rc = cs.R.base + off + p * geo.rc;
+      const uint8_t* rc2 = nt2 ? rc + tb : rc;
       if (dt == kQ4_K) {
         p0 = row_q4k(rc, KC, geo.o_aux, ul, csel, X);
-        if (nt2) p1 = row_q4k(rc + tb, KC, geo.o_aux, ul, csel, X);
+        p1 = row_q4k(rc2, KC, geo.o_aux, ul, csel, X);
       } else if (dt == kQ6_K) {
         p0 = row_q6k(rc, KC, geo.o_aux, geo.o_aux2, ul, X);
-        if (nt2) p1 = row_q6k(rc + tb, KC, geo.o_aux, geo.o_aux2, ul, X);
+        p1 = row_q6k(rc2, KC, geo.o_aux, geo.o_aux2, ul, X);
       } else {
         p0 = row_q80(rc, KC, geo.o_aux, ul, X);
-        if (nt2) p1 = row_q80(rc + tb, KC, geo.o_aux, ul, X);
+        p1 = row_q80(rc2, KC, geo.o_aux, ul, X);
       }
     }
     __syncwarp();
@@ -513,6 +564,12 @@ __device__ __forceinline__ void consume_phase(Consumer& cs, const CtaPhase& ph, 
       ++c;
     }
   }
+#ifdef B2Q_DECODE_TRACE
+  if (threadIdx.x == 0 && tph >= 0 && tph < 160 && blockIdx.x < 160) {
+    g_dec_wait[(blockIdx.x * 160 + tph) * 2] = wsum;
+    g_dec_wait[(blockIdx.x * 160 + tph) * 2 + 1] = clock64() - tc0;
+  }
+#endif
   consumer_sync();
 }
 
@@ -523,21 +580,22 @@ __device__ __forceinline__ float dec_racc(const float* racc, int rows, int nw, i
 }
 
 // ---------------------------------------------------------------------------
-// attention item (KV head g, split z) on a 128-thread group: the work of
+// attention item (KV head g, split z) on the 16 consumer warps: the work of
 // rope_kv_kernel (for this head group) + attn_split_kernel + (last split of
 // head g to finish) attn_combine_kernel, with the same arithmetic.  The
 // split holding `pos` takes this token's k/v from registers (and appends
-// them to the cache); the other rows arrive by bulk copy.
+// them to the cache); the other rows arrive by bulk copy.  Every global
+// load of a step is issued before any of them is used.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 template <int G>
-__device__ __noinline__ void attn_item(const DecodeArgs& a, const DecLayer& Ly, int g, int z, int nz,
-                                       AttnTile<G>& T, int grp, uint64_t* bar, int* uses, int* s_last) {
+__device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& Ly, int g, int z, int nz,
+                                          AttnTile<G>& T, uint64_t* bar, int& uses, int* s_last, int tl) {
   constexpr int HD = kHeadDim, HALF = kHeadDim / 2;
-  const int gt = threadIdx.x & 127;
+  const int gt = threadIdx.x;  // 0..511
   const int pos = a.pos, cap = a.max_seq;
   const int H = a.H, KV = a.KV;
   const int t_begin = z * kAttnTile;
@@ -552,107 +610,146 @@ __device__ __noinline__ void attn_item(const DecodeArgs& a, const DecLayer& Ly, 
   const float* cs = a.rope_cos + (int64_t)p_rope * HALF;
   const float* sn = a.rope_sin + (int64_t)p_rope * HALF;
   const float* row = a.qkv;
-  for (int idx = gt; idx < G * HALF; idx += 128) {
-    const int hh = idx / HALF, j = idx % HALF;
-    const int h = g * G + hh;
-    float x0 = __ldcg(row + h * HD + j), x1 = __ldcg(row + h * HD + HALF + j);
-    if (Ly.qb != nullptr) { x0 += Ly.qb[h * HD + j]; x1 += Ly.qb[h * HD + HALF + j]; }
-    const float c = cs[j], sv = sn[j];
-    T.q[hh][j] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sv));
-    T.q[hh][HALF + j] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sv));
-  }
-  if (last) {  // this token's k (rotated) and v: into the tile and the cache
-    const int r = nv - 1;
-    for (int j = gt; j < HALF; j += 128) {
+  // work index w < G*64: one q pair; [G*64, G*64 + 64): a k pair of this
+  // token (last split); [G*64 + 64, G*64 + 192): a v value.  Up to two
+  // indices per thread, all loads issued first.
+  const int qn = G * HALF, nwork = qn + (last ? HALF + HD : 0);
+  float x0[2], x1[2], c[2], sv[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int w = gt + kAttnThreads * r;
+    x0[r] = x1[r] = c[r] = sv[r] = 0.0f;
+    if (w < qn) {
+      const int hh = w / HALF, j = w % HALF, h = g * G + hh;
+      x0[r] = __ldcg(row + h * HD + j);
+      x1[r] = __ldcg(row + h * HD + HALF + j);
+      c[r] = cs[j];
+      sv[r] = sn[j];
+      if (Ly.qb != nullptr) { x0[r] += Ly.qb[h * HD + j]; x1[r] += Ly.qb[h * HD + HALF + j]; }
+    } else if (w < qn + HALF && w < nwork) {
+      const int j = w - qn;
       const float* kr = row + (H + g) * HD;
-      float x0 = __ldcg(kr + j), x1 = __ldcg(kr + HALF + j);
-      if (Ly.kb != nullptr) { x0 += Ly.kb[g * HD + j]; x1 += Ly.kb[g * HD + HALF + j]; }
-      const float c = cs[j], sv = sn[j];
-      const __half y0 = __float2half_rn(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sv)));
-      const __half y1 = __float2half_rn(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sv)));
+      x0[r] = __ldcg(kr + j);
+      x1[r] = __ldcg(kr + HALF + j);
+      c[r] = cs[j];
+      sv[r] = sn[j];
+      if (Ly.kb != nullptr) { x0[r] += Ly.kb[g * HD + j]; x1[r] += Ly.kb[g * HD + HALF + j]; }
+    } else if (w < nwork) {
+      const int j = w - qn - HALF;
+      x0[r] = __ldcg(row + (H + KV) * HD + g * HD + j);
+      if (Ly.vb != nullptr) x0[r] += Ly.vb[g * HD + j];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int w = gt + kAttnThreads * r;
+    if (w < qn) {
+      const int hh = w / HALF, j = w % HALF;
+      T.q[hh][j] = __fsub_rn(__fmul_rn(x0[r], c[r]), __fmul_rn(x1[r], sv[r]));
+      T.q[hh][HALF + j] = __fadd_rn(__fmul_rn(x1[r], c[r]), __fmul_rn(x0[r], sv[r]));
+    } else if (w < qn + HALF && w < nwork) {  // this token's k, rotated: into the tile and the cache
+      const int j = w - qn;
+      const __half y0 = __float2half_rn(__fsub_rn(__fmul_rn(x0[r], c[r]), __fmul_rn(x1[r], sv[r])));
+      const __half y1 = __float2half_rn(__fadd_rn(__fmul_rn(x1[r], c[r]), __fmul_rn(x0[r], sv[r])));
       __half* dst = Ly.kc + ((int64_t)g * cap + pos) * HD;
       dst[j] = y0;
       dst[HALF + j] = y1;
-      T.k[r * HD + j] = y0;
-      T.k[r * HD + HALF + j] = y1;
-    }
-    for (int d = gt; d < HD; d += 128) {
-      float v = __ldcg(row + (H + KV) * HD + g * HD + d);
-      if (Ly.vb != nullptr) v += Ly.vb[g * HD + d];
-      const __half hv = __float2half_rn(v);
-      Ly.vc[((int64_t)g * cap + pos) * HD + d] = hv;
-      T.v[r * HD + d] = hv;
+      T.k[(nv - 1) * HD + j] = y0;
+      T.k[(nv - 1) * HD + HALF + j] = y1;
+    } else if (w < nwork) {
+      const int j = w - qn - HALF;
+      const __half hv = __float2half_rn(x0[r]);
+      Ly.vc[((int64_t)g * cap + pos) * HD + j] = hv;
+      T.v[(nv - 1) * HD + j] = hv;
     }
   }
+  B2Q_FTRACE(tl, 10);
   if (nload > 0) {
-    mbar_wait_bounded(bar, (uint32_t)(*uses & 1));  // a timeout is recorded in the device error word
-    ++*uses;
+    mbar_wait_bounded(bar, (uint32_t)(uses & 1));  // a timeout is recorded in the device error word
+    ++uses;
   }
-  group_sync(grp);
-  attn_tile_compute<G>(T, nv, a.scale, a.part, g, z, a.nsplit, [grp] { group_sync(grp); });
+  B2Q_FTRACE(tl, 11);
+  consumer_sync();
+  attn_tile_compute<G>(T, nv, a.scale, a.part, g, z, a.nsplit, [] { consumer_sync(); });
   // the last split of this KV head to finish merges all of them
-  group_sync(grp);
+  consumer_sync();
+  B2Q_FTRACE(tl, 12);
   if (gt == 0) {
     __threadfence();
     const unsigned int old = atomicAdd(&a.sync->attn_cnt[g], 1u);
     *s_last = old == (unsigned int)(nz - 1);
   }
-  group_sync(grp);
+  consumer_sync();
+  B2Q_FTRACE(tl, 13);
   if (*s_last) {
-    // merge (attn_combine_kernel's arithmetic): the partials of all splits
-    // are staged into the idle tile with independent loads, then reduced in
-    // split order from shared memory
+    // merge (attn_combine_kernel's arithmetic, same order): the partials of
+    // up to kZc splits per head are brought into the idle tile with bulk
+    // copies (one round trip), then reduced in split order
     __threadfence();
     const int nsplit = a.nsplit;
-    float* ml = reinterpret_cast<float*>(T.v);  // [G][nz] x {max, sum}
-    float* ob = reinterpret_cast<float*>(T.k);  // [zc][G][HD] O chunk
-    constexpr int kZc = (kAttnTile * HD / 2) / (G * HD);  // splits per O chunk (T.k as floats)
-    for (int i = gt; i < G * nz; i += 128) {
-      const int hh = i / nz, zz = i % nz;
-      const float* pp = a.part + ((int64_t)(g * G + hh) * nsplit + zz) * (HD + 2);
-      ml[2 * i] = __ldcg(pp);
-      ml[2 * i + 1] = __ldcg(pp + 1);
-    }
-    group_sync(grp);
-    float M[(G * HD + 127) / 128], Ls[(G * HD + 127) / 128], O[(G * HD + 127) / 128];
+    constexpr int kZc = (2 * kAttnTile * HD / 2) / (G * kPartStride);  // splits per chunk (T.k + T.v)
+    float* pb = reinterpret_cast<float*>(T.k);                          // [G][zc][kPartStride]
+    constexpr int R = (G * HD + kAttnThreads - 1) / kAttnThreads;
+    float M[R], Ls[R], O[R];
 #pragma unroll
-    for (int r = 0; r < (G * HD + 127) / 128; ++r) {
-      const int i = gt + 128 * r, hh = i / HD;
-      float mx = -INFINITY;
-      if (i < G * HD)
-        for (int zz = 0; zz < nz; ++zz) mx = fmaxf(mx, ml[2 * (hh * nz + zz)]);
-      M[r] = mx;
+    for (int r = 0; r < R; ++r) {
+      M[r] = -INFINITY;
       Ls[r] = 0.0f;
       O[r] = 0.0f;
     }
-    for (int z0 = 0; z0 < nz; z0 += kZc) {
-      const int zn = min(kZc, nz - z0);
-      group_sync(grp);  // previous chunk consumed
-      for (int i = gt; i < zn * G * HD; i += 128) {
-        const int zz = i / (G * HD), rem = i % (G * HD), hh = rem / HD, d = rem % HD;
-        ob[i] = __ldcg(a.part + ((int64_t)(g * G + hh) * nsplit + z0 + zz) * (HD + 2) + 2 + d);
-      }
-      group_sync(grp);
+    if (nz > kZc) {  // long context: the maxima of every split first, 8 loads in flight
 #pragma unroll
-      for (int r = 0; r < (G * HD + 127) / 128; ++r) {
-        const int i = gt + 128 * r, hh = i / HD, d = i % HD;
+      for (int r = 0; r < R; ++r) {
+        const int i = gt + kAttnThreads * r;
         if (i >= G * HD) continue;
-        for (int zz = 0; zz < zn; ++zz) {
-          const float mz = ml[2 * (hh * nz + z0 + zz)];
-          const float f = mz == -INFINITY ? 0.0f : expf(mz - M[r]);
-          Ls[r] = fmaf(f, ml[2 * (hh * nz + z0 + zz) + 1], Ls[r]);
-          O[r] = fmaf(f, ob[(zz * G + hh) * HD + d], O[r]);
+        const float* ph = a.part + (int64_t)(g * G + i / HD) * nsplit * kPartStride;
+        for (int zz0 = 0; zz0 < nz; zz0 += 8) {
+          float mv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) mv[u] = zz0 + u < nz ? __ldcg(ph + (zz0 + u) * kPartStride) : -INFINITY;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) M[r] = fmaxf(M[r], mv[u]);
         }
       }
     }
+    for (int z0 = 0; z0 < nz; z0 += kZc) {
+      const int zn = min(kZc, nz - z0);
+      if (gt == 0) {
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        fence_proxy_async_smem();
+        const uint32_t bytes = (uint32_t)zn * kPartStride * 4;
+        mbar_arrive_expect_tx(bar, bytes * G);
+        for (int h = 0; h < G; ++h)
+          bulk_g2s(pb + h * zn * kPartStride, a.part + ((int64_t)(g * G + h) * nsplit + z0) * kPartStride, bytes, bar);
+      }
+      mbar_wait_bounded(bar, (uint32_t)(uses & 1));
+      ++uses;
 #pragma unroll
-    for (int r = 0; r < (G * HD + 127) / 128; ++r) {
-      const int i = gt + 128 * r;
+      for (int r = 0; r < R; ++r) {
+        const int i = gt + kAttnThreads * r;
+        if (i >= G * HD) continue;
+        const int h = i / HD, d = i % HD;
+        const float* ph = pb + h * zn * kPartStride;
+        if (nz <= kZc)  // one chunk holds every split: maxima from shared memory
+          for (int zz = 0; zz < zn; ++zz) M[r] = fmaxf(M[r], ph[zz * kPartStride]);
+        for (int zz = 0; zz < zn; ++zz) {
+          const float m = ph[zz * kPartStride];
+          const float f = m == -INFINITY ? 0.0f : expf(m - M[r]);
+          Ls[r] = fmaf(f, ph[zz * kPartStride + 1], Ls[r]);
+          O[r] = fmaf(f, ph[zz * kPartStride + 2 + d], O[r]);
+        }
+      }
+      consumer_sync();  // chunk consumed before the next copy lands
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int i = gt + kAttnThreads * r;
       if (i < G * HD) a.attn[(g * G + i / HD) * HD + i % HD] = O[r] * (1.0f / fmaxf(Ls[r], 1e-12f));
     }
     if (gt == 0) a.sync->attn_cnt[g] = 0u;
+    B2Q_FTRACE(tl, 14);
   }
-  group_sync(grp);  // the tile and s_last are reused by the group's next item
+  consumer_sync();  // the tile and s_last are reused by the next item
 }
 
 // ---------------------------------------------------------------------------
@@ -720,6 +817,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
   cs.R.empty = empty_bar;
   cs.R.cap = a.cap;
   unsigned long long* bar = &a.sync->bar;
+  int nbar = 0;  // grid barriers passed
 
   // this CTA's phase table, and the token embedding (embed_rows_kernel's
   // values) spread over the grid
@@ -734,11 +832,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
     for (int64_t sl = (int64_t)blockIdx.x * 512 + threadIdx.x; sl < slots; sl += (int64_t)gridDim.x * 512)
       dequant_slot(rowp, a.tok_dtype, sl, a.x);
   }
-  grid_sync(bar, okp);
+  grid_sync(bar, nbar, okp);
 
   const int nz = a.pos / kAttnTile + 1;
-  const int grp = warp >> 2;
-  int attn_uses = 0;  // completed phases of this group's attention mbarrier
+  int attn_uses = 0;  // completed phases of the attention mbarrier
   const int kp_e = round_up_int(a.E, 256);
   float* xcopy = reinterpret_cast<float*>(xs + xq_smem_bytes(kp_e));
   float best = -INFINITY;
@@ -753,28 +850,31 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
     const bool head = l == a.n_layers;
     if (head && k > 0) break;
     const int tslot = (l * 5 + k) * 3;
+    (void)tslot;
     B2Q_TRACE(tslot);
+    B2Q_FTRACE(l, 16 + k);
     if (k == 1) {  // RoPE, KV append, attention
       const DecLayer& Ly = a.layers[l];
-      if (grp < a.ngrp) {
-        AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(xs + (size_t)grp * a.tile_bytes);
-        for (int it = blockIdx.x + gridDim.x * grp; it < a.KV * nz; it += gridDim.x * a.ngrp)
-          attn_item<G>(a, Ly, it / nz, it % nz, nz, T, grp, &attn_bar[grp], &attn_uses, &attn_last[grp]);
-      }
+      AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(xs);
+      for (int it = blockIdx.x; it < a.KV * nz; it += gridDim.x)
+        attn_item<G>(a, Ly, it / nz, it % nz, nz, T, &attn_bar[0], attn_uses, &attn_last[0], l);
       B2Q_TRACE(tslot + 2);
-      grid_sync(bar, okp);
+      grid_sync(bar, nbar, okp);
       continue;
     }
     const CtaPhase& ph = tab[head ? 4 * a.n_layers : 4 * l + (k == 0 ? 0 : k - 1)];
     if (ph.gb < ph.ge) {
       const bool add = k == 2 || k == 4;
       const int row0 = ph.gb * 8, nrows = min(ph.ge * 8, ph.n) - row0;
-      // residual rows of this CTA, fetched while the input is staged
-      float xr0 = 0.0f, xr1 = 0.0f;
-      if (add) {
-        if (threadIdx.x < nrows) xr0 = __ldcg(a.x + row0 + threadIdx.x);
-        if (threadIdx.x + 512 < nrows) xr1 = __ldcg(a.x + row0 + threadIdx.x + 512);
-      }
+      const int rows = (ph.ge - ph.gb) * 8;
+      // residual rows of this CTA: copied (L2 -> shared, asynchronously)
+      // behind the accumulators while the input is staged
+      float* resid = racc + 2 * rows;
+      if (add)
+        for (int r4 = threadIdx.x; 4 * r4 < nrows; r4 += kGemvConsumerWarps * 32)
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(resid + 4 * r4)),
+                       "l"(a.x + row0 + 4 * r4)
+                       : "memory");
       // stage the input: rmsnorm(x) for QKV, gate/up and the head; attn; h
       XQ q;
       if (k == 2) {
@@ -786,19 +886,24 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       } else {
         q = smem_xq(xs, kp_e);
         const float* nw = head ? a.out_norm : (k == 0 ? a.layers[l].attn_norm : a.layers[l].ffn_norm);
-        stage_rmsnorm(a.x, nw, a.E, a.eps, q, xcopy, red);
+        stage_rmsnorm(a.x, nw, a.E, a.eps, q, xcopy, red, l, k == 0 ? 0 : 4);
       }
       B2Q_TRACE(tslot + 1);
+      B2Q_FTRACE(l, 21 + k);
       const bool pair = k == 3;
-      consume_phase(cs, ph, pair, smem_sx(q), ok, racc);
+      consume_phase(cs, ph, pair, smem_sx(q), ok, racc, head ? 4 * a.n_layers : 4 * l + (k == 0 ? 0 : k - 1));
       // epilogue
+      if (add) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        consumer_sync();
+      }
       if (ok) {
-        const int rows = (ph.ge - ph.gb) * 8, nw = pair ? 2 : 1;
+        const int nw = pair ? 2 : 1;
         float* y = (head ? a.logits : k == 0 ? a.qkv : pair ? a.h : a.x) + ph.ycol + row0;
         for (int r = threadIdx.x; r < nrows; r += kGemvConsumerWarps * 32) {
           const float v = dec_racc(racc, rows, nw, r, 0);
           if (pair) y[r] = silu_f(v) * dec_racc(racc, rows, nw, r, 1);
-          else if (add) y[r] = (r < 512 ? xr0 : r < 1024 ? xr1 : __ldcg(y + r)) + v;
+          else if (add) y[r] = resid[r] + v;
           else y[r] = v;
           if (head && v > best) { best = v; idx = row0 + r; }
         }
@@ -813,7 +918,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       }
 #endif
     }
-    if (!head) grid_sync(bar, okp);
+    if (!head) grid_sync(bar, nbar, okp);
   }
   warp_argmax(best, idx);
   if (lane == 0) { s_bv[warp] = best; s_bi[warp] = idx; }
@@ -840,6 +945,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       *a.argmax = r;
       if (a.argmax2 != nullptr) *a.argmax2 = r;
       a.sync->head_cnt = 0u;
+      a.sync->bar = 0ull;  // every CTA has passed its last barrier
     }
   }
 }

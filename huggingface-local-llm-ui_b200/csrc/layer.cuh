@@ -8,6 +8,9 @@
 namespace b2q {
 
 constexpr int kAttnTile = 64;  // key tokens per attention split
+// One split partial: {max, sum, O[128]} padded to 132 floats (528 bytes, a
+// multiple of 16, so a head's partials can be moved with one bulk copy).
+constexpr int kPartStride = 132;
 constexpr int kHeadDim = 128;
 
 // RMSNorm of each row (rms_norm_rows, inference.rs:1501-1512) fused with the
@@ -102,19 +105,22 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int m, int H, int KV, in
 // ---------------------------------------------------------------------------
 // Split GQA attention over the f16 KV cache (inference.rs:2782-2820).  The
 // cached keys of a query are cut into splits of kAttnTile tokens; one item =
-// (KV head g, split z) on 128 threads computes, for the G query heads of g,
-// the split's softmax partial (max, sum, unnormalised P*V).  The K and V rows
-// of the split are brought into shared memory with two bulk async copies (one
-// round trip to HBM), then everything runs from shared memory.  The same
-// item code serves the per-kernel path (attn_split_kernel) and the persistent
-// decode kernel, so both give the same bits.
+// (KV head g, split z) on kAttnThreads threads computes, for the G query
+// heads of g, the split's softmax partial (max, sum, unnormalised P*V).  The
+// K and V rows of the split are brought into shared memory with two bulk
+// async copies (one round trip to HBM), then everything runs from shared
+// memory.  The same item code serves the per-kernel path
+// (attn_split_kernel) and the persistent decode kernel, so both give the
+// same bits.
 // ---------------------------------------------------------------------------
+constexpr int kAttnThreads = 512;
+
 template <int G>
 struct AttnTile {
-  __half k[kAttnTile * kHeadDim];  // rows t_begin.. of the split (reused for the P*V halves)
-  __half v[kAttnTile * kHeadDim];
+  __half k[kAttnTile * kHeadDim];  // rows t_begin.. of the split; K and V are
+  __half v[kAttnTile * kHeadDim];  // reused for the P*V partial sums
   float q[G][kHeadDim];            // rotated queries
-  float sp[2][G][kAttnTile];       // score halves; sp[0] then holds the probabilities
+  float sp[G][kAttnTile];          // scores, then probabilities
   float m[G], l[G];                // softmax max and sum per head
 };
 
@@ -129,98 +135,105 @@ __device__ __forceinline__ void attn_tile_load(AttnTile<G>& T, const __half* kc,
   bulk_g2s(T.v, vc + ((int64_t)g * cap + t0) * kHeadDim, bytes, bar);
 }
 
-// The split partial of one item; T.q and the first `nv` rows of T.k / T.v
-// are in place.  `sync` is the 128-thread barrier of the item.  Writes
-// part[(h * nsplit + z) * 130] = {max, sum, O[128]} for the G heads of
-// head group g (h = g*G + i).
+// The split partial of one item on kAttnThreads threads; T.q and the first
+// `nv` rows of T.k / T.v are in place.  `sync` is the item's barrier.
+// Writes part[(h * nsplit + z) * kPartStride] = {max, sum, O[128]} for the G
+// heads of head group g (h = g*G + i).
 template <int G, class Sync>
 __device__ __forceinline__ void attn_tile_compute(AttnTile<G>& T, int nv, float scale, float* part, int g, int z,
                                                   int nsplit, Sync sync) {
   constexpr int HD = kHeadDim;
-  const int tid = threadIdx.x & 127, lane = threadIdx.x & 31, w = tid >> 5;
-  // scores: thread = (token t, half dh of the dims); 16-byte chunks read in
-  // a per-token rotated order (conflict-free shared-memory phases)
+  const int tid = threadIdx.x & (kAttnThreads - 1), lane = threadIdx.x & 31, w = tid >> 5;
+  // scores: thread (token t, eighth e) sums dims 8e..8e+7 and 64+8e..64+8e+7,
+  // then the 8 lanes of a token add their partials (fixed butterfly)
   {
-    const int t = tid & (kAttnTile - 1), dh = tid >> 6;
+    const int t = tid >> 3, e = tid & 7;
     float acc[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) acc[h] = 0.0f;
     if (t < nv) {
-      const __half* kr = T.k + t * HD + dh * 64;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const int cc = (c + t) & 7;
-        const uint4 pk = *reinterpret_cast<const uint4*>(kr + cc * 8);
+      for (int hf = 0; hf < 2; ++hf) {
+        const int d0 = hf * 64 + 8 * e;
+        const uint4 pk = *reinterpret_cast<const uint4*>(T.k + t * HD + d0);
         const __half2* h2 = reinterpret_cast<const __half2*>(&pk);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 kf = __half22float2(h2[e]);
-          const int d = dh * 64 + cc * 8 + 2 * e;
+        for (int i = 0; i < 4; ++i) {
+          const float2 kf = __half22float2(h2[i]);
 #pragma unroll
           for (int h = 0; h < G; ++h) {
-            acc[h] = fmaf(T.q[h][d], kf.x, acc[h]);
-            acc[h] = fmaf(T.q[h][d + 1], kf.y, acc[h]);
+            acc[h] = fmaf(T.q[h][d0 + 2 * i], kf.x, acc[h]);
+            acc[h] = fmaf(T.q[h][d0 + 2 * i + 1], kf.y, acc[h]);
           }
         }
       }
     }
 #pragma unroll
-    for (int h = 0; h < G; ++h) T.sp[dh][h][t] = acc[h];
+    for (int h = 0; h < G; ++h) {
+      acc[h] += __shfl_xor_sync(B2Q_FULL, acc[h], 1);
+      acc[h] += __shfl_xor_sync(B2Q_FULL, acc[h], 2);
+      acc[h] += __shfl_xor_sync(B2Q_FULL, acc[h], 4);
+    }
+    if (e == 0) {
+#pragma unroll
+      for (int h = 0; h < G; ++h) T.sp[h][t] = acc[h];
+    }
   }
   sync();
-  // softmax per head: warp w takes heads w, w + 4; lane holds tokens lane, lane + 32
-  for (int h = w; h < G; h += 4) {
-    const int t0 = lane, t1 = lane + 32;
-    const float s0 = t0 < nv ? (T.sp[0][h][t0] + T.sp[1][h][t0]) * scale : -INFINITY;
-    const float s1 = t1 < nv ? (T.sp[0][h][t1] + T.sp[1][h][t1]) * scale : -INFINITY;
+  // softmax: warp h takes head h; lane holds tokens lane, lane + 32
+  if (w < G) {
+    const int h = w, t0 = lane, t1 = lane + 32;
+    const float s0 = t0 < nv ? T.sp[h][t0] * scale : -INFINITY;
+    const float s1 = t1 < nv ? T.sp[h][t1] * scale : -INFINITY;
     const float mx = warp_max(fmaxf(s0, s1));
     const float p0 = t0 < nv ? expf(s0 - mx) : 0.0f;
     const float p1 = t1 < nv ? expf(s1 - mx) : 0.0f;
     const float sum = warp_sum(p0 + p1);
-    T.sp[0][h][t0] = p0;
-    T.sp[0][h][t1] = p1;
+    T.sp[h][t0] = p0;
+    T.sp[h][t1] = p1;
     if (lane == 0) { T.m[h] = mx; T.l[h] = sum; }
   }
   sync();
-  // P * V: thread = (dims 2dp, 2dp+1; token half th); halves summed after
-  {
-    const int dp = tid & 63, th = tid >> 6;
-    float o[G][2];
+  // P * V: thread (dims 2dp, 2dp+1; token eighth tg = tokens 8tg..8tg+7)
+  const int dp = tid & 63, tg = tid >> 6;
+  float o[G][2];
 #pragma unroll
-    for (int h = 0; h < G; ++h) o[h][0] = o[h][1] = 0.0f;
-    for (int j = 0; j < kAttnTile / 2; ++j) {
-      const int t = th * (kAttnTile / 2) + j;
-      if (t >= nv) break;
-      const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(T.v + t * HD + 2 * dp));
+  for (int h = 0; h < G; ++h) o[h][0] = o[h][1] = 0.0f;
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float ph = T.sp[0][h][t];
-        o[h][0] = fmaf(ph, vf.x, o[h][0]);
-        o[h][1] = fmaf(ph, vf.y, o[h][1]);
-      }
-    }
-    float* o2 = reinterpret_cast<float*>(T.k);  // [2][G][HD], K is no longer read
+  for (int j = 0; j < 8; ++j) {
+    const int t = 8 * tg + j;
+    if (t >= nv) break;
+    const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(T.v + t * HD + 2 * dp));
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      o2[(th * G + h) * HD + 2 * dp] = o[h][0];
-      o2[(th * G + h) * HD + 2 * dp + 1] = o[h][1];
+      const float ph = T.sp[h][t];
+      o[h][0] = fmaf(ph, vf.x, o[h][0]);
+      o[h][1] = fmaf(ph, vf.y, o[h][1]);
     }
   }
+  sync();  // K and V are no longer read
+  float* o8 = reinterpret_cast<float*>(T.k);  // [8][G][HD] (spans K and V)
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+    *reinterpret_cast<float2*>(o8 + (tg * G + h) * HD + 2 * dp) = make_float2(o[h][0], o[h][1]);
   sync();
-  const float* o2 = reinterpret_cast<const float*>(T.k);
-  for (int i = tid; i < G * HD; i += 128) {
+  for (int i = tid; i < G * HD; i += kAttnThreads) {
     const int h = i / HD, d = i % HD;
-    float* pp = part + ((int64_t)(g * G + h) * nsplit + z) * (HD + 2);
+    float O = o8[h * HD + d];
+#pragma unroll
+    for (int q = 1; q < 8; ++q) O += o8[(q * G + h) * HD + d];
+    float* pp = part + ((int64_t)(g * G + h) * nsplit + z) * kPartStride;
     if (d == 0) { pp[0] = T.m[h]; pp[1] = T.l[h]; }
-    pp[2 + d] = o2[h * HD + d] + o2[(G + h) * HD + d];
+    pp[2 + d] = O;
   }
 }
 
-// Per-kernel path: grid (KV, m, nsplit), 128 threads, sizeof(AttnTile<G>)
-// bytes of dynamic shared memory.  Query s sits at position start+s and sees
-// keys t < start+s+1 (causal); q was rotated in place by rope_kv_kernel.
+// Per-kernel path: grid (KV, m, nsplit), kAttnThreads threads,
+// sizeof(AttnTile<G>) bytes of dynamic shared memory.  Query s sits at
+// position start+s and sees keys t < start+s+1 (causal); q was rotated in
+// place by rope_kv_kernel.
 template <int G>
-__global__ void __launch_bounds__(128) attn_split_kernel(
+__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
     const float* __restrict__ qkv, int m, int H, int KV, const int* __restrict__ pos_dev, int cap,
     const __half* __restrict__ kc, const __half* __restrict__ vc, float scale, int nsplit,
     float* __restrict__ part) {
@@ -233,10 +246,10 @@ __global__ void __launch_bounds__(128) attn_split_kernel(
   const int start = *pos_dev;
   const int valid = min(start + s + 1, cap);
   const int t_begin = z * kAttnTile;
-  float* ps = part + (int64_t)s * H * nsplit * (HD + 2);
+  float* ps = part + (int64_t)s * H * nsplit * kPartStride;
   if (t_begin >= valid) {
     if (threadIdx.x < G) {
-      float* p = ps + ((int64_t)(g * G + threadIdx.x) * nsplit + z) * (HD + 2);
+      float* p = ps + ((int64_t)(g * G + threadIdx.x) * nsplit + z) * kPartStride;
       p[0] = -INFINITY;
       p[1] = 0.0f;
     }
@@ -270,15 +283,15 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int m, int H
   const int start = *pos_dev;
   const int valid = min(start + s + 1, cap);
   const int ns = min(nsplit, (valid + kAttnTile - 1) / kAttnTile);
-  const float* pp = part + ((int64_t)s * H + h) * nsplit * (HD + 2);
+  const float* pp = part + ((int64_t)s * H + h) * nsplit * kPartStride;
   float M = -INFINITY;
-  for (int z = 0; z < ns; ++z) M = fmaxf(M, pp[z * (HD + 2)]);
+  for (int z = 0; z < ns; ++z) M = fmaxf(M, pp[z * kPartStride]);
   float L = 0.0f, O = 0.0f;
   for (int z = 0; z < ns; ++z) {
-    const float mz = pp[z * (HD + 2)];
+    const float mz = pp[z * kPartStride];
     const float f = mz == -INFINITY ? 0.0f : expf(mz - M);
-    L = fmaf(f, pp[z * (HD + 2) + 1], L);
-    O = fmaf(f, pp[z * (HD + 2) + 2 + d], O);
+    L = fmaf(f, pp[z * kPartStride + 1], L);
+    O = fmaf(f, pp[z * kPartStride + 2 + d], O);
   }
   const float v = O * (1.0f / fmaxf(L, 1e-12f));
   const int col0 = g * G * HD;

@@ -252,7 +252,7 @@ b2q_status b2q_model_finalize(b2q_model* M) {
   if (err == cudaSuccess) err = dalloc(&M->y_loc, (size_t)mm * E);
   if (err == cudaSuccess) err = dalloc(&M->logits, (size_t)c.n_vocab);
   if (err == cudaSuccess) err = dalloc(&M->logits_loc, (size_t)M->V_loc);
-  if (err == cudaSuccess) err = dalloc(&M->part, (size_t)mm * M->H_loc * M->nsplit * (hd + 2));
+  if (err == cudaSuccess) err = dalloc(&M->part, (size_t)mm * M->H_loc * M->nsplit * kPartStride);
   if (err == cudaSuccess) err = dalloc(&M->tokens, (size_t)2 * mm);  // ids + host staging
   if (err == cudaSuccess) err = dalloc(&M->argmax, 1);
   if (err == cudaSuccess) err = dalloc(&M->pos, 1);
@@ -279,11 +279,11 @@ b2q_status b2q_model_finalize(b2q_model* M) {
   }
   err = cudaDeviceSynchronize();
   if (err != cudaSuccess) return cuda_error(err, "b2q_model_finalize: sync");
-  if (c.no_graph == 2) {
+  if (c.no_graph == 0) {
     err = setup_decode(M);
     if (err != cudaSuccess) return cuda_error(err, "b2q_model_finalize: persistent decode set-up");
   }
-  if (c.no_graph == 0 || (c.no_graph == 2 && !M->dec_on)) {
+  if ((c.no_graph == 0 && !M->dec_on) || c.no_graph == 2) {
     err = build_decode_graph(M);
     if (err != cudaSuccess) return cuda_error(err, "b2q_model_finalize: decode graph capture");
   }

@@ -218,7 +218,7 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
       float* aout = P > 1 ? M->attn_loc : M->attn;
       const size_t tile = G == 4 ? sizeof(AttnTile<4>) : G == 8 ? sizeof(AttnTile<8>)
                         : G == 2 ? sizeof(AttnTile<2>) : sizeof(AttnTile<1>);
-      cudaLaunchConfig_t cfg = lcfg(dim3(KVl, m, M->nsplit), dim3(128), tile, st, attr, pdl);
+      cudaLaunchConfig_t cfg = lcfg(dim3(KVl, m, M->nsplit), dim3(kAttnThreads), tile, st, attr, pdl);
       launch_counted(e, 1);
       if (G == 4)
         err = cudaLaunchKernelEx(&cfg, attn_split_kernel<4>, (const float*)M->qkv, m, Hl, KVl,
@@ -470,6 +470,7 @@ static cudaError_t setup_decode(b2q_model* M) {
   const b2q_model_config& c = M->c;
   b2q_engine* e = M->eng;
   M->dec_on = false;
+  // one GPU; KV heads within the arrival counters
   if (c.tp_size != 1 || c.n_kv_heads > 64) return cudaSuccess;
   const int H = c.n_heads, KV = c.n_kv_heads, G = H / KV, hd = c.head_dim;
   size_t attn_one = 0;
@@ -518,7 +519,10 @@ static cudaError_t setup_decode(b2q_model* M) {
     for (int p = 0; p < nph; ++p) {
       const CtaPhase r = cta_phase(*phases[(size_t)p], b);
       tab[(size_t)b * nph + p] = r;
-      racc = std::max(racc, (size_t)2 * (phases[(size_t)p]->pair ? 2 : 1) * (r.ge - r.gb) * 8 * sizeof(float));
+      // accumulators [2][nw][rows]; O and down also keep their residual rows
+      const bool add = p < 4 * c.n_layers && (p % 4 == kPhO || p % 4 == kPhDown);
+      const size_t per_row = phases[(size_t)p]->pair ? 4 : add ? 3 : 2;
+      racc = std::max(racc, per_row * (r.ge - r.gb) * 8 * sizeof(float));
     }
   racc = round128(racc);
   // shared memory: [ring][staging][accumulators][phase table]; attention
@@ -529,7 +533,6 @@ static cudaError_t setup_decode(b2q_model* M) {
   size_t stage = std::max(xq_smem_bytes(kpmax), xq_smem_bytes(kp_e) + (size_t)4 * c.n_embd);
   if (stage + racc < tile) stage = tile - racc;
   stage = round128(stage);
-  const int ngrp = (int)std::min<size_t>(4, (stage + racc) / tile);
   const size_t tabb = round128((size_t)nph * sizeof(CtaPhase));
   cudaFuncAttributes fa;
   cudaError_t err = cudaFuncGetAttributes(&fa, kern);
@@ -584,8 +587,6 @@ static cudaError_t setup_decode(b2q_model* M) {
   a.cap = (int)cap;
   a.stage_bytes = (int)stage;
   a.racc_bytes = (int)racc;
-  a.tile_bytes = (int)tile;
-  a.ngrp = ngrp;
   M->dec_smem = smem;
   M->dec_G = G;
   M->dec_on = true;

@@ -43,94 +43,84 @@ __host__ __device__ inline int xswz(int pos) { return xswz_chunk(pos >> 6, (pos 
 
 // Quantise one 64-element block held two values per lane (lane i holds
 // elements 64*j + i and 64*j + 32 + i of row t) and store it into `xq`.
-// All 32 lanes call it.
+// All 32 lanes call it.  The block maximum of |x| is a warp reduction of
+// the float bit patterns (for non-negative floats the integer order is the
+// float order), the quarter sums are integer reductions: single redux.sync
+// instructions, exact, so every ordering gives the same bits.  A NaN in the
+// block makes the maximum a NaN and the block quantises to zeros.
+__device__ __forceinline__ int xq_quant(float v, float inv) {
+  return max(-kXMax, min(kXMax, __float2int_rn(v * inv)));
+}
+
 __device__ __forceinline__ void xq_store_block(float v0, float v1, int lane, int t, int j, const XQ& xq) {
-  float amax = fmaxf(fabsf(v0), fabsf(v1));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(B2Q_FULL, amax, o));
+  const uint32_t mbits = __reduce_max_sync(B2Q_FULL, max(__float_as_uint(fabsf(v0)), __float_as_uint(fabsf(v1))));
+  const float amax = __uint_as_float(mbits);
   int q0 = 0, q1 = 0;
   float scale = 0.0f;
   if (amax > 0.0f && amax <= 3.0e38f) {
     scale = amax / (float)kXMax;
     const float inv = (float)kXMax / amax;
-    q0 = max(-kXMax, min(kXMax, __float2int_rn(v0 * inv)));
-    q1 = max(-kXMax, min(kXMax, __float2int_rn(v1 * inv)));
+    q0 = xq_quant(v0, inv);
+    q1 = xq_quant(v1, inv);
   }
   const int kp = xq.kpad;
   int16_t* qr = xq.q + (int64_t)t * kp;
   qr[xswz(j * 64 + lane)] = (int16_t)q0;
   qr[xswz(j * 64 + 32 + lane)] = (int16_t)q1;
-  int s0 = q0, s1 = q1;
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) {  // sums within 16-lane halves
-    s0 += __shfl_xor_sync(B2Q_FULL, s0, o);
-    s1 += __shfl_xor_sync(B2Q_FULL, s1, o);
-  }
-  int32_t* sr = xq.s16 + (int64_t)t * (kp / 16) + 4 * j;
+  const bool lo = lane < 16;
+  const int s0 = __reduce_add_sync(B2Q_FULL, lo ? q0 : 0), s1 = __reduce_add_sync(B2Q_FULL, lo ? 0 : q0);
+  const int s2 = __reduce_add_sync(B2Q_FULL, lo ? q1 : 0), s3 = __reduce_add_sync(B2Q_FULL, lo ? 0 : q1);
   if (lane == 0) {
-    sr[0] = s0;
-    sr[2] = s1;
+    int32_t* sr = xq.s16 + (int64_t)t * (kp / 16) + 4 * j;
+    *reinterpret_cast<int4*>(sr) = make_int4(s0, s1, s2, s3);
     xq.scale[(int64_t)t * (kp / 64) + j] = scale;
-  } else if (lane == 16) {
-    sr[1] = s0;
-    sr[3] = s1;
   }
 }
 
-// The same for N blocks at once (block i = j0 + i * jstride, skipped when
-// >= nb), with the reductions of the N blocks interleaved so that their
-// shuffle chains overlap instead of running one after another.  Values are
-// those of xq_store_block.
+// The same for up to N blocks at once (block i = j0 + i * jstride, skipped
+// when >= nb; warp-uniform), so that the reductions of the blocks overlap.
 template <int N>
 __device__ __forceinline__ void xq_store_blocks(const float (&v0)[N], const float (&v1)[N], int lane, int t, int j0,
                                                 int jstride, int nb, const XQ& xq) {
-  float amax[N];
 #pragma unroll
-  for (int i = 0; i < N; ++i) amax[i] = fmaxf(fabsf(v0[i]), fabsf(v1[i]));
+  for (int i = 0; i < N; ++i)
+    if (j0 + i * jstride < nb) xq_store_block(v0[i], v1[i], lane, t, j0 + i * jstride, xq);
+}
+
+// The same values with 8 lanes per block: lanes 8b..8b+7 of a warp hold
+// block j (each lane one 16-byte chunk c = lane & 7, elements 8c..8c+7), so
+// the block maximum and the quarter sums need only lane-local work and four
+// shuffles, and each lane writes its chunk with one 16-byte store.  The
+// values are those of xq_store_block (exact reductions, same scale).
+// `valid`: this lane group's block exists (all lanes call it).
+__device__ __forceinline__ void xq_store_chunk8(const float (&v)[8], int lane, int t, int j, bool valid,
+                                                const XQ& xq) {
+  uint32_t mb = 0u;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
+  for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(fabsf(v[i])));
+  mb = max(mb, __shfl_xor_sync(B2Q_FULL, mb, 1));
+  mb = max(mb, __shfl_xor_sync(B2Q_FULL, mb, 2));
+  mb = max(mb, __shfl_xor_sync(B2Q_FULL, mb, 4));
+  const float amax = __uint_as_float(mb);
+  const bool nz = amax > 0.0f && amax <= 3.0e38f;
+  const float inv = nz ? (float)kXMax / amax : 0.0f;
+  int q[8], s8 = 0;
 #pragma unroll
-    for (int i = 0; i < N; ++i) amax[i] = fmaxf(amax[i], __shfl_xor_sync(B2Q_FULL, amax[i], o));
-  int s0[N], s1[N];
-  const int kp = xq.kpad;
-  int16_t* qr = xq.q + (int64_t)t * kp;
-#pragma unroll
-  for (int i = 0; i < N; ++i) {
-    int q0 = 0, q1 = 0;
-    if (amax[i] > 0.0f && amax[i] <= 3.0e38f) {
-      const float inv = (float)kXMax / amax[i];
-      q0 = max(-kXMax, min(kXMax, __float2int_rn(v0[i] * inv)));
-      q1 = max(-kXMax, min(kXMax, __float2int_rn(v1[i] * inv)));
-    }
-    const int j = j0 + i * jstride;
-    if (j < nb) {
-      qr[xswz(j * 64 + lane)] = (int16_t)q0;
-      qr[xswz(j * 64 + 32 + lane)] = (int16_t)q1;
-    }
-    s0[i] = q0;
-    s1[i] = q1;
+  for (int i = 0; i < 8; ++i) {
+    q[i] = nz ? xq_quant(v[i], inv) : 0;
+    s8 += q[i];
   }
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1)
-#pragma unroll
-    for (int i = 0; i < N; ++i) {
-      s0[i] += __shfl_xor_sync(B2Q_FULL, s0[i], o);
-      s1[i] += __shfl_xor_sync(B2Q_FULL, s1[i], o);
-    }
-#pragma unroll
-  for (int i = 0; i < N; ++i) {
-    const int j = j0 + i * jstride;
-    if (j >= nb) continue;
-    int32_t* sr = xq.s16 + (int64_t)t * (kp / 16) + 4 * j;
-    if (lane == 0) {
-      sr[0] = s0[i];
-      sr[2] = s1[i];
-      xq.scale[(int64_t)t * (kp / 64) + j] = (amax[i] > 0.0f && amax[i] <= 3.0e38f) ? amax[i] / (float)kXMax : 0.0f;
-    } else if (lane == 16) {
-      sr[1] = s0[i];
-      sr[3] = s1[i];
-    }
-  }
+  const int s16 = s8 + __shfl_xor_sync(B2Q_FULL, s8, 1);
+  if (!valid) return;
+  const int c = lane & 7, kp = xq.kpad;
+  int4 pk;
+  pk.x = (q[0] & 0xffff) | (q[1] << 16);
+  pk.y = (q[2] & 0xffff) | (q[3] << 16);
+  pk.z = (q[4] & 0xffff) | (q[5] << 16);
+  pk.w = (q[6] & 0xffff) | (q[7] << 16);
+  *reinterpret_cast<int4*>(xq.q + (int64_t)t * kp + xswz_chunk(j, c)) = pk;
+  if ((c & 1) == 0) xq.s16[(int64_t)t * (kp / 16) + 4 * j + (c >> 1)] = s16;
+  if (c == 0) xq.scale[(int64_t)t * (kp / 64) + j] = nz ? amax / (float)kXMax : 0.0f;
 }
 
 // x [m][k] f32 -> XQ (all kpad/64 blocks of every row, zero tail).

@@ -33,20 +33,20 @@ class StandardNativeEngine:
     """Llama-family decoder on one device, or one tensor-parallel rank."""
 
     # single-token step modes (b2q_model_config.no_graph)
-    DECODE_MODES = {"graph": 0, "eager": 1, "persistent": 2}
+    DECODE_MODES = {"persistent": 0, "eager": 1, "graph": 2}
 
     def __init__(self, engine: CudaEngine, cfg: dict, max_seq: int = 8192, tp_rank: int = 0,
                  tp_size: int = 1, tp_id: bytes | None = None, use_graph: bool = True,
                  decode: str | None = None):
-        """`decode` picks how single-token steps run: "graph" (default: the
-        captured graph of the per-layer kernels), "eager" (the same kernels
-        launched one by one; also use_graph=False) or "persistent" (one
-        persistent kernel per token on one GPU; the graph under tensor
-        parallelism).  All three give the same logits bit for bit."""
+        """`decode` picks how single-token steps run: "persistent" (default:
+        one persistent kernel per token on one GPU; the captured graph under
+        tensor parallelism), "graph" (the captured graph of the per-layer
+        kernels) or "eager" (the same kernels launched one by one; also
+        use_graph=False).  All three give the same logits bit for bit."""
         self.engine = engine
         self.cfg = dict(cfg)
         self.max_seq = max_seq
-        mode = decode or ("graph" if use_graph else "eager")
+        mode = decode or ("persistent" if use_graph else "eager")
         if mode not in self.DECODE_MODES:
             raise ValueError(f"decode must be one of {sorted(self.DECODE_MODES)}")
         self.decode_mode = mode

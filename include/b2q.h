@@ -153,11 +153,12 @@ typedef struct {
   int max_seq;       /* KV capacity in tokens; positions clamp at 8191 for RoPE */
   int tp_rank;       /* tensor-parallel rank of this process (0 for 1 GPU) */
   int tp_size;       /* tensor-parallel world size (1 for 1 GPU) */
-  int no_graph;      /* single-token steps: 0 (default) the captured CUDA graph of
-                        the per-layer kernels; 1 the same kernels launched
-                        eagerly; 2 one persistent kernel per token on one GPU
-                        (the graph under tensor parallelism or where the model
-                        does not fit it).  The three give bit-identical logits. */
+  int no_graph;      /* single-token steps: 0 (default) one persistent kernel per
+                        token on one GPU (the captured graph under tensor
+                        parallelism or where the model does not fit it); 1 the
+                        per-layer kernels launched eagerly; 2 the captured CUDA
+                        graph of those kernels.  The three give bit-identical
+                        logits. */
 } b2q_model_config;
 
 /* Unique id for NCCL communicator setup (ncclGetUniqueId); rank 0 creates
