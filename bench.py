@@ -268,6 +268,8 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--layers", type=int, default=32,
+                    help="decoder layers (32 = Llama-3-8B; fewer only for kernel profiles on a small case)")
     ap.add_argument("--decode", default="persistent", choices=["persistent", "graph", "eager"],
                     help="single-token step: captured kernel graph, one persistent kernel, or eager")
     ap.add_argument("--no-gemv-shapes", action="store_true", help="skip the per-shape GEMV timings")
@@ -313,7 +315,7 @@ def main():
         dist.broadcast_object_list(obj, src=0)
         tp_id = obj[0]
 
-    cfg = dict(model.LLAMA3_8B)
+    cfg = dict(model.LLAMA3_8B, n_layers=args.layers)
     max_seq = args.prefill + args.warmup + args.steps + args.e2e_steps + 8
     t_load = time.perf_counter()
     m, host = build_model(pkg, engine, cfg, args.seed, rank, world, tp_id, max_seq, decode=args.decode)
@@ -416,7 +418,7 @@ def main():
                 "ms_per_step": round(ms_step, 4), "higher_is_better": True,
                 "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
                 "dtype": "int16xint8 dp2a, f32 accum", "data": "synthetic",
-                "config": {"workload": "llama3-8b-q4_k_m-decode", "layers": 32, "hidden": 4096,
+                "config": {"workload": "llama3-8b-q4_k_m-decode", "layers": cfg["n_layers"], "hidden": 4096,
                            "heads": "32/8", "ffn": 14336, "vocab": 128256, "prefill": args.prefill,
                            "batch": 1, "kv_cache": "f16", "tp": world, "decode": m.decode_mode,
                            "l2": "inputs larger than L2 (4.9 GB weights per step)"},

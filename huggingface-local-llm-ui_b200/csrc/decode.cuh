@@ -480,23 +480,24 @@ struct Consumer {
   int ro = 0;  // next read offset
 };
 
-__device__ __forceinline__ void consume_phase(Consumer& cs, const CtaPhase& ph, bool pair, const SX& sx, bool& ok,
-                                              float* racc, int tph = -1) {
-#ifdef B2Q_DECODE_TRACE
-  long long wsum = 0;
-  const long long tc0 = clock64();
-#endif
+// The stage loop (DT: the GGML type, or -1 to read it from the phase; one
+// runtime-typed copy keeps the kernel within its registers).  Software-pipelined: the warp
+// reductions and accumulator updates of stage j are issued after the dot
+// products of stage j + 1 have started, in the same straight-line block, so
+// the shuffle latency overlaps integer work.
+template <int DT>
+__device__ __forceinline__ void consume_loop(Consumer& cs, const CtaPhase& ph, bool pair, const SX& sx, bool& ok,
+                                             float* racc, long long& wsum) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int p = warp >> 1, hf = warp & 1;  // row p of every tile; unit half hf
   const int gb = ph.gb, ge = ph.ge;
-  const int dt = ph.dtype_nr & 0xff, nr = ph.dtype_nr >> 8;
+  const int nr = ph.dtype_nr >> 8;
   const int KC = ph.KC, C = ph.C, U = ph.U;
+  const int dt = DT >= 0 ? DT : (ph.dtype_nr & 0xff);  // uniform over the CTA
   const RcGeom geo = rc_geom(dt, KC);
   const int tb = 8 * geo.rc;
   const int rows = (ge - gb) * 8;
   const int nw = pair ? 2 : 1;
-  for (int i = threadIdx.x; i < 2 * nw * rows; i += kGemvConsumerWarps * 32) racc[i] = 0.0f;
-  consumer_sync();
   const int step = (pair || nr == 1) ? 1 : 2;
   const bool two = pair || nr == 2;
   const XPhase xp = make_xphase(lane);
@@ -505,6 +506,8 @@ __device__ __forceinline__ void consume_phase(Consumer& cs, const CtaPhase& ph, 
   float* acc = racc + hf * nw * rows + p;  // this warp's row p, half hf
   XUnit X;
   bool uok = false;
+  float q0 = 0.0f, q1 = 0.0f;  // previous stage's lane partials
+  int d0 = 0, d1 = 0;          // their accumulator offsets
   for (int c = 0, g = gb; c < C && gb < ge;) {
     if (g == gb) {  // new chunk pass: this lane's activations
       const int u = c * KC + ul;
@@ -528,48 +531,70 @@ __device__ __forceinline__ void consume_phase(Consumer& cs, const CtaPhase& ph, 
 #ifdef B2Q_DECODE_TRACE
     wsum += clock64() - tw0;
 #endif
-    float p0 = 0.0f, p1 = 0.0f;
-    if (ok && uok) {
-      // both rows unconditionally (the second re-reads the first tile when
-      // the stage has one), so their instruction streams interleave
-      const uint8_t* rc = cs.R.base + off + p * geo.rc;
-      const uint8_t* rc2 = nt2 ? rc + tb : rc;
-      if (dt == kQ4_K) {
-        p0 = row_q4k(rc, KC, geo.o_aux, ul, csel, X);
-        p1 = row_q4k(rc2, KC, geo.o_aux, ul, csel, X);
-      } else if (dt == kQ6_K) {
-        p0 = row_q6k(rc, KC, geo.o_aux, geo.o_aux2, ul, X);
-        p1 = row_q6k(rc2, KC, geo.o_aux, geo.o_aux2, ul, X);
-      } else {
-        p0 = row_q80(rc, KC, geo.o_aux, ul, X);
-        p1 = row_q80(rc2, KC, geo.o_aux, ul, X);
-      }
+    // both rows unconditionally (the second re-reads the first tile when the
+    // stage has one; lanes past the chunk compute on padding), masked after
+    const uint8_t* rc = cs.R.base + off + p * geo.rc;
+    const uint8_t* rc2 = nt2 ? rc + tb : rc;
+    float p0, p1;
+    if (dt == kQ4_K) {
+      p0 = row_q4k(rc, KC, geo.o_aux, ul, csel, X);
+      p1 = row_q4k(rc2, KC, geo.o_aux, ul, csel, X);
+    } else if (dt == kQ6_K) {
+      p0 = row_q6k(rc, KC, geo.o_aux, geo.o_aux2, ul, X);
+      p1 = row_q6k(rc2, KC, geo.o_aux, geo.o_aux2, ul, X);
+    } else {
+      p0 = row_q80(rc, KC, geo.o_aux, ul, X);
+      p1 = row_q80(rc2, KC, geo.o_aux, ul, X);
     }
+    // the previous stage: reduce across the warp and accumulate
+    q0 = warp_sum(q0);
+    q1 = warp_sum(q1);
+    if (lane == 0) {
+      acc[d0] += q0;
+      acc[d1] += q1;
+    }
+    const bool live = ok && uok;
+    q0 = live ? p0 : 0.0f;
+    q1 = live && nt2 ? p1 : 0.0f;
     __syncwarp();
     if (lane == 0) mbar_arrive(&cs.R.empty[slot]);  // the stage may be refilled
     ++cs.j;
-    p0 = warp_sum(p0);
-    if (nt2) p1 = warp_sum(p1);
-    if (lane == 0) {
-      const int r = (g - gb) * 8;
-      acc[r] += p0;
-      if (nt2) {
-        if (pair) acc[rows + r] += p1;  // up tile, same row
-        else acc[r + 8] += p1;          // next 8-row group
-      }
-    }
+    const int r = (g - gb) * 8;
+    d0 = r;
+    d1 = !nt2 ? r : pair ? rows + r : r + 8;  // up tile (same row) / next 8-row group
     g += step;
     if (g >= ge) {
       g = gb;
       ++c;
     }
   }
+  q0 = warp_sum(q0);
+  q1 = warp_sum(q1);
+  if (lane == 0) {
+    acc[d0] += q0;
+    acc[d1] += q1;
+  }
+}
+
+__device__ __forceinline__ void consume_phase(Consumer& cs, const CtaPhase& ph, bool pair, const SX& sx, bool& ok,
+                                              float* racc, int tph = -1) {
+  long long wsum = 0;
+#ifdef B2Q_DECODE_TRACE
+  const long long tc0 = clock64();
+#endif
+  const int rows = (ph.ge - ph.gb) * 8;
+  const int nw = pair ? 2 : 1;
+  for (int i = threadIdx.x; i < 2 * nw * rows; i += kGemvConsumerWarps * 32) racc[i] = 0.0f;
+  consumer_sync();
+  consume_loop<-1>(cs, ph, pair, sx, ok, racc, wsum);
 #ifdef B2Q_DECODE_TRACE
   if (threadIdx.x == 0 && tph >= 0 && tph < 160 && blockIdx.x < 160) {
     g_dec_wait[(blockIdx.x * 160 + tph) * 2] = wsum;
     g_dec_wait[(blockIdx.x * 160 + tph) * 2 + 1] = clock64() - tc0;
   }
 #endif
+  (void)wsum;
+  (void)tph;
   consumer_sync();
 }
 
