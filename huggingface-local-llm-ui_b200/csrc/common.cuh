@@ -146,7 +146,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait: returns false (and raises the device error word) if the
 // phase did not complete within kSpinLimitCycles.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  long long t0 = clock64();
+  if (mbar_try_wait(bar, parity)) return true;  // the common case: no clock reads
+  const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (clock64() - t0 > kSpinLimitCycles) {
       atomicExch(&g_b2q_device_error, 5);
@@ -182,6 +183,17 @@ __device__ __forceinline__ float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(B2Q_FULL, v, o);
   return v;
 }
+// Sums of a and b over the warp with two halves of one reduction tree:
+// lane 0 returns the sum of a, lane 16 the sum of b, each with the bits of
+// warp_sum (the same additions in the same order), in 5 shuffles for both.
+__device__ __forceinline__ float warp_sum2(float a, float b, int lane) {
+  const bool lo = lane < 16;
+  float v = (lo ? a : b) + __shfl_xor_sync(B2Q_FULL, lo ? b : a, 16);
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(B2Q_FULL, v, o);
+  return v;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(B2Q_FULL, v, o));

@@ -507,7 +507,7 @@ __device__ __forceinline__ void consume_loop(Consumer& cs, const CtaPhase& ph, b
   XUnit X;
   bool uok = false;
   float q0 = 0.0f, q1 = 0.0f;  // previous stage's lane partials
-  int d0 = 0, d1 = 0;          // their accumulator offsets
+  int d0 = 0, d1 = -1;         // their accumulator offsets (-1: none)
   for (int c = 0, g = gb; c < C && gb < ge;) {
     if (g == gb) {  // new chunk pass: this lane's activations
       const int u = c * KC + ul;
@@ -546,12 +546,12 @@ __device__ __forceinline__ void consume_loop(Consumer& cs, const CtaPhase& ph, b
       p0 = row_q80(rc, KC, geo.o_aux, ul, X);
       p1 = row_q80(rc2, KC, geo.o_aux, ul, X);
     }
-    // the previous stage: reduce across the warp and accumulate
-    q0 = warp_sum(q0);
-    q1 = warp_sum(q1);
-    if (lane == 0) {
-      acc[d0] += q0;
-      acc[d1] += q1;
+    // the previous stage: reduce across the warp and accumulate (lane 0:
+    // first row, lane 16: second row, when the stage had one)
+    {
+      const float sum = warp_sum2(q0, q1, lane);
+      if (lane == 0) acc[d0] += sum;
+      if (lane == 16 && d1 >= 0) acc[d1] += sum;
     }
     const bool live = ok && uok;
     q0 = live ? p0 : 0.0f;
@@ -561,18 +561,17 @@ __device__ __forceinline__ void consume_loop(Consumer& cs, const CtaPhase& ph, b
     ++cs.j;
     const int r = (g - gb) * 8;
     d0 = r;
-    d1 = !nt2 ? r : pair ? rows + r : r + 8;  // up tile (same row) / next 8-row group
+    d1 = !nt2 ? -1 : pair ? rows + r : r + 8;  // up tile (same row) / next 8-row group
     g += step;
     if (g >= ge) {
       g = gb;
       ++c;
     }
   }
-  q0 = warp_sum(q0);
-  q1 = warp_sum(q1);
-  if (lane == 0) {
-    acc[d0] += q0;
-    acc[d1] += q1;
+  {
+    const float sum = warp_sum2(q0, q1, lane);
+    if (lane == 0) acc[d0] += sum;
+    if (lane == 16 && d1 >= 0) acc[d1] += sum;
   }
 }
 

@@ -133,7 +133,7 @@ struct XUnit {
   int4 v[8];
   float xs;      // Q4_K / Q8_0: scale of the unit's block
   float2 xs2;    // Q6_K: scales of its two blocks
-  int4 s16;      // Q4_K: sums of the 4 quarters; Q6_K: .x..w = sums of groups 0..3
+  int4 s16;      // Q4_K: .x, .y = sums of each 32-element half; Q6_K: .x..w = 32 * sums of groups 0..3
 };
 
 // Q4_K unit u = activation block u: chunks 0..7 of group u.
@@ -142,7 +142,8 @@ __device__ __forceinline__ void xload_q4k(XUnit& X, const SX& sx, int t, int u, 
 #pragma unroll
   for (int c = 0; c < 8; ++c) X.v[c] = xld(gb, c, F);
   X.xs = sx.scale[t * (sx.kpad >> 6) + u];
-  X.s16 = *reinterpret_cast<const int4*>(sx.s16 + t * (sx.kpad >> 4) + 4 * u);
+  const int4 q = *reinterpret_cast<const int4*>(sx.s16 + t * (sx.kpad >> 4) + 4 * u);
+  X.s16 = make_int4(q.x + q.y, q.z + q.w, 0, 0);
 }
 
 // Q6_K unit u = 4b + 2h + s: group g = 16 elements of block grp0 + (g >> 1),
@@ -208,7 +209,7 @@ __device__ __forceinline__ float row_q4k(const uint8_t* rc, int KC, int o_aux, i
   B2Q_Q4K_WORD(b.w, ia1, ib1, X.v[3].z, X.v[3].w, X.v[7].z, X.v[7].w)
   // sum_l (d sc q_l - dmin m) x_l over both sub-blocks, in units of xs
   const int isum = (int)(h & 63u) * (ia0 + ia1) + (int)((h >> 6) & 63u) * ((ib0 + ib1) >> 4);
-  const int msum = (int)((h >> 12) & 63u) * (X.s16.x + X.s16.y) + (int)((h >> 18) & 63u) * (X.s16.z + X.s16.w);
+  const int msum = (int)((h >> 12) & 63u) * X.s16.x + (int)((h >> 18) & 63u) * X.s16.y;
   return X.xs * (d * (float)isum - dm * (float)msum);
 }
 #undef B2Q_Q4K_WORD

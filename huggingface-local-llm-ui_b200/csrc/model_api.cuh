@@ -66,8 +66,10 @@ b2q_status b2q_model_create(b2q_engine* e, const b2q_model_config* cfg, const un
   return B2Q_OK;
 }
 
-b2q_status b2q_model_shard_rows(b2q_model* M, const char* name, int64_t n, int64_t* b, int64_t* e) {
-  if (!M || !name || !b || !e) return set_error(B2Q_EINVAL, "b2q_model_shard_rows: NULL argument");
+b2q_status b2q_tp_shard_rows(const b2q_model_config* cfg, const char* name, int64_t n, int64_t* b, int64_t* e) {
+  if (!cfg || !name || !b || !e) return set_error(B2Q_EINVAL, "b2q_tp_shard_rows: NULL argument");
+  if (cfg->tp_size < 1 || cfg->tp_rank < 0 || cfg->tp_rank >= cfg->tp_size)
+    return set_error(B2Q_EINVAL, "b2q_tp_shard_rows: tp_rank %d of tp_size %d", cfg->tp_rank, cfg->tp_size);
   int layer = -1;
   std::string role = role_of(name, &layer);
   if (role == "token_embd" || role == "output_norm" || role == "attn_norm" || role == "ffn_norm") {
@@ -75,8 +77,13 @@ b2q_status b2q_model_shard_rows(b2q_model* M, const char* name, int64_t n, int64
     *e = n;
     return B2Q_OK;
   }
-  shard_range(M, role, n, b, e);
+  shard_range_cfg(*cfg, role, n, b, e);
   return B2Q_OK;
+}
+
+b2q_status b2q_model_shard_rows(b2q_model* M, const char* name, int64_t n, int64_t* b, int64_t* e) {
+  if (!M || !name || !b || !e) return set_error(B2Q_EINVAL, "b2q_model_shard_rows: NULL argument");
+  return b2q_tp_shard_rows(&M->c, name, n, b, e);
 }
 
 static b2q_status set_tensor_impl(b2q_model* M, const char* name, int dtype, const int64_t* dims,

@@ -109,9 +109,9 @@ static cudaLaunchConfig_t lcfg(dim3 g, dim3 b, size_t smem, cudaStream_t st, cud
 // Split the rows of an [n][...] tensor for tensor parallelism.
 //  attn_q / attn_k / attn_v: by KV head groups (whole heads per rank)
 //  attn_output, ffn_gate/up/down, output: contiguous row ranges
-static void shard_range(const b2q_model* m, const std::string& role, int64_t n, int64_t* b,
-                        int64_t* e) {
-  const int r = m->c.tp_rank, P = m->c.tp_size;
+static void shard_range_cfg(const b2q_model_config& c, const std::string& role, int64_t n, int64_t* b,
+                            int64_t* e) {
+  const int r = c.tp_rank, P = c.tp_size;
   if (P <= 1) {
     *b = 0;
     *e = n;
@@ -120,11 +120,15 @@ static void shard_range(const b2q_model* m, const std::string& role, int64_t n, 
   int64_t unit = 1;
   if (role == "attn_q" || role == "attn_k" || role == "attn_v" || role == "attn_q.bias" ||
       role == "attn_k.bias" || role == "attn_v.bias")
-    unit = m->c.head_dim;
+    unit = c.head_dim;
   const int64_t units = n / unit;
   const int64_t per = units / P;
   *b = per * r * unit;
   *e = per * (r + 1) * unit;
+}
+
+static void shard_range(const b2q_model* m, const std::string& role, int64_t n, int64_t* b, int64_t* e) {
+  shard_range_cfg(m->c, role, n, b, e);
 }
 
 static std::string role_of(const std::string& name, int* layer) {

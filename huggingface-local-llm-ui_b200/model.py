@@ -23,6 +23,16 @@ LLAMA3_70B = dict(n_layers=80, n_embd=8192, n_heads=64, n_kv_heads=8, head_dim=1
                   n_vocab=128256, rms_eps=1e-5, rope_theta=500000.0)
 
 
+def tp_shard_rows(cfg: dict, name: str, n: int, tp_rank: int, tp_size: int) -> tuple[int, int]:
+    """Rows [begin, end) of tensor `name` ([n][...]) owned by `tp_rank` of
+    `tp_size` (b2q_tp_shard_rows; no device needed)."""
+    c = ModelConfig(cfg["n_layers"], cfg["n_embd"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"],
+                    cfg["n_ff"], cfg["n_vocab"], cfg["rms_eps"], cfg["rope_theta"], 8, tp_rank, tp_size, 0)
+    b, e = C.c_int64(), C.c_int64()
+    check(lib().b2q_tp_shard_rows(C.byref(c), name.encode(), n, C.byref(b), C.byref(e)))
+    return b.value, e.value
+
+
 def tp_unique_id() -> bytes:
     buf = (C.c_ubyte * 128)()
     check(lib().b2q_tp_unique_id(buf))

@@ -190,6 +190,15 @@ b2q_status b2q_model_set_tensor_rows(b2q_model* m, const char* name, int ggml_ty
 b2q_status b2q_model_shard_rows(b2q_model* m, const char* name, int64_t n,
                                 int64_t* row_begin, int64_t* row_end);
 
+/* The same range from a configuration alone (cfg->tp_rank of cfg->tp_size),
+   without a device: attn_q/k/v are split by whole heads (rank r owns KV heads
+   [r*KV/P, (r+1)*KV/P) and their query heads), attn_output, ffn_* and output
+   by contiguous rows; norms and token_embd are replicated.  Loader-side
+   counterpart of the reference's per-tensor placement in from_gguf
+   (inference.rs:2605-2616), which has no tensor parallelism. */
+b2q_status b2q_tp_shard_rows(const b2q_model_config* cfg, const char* name, int64_t n,
+                             int64_t* row_begin, int64_t* row_end);
+
 /* Validate that every tensor is present, allocate the KV cache and build
  * the decode graphs. */
 b2q_status b2q_model_finalize(b2q_model* m);

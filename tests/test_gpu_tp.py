@@ -1,0 +1,38 @@
+"""Tensor parallelism across 2 GPUs of one box (row-sharded weights, KV
+heads split per GPU, NCCL all-gathers): logits of a prompt and of greedy
+decode steps must equal the one-GPU path bit for bit.  Runs
+tests/tp_worker.py under torch.distributed.run; skipped with fewer than two
+visible GPUs."""
+from __future__ import annotations
+
+import json
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+HERE = Path(__file__).resolve().parent
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_tp2_matches_single_gpu(tmp_path):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = tmp_path / "tp.json"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           str(HERE / "tp_worker.py"), "--out", str(out)]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=dict(os.environ))
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    verdict = json.loads(out.read_text())
+    assert verdict["bit_identical"], verdict

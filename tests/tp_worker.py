@@ -1,0 +1,88 @@
+"""Two-rank tensor-parallel decode on GPUs (launched by tests/test_gpu_tp.py
+through torch.distributed.run): every rank builds its row shards of a
+Llama-shaped model, the ranks run a prompt and greedy decode steps, and rank
+0 compares each step's logits with a one-GPU eager model of the same weights.
+The per-row arithmetic, the per-head attention and the gathers do not depend
+on the sharding, so the logits must agree bit for bit.  Writes a JSON
+verdict to --out."""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", required=True)
+    ap.add_argument("--layers", type=int, default=2)
+    args = ap.parse_args()
+    import torch
+    import torch.distributed as dist
+    from conftest import load_pkg
+    load_pkg()
+    from hf_llm_b200 import model, synth
+    from hf_llm_b200.engine import CudaEngine
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    cfg = dict(model.LLAMA3_8B, n_layers=args.layers, n_vocab=32000)
+    eng = CudaEngine(local)
+    obj = [model.tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    specs = synth.llama_specs(cfg, model.q4_k_m_types())
+    m = model.StandardNativeEngine(eng, cfg, max_seq=160, tp_rank=rank, tp_size=world, tp_id=obj[0])
+    for spec in specs:
+        name, t, dims, _ = spec
+        if len(dims) == 1:
+            m.set_tensor(name, t, dims, synth.llama_tensor(spec, 9, dist="unit"))
+            continue
+        b, e = m.shard_rows(name, dims[0])
+        m.set_tensor(name, t, dims, synth.llama_tensor(spec, 9, b, e, dist="unit"), b, e)
+    m.finalize()
+    ref = None
+    if rank == 0:
+        full = synth.llama_tensors(cfg, model.q4_k_m_types(), 9, dist="unit")
+        ref = model.StandardNativeEngine.from_tensors(eng, cfg, full, max_seq=160, decode="eager")
+    rng = np.random.default_rng(4)
+    prompt = rng.integers(0, cfg["n_vocab"], 70).tolist()  # > one forward chunk (64)
+    steps, same, pos = [], True, 0
+    tok_list = [prompt]
+    for s in range(6):
+        toks = tok_list[-1]
+        lt = m.forward(toks, pos)
+        if rank == 0:
+            lr = ref.forward(toks, pos)
+            eq = bool(np.array_equal(lt.view(np.uint32), lr.view(np.uint32)))
+            same &= eq
+            steps.append({"pos": pos, "n": len(toks), "bit_identical": eq,
+                          "max_abs_diff": float(np.max(np.abs(lt - lr)))})
+            nxt = int(np.argmax(lr))
+        else:
+            nxt = 0
+        o = [nxt]
+        dist.broadcast_object_list(o, src=0)
+        pos += len(toks)
+        tok_list.append([o[0]])
+    dist.barrier()
+    if rank == 0:
+        Path(args.out).write_text(json.dumps({"world": world, "bit_identical": same, "steps": steps}))
+    m.close()
+    if ref is not None:
+        ref.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
