@@ -44,6 +44,7 @@ namespace b2q {
 constexpr int kDecSegs = 3;
 enum : int { kPhQKV = 0, kPhO = 1, kPhGU = 2, kPhDown = 3, kDecPhases = 4 };
 constexpr int kRingSlots = 16;  // mbarrier pairs of the byte ring (stages in flight)
+constexpr int kMaxTp = 8;       // tensor-parallel ranks of one box
 
 // Producer view of a phase: which CTAs own which weight (segment).
 struct DecSeg {
@@ -105,17 +106,29 @@ struct DecodeArgs {
   const float* rope_sin;
   const uint32_t* token;  // this step's token id (device)
   int pos;                // its position
-  float* x;               // [E] residual stream
-  float* qkv;             // [(H + 2 KV) * 128]
-  float* attn;            // [H * 128]
-  float* h;               // [F]
-  float* logits;          // [V]
-  float* part;            // [H][nsplit][130] attention split partials
+  float* qkv;             // [(H + 2 KV) * 128] this rank's heads
+  float* part;            // [H][nsplit][kPartStride] attention split partials
   int nsplit;
   DecSync* sync;
-  int2* cand;             // [grid] per-CTA argmax candidate (value bits, index)
   uint32_t* argmax;       // model's argmax word
   uint32_t* argmax2;      // optional caller's copy
+  // Tensor parallelism: this is rank `rank` of `tp` (tp = 1 on one GPU).  H,
+  // KV are this rank's heads; the vectors every rank needs whole live in
+  // every rank's memory, and xg[p], attng[p], hg[p], logitsg[p], candg[p]
+  // point at rank p's copy (peer memory over NVLink for p != rank): each
+  // epilogue stores its slice into all of them.
+  int tp, rank;
+  int Hg;                 // query heads over all ranks
+  int o_off, f_off, v_off, h_off;  // first global row (head) of this rank's slices
+  float* xg[kMaxTp];      // [E] residual stream
+  float* attng[kMaxTp];   // [Hg * 128] attention output
+  float* hg[kMaxTp];      // [F] SwiGLU output
+  float* logitsg[kMaxTp]; // [V]
+  int2* candg[kMaxTp];    // [tp * grid] per-CTA argmax candidates (value bits, global row)
+  unsigned long long* xflagg[kMaxTp];  // [kMaxTp] per-source-rank barrier epochs
+  // this launch's grid-barrier counter base and all-rank epoch base (the
+  // counter and the epochs only grow)
+  unsigned long long lbase, xepoch;
   // shared memory: [ring cap][staging stage_bytes][accumulators racc_bytes][phase table]
   int cap;
   int stage_bytes;
@@ -188,16 +201,19 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
   return v;
 }
 
-// Barrier over the consumer warps of every CTA.  The counter starts every
-// launch at 0 (the last CTA to finish resets it), so barrier number k
-// completes at (k + 1) * gridDim.x arrivals: the arrival is a release
-// reduction that does not wait for a reply.  `s_ok` (shared) turns 0 when
-// this CTA's wait gave up; later barriers are then skipped.
-__device__ __forceinline__ void grid_sync(unsigned long long* bar, int& k, volatile int* s_ok) {
+// Barrier over the consumer warps of every CTA of this GPU.  The counter
+// only grows: barrier number k of a launch completes at base + (k + 1) *
+// gridDim.x arrivals (base: the count every earlier launch left).  The
+// arrival is a release reduction that does not wait for a reply.  `s_ok`
+// (shared) turns 0 when this CTA's wait gave up; later waits are skipped.
+__device__ __forceinline__ void grid_sync(unsigned long long* bar, unsigned long long base, int& k,
+                                          volatile int* s_ok, bool sys = false) {
   consumer_sync();
   if (threadIdx.x == 0 && *s_ok) {
-    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
-    const unsigned long long target = (unsigned long long)(k + 1) * gridDim.x;
+    // sys: the release also orders this CTA's stores into peer memory
+    if (sys) asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
+    else asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
+    const unsigned long long target = base + (unsigned long long)(k + 1) * gridDim.x;
     const long long t0 = clock64();
     while (ld_acquire_u64(bar) < target) {
       if (clock64() - t0 > kSpinLimitCycles) {
@@ -208,6 +224,48 @@ __device__ __forceinline__ void grid_sync(unsigned long long* bar, int& k, volat
     }
   }
   ++k;
+  consumer_sync();
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Barrier over every CTA of every rank, in two levels so that no address
+// takes more than one write per rank over NVLink: the CTAs of this GPU meet
+// at a grid barrier whose arrivals are system-scope releases (ordering their
+// stores into peer memory), then one thread per rank publishes the barrier's
+// epoch into every peer's flag slot for this rank (release, system scope),
+// and every CTA waits until all peers' slots in its own memory carry the
+// epoch.  One GPU: the grid barrier alone.
+__device__ __forceinline__ void xgrid_sync(const DecodeArgs& a, unsigned long long* bar, int& k, int& kx,
+                                           volatile int* s_ok) {
+  grid_sync(bar, a.lbase, k, s_ok, a.tp > 1);
+  if (a.tp == 1) return;
+  const unsigned long long epoch = a.xepoch + (unsigned long long)(++kx);
+  if (threadIdx.x == 0 && *s_ok) {
+    if (blockIdx.x == 0)
+      for (int p = 0; p < a.tp; ++p)
+        if (p != a.rank) st_release_sys_u64(a.xflagg[p] + a.rank, epoch);
+    const unsigned long long* mine = a.xflagg[a.rank];
+    const long long t0 = clock64();
+    for (int p = 0; p < a.tp; ++p) {
+      if (p == a.rank) continue;
+      while (ld_acquire_sys_u64(mine + p) < epoch) {
+        if (clock64() - t0 > kSpinLimitCycles) {
+          atomicExch(&g_b2q_device_error, 5);
+          *s_ok = 0;
+          break;
+        }
+      }
+    }
+  }
   consumer_sync();
 }
 
@@ -768,7 +826,11 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int i = gt + kAttnThreads * r;
-      if (i < G * HD) a.attn[(g * G + i / HD) * HD + i % HD] = O[r] * (1.0f / fmaxf(Ls[r], 1e-12f));
+      if (i < G * HD) {
+        const float v = O[r] * (1.0f / fmaxf(Ls[r], 1e-12f));
+        const int o = (a.h_off + g * G + i / HD) * HD + i % HD;
+        for (int p = 0; p < a.tp; ++p) a.attng[p][o] = v;
+      }
     }
     if (gt == 0) a.sync->attn_cnt[g] = 0u;
     B2Q_FTRACE(tl, 14);
@@ -805,7 +867,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
   __shared__ int s_ok;
   __shared__ float s_bv[kGemvConsumerWarps];
   __shared__ int s_bi[kGemvConsumerWarps];
-  __shared__ int s_last;
   __shared__ uint64_t attn_bar[4];
   __shared__ int attn_last[4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -841,7 +902,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
   cs.R.empty = empty_bar;
   cs.R.cap = a.cap;
   unsigned long long* bar = &a.sync->bar;
-  int nbar = 0;  // grid barriers passed
+  int nbar = 0, nxbar = 0;  // this-GPU and all-rank barriers passed
+  float* const x = a.xg[a.rank];
 
   // this CTA's phase table, and the token embedding (embed_rows_kernel's
   // values) spread over the grid
@@ -854,9 +916,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
     const uint8_t* rowp = a.tok_raw + (int64_t)tok * a.tok_row_bytes;
     const int64_t slots = dequant_slots(a.tok_dtype, a.E);
     for (int64_t sl = (int64_t)blockIdx.x * 512 + threadIdx.x; sl < slots; sl += (int64_t)gridDim.x * 512)
-      dequant_slot(rowp, a.tok_dtype, sl, a.x);
+      dequant_slot(rowp, a.tok_dtype, sl, x);
   }
-  grid_sync(bar, nbar, okp);
+  grid_sync(bar, a.lbase, nbar, okp);
 
   const int nz = a.pos / kAttnTile + 1;
   int attn_uses = 0;  // completed phases of the attention mbarrier
@@ -883,7 +945,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       for (int it = blockIdx.x; it < a.KV * nz; it += gridDim.x)
         attn_item<G>(a, Ly, it / nz, it % nz, nz, T, &attn_bar[0], attn_uses, &attn_last[0], l);
       B2Q_TRACE(tslot + 2);
-      grid_sync(bar, nbar, okp);
+      xgrid_sync(a, bar, nbar, nxbar, okp);  // the O projection needs every rank's heads
       continue;
     }
     const CtaPhase& ph = tab[head ? 4 * a.n_layers : 4 * l + (k == 0 ? 0 : k - 1)];
@@ -891,26 +953,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       const bool add = k == 2 || k == 4;
       const int row0 = ph.gb * 8, nrows = min(ph.ge * 8, ph.n) - row0;
       const int rows = (ph.ge - ph.gb) * 8;
+      // global row of local row 0 (O/down: x rows, gate/up: h rows, head: vocab)
+      const int grow0 = row0 + (add ? a.o_off : k == 3 ? a.f_off : head ? a.v_off : 0);
       // residual rows of this CTA: copied (L2 -> shared, asynchronously)
       // behind the accumulators while the input is staged
       float* resid = racc + 2 * rows;
       if (add)
         for (int r4 = threadIdx.x; 4 * r4 < nrows; r4 += kGemvConsumerWarps * 32)
           asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(resid + 4 * r4)),
-                       "l"(a.x + row0 + 4 * r4)
+                       "l"(x + grow0 + 4 * r4)
                        : "memory");
       // stage the input: rmsnorm(x) for QKV, gate/up and the head; attn; h
       XQ q;
       if (k == 2) {
-        q = smem_xq(xs, round_up_int(a.H * kHeadDim, 256));
-        stage_plain(a.attn, a.H * kHeadDim, q);
+        q = smem_xq(xs, round_up_int(a.Hg * kHeadDim, 256));
+        stage_plain(a.attng[a.rank], a.Hg * kHeadDim, q);
       } else if (k == 4) {
         q = smem_xq(xs, round_up_int(a.F, 256));
-        stage_plain(a.h, a.F, q);
+        stage_plain(a.hg[a.rank], a.F, q);
       } else {
         q = smem_xq(xs, kp_e);
         const float* nw = head ? a.out_norm : (k == 0 ? a.layers[l].attn_norm : a.layers[l].ffn_norm);
-        stage_rmsnorm(a.x, nw, a.E, a.eps, q, xcopy, red, l, k == 0 ? 0 : 4);
+        stage_rmsnorm(x, nw, a.E, a.eps, q, xcopy, red, l, k == 0 ? 0 : 4);
       }
       B2Q_TRACE(tslot + 1);
       B2Q_FTRACE(l, 21 + k);
@@ -923,13 +987,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       }
       if (ok) {
         const int nw = pair ? 2 : 1;
-        float* y = (head ? a.logits : k == 0 ? a.qkv : pair ? a.h : a.x) + ph.ycol + row0;
         for (int r = threadIdx.x; r < nrows; r += kGemvConsumerWarps * 32) {
           const float v = dec_racc(racc, rows, nw, r, 0);
-          if (pair) y[r] = silu_f(v) * dec_racc(racc, rows, nw, r, 1);
-          else if (add) y[r] = resid[r] + v;
-          else y[r] = v;
-          if (head && v > best) { best = v; idx = row0 + r; }
+          if (k == 0 && !head) {  // q/k/v: this rank's heads, local
+            a.qkv[ph.ycol + row0 + r] = v;
+            continue;
+          }
+          const float out = pair ? silu_f(v) * dec_racc(racc, rows, nw, r, 1) : add ? resid[r] + v : v;
+          float* const* yg = head ? a.logitsg : pair ? a.hg : a.xg;
+          for (int p = 0; p < a.tp; ++p) yg[p][grow0 + r] = out;
+          if (head && v > best) { best = v; idx = grow0 + r; }
         }
       }
       B2Q_TRACE(tslot + 2);
@@ -942,25 +1009,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       }
 #endif
     }
-    if (!head) grid_sync(bar, nbar, okp);
+    if (head) break;
+    if (k == 0) grid_sync(bar, a.lbase, nbar, okp);  // attention is local to the rank
+    else xgrid_sync(a, bar, nbar, nxbar, okp);
   }
   warp_argmax(best, idx);
   if (lane == 0) { s_bv[warp] = best; s_bi[warp] = idx; }
   consumer_sync();
   if (threadIdx.x == 0) {
     for (int w = 1; w < kGemvConsumerWarps; ++w) argmax_merge(best, idx, s_bv[w], s_bi[w]);
-    a.cand[blockIdx.x] = make_int2(__float_as_int(best), idx);
-    __threadfence();
-    const unsigned int old = atomicAdd(&a.sync->head_cnt, 1u);
-    s_last = old == gridDim.x - 1;
+    const int2 cv = make_int2(__float_as_int(best), idx);
+    for (int p = 0; p < a.tp; ++p) a.candg[p][a.rank * gridDim.x + blockIdx.x] = cv;
   }
-  consumer_sync();
-  if (s_last && warp == 0) {
-    __threadfence();
+  xgrid_sync(a, bar, nbar, nxbar, okp);  // every CTA's candidate, every rank's logits
+  if (blockIdx.x == 0 && warp == 0) {
     best = -INFINITY;
     idx = 0x7fffffff;
-    for (int c = lane; c < (int)gridDim.x; c += 32) {
-      const int2 cv = __ldcg(a.cand + c);
+    const int2* cand = a.candg[a.rank];
+    for (int c = lane; c < a.tp * (int)gridDim.x; c += 32) {
+      const int2 cv = __ldcg(cand + c);
       argmax_merge(best, idx, __int_as_float(cv.x), cv.y);
     }
     warp_argmax(best, idx);
@@ -968,8 +1035,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       const uint32_t r = idx == 0x7fffffff ? 0u : (uint32_t)idx;
       *a.argmax = r;
       if (a.argmax2 != nullptr) *a.argmax2 = r;
-      a.sync->head_cnt = 0u;
-      a.sync->bar = 0ull;  // every CTA has passed its last barrier
     }
   }
 }

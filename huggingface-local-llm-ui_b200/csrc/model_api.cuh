@@ -326,6 +326,7 @@ static b2q_status forward_impl(b2q_model* M, const uint32_t* tokens, bool tok_on
     if (m == 1 && M->dec_on) {
       // one persistent kernel for the whole step (validates the id itself)
       err = launch_decode(M, src, start + off, argmax_dev, st);
+      M->last_logits = M->dec_logits;
       if (err == cudaSuccess && argmax_done) *argmax_done = argmax_dev != nullptr;
       if (err == cudaSuccess && !tok_on_dev && off + m < n) err = cudaStreamSynchronize(st);
       continue;
@@ -340,6 +341,7 @@ static b2q_status forward_impl(b2q_model* M, const uint32_t* tokens, bool tok_on
     } else {
       err = forward_pass(M, m, false, st);
     }
+    M->last_logits = M->logits;
     // the pinned staging is reused by the next chunk: wait for its copy
     if (err == cudaSuccess && !tok_on_dev && off + m < n) err = cudaStreamSynchronize(st);
   }
@@ -359,7 +361,7 @@ b2q_status b2q_forward_dev(b2q_model* M, const uint32_t* tokens_dev, int n, int 
   if (s != B2Q_OK) return s;
   cudaError_t err = cudaSuccess;
   if (logits_dev)
-    err = cudaMemcpyAsync(logits_dev, M->logits, sizeof(float) * M->c.n_vocab, cudaMemcpyDeviceToDevice, st);
+    err = cudaMemcpyAsync(logits_dev, M->last_logits, sizeof(float) * M->c.n_vocab, cudaMemcpyDeviceToDevice, st);
   if (err == cudaSuccess && argmax_dev && !argmax_done)
     err = cudaMemcpyAsync(argmax_dev, M->argmax, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st);
   if (err != cudaSuccess) return cuda_error(err, "b2q_forward_dev: copy out");
@@ -376,7 +378,7 @@ b2q_status b2q_forward(b2q_model* M, const uint32_t* tokens, int n, int start, f
   if (s != B2Q_OK) return s;
   cudaError_t err = cudaSuccess;
   if (logits)
-    err = cudaMemcpyAsync(logits, M->logits, sizeof(float) * M->c.n_vocab, cudaMemcpyDeviceToHost, M->st);
+    err = cudaMemcpyAsync(logits, M->last_logits, sizeof(float) * M->c.n_vocab, cudaMemcpyDeviceToHost, M->st);
   if (err == cudaSuccess && argmax)
     err = cudaMemcpyAsync(argmax, M->argmax, sizeof(uint32_t), cudaMemcpyDeviceToHost, M->st);
   if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
@@ -394,8 +396,14 @@ b2q_status b2q_clear_state(b2q_model* M) {
     // a wait can leave them inconsistent)
     std::lock_guard<std::mutex> lk(M->eng->mu);
     cudaSetDevice(M->eng->device);
+    // (all ranks of a tensor-parallel model call it together)
     cudaError_t err = cudaMemsetAsync(M->dec_sync, 0, sizeof(b2q::DecSync), M->st);
+    const b2q::XBlock xl = b2q::xblock_layout(M->c.n_embd, M->c.n_heads * M->c.head_dim, M->c.n_ff,
+                                              M->c.n_vocab, M->c.tp_size, M->eng->num_sms);
+    if (err == cudaSuccess)
+      err = cudaMemsetAsync(static_cast<uint8_t*>(M->dec_xblock) + xl.bar, 0, 8 * b2q::kMaxTp, M->st);
     if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
+    M->dec_launches = 0;
     if (err != cudaSuccess) return cuda_error(err, "b2q_clear_state");
   }
   return B2Q_OK;
@@ -421,7 +429,9 @@ b2q_status b2q_model_destroy(b2q_model* M) {
   b2q_weight_free(M->output);
   void* ps[] = {M->tok_raw, M->output_norm, M->x, M->qkv, M->attn, M->attn_loc, M->hbuf, M->h_loc,
                 M->y_loc, M->logits, M->logits_loc, M->part, M->tokens, M->argmax, M->pos,
-                M->rope_cos, M->rope_sin, M->dec_layers, M->dec_tab, M->dec_sync, M->dec_cand};
+                M->rope_cos, M->rope_sin, M->dec_layers, M->dec_tab, M->dec_sync, M->dec_xblock};
+  for (int p = 0; p < b2q::kMaxTp; ++p)
+    if (M->dec_peer[p] && p != M->c.tp_rank) cudaIpcCloseMemHandle(M->dec_peer[p]);
   for (void* p : ps)
     if (p) cudaFree(p);
   xq_free(&M->xq_e);

@@ -68,8 +68,12 @@ struct b2q_model {
   // persistent decode kernel (m = 1, one GPU)
   b2q::DecLayer* dec_layers = nullptr;
   b2q::CtaPhase* dec_tab = nullptr;
+  void* dec_xblock = nullptr;              // exchanged vectors of this rank (see DecodeArgs)
+  void* dec_peer[b2q::kMaxTp] = {nullptr};  // peers' blocks (IPC-mapped), tensor parallelism
+  float* dec_logits = nullptr;
+  uint64_t dec_launches = 0;
+  const float* last_logits = nullptr;       // where the last forward left its logits
   b2q::DecSync* dec_sync = nullptr;
-  int2* dec_cand = nullptr;
   b2q::DecodeArgs dec{};
   size_t dec_smem = 0;
   int dec_G = 0;
@@ -466,6 +470,32 @@ static void* decode_kernel_ptr(int G, size_t* attn_smem) {
 
 static size_t round128(size_t v) { return (v + 127) / 128 * 128; }
 
+// One rank's block of the vectors every rank needs whole (DecodeArgs xg,
+// attng, hg, logitsg, candg, xbarg): one allocation, so that one IPC handle
+// maps it into the peers.
+struct XBlock {
+  size_t x, attn, h, logits, cand, bar, total;
+};
+static XBlock xblock_layout(int E, int Hhd, int F, int V, int tp, int grid) {
+  auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+  XBlock b;
+  size_t o = 0;
+  b.x = o;
+  o += al((size_t)E * 4);
+  b.attn = o;
+  o += al((size_t)Hhd * 4);
+  b.h = o;
+  o += al((size_t)F * 4);
+  b.logits = o;
+  o += al((size_t)V * 4);
+  b.cand = o;
+  o += al((size_t)tp * grid * sizeof(int2));
+  b.bar = o;  // kMaxTp 64-bit epoch slots, one per source rank
+  o += 256;
+  b.total = o;
+  return b;
+}
+
 // Builds the persistent decode plan.  Leaves dec_on false (single-token
 // steps then use the captured graph) when the model does not fit it:
 // tensor parallelism, an unsupported head grouping, or too little shared
@@ -474,9 +504,10 @@ static cudaError_t setup_decode(b2q_model* M) {
   const b2q_model_config& c = M->c;
   b2q_engine* e = M->eng;
   M->dec_on = false;
-  // one GPU; KV heads within the arrival counters
-  if (c.tp_size != 1 || c.n_kv_heads > 64) return cudaSuccess;
-  const int H = c.n_heads, KV = c.n_kv_heads, G = H / KV, hd = c.head_dim;
+  // KV heads within the arrival counters; ranks within the peer tables
+  const int P = c.tp_size, rk = c.tp_rank;
+  if (M->KV_loc > 64 || P > kMaxTp) return cudaSuccess;
+  const int H = M->H_loc, KV = M->KV_loc, G = H / KV, hd = c.head_dim;
   size_t attn_one = 0;
   void* kern = decode_kernel_ptr(G, &attn_one);
   if (!kern) return cudaSuccess;
@@ -558,8 +589,26 @@ static cudaError_t setup_decode(b2q_model* M) {
   if (err == cudaSuccess)
     err = cudaMemcpy(M->dec_tab, tab.data(), tab.size() * sizeof(CtaPhase), cudaMemcpyHostToDevice);
   if (err == cudaSuccess) err = dalloc(&M->dec_sync, 1);
-  if (err == cudaSuccess) err = dalloc(&M->dec_cand, (size_t)grid);
+  const XBlock xl = xblock_layout(c.n_embd, c.n_heads * hd, c.n_ff, c.n_vocab, P, grid);
+  if (err == cudaSuccess) err = dalloc(reinterpret_cast<uint8_t**>(&M->dec_xblock), xl.total);
   if (err != cudaSuccess) return err;
+  M->dec_peer[rk] = M->dec_xblock;
+  if (P > 1) {
+    // map every rank's block into this process: IPC handles gathered over NCCL
+    cudaIpcMemHandle_t mine;
+    err = cudaIpcGetMemHandle(&mine, M->dec_xblock);
+    uint8_t* hb = nullptr;
+    if (err == cudaSuccess) err = dalloc(&hb, sizeof(cudaIpcMemHandle_t) * (size_t)(P + 1));
+    if (err == cudaSuccess) err = cudaMemcpy(hb, &mine, sizeof mine, cudaMemcpyHostToDevice);
+    if (err == cudaSuccess) err = tp_allgather_bytes(M->tp, hb, hb + sizeof mine, sizeof mine, M->st);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
+    std::vector<cudaIpcMemHandle_t> all((size_t)P);
+    if (err == cudaSuccess) err = cudaMemcpy(all.data(), hb + sizeof mine, sizeof mine * P, cudaMemcpyDeviceToHost);
+    if (hb) cudaFree(hb);
+    for (int p = 0; p < P && err == cudaSuccess; ++p)
+      if (p != rk) err = cudaIpcOpenMemHandle(&M->dec_peer[p], all[(size_t)p], cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess) return err;
+  }
   a.layers = M->dec_layers;
   a.ctab = M->dec_tab;
   a.nph = nph;
@@ -567,6 +616,7 @@ static cudaError_t setup_decode(b2q_model* M) {
   a.E = c.n_embd;
   a.H = H;
   a.KV = KV;
+  a.Hg = c.n_heads;
   a.F = c.n_ff;
   a.V = c.n_vocab;
   a.eps = c.rms_eps;
@@ -578,16 +628,27 @@ static cudaError_t setup_decode(b2q_model* M) {
   a.tok_row_bytes = M->tok_row_bytes;
   a.rope_cos = M->rope_cos;
   a.rope_sin = M->rope_sin;
-  a.x = M->x;
   a.qkv = M->qkv;
-  a.attn = M->attn;
-  a.h = M->hbuf;
-  a.logits = M->logits;
   a.part = M->part;
   a.nsplit = M->nsplit;
   a.sync = M->dec_sync;
-  a.cand = M->dec_cand;
   a.argmax = M->argmax;
+  a.tp = P;
+  a.rank = rk;
+  a.o_off = rk * (c.n_embd / P);
+  a.f_off = rk * M->F_loc;
+  a.v_off = rk * M->V_loc;
+  a.h_off = rk * M->H_loc;
+  for (int p = 0; p < P; ++p) {
+    uint8_t* base = static_cast<uint8_t*>(M->dec_peer[p]);
+    a.xg[p] = reinterpret_cast<float*>(base + xl.x);
+    a.attng[p] = reinterpret_cast<float*>(base + xl.attn);
+    a.hg[p] = reinterpret_cast<float*>(base + xl.h);
+    a.logitsg[p] = reinterpret_cast<float*>(base + xl.logits);
+    a.candg[p] = reinterpret_cast<int2*>(base + xl.cand);
+    a.xflagg[p] = reinterpret_cast<unsigned long long*>(base + xl.bar);
+  }
+  M->dec_logits = a.logitsg[rk];
   a.cap = (int)cap;
   a.stage_bytes = (int)stage;
   a.racc_bytes = (int)racc;
@@ -603,6 +664,12 @@ static cudaError_t launch_decode(b2q_model* M, const uint32_t* tok, int pos, uin
   a.token = tok;
   a.pos = pos;
   a.argmax2 = argmax2;
+  // every earlier launch passed 5L + 2 grid barriers (1 + L of them local
+  // only, 4L + 1 as the first level of an all-rank barrier) and 4L + 1
+  // all-rank epochs
+  const unsigned long long seq = M->dec_launches++, grid = (unsigned long long)M->eng->num_sms;
+  a.lbase = seq * (5ull * a.n_layers + 2ull) * grid;
+  a.xepoch = seq * (4ull * a.n_layers + 1ull);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M->eng->num_sms);
   cfg.blockDim = dim3(kGemvThreads);

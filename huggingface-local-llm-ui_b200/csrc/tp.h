@@ -20,6 +20,7 @@ namespace b2q {
 typedef int nccl_result_t;
 typedef void* nccl_comm_t;
 struct nccl_unique_id { char internal[128]; };
+constexpr int kNcclUint8 = 1;
 constexpr int kNcclFloat32 = 7;
 
 struct NcclApi {
@@ -123,6 +124,12 @@ inline cudaError_t tp_gather_core(TpComm& t, const float* loc, float* full, int 
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
   tp_scatter_rows_kernel<<<blocks, 256, 0, st>>>(t.stage, full, t.size, m, n_loc, add);
   return cudaGetLastError();
+}
+
+// Every rank's `bytes` bytes at send (device) -> recv [P][bytes] (device).
+inline cudaError_t tp_allgather_bytes(TpComm& t, const void* send, void* recv, size_t bytes, cudaStream_t st) {
+  nccl_result_t r = nccl().all_gather(send, recv, bytes, kNcclUint8, t.comm, st);
+  return r == 0 ? cudaSuccess : cudaErrorUnknown;
 }
 
 inline cudaError_t tp_allgather_rows(TpComm& t, const float* loc, float* full, int m, int n_loc,
