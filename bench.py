@@ -73,10 +73,10 @@ def measured_peaks() -> tuple[float, str]:
     return HBM_FALLBACK_GBS, "fallback"
 
 
-def profile_traffic() -> float | None:
-    """DRAM bytes per launch of the Q4_K 14336x4096 GEMV from the committed
-    ncu summary (profiles/), if one has been captured."""
-    p = REPO / "profiles" / "gemv_q4k_14336x4096.md"
+def profile_traffic(name: str = "gemv_q4k_14336x4096.md") -> float | None:
+    """DRAM bytes per launch from a committed ncu summary under profiles/
+    (its "traffic_bytes_per_launch:" line), if one has been captured."""
+    p = REPO / "profiles" / name
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -164,6 +164,27 @@ def build_model(pkg, engine, cfg, seed, rank, size, tp_id, max_seq, dist="bench"
     return m, host
 
 
+def step_algorithmic_bytes(cfg, rank: int, world: int, ctx: int) -> int:
+    """Bytes one single-token step must read on `rank`: every weight row it
+    owns (all matvec weights of every layer and the output head; one row of
+    token_embd), the norms, and the f16 K/V rows of its KV heads for `ctx`
+    cached tokens."""
+    from hf_llm_b200 import ggml, model, synth
+    total = 0
+    for name, t, dims, _ in synth.llama_specs(cfg, model.q4_k_m_types()):
+        if len(dims) == 1:
+            total += 4 * dims[0]
+            continue
+        n, k = dims
+        if name == "token_embd.weight":
+            total += ggml.row_bytes(t, k)
+            continue
+        b, e = model.tp_shard_rows(cfg, name, n, rank, world)
+        total += (e - b) * ggml.row_bytes(t, k)
+    total += cfg["n_layers"] * 2 * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * 2 * ctx
+    return total
+
+
 def cpu_decode_rate(orc, cfg, host, steps: int, warmup: int, threads: int) -> dict:
     """The reference CPU path: decode tok/s of the same model (prefill 8
     tokens, then `steps` timed greedy decode steps)."""
@@ -239,17 +260,17 @@ def run_reference_arm(args):
     pkg = load_pkg()
     orc = load_oracle()
     from hf_llm_b200 import model, synth
-    cfg = dict(model.LLAMA3_8B)
+    cfg = dict(model.LLAMA3_70B if args.model == "70b" else model.LLAMA3_8B)
     host = synth.llama_tensors(cfg, model.q4_k_m_types(), args.seed)
     threads = os.cpu_count() or 1
     steps = max(1, min(args.steps, args.cpu_steps))
     warm = max(0, min(args.warmup, 1))
     r = cpu_decode_rate(orc, cfg, host, steps, warm, threads)
-    line = {"metric": "decode tok/s at Llama-3-8B Q4_K_M shape", "value": r["value"], "unit": "tok/s",
-            "impl": "reference", "n_gpus": args.gpus, "steps": steps, "warmup": warm,
+    line = {"metric": f"decode tok/s at Llama-3-{args.model.upper()} Q4_K_M shape", "value": r["value"],
+            "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus, "steps": steps, "warmup": warm,
             "ms_per_step": 1000.0 / r["value"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8/f32", "data": "synthetic",
-            "config": {"workload": "llama3-8b-q4_k_m-decode", "prefill": 8, "batch": 1},
+            "config": {"workload": f"llama3-{args.model}-q4_k_m-decode", "prefill": 8, "batch": 1},
             "cpu_baseline": r,
             "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -268,8 +289,10 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--e2e-steps", type=int, default=64)
-    ap.add_argument("--layers", type=int, default=32,
-                    help="decoder layers (32 = Llama-3-8B; fewer only for kernel profiles on a small case)")
+    ap.add_argument("--model", default="8b", choices=["8b", "70b"],
+                    help="Llama-3-8B (the headline workload) or Llama-3-70B shape")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decoder layers (default: the model's; fewer only for kernel profiles on a small case)")
     ap.add_argument("--decode", default="persistent", choices=["persistent", "graph", "eager"],
                     help="single-token step: captured kernel graph, one persistent kernel, or eager")
     ap.add_argument("--no-gemv-shapes", action="store_true", help="skip the per-shape GEMV timings")
@@ -315,7 +338,8 @@ def main():
         dist.broadcast_object_list(obj, src=0)
         tp_id = obj[0]
 
-    cfg = dict(model.LLAMA3_8B, n_layers=args.layers)
+    base = model.LLAMA3_70B if args.model == "70b" else model.LLAMA3_8B
+    cfg = dict(base, n_layers=args.layers or base["n_layers"])
     max_seq = args.prefill + args.warmup + args.steps + args.e2e_steps + 8
     t_load = time.perf_counter()
     m, host = build_model(pkg, engine, cfg, args.seed, rank, world, tp_id, max_seq, decode=args.decode)
@@ -381,9 +405,23 @@ def main():
            "d2h_bytes_per_step": 4 * cfg["n_vocab"],
            "note": "b2q_forward with host token ids and host logits; host wall clock"}
 
-    # ---- roofline of the dominant kernel (Q4_K GEMV, FFN gate shape) ----
+    # ---- roofline of the dominant kernel ----
+    # persistent path: the decode kernel itself (the only kernel of a step);
+    # bytes = what one step must read (weights it owns + KV rows) per launch
     peak, peak_kind = measured_peaks()
+    ctx = args.prefill + args.warmup + args.steps // 2
+    step_bytes = step_algorithmic_bytes(cfg, rank, world, ctx)
+    step_gbs = step_bytes / (ms_step * 1e-3) / 1e9
     roof = None
+    if m.decode_mode == "persistent":
+        roof = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(step_gbs / peak, 4),
+                "traffic": profile_traffic(f"decode_kernel_llama3_{args.model}.md") if world == 1 else None,
+                "kernel": "decode_kernel (persistent single-token step)",
+                "algorithmic_bytes_per_launch": int(step_bytes), "peak_kind": peak_kind,
+                "launch_us": round(ms_step * 1000, 2)}
+    # the standalone GEMV (Q4_K, FFN gate shape) and the other matvec shapes
+    gemv_roof = None
     gemv_shapes = {}
     if rank == 0:
         keys = ["q4k_14336x4096"] if args.no_gemv_shapes else list(GEMV_SHAPES)
@@ -393,15 +431,13 @@ def main():
                                 "bytes": alg}
             if key == "q4k_14336x4096":
                 ach = alg / (ms_l * 1e-3) / 1e9
-                roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                        "frac": round(ach / peak, 4), "traffic": profile_traffic(),
-                        "kernel": "gemv_kernel (Q4_K, 14336x4096)",
-                        "algorithmic_bytes_per_launch": alg, "peak_kind": peak_kind,
-                        "launch_us": round(ms_l * 1000, 3)}
-    # decode-step bandwidth: weights + KV read per token
-    kv_bytes = cfg["n_layers"] * 2 * cfg["n_kv_heads"] * cfg["head_dim"] * 2 * (args.prefill + args.warmup +
-                                                                                  args.steps // 2)
-    step_bytes = m.weight_bytes - 4 * 0 + kv_bytes
+                gemv_roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(ach / peak, 4), "traffic": profile_traffic(),
+                             "kernel": "gemv_kernel (Q4_K, 14336x4096), one launch",
+                             "algorithmic_bytes_per_launch": alg, "peak_kind": peak_kind,
+                             "launch_us": round(ms_l * 1000, 3)}
+    if roof is None:
+        roof = gemv_roof
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -413,18 +449,19 @@ def main():
     del host
 
     if rank == 0:
-        line = {"metric": "decode tok/s at Llama-3-8B Q4_K_M shape", "value": round(value, 2),
+        line = {"metric": f"decode tok/s at Llama-3-{args.model.upper()} Q4_K_M shape", "value": round(value, 2),
                 "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(ms_step, 4), "higher_is_better": True,
                 "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
                 "dtype": "int16xint8 dp2a, f32 accum", "data": "synthetic",
-                "config": {"workload": "llama3-8b-q4_k_m-decode", "layers": cfg["n_layers"], "hidden": 4096,
-                           "heads": "32/8", "ffn": 14336, "vocab": 128256, "prefill": args.prefill,
+                "config": {"workload": f"llama3-{args.model}-q4_k_m-decode", "layers": cfg["n_layers"],
+                           "hidden": cfg["n_embd"], "heads": f"{cfg['n_heads']}/{cfg['n_kv_heads']}",
+                           "ffn": cfg["n_ff"], "vocab": cfg["n_vocab"], "prefill": args.prefill,
                            "batch": 1, "kv_cache": "f16", "tp": world, "decode": m.decode_mode,
-                           "l2": "inputs larger than L2 (4.9 GB weights per step)"},
-                "decode_step": {"bytes_per_step_rank0": int(step_bytes),
-                                "GBps_rank0": round(step_bytes / (ms_step * 1e-3) / 1e9, 1)},
-                "roofline": roof, "gemv_shapes": gemv_shapes, "cpu_baseline": cpu, "e2e": e2e,
+                           "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB read per step)"},
+                "decode_step": {"bytes_per_step_rank0": int(step_bytes), "GBps_rank0": round(step_gbs, 1)},
+                "roofline": roof, "gemv_roofline": gemv_roof, "gemv_shapes": gemv_shapes,
+                "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": int(launches), "clocks": clk.summary(),
                 "load_s": round(t_load, 1)}
         print(json.dumps(line), flush=True)

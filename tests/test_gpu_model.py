@@ -157,6 +157,23 @@ def test_persistent_decode_llama3_8b_geometry(engine, orc, pkg):
     engine.check_device_error()
 
 
+def test_persistent_decode_llama3_70b_geometry(engine, pkg):
+    """Llama-3-70B widths (hidden 8192, 64:8 heads, FFN 28672), one layer,
+    a reduced vocabulary: the persistent kernel (64 KB of staged FFN input,
+    eight query heads per KV head) equals the eager kernels bit for bit."""
+    from hf_llm_b200 import model, synth
+    cfg = dict(model.LLAMA3_70B, n_layers=1, n_vocab=4000)
+    t = synth.llama_tensors(cfg, model.q4_k_m_types(), 23, dist="unit")
+    pm = model.StandardNativeEngine.from_tensors(engine, cfg, t, max_seq=96, decode="persistent")
+    em = model.StandardNativeEngine.from_tensors(engine, cfg, t, max_seq=96, decode="eager")
+    toks = list(range(7, 77))
+    assert np.array_equal(pm.forward(toks, 0), em.forward(toks, 0))
+    for step, tok in enumerate((11, 3999, 0)):
+        a, b = pm.forward([tok], 70 + step), em.forward([tok], 70 + step)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), step
+    engine.check_device_error()
+
+
 def test_greedy_generation_follows_fp64_argmax(engine, orc, pkg):
     dev, ref = _pair(engine, orc, pkg, TOY, seed=3)
     out = dev.generate_greedy([5, 6, 7], 6)
