@@ -62,6 +62,21 @@ SIGNATURES = [
     ("b2q_forward", _I, [_VP, _U32P, _I, _I, _FP, _U32P]),
     ("b2q_forward_dev", _I, [_VP, _VP, _I, _I, _VP, _VP, _VP]),
     ("b2q_clear_state", _I, [_VP]),
+    ("b2q_gguf_open", _I, [C.c_char_p, C.POINTER(_VP)]),
+    ("b2q_gguf_close", _I, [_VP]),
+    ("b2q_gguf_version", _I, [_VP]),
+    ("b2q_gguf_n_tensors", _I64, [_VP]),
+    ("b2q_gguf_n_kv", _I64, [_VP]),
+    ("b2q_gguf_kv_key", _I, [_VP, _I64, C.POINTER(C.c_char_p), C.POINTER(_I)]),
+    ("b2q_gguf_tensor_info", _I, [_VP, _I64, C.POINTER(C.c_char_p), C.POINTER(_I), C.POINTER(_I),
+                                  C.POINTER(_I64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
+    ("b2q_gguf_find_tensor", _I, [_VP, C.c_char_p, C.POINTER(_I64)]),
+    ("b2q_gguf_tensor_data", _VP, [_VP, _I64]),
+    ("b2q_gguf_get_usize", _I, [_VP, C.c_char_p, C.POINTER(C.c_uint64)]),
+    ("b2q_gguf_get_f32", _I, [_VP, C.c_char_p, C.POINTER(C.c_float)]),
+    ("b2q_gguf_get_str", _I, [_VP, C.c_char_p, C.POINTER(_VP), C.POINTER(_SZ)]),
+    ("b2q_gguf_llama_config", _I, [_VP, C.c_char_p, C.POINTER(ModelConfig)]),
+    ("b2q_model_load_gguf", _I, [_VP, _VP]),
     ("b2q_model_weight_bytes", _SZ, [_VP]),
     ("b2q_model_destroy", _I, [_VP]),
     ("b2q_time_gemv", _I, [_VP, C.POINTER(_VP), _I, _VP, _I, _I, _VP, C.POINTER(C.c_float)]),

@@ -741,3 +741,4 @@ b2q_status b2q_check_device_error(b2q_engine* e) {
 }  // extern "C"
 
 #include "model_api.cuh"
+#include "gguf_api.cuh"

@@ -100,6 +100,23 @@ class StandardNativeEngine:
         m.finalize()
         return m
 
+    @classmethod
+    def from_gguf(cls, engine: CudaEngine, gguf, arch: str = "llama", max_seq: int = 8192,
+                  **kw) -> "StandardNativeEngine":
+        """StandardNativeEngine::from_gguf (inference.rs:2513-2620): the
+        hyperparameters and every tensor from a GGUF file (a path or an open
+        GgufFile); under tensor parallelism each rank uploads its own rows."""
+        from .gguf_file import GgufFile
+        f = gguf if isinstance(gguf, GgufFile) else GgufFile(gguf)
+        try:
+            m = cls(engine, f.llama_config(arch), max_seq=max_seq, **kw)
+            check(lib().b2q_model_load_gguf(m._h, f.handle))
+            m.finalize()
+        finally:
+            if f is not gguf:
+                f.close()
+        return m
+
     @property
     def weight_bytes(self) -> int:
         return int(lib().b2q_model_weight_bytes(self._h))

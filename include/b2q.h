@@ -221,6 +221,62 @@ b2q_status b2q_forward_dev(b2q_model* m, const uint32_t* tokens_dev, int n_token
 /* Replaces StandardNativeEngine::clear_state (inference.rs:2688-2693). */
 b2q_status b2q_clear_state(b2q_model* m);
 
+/* ---- GGUF files (GgufModelFile, inference.rs:235-510) ----
+ * A read-only POSIX mapping of the file, parsed as GgufModelFile::open
+ * does (inference.rs:343-446): versions 1..3, metadata types 0..12, dims
+ * reversed to [outer.., inner], data section aligned to general.alignment
+ * (default 32), every tensor checked to end inside the file.  Names and
+ * string values returned below point into the handle and stay valid until
+ * b2q_gguf_close.  Errors are B2Q_EINVAL with the reason in
+ * b2q_last_error() (the reference's anyhow messages). */
+typedef struct b2q_gguf b2q_gguf;
+
+/* GgufModelFile::open (inference.rs:343-446). */
+b2q_status b2q_gguf_open(const char* path, b2q_gguf** out);
+/* Drop of GgufModelFile: unmaps the file. */
+b2q_status b2q_gguf_close(b2q_gguf* g);
+int b2q_gguf_version(const b2q_gguf* g);
+int64_t b2q_gguf_n_tensors(const b2q_gguf* g);
+/* Metadata keys in file order; value_type is the GGUF value type (0..12). */
+int64_t b2q_gguf_n_kv(const b2q_gguf* g);
+b2q_status b2q_gguf_kv_key(const b2q_gguf* g, int64_t index, const char** key, int* value_type);
+/* GgufTensorDesc (inference.rs:236-244) of tensor `index` (file order):
+ * dims has room for 8 entries, [outer.., inner]; abs_offset is
+ * data_offset + the tensor's relative offset; byte_len is
+ * elements / block_size * type_size.  Any pointer may be NULL. */
+b2q_status b2q_gguf_tensor_info(const b2q_gguf* g, int64_t index, const char** name, int* ggml_type,
+                                int* n_dims, int64_t* dims, uint64_t* abs_offset, uint64_t* byte_len);
+/* Index of tensor `name`; B2Q_EINVAL "tensor '...' not found in GGUF". */
+b2q_status b2q_gguf_find_tensor(const b2q_gguf* g, const char* name, int64_t* index);
+/* Host pointer to the tensor's bytes inside the mapping (NULL if out of range). */
+const void* b2q_gguf_tensor_data(const b2q_gguf* g, int64_t index);
+/* GgufModelFile::get_usize / get_f32 (inference.rs:447-460) with
+ * GgufValue::as_usize / as_f32 (:203-223): u8/u16/u32/u64 and non-negative
+ * i32/i64 read as integers; f32, f64, u32 and i32 read as floats. */
+b2q_status b2q_gguf_get_usize(const b2q_gguf* g, const char* key, uint64_t* out);
+b2q_status b2q_gguf_get_f32(const b2q_gguf* g, const char* key, float* out);
+/* A string value (not NUL-terminated): pointer into the mapping and length. */
+b2q_status b2q_gguf_get_str(const b2q_gguf* g, const char* key, const char** s, size_t* len);
+
+/* Hyperparameters of StandardNativeEngine::from_gguf (inference.rs:2513-2537):
+ * "{arch}." keys, or "llama." when "{arch}.block_count" is absent
+ * (arch NULL means "llama"); head_count_kv defaults to head_count,
+ * key_length to embedding_length / head_count, the RMS epsilon to 1e-5,
+ * rope.freq_base to 10000; n_ff and n_vocab are the row counts of
+ * blk.0.ffn_gate.weight and token_embd.weight.  Fills those fields of
+ * *cfg and leaves max_seq, tp_rank, tp_size and no_graph as the caller set
+ * them. */
+b2q_status b2q_gguf_llama_config(const b2q_gguf* g, const char* arch, b2q_model_config* cfg);
+
+/* Tensor loading of from_gguf (inference.rs:2551-2587) into a model made by
+ * b2q_model_create: token_embd, output_norm, output (tied to token_embd when
+ * the file has none), and for every block attn_norm, attn_q/k/v, the
+ * optional attn_{q,k,v}.bias, attn_output, ffn_norm, ffn_gate/up/down.  Each
+ * rank uploads only its tensor-parallel rows, read from the mapping;
+ * 1-D F16/BF16 tensors are widened to F32 on the host.  Call
+ * b2q_model_finalize afterwards. */
+b2q_status b2q_model_load_gguf(b2q_model* m, const b2q_gguf* g);
+
 /* Device bytes held by the model's weights on this rank. */
 size_t b2q_model_weight_bytes(const b2q_model* m);
 
