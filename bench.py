@@ -73,6 +73,18 @@ def measured_peaks() -> tuple[float, str]:
     return HBM_FALLBACK_GBS, "fallback"
 
 
+def load_peaks() -> dict:
+    """MEASURED_PEAKS.json (driver-measured copy bandwidth and bf16 GEMM
+    throughput on this pool's B200s), or the fallback figures."""
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            pass
+    return {"hbm_gbs": HBM_FALLBACK_GBS, "bf16_tflops": 1590.0}
+
+
 def profile_traffic(name: str = "gemv_q4k_14336x4096.md") -> float | None:
     """DRAM bytes per launch from a committed ncu summary under profiles/
     (its "traffic_bytes_per_launch:" line), if one has been captured."""
@@ -182,6 +194,18 @@ def step_algorithmic_bytes(cfg, rank: int, world: int, ctx: int) -> int:
         b, e = model.tp_shard_rows(cfg, name, n, rank, world)
         total += (e - b) * ggml.row_bytes(t, k)
     total += cfg["n_layers"] * 2 * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * 2 * ctx
+    return total
+
+
+def prefill_matmul_params(cfg, rank: int, world: int) -> int:
+    """Weights (elements) of the per-layer projections this rank multiplies
+    in a prompt pass: q, k, v, o, gate, up, down of every layer."""
+    from hf_llm_b200 import model, synth
+    total = 0
+    for name, t, dims, _ in synth.llama_specs(cfg, model.q4_k_m_types()):
+        if len(dims) == 2 and name.startswith("blk."):
+            b, e = model.tp_shard_rows(cfg, name, dims[0], rank, world)
+            total += (e - b) * dims[1]
     return total
 
 
@@ -439,6 +463,34 @@ def main():
     if roof is None:
         roof = gemv_roof
 
+    # ---- prompt pass (prefill) on the tensor cores: the same prompt again ----
+    prefill = None
+    if args.prefill >= 16:
+        reps = 3
+        with torch.cuda.stream(stream):
+            m.forward_dev(prompt.data_ptr(), args.prefill, 0, 0, tok.data_ptr(), sp)  # warm-up
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if dist:
+            dist.barrier()
+        e0.record(stream)
+        for _ in range(reps):
+            m.forward_dev(prompt.data_ptr(), args.prefill, 0, 0, tok.data_ptr(), sp)
+        e1.record(stream)
+        e1.synchronize()
+        pms = e0.elapsed_time(e1) / reps
+        if dist:
+            t = torch.tensor([pms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            pms = float(t.item())
+        flops = 2.0 * args.prefill * prefill_matmul_params(cfg, rank, world)
+        tf = flops / (pms * 1e-3) / 1e12
+        pk = load_peaks().get("bf16_tflops")
+        prefill = {"tokens": args.prefill, "ms": round(pms, 3), "tok_s": round(args.prefill / (pms * 1e-3), 1),
+                   "matmul_tflops_rank0": round(tf, 1),
+                   "frac_of_bf16_peak": round(tf / pk, 4) if pk else None,
+                   "note": "whole prompt pass (norms, attention, f16 tensor-core projections); "
+                           "flops = 2 x tokens x projection weights of the layers (head excluded)"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
@@ -460,7 +512,7 @@ def main():
                            "batch": 1, "kv_cache": "f16", "tp": world, "decode": m.decode_mode,
                            "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB read per step)"},
                 "decode_step": {"bytes_per_step_rank0": int(step_bytes), "GBps_rank0": round(step_gbs, 1)},
-                "roofline": roof, "gemv_roofline": gemv_roof, "gemv_shapes": gemv_shapes,
+                "roofline": roof, "gemv_roofline": gemv_roof, "gemv_shapes": gemv_shapes, "prefill": prefill,
                 "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": int(launches), "clocks": clk.summary(),
                 "load_s": round(t_load, 1)}

@@ -157,6 +157,10 @@ cudaError_t launch_gemv(b2q_engine* e, GemvArgs& a, int epi, int mt, cudaStream_
   return mt == 1 ? launch_gemv_t<1, kEpiAdd>(e, a, st, pdl) : launch_gemv_t<2, kEpiAdd>(e, a, st, pdl);
 }
 
+}  // namespace b2q
+#include "tc_host.cuh"
+namespace b2q {
+
 // Largest token count per GEMV pass: each consumer lane keeps the
 // activations of every token of the pass in registers (32 per token), so
 // passes carry at most two tokens; larger prompts loop over passes.
@@ -301,6 +305,7 @@ static void ws_free(b2q_engine* e) {
   if (e->ws_h) cudaFree(e->ws_h);
   xq_free(&e->ws_xq);
   xq_free(&e->ws_hq);
+  tc_free(e);
   e->ws_x = e->ws_y = e->ws_h = nullptr;
   e->ws_x_cap = e->ws_y_cap = e->ws_h_cap = 0;
 }
@@ -477,6 +482,17 @@ static b2q_status matmul_group_core(b2q_engine* e, const b2q_weight* const* ws, 
     b2q_status s = check_weight(ws[i], ns[i], k, "matmul");
     if (s != B2Q_OK) return s;
   }
+  if (m >= kTcMinTokens) {
+    // many tokens per weight row: tensor cores
+    int64_t off = 0;
+    for (int i = 0; i < count; ++i) {
+      const int col0 = 0;
+      cudaError_t err = tc_matmul(e, x_dev, k, m, k, &ws[i], 1, kEpiStore, y_dev + off, ns[i], &col0, st, false);
+      if (err != cudaSuccess) return cuda_error(err, "matmul: tensor-core launch");
+      off += (int64_t)m * ns[i];
+    }
+    return B2Q_OK;
+  }
   cudaError_t err = ws_xq(&e->ws_xq, m, k);
   if (err != cudaSuccess) return cuda_error(err, "matmul: workspace");
   err = launch_quantize(e, x_dev, m, k, e->ws_xq, st, false);
@@ -549,6 +565,17 @@ static b2q_status ffn_core(b2q_engine* e, const b2q_weight* gate, const b2q_weig
   if (s != B2Q_OK) return s;
   if (gate->dtype != up->dtype)
     return set_error(B2Q_EUNSUP, "ffn_swiglu: gate and up must share a GGML type");
+  if (m >= kTcMinTokens) {
+    cudaError_t err = ws_reserve(&e->ws_h, &e->ws_h_cap, (size_t)m * ffn_inter * 4);
+    const b2q_weight* gu[2] = {gate, up};
+    const int col0 = 0;
+    if (err == cudaSuccess)
+      err = tc_matmul(e, x_dev, n_embd, m, n_embd, gu, 2, kEpiSwiglu, e->ws_h, ffn_inter, &col0, st, false);
+    if (err == cudaSuccess)
+      err = tc_matmul(e, e->ws_h, ffn_inter, m, ffn_inter, &down, 1, kEpiStore, y_dev, n_embd, &col0, st, false);
+    if (err != cudaSuccess) return cuda_error(err, "ffn_swiglu: tensor-core launch");
+    return B2Q_OK;
+  }
   cudaError_t err = ws_xq(&e->ws_xq, m, n_embd);
   if (err == cudaSuccess) err = ws_xq(&e->ws_hq, m, ffn_inter);
   if (err == cudaSuccess) err = ws_reserve(&e->ws_h, &e->ws_h_cap, (size_t)m * ffn_inter * 4);

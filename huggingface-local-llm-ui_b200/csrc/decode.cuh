@@ -240,29 +240,27 @@ __device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsign
 // Barrier over every CTA of every rank, in two levels so that no address
 // takes more than one write per rank over NVLink: the CTAs of this GPU meet
 // at a grid barrier whose arrivals are system-scope releases (ordering their
-// stores into peer memory), then one thread per rank publishes the barrier's
-// epoch into every peer's flag slot for this rank (release, system scope),
-// and every CTA waits until all peers' slots in its own memory carry the
-// epoch.  One GPU: the grid barrier alone.
+// stores into peer memory); then on CTA 0 lane p of warp 0 publishes the
+// barrier's epoch into peer p's flag slot for this rank (a system-scope
+// release), and on every CTA lane p polls peer p's slot in its own memory
+// (system-scope acquires) until it carries the epoch.  The lanes work in
+// parallel, so the cost does not grow with the number of ranks.  One GPU:
+// the grid barrier alone.
 __device__ __forceinline__ void xgrid_sync(const DecodeArgs& a, unsigned long long* bar, int& k, int& kx,
                                            volatile int* s_ok) {
   grid_sync(bar, a.lbase, k, s_ok, a.tp > 1);
   if (a.tp == 1) return;
   const unsigned long long epoch = a.xepoch + (unsigned long long)(++kx);
-  if (threadIdx.x == 0 && *s_ok) {
-    if (blockIdx.x == 0)
-      for (int p = 0; p < a.tp; ++p)
-        if (p != a.rank) st_release_sys_u64(a.xflagg[p] + a.rank, epoch);
-    const unsigned long long* mine = a.xflagg[a.rank];
+  const int p = threadIdx.x;
+  if (p < a.tp && p != a.rank && *s_ok) {
+    if (blockIdx.x == 0) st_release_sys_u64(a.xflagg[p] + a.rank, epoch);
+    const unsigned long long* slot = a.xflagg[a.rank] + p;
     const long long t0 = clock64();
-    for (int p = 0; p < a.tp; ++p) {
-      if (p == a.rank) continue;
-      while (ld_acquire_sys_u64(mine + p) < epoch) {
-        if (clock64() - t0 > kSpinLimitCycles) {
-          atomicExch(&g_b2q_device_error, 5);
-          *s_ok = 0;
-          break;
-        }
+    while (ld_acquire_sys_u64(slot) < epoch) {
+      if (clock64() - t0 > kSpinLimitCycles) {
+        atomicExch(&g_b2q_device_error, 5);
+        *s_ok = 0;
+        break;
       }
     }
   }

@@ -1,0 +1,463 @@
+// gemm_tc.cuh -- multi-token matmul (prompt prefill) on the 5th-generation
+// tensor cores: Y[t][r] = sum_k W[r][k] * X[t][k] for many tokens t.
+//
+// The batched path of MmapWeight::matmul_batched (src/inference.rs:589-760,
+// m > 1) and of the prompt pass of StandardNativeEngine::forward.  With
+// hundreds of tokens per weight row the work is tensor-core bound, not
+// HBM-bound, so the weights are dequantised once per CTA tile into f16 in
+// shared memory and multiplied by tcgen05.mma with the accumulator in TMEM.
+//
+// Per CTA: 128 weight rows (the UMMA M) x N tokens (the UMMA N, a multiple
+// of 16, <= 256) x a range of k-stages of 64 elements (split-K over
+// gridDim.z).  Warp roles:
+//   warps 0-7   dequantise the weight tile of each stage: thread (row r,
+//               half h) reads its bytes straight from the GEMV tile layout
+//               (quant.cuh), computes the f32 value bit-exactly as
+//               dequantize_slice does and rounds it to f16, and writes the
+//               no-swizzle K-major core-matrix layout UMMA reads;
+//   warp 8      streams the activation stage (pre-arranged in global memory
+//               in the same layout, f16) with one 1-D bulk copy per stage;
+//   warp 9      allocates TMEM and issues the MMAs (one thread), committing
+//               each stage back to its producers;
+//   warps 0-3   after the last stage, read the accumulator out of TMEM
+//               (tcgen05.ld, one weight row per thread) and store f32 partial
+//               sums [split][token][row] for gemm_reduce_kernel.
+// Precision: every f32 operand v is carried as two f16 values, hi = f16(v)
+// and lo = f16(v - hi), and each k16 slice is three MMAs, hi*hi + lo*hi +
+// hi*lo (the lo*lo term, ~2^-22 relative, is dropped): the products are
+// those of f32 operands to ~2^-21, so the matmul holds the decode path's
+// fp64 tolerance where single f16 operands (2^-11 per weight and per
+// activation) do not.  Activations are scaled per token by a power of two
+// so that the largest |x| of the token lies in [2^13, 2^14): no overflow,
+// no subnormal hi parts (the scale is undone exactly in the reduce).  Weight
+// values are the f32 of dequantize_slice before the split.  All waits are
+// bounded; on a timeout the kernel records an error, drains the work it
+// issued and frees its TMEM.
+#pragma once
+
+#include "gemv.cuh"
+
+namespace b2q {
+
+constexpr int kTcM = 128;          // weight rows per tile (UMMA M)
+constexpr int kTcK = 64;           // k per pipeline stage
+constexpr int kTcStagesMax = 4;
+constexpr int kTcNMax = 128;       // tokens per tile (UMMA N)
+constexpr int kTcDequantWarps = 8;
+constexpr int kTcThreads = (kTcDequantWarps + 2) * 32;
+constexpr int kTcABytes = kTcM * kTcK * 2;  // one f16 image of the weight tile: 16 KB
+constexpr int kTcMinTokens = 16;   // below this the GEMV path is used
+constexpr int kTcSmemBudget = 200 * 1024;
+
+// Bytes of the activation stage (hi and lo images of N tokens x 64 k).
+__host__ __device__ inline int tc_b_bytes(int N) { return 2 * N * kTcK * 2; }
+__host__ __device__ inline int tc_stage_bytes(int N) { return 2 * kTcABytes + tc_b_bytes(N); }
+__host__ __device__ inline int tc_stages(int N) {
+  const int s = kTcSmemBudget / tc_stage_bytes(N);
+  return s < kTcStagesMax ? s : kTcStagesMax;
+}
+__host__ __device__ inline int tc_tmem_cols(int N) {
+  int c = 32;
+  while (c < N) c <<= 1;
+  return c;
+}
+
+// Offset (in f16 elements) of element (row, kk) of a stage image with `rows`
+// rows (a multiple of 8) and 64 k: [k16 slice][8-row group][8-k chunk][row][8].
+__host__ __device__ inline int tc_img_off(int row, int kk, int rows) {
+  return (((kk >> 4) * (rows >> 3) + (row >> 3)) * 2 + ((kk >> 3) & 1)) * 64 + (row & 7) * 8 + (kk & 7);
+}
+
+// UMMA shared-memory descriptor, K-major, no swizzle: core matrices of 8
+// rows x 16 bytes stored contiguously; `lbo` = bytes between the two 8-k
+// halves of a k16 slice, `sbo` = bytes between 8-row groups; version 1.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// Instruction descriptor of tcgen05.mma.kind::f16: D f32, A and B f16,
+// both K-major, M = 128, N tokens.
+__host__ __device__ inline uint32_t umma_idesc_f16(int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
+}
+
+struct TcArgs {
+  WeightDev w;
+  const __half* xh;    // activation images [token tile][k-stage][N * 64]
+  int KS;              // k-stages of the whole row (kpad / 64)
+  int N;               // tokens per tile (multiple of 16, <= 256)
+  int m;               // valid tokens
+  int n;               // valid rows
+  int splits;          // split-K factor (gridDim.z)
+  float* part;         // [split][mpad][n] partial sums (scaled activations)
+  int mpad;            // token tiles * N
+  int stages;          // pipeline depth (<= kTcStagesMax)
+};
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ uint4 ldg_nc128(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ldg_nc32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// hi = f16(v), lo = f16(v - hi) of two values, as packed f16 pairs.
+__device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 f = __half22float2(h);
+  const __half2 l = __floats2half2_rn(a - f.x, b - f.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// Write 8 values (k = kk..kk+7 of image row `row`, `rows` rows) as hi and lo
+// f16 into the two images of a stage (lo image `lo_off` bytes after hi).
+__device__ __forceinline__ void st_img8(uint8_t* img, int lo_off, int row, int kk, int rows, const float (&v)[8]) {
+  uint4 h, l;
+  split_h2(v[0], v[1], h.x, l.x);
+  split_h2(v[2], v[3], h.y, l.y);
+  split_h2(v[4], v[5], h.z, l.z);
+  split_h2(v[6], v[7], h.w, l.w);
+  uint8_t* p = img + 2 * tc_img_off(row, kk, rows);
+  *reinterpret_cast<uint4*>(p) = h;
+  *reinterpret_cast<uint4*>(p + lo_off) = l;
+}
+
+__device__ __forceinline__ void zero_img8(uint8_t* img, int lo_off, int row, int kk) {
+  uint8_t* p = img + 2 * tc_img_off(row, kk, kTcM);
+  *reinterpret_cast<uint4*>(p) = make_uint4(0, 0, 0, 0);
+  *reinterpret_cast<uint4*>(p + lo_off) = make_uint4(0, 0, 0, 0);
+}
+
+// Dequantise this thread's 32 weights of stage `ks` (tile row r, half hf)
+// into the A image.  Values are those of dequantize_slice (inference.rs:
+// 1367-1458), f32 operations in the reference's order, then rounded to f16.
+__device__ __forceinline__ void tc_dequant(const WeightDev& w, int64_t R, int r, int hf, int ks, uint8_t* img) {
+  const TileLayout& L = w.L;
+  const int dt = L.dtype;
+  // unit of this thread and its k offsets within the stage
+  int u;
+  if (dt == kQ8_0) u = 2 * ks + hf;
+  else if (dt == kQ6_K) u = 4 * (ks >> 2) + 2 * ((ks & 3) >> 1) + hf;
+  else u = ks;
+  const bool live = R < (int64_t)L.G * 8 && u < L.U;
+  // k offsets (within the stage) of the four 8-element outputs
+  int kk[4];
+  if (dt == kQ8_0) { kk[0] = 32 * hf; kk[1] = 32 * hf + 8; kk[2] = 32 * hf + 16; kk[3] = 32 * hf + 24; }
+  else if (dt == kQ6_K) { kk[0] = 16 * hf; kk[1] = 16 * hf + 8; kk[2] = 32 + 16 * hf; kk[3] = 40 + 16 * hf; }
+  else { kk[0] = 16 * hf; kk[1] = 16 * hf + 8; kk[2] = 32 + 16 * hf; kk[3] = 40 + 16 * hf; }
+  if (!live) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) zero_img8(img, kTcABytes, r, kk[j]);
+    return;
+  }
+  const int c = u / L.KC, ul = u - c * L.KC;
+  const uint8_t* rc = w.base + (((R >> 3) * L.C + c) * 8 + (R & 7)) * (int64_t)L.rc;
+  float v[4][8];
+  if (dt == kQ4_K) {
+    const uint4 q = ldg_nc128(rc + 16 * (hf * L.KC + ul));
+    const uint4 hb = ldg_nc128(rc + L.o_aux + 16 * (ul >> 2));
+    const uint32_t sel = ul & 3;
+    const uint32_t h = sel == 0 ? hb.x : sel == 1 ? hb.y : sel == 2 ? hb.z : hb.w;
+    const uint32_t dd = __byte_perm(__byte_perm(hb.x, hb.y, 0x0073), __byte_perm(hb.z, hb.w, 0x0073), 0x5410);
+    const float d = f16_bits_exact(dd & 0xffffu), dmin = f16_bits_exact(dd >> 16);
+    const float d1 = __fmul_rn(d, (float)(h & 63u)), m1 = __fmul_rn(dmin, (float)((h >> 12) & 63u));
+    const float d2 = __fmul_rn(d, (float)((h >> 6) & 63u)), m2 = __fmul_rn(dmin, (float)((h >> 18) & 63u));
+    const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t b = (wd[i >> 2] >> (8 * (i & 3))) & 0xffu;
+      v[i >> 3][i & 7] = __fsub_rn(__fmul_rn(d1, (float)(b & 15u)), m1);
+      v[2 + (i >> 3)][i & 7] = __fsub_rn(__fmul_rn(d2, (float)(b >> 4)), m2);
+    }
+  } else if (dt == kQ6_K) {
+    const uint4 qa = ldg_nc128(rc + 16 * ul);
+    const uint4 qb = ldg_nc128(rc + 16 * (L.KC + ul));
+    const uint4 qh = ldg_nc128(rc + 16 * (2 * L.KC + ul));
+    const uint32_t sw = ldg_nc32(rc + L.o_aux + 4 * ul);
+    const uint32_t dw = ldg_nc32(rc + L.o_aux2 + 4 * (ul >> 3));
+    const float d = f16_bits_exact(((ul >> 2) & 1) ? dw >> 16 : dw & 0xffffu);
+    const int hi = (ks & 1);  // groups 2,3 (high nibbles) or 0,1 (low nibbles)
+    const float s0 = __fmul_rn(d, (float)(int8_t)((sw >> (8 * (2 * hi))) & 0xffu));
+    const float s1 = __fmul_rn(d, (float)(int8_t)((sw >> (8 * (2 * hi + 1))) & 0xffu));
+    const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wb[4] = {qb.x, qb.y, qb.z, qb.w};
+    const uint32_t wh[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int sh = 8 * (i & 3);
+      const uint32_t a = (wa[i >> 2] >> sh) & 0xffu, b = (wb[i >> 2] >> sh) & 0xffu;
+      const uint32_t hh = (wh[i >> 2] >> sh) & 0xffu;
+      int q0, q1;
+      if (hi) {
+        q0 = (int)((a >> 4) | (((hh >> 4) & 3u) << 4)) - 32;
+        q1 = (int)((b >> 4) | (((hh >> 6) & 3u) << 4)) - 32;
+      } else {
+        q0 = (int)((a & 15u) | ((hh & 3u) << 4)) - 32;
+        q1 = (int)((b & 15u) | (((hh >> 2) & 3u) << 4)) - 32;
+      }
+      v[i >> 3][i & 7] = __fmul_rn(s0, (float)q0);
+      v[2 + (i >> 3)][i & 7] = __fmul_rn(s1, (float)q1);
+    }
+  } else {  // Q8_0
+    const uint4 qa = ldg_nc128(rc + 16 * ul);
+    const uint4 qb = ldg_nc128(rc + 16 * (L.KC + ul));
+    const uint32_t dw = ldg_nc32(rc + L.o_aux + 4 * (ul >> 1));
+    const float d = f16_bits_exact((ul & 1) ? dw >> 16 : dw & 0xffffu);
+    const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wb[4] = {qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int sh = 8 * (i & 3);
+      v[i >> 3][i & 7] = __fmul_rn(d, (float)(int8_t)((wa[i >> 2] >> sh) & 0xffu));
+      v[2 + (i >> 3)][i & 7] = __fmul_rn(d, (float)(int8_t)((wb[i >> 2] >> sh) & 0xffu));
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) st_img8(img, kTcABytes, r, kk[j], kTcM, v[j]);
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ TcArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t a_full[kTcStagesMax], b_full[kTcStagesMax], empty[kTcStagesMax], done_bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int s_ok_;
+  volatile int* s_ok = &s_ok_;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int N = a.N;
+  const int S = a.stages;
+  const int bb = tc_b_bytes(N);
+  uint8_t* As = smem;                                 // per stage: hi, lo weight images
+  uint8_t* Bs = smem + (size_t)S * 2 * kTcABytes;     // per stage: hi, lo activation images
+  const int row0 = blockIdx.x * kTcM;
+  const int tile = blockIdx.y;
+  const int z = blockIdx.z;
+  const int ks0 = (int)((int64_t)a.KS * z / a.splits), ks1 = (int)((int64_t)a.KS * (z + 1) / a.splits);
+  const int nst = ks1 - ks0;
+  const int ncols = tc_tmem_cols(N);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&a_full[s], kTcDequantWarps);
+      mbar_init(&b_full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done_bar, 1);
+    *s_ok = 1;
+    fence_mbar_init();
+  }
+  if (warp == kTcDequantWarps + 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp < kTcDequantWarps) {
+    // ---- weight producers ----
+    const int d = threadIdx.x;
+    const int r = d & (kTcM - 1), hf = d >> 7;
+    const int64_t R = (int64_t)row0 + r;
+    for (int i = 0; i < nst; ++i) {
+      const int s = i % S;
+      if (i >= S && !mbar_wait_bounded(&empty[s], ((i / S) - 1) & 1)) {
+        *s_ok = 0;
+        break;
+      }
+      tc_dequant(a.w, R, r, hf, ks0 + i, As + (size_t)s * 2 * kTcABytes);
+      fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[s]);
+    }
+  } else if (warp == kTcDequantWarps) {
+    // ---- activation producer ----
+    if (lane == 0) {
+      const uint8_t* xt = reinterpret_cast<const uint8_t*>(a.xh) + (size_t)tile * a.KS * bb;
+      int issued = 0;
+      for (int i = 0; i < nst; ++i) {
+        const int s = i % S;
+        if (i >= S && !mbar_wait_bounded(&empty[s], ((i / S) - 1) & 1)) {
+          *s_ok = 0;
+          break;
+        }
+        mbar_arrive_expect_tx(&b_full[s], (uint32_t)bb);
+        bulk_g2s(Bs + (size_t)s * bb, xt + (size_t)(ks0 + i) * bb, (uint32_t)bb, &b_full[s]);
+        ++issued;
+      }
+      // copies in flight must land before the CTA may exit
+      for (int i = max(0, issued - S); i < issued; ++i)
+        if (!mbar_wait_bounded(&b_full[i % S], (i / S) & 1)) *s_ok = 0;
+    }
+  } else {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(N);
+      int issued = 0;
+      for (int i = 0; i < nst; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
+        if (!mbar_wait_bounded(&a_full[s], ph) || !mbar_wait_bounded(&b_full[s], ph)) {
+          *s_ok = 0;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ahi = smem_u32(As + (size_t)s * 2 * kTcABytes), alo = ahi + kTcABytes;
+        const uint32_t bhi = smem_u32(Bs + (size_t)s * bb), blo = bhi + bb / 2;
+#pragma unroll
+        for (int j = 0; j < kTcK / 16; ++j) {
+          const uint32_t ao = j * (kTcM / 8) * 256, bo = j * (N / 8) * 256;
+          // hi*hi, lo*hi, hi*lo
+          const uint64_t ad[3] = {umma_desc(ahi + ao, 128, 256), umma_desc(alo + ao, 128, 256),
+                                  umma_desc(ahi + ao, 128, 256)};
+          const uint64_t bd[3] = {umma_desc(bhi + bo, 128, 256), umma_desc(bhi + bo, 128, 256),
+                                  umma_desc(blo + bo, 128, 256)};
+#pragma unroll
+          for (int q = 0; q < 3; ++q) {
+            const uint32_t acc = (i > 0 || j > 0 || q > 0) ? 1u : 0u;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
+                "l"(ad[q]), "l"(bd[q]), "r"(idesc), "r"(acc)
+                : "memory");
+          }
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&empty[s]))
+                     : "memory");
+        ++issued;
+      }
+      // everything issued has completed once done_bar flips
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       smem_u32(&done_bar))
+                   : "memory");
+      if (issued < nst) *s_ok = 0;
+    }
+  }
+
+  // ---- epilogue: warps 0-3 read rows 32w..32w+31 of the accumulator ----
+  if (warp < 4) {
+    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&done_bar, 0)) && *s_ok;
+    tc_fence_after();
+    if (ok && nst > 0) {
+      const int r = warp * 32 + lane;
+      const int64_t R = (int64_t)row0 + r;
+      const int t0 = tile * N;
+      float* outp = a.part + ((size_t)z * a.mpad) * a.n;
+      for (int c0 = 0; c0 < N; c0 += 16) {
+        uint32_t v[16];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+            "%13, %14, %15}, [%16];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+              "=r"(v[15])
+            : "r"(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (R < a.n) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int t = t0 + c0 + j;
+            if (t < a.m) outp[(size_t)t * a.n + R] = __uint_as_float(v[j]);
+          }
+        }
+      }
+    } else if (!ok) {
+      if (lane == 0) atomicExch(&g_b2q_device_error, 5);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kTcDequantWarps + 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+  }
+}
+
+// X f32 [m][ldx] (k valid columns) -> f16 stage images [token tile][k-stage]
+// [hi, lo][N * 64] (zero beyond m and k) and the per-token inverse scales
+// inv[t] = 2^(e-14), amax(x_t) = f * 2^e, f in [0.5, 1).  One block of 8
+// warps per 8 tokens.
+__global__ void tc_act_kernel(const float* __restrict__ x, int ldx, int m, int k, int KS, int N,
+                              __half* __restrict__ img, float* __restrict__ inv) {
+  pdl_wait();
+  __shared__ float s_scale[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tb = blockIdx.x * 8;  // first token of this block
+  {
+    const int t = tb + warp;
+    float mx = 0.0f;
+    if (t < m)
+      for (int i = lane; i < k; i += 32) mx = fmaxf(mx, fabsf(x[(size_t)t * ldx + i]));
+    mx = warp_max(mx);
+    float sc = 1.0f, iv = 1.0f;
+    if (mx > 0.0f && mx <= 3.0e38f) {
+      int e;
+      frexpf(mx, &e);
+      sc = ldexpf(1.0f, 14 - e);
+      iv = ldexpf(1.0f, e - 14);
+    }
+    if (lane == 0) {
+      s_scale[warp] = sc;
+      if (t < m) inv[t] = iv;
+    }
+  }
+  __syncthreads();
+  // chunks of 8 k per token: (stage ks, k8 index 0..7); thread -> (token tb + (id & 7), chunk id >> 3)
+  const int nch = KS * 8;
+  const int tile = tb / N, tt0 = tb - tile * N;
+  for (int id = threadIdx.x; id < nch * 8; id += blockDim.x) {
+    const int tr = id & 7, ch = id >> 3;
+    const int t = tb + tr;
+    const int ks = ch >> 3, kk = (ch & 7) * 8;
+    const int k0 = ks * kTcK + kk;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int kx = k0 + e;
+      v[e] = (t < m && kx < k) ? x[(size_t)t * ldx + kx] * s_scale[tr] : 0.0f;
+    }
+    uint8_t* stage = reinterpret_cast<uint8_t*>(img) + ((size_t)tile * KS + ks) * (size_t)tc_b_bytes(N);
+    st_img8(stage, N * kTcK * 2, tt0 + tr, kk, N, v);
+  }
+  pdl_launch_dependents();
+}
+
+// y[t][col0 + r] = epi(inv[t] * sum_s part[s][t][r]) for t < m, r < n.
+// EPI kEpiStore / kEpiAdd (y +=) / kEpiSwiglu (part2 = up partials:
+// silu(g) * u).
+template <int EPI>
+__global__ void tc_reduce_kernel(const float* __restrict__ part, const float* __restrict__ part2, int splits,
+                                 int mpad, int m, int n, const float* __restrict__ inv, float* __restrict__ y,
+                                 int ldy, int col0) {
+  pdl_wait();
+  const int64_t total = (int64_t)m * n;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / n), r = (int)(i - (int64_t)t * n);
+    float g = 0.0f, u = 0.0f;
+    for (int s = 0; s < splits; ++s) {
+      g += part[((size_t)s * mpad + t) * n + r];
+      if (EPI == kEpiSwiglu) u += part2[((size_t)s * mpad + t) * n + r];
+    }
+    g *= inv[t];
+    float* yp = y + (size_t)t * ldy + col0 + r;
+    if (EPI == kEpiSwiglu) *yp = silu_f(g) * (u * inv[t]);
+    else if (EPI == kEpiAdd) *yp += g;
+    else *yp = g;
+  }
+  pdl_launch_dependents();
+}
+
+}  // namespace b2q

@@ -11,6 +11,7 @@
 #include "gemv.cuh"
 #include "layer.cuh"
 #include "decode.cuh"
+#include "gemm_tc.cuh"
 
 namespace b2q {
 
@@ -18,6 +19,15 @@ struct XQBuf {
   void* mem = nullptr;
   XQ x{};
   int m = 0, k = 0, kpad = 0;
+};
+
+// Scratch of the tensor-core multi-token matmul (grown on demand).
+struct TcScratch {
+  __half* img = nullptr;   // f16 activation images
+  float* inv = nullptr;    // per-token inverse scales
+  float* part = nullptr;   // split-K partials
+  float* part2 = nullptr;  // partials of the up projection (SwiGLU)
+  size_t img_cap = 0, inv_cap = 0, part_cap = 0, part2_cap = 0;  // bytes
 };
 
 b2q_status set_error(b2q_status st, const char* fmt, ...);
@@ -44,6 +54,7 @@ struct b2q_engine {
   float* ws_h = nullptr;
   size_t ws_x_cap = 0, ws_y_cap = 0, ws_h_cap = 0;
   b2q::XQBuf ws_xq, ws_hq;
+  b2q::TcScratch tc;
 };
 
 struct b2q_weight {
@@ -63,4 +74,11 @@ cudaError_t run_gemv(b2q_engine* e, const GemvSeg* segs, int nseg, const XQBuf& 
                      cudaStream_t st, bool pdl);
 cudaError_t launch_quantize(b2q_engine* e, const float* x, int m, int k, XQBuf& xq, cudaStream_t st,
                             bool pdl);
+// Multi-token matmul on the tensor cores (gemm_tc.cuh): for weight i of
+// `ws`, y[t][col0[i] + r] = (X W_i^T)[t][r] (epi kEpiStore / kEpiAdd), or
+// with ws = {gate, up} and epi kEpiSwiglu, y[t][col0[0] + r] =
+// silu(g) * u.  x is [m][ldx] f32 on the device, m >= kTcMinTokens.
+cudaError_t tc_matmul(b2q_engine* e, const float* x, int ldx, int m, int k, const b2q_weight* const* ws,
+                      int nw, int epi, float* y, int ldy, const int* col0, cudaStream_t st, bool pdl);
+void tc_free(b2q_engine* e);
 }  // namespace b2q

@@ -44,6 +44,7 @@ struct b2q_model {
   b2q::TpComm tp;
   // activations
   float* x = nullptr;       // [mmax][E] residual stream
+  float* xn = nullptr;      // [mmax][E] normalised rows (tensor-core prompt pass)
   float* qkv = nullptr;     // [mmax][(H_loc + 2 KV_loc) hd]
   float* attn = nullptr;    // [mmax][H hd] (gathered under TP)
   float* attn_loc = nullptr;
@@ -183,6 +184,10 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
   }
   const float scale = 1.0f / sqrtf((float)hd);
   const int width_loc = (Hl + 2 * KVl) * hd;
+  // prompt passes of kTcMinTokens or more tokens run their projections on
+  // the tensor cores (gemm_tc.cuh); shorter passes and single-token steps
+  // stream the weights through the GEMV
+  const bool tc = m >= kTcMinTokens && M->xn != nullptr;
   for (int l = 0; l < c.n_layers; ++l) {
     LayerW& Lw = M->L[l];
     // attention norm + quantise
@@ -190,11 +195,16 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
       cudaLaunchConfig_t cfg = lcfg(dim3(m), dim3(1024), 0, st, attr, pdl);
       launch_counted(e, 1);
       err = cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, (const float*)M->x, E, 0,
-                               (const float*)Lw.attn_norm, E, c.rms_eps, M->xq_e.x, (float*)nullptr);
+                               (const float*)Lw.attn_norm, E, c.rms_eps, M->xq_e.x, tc ? M->xn : (float*)nullptr);
       if (err != cudaSuccess) return err;
     }
     // q, k, v projections (one launch, outputs interleaved per token)
-    {
+    if (tc) {
+      const b2q_weight* ws[3] = {Lw.q, Lw.k, Lw.v};
+      const int col0[3] = {0, (int)Lw.q->n, (int)(Lw.q->n + Lw.k->n)};
+      err = tc_matmul(e, M->xn, E, m, E, ws, 3, kEpiStore, M->qkv, width_loc, col0, st, pdl);
+      if (err != cudaSuccess) return err;
+    } else {
       GemvSeg segs[3];
       memset(segs, 0, sizeof segs);
       b2q_weight* ws[3] = {Lw.q, Lw.k, Lw.v};
@@ -258,7 +268,15 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
       }
     }
     // o-projection + residual
-    {
+    if (tc) {
+      const int col0 = 0;
+      const b2q_weight* wo = Lw.o;
+      err = P > 1 ? tc_matmul(e, M->attn, H * hd, m, H * hd, &wo, 1, kEpiStore, M->y_loc, (int)Lw.o->n, &col0, st, pdl)
+                  : tc_matmul(e, M->attn, H * hd, m, H * hd, &wo, 1, kEpiAdd, M->x, E, &col0, st, pdl);
+      if (err == cudaSuccess && P > 1)
+        err = tp_allgather_add_rows(M->tp, M->y_loc, M->x, m, (int)Lw.o->n, E, st);
+      if (err != cudaSuccess) return err;
+    } else {
       GemvSeg sg;
       memset(&sg, 0, sizeof sg);
       sg.w = Lw.o->view;
@@ -281,13 +299,19 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
       cudaLaunchConfig_t cfg = lcfg(dim3(m), dim3(1024), 0, st, attr, pdl);
       launch_counted(e, 1);
       err = cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, (const float*)M->x, E, 0,
-                               (const float*)Lw.ffn_norm, E, c.rms_eps, M->xq_e.x, (float*)nullptr);
+                               (const float*)Lw.ffn_norm, E, c.rms_eps, M->xq_e.x, tc ? M->xn : (float*)nullptr);
       if (err != cudaSuccess) return err;
     }
     // gate/up with fused SwiGLU, per token
     {
       float* hout = P > 1 ? M->h_loc : M->hbuf;
-      for (int t = 0; t < m; ++t) {
+      if (tc) {
+        const b2q_weight* ws[2] = {Lw.gate, Lw.up};
+        const int col0 = 0;
+        err = tc_matmul(e, M->xn, E, m, E, ws, 2, kEpiSwiglu, hout, Fl, &col0, st, pdl);
+        if (err != cudaSuccess) return err;
+      }
+      for (int t = 0; t < (tc ? 0 : m); ++t) {
         GemvArgs a;
         memset(&a, 0, sizeof a);
         a.nseg = 1;
@@ -308,11 +332,20 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
         err = tp_allgather_rows(M->tp, M->h_loc, M->hbuf, m, Fl, st);
         if (err != cudaSuccess) return err;
       }
-      err = launch_quantize(e, M->hbuf, m, c.n_ff, M->xq_f, st, pdl);
+      if (!tc) err = launch_quantize(e, M->hbuf, m, c.n_ff, M->xq_f, st, pdl);
       if (err != cudaSuccess) return err;
     }
     // down projection + residual
-    {
+    if (tc) {
+      const int col0 = 0;
+      const b2q_weight* wd = Lw.down;
+      err = P > 1 ? tc_matmul(e, M->hbuf, c.n_ff, m, c.n_ff, &wd, 1, kEpiStore, M->y_loc, (int)Lw.down->n, &col0,
+                              st, pdl)
+                  : tc_matmul(e, M->hbuf, c.n_ff, m, c.n_ff, &wd, 1, kEpiAdd, M->x, E, &col0, st, pdl);
+      if (err == cudaSuccess && P > 1)
+        err = tp_allgather_add_rows(M->tp, M->y_loc, M->x, m, (int)Lw.down->n, E, st);
+      if (err != cudaSuccess) return err;
+    } else {
       GemvSeg sg;
       memset(&sg, 0, sizeof sg);
       sg.w = Lw.down->view;
