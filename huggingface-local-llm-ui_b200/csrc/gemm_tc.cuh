@@ -10,14 +10,14 @@
 // Per CTA: 128 weight rows (the UMMA M) x N tokens (the UMMA N, a multiple
 // of 16, <= 256) x a range of k-stages of 64 elements (split-K over
 // gridDim.z).  Warp roles:
-//   warps 0-7   dequantise the weight tile of each stage: thread (row r,
-//               half h) reads its bytes straight from the GEMV tile layout
+//   warps 0-15  dequantise the weight tile of each stage: thread (row r,
+//               quarter q) reads its bytes straight from the GEMV tile layout
 //               (quant.cuh), computes the f32 value bit-exactly as
 //               dequantize_slice does and rounds it to f16, and writes the
 //               no-swizzle K-major core-matrix layout UMMA reads;
-//   warp 8      streams the activation stage (pre-arranged in global memory
+//   warp 16     streams the activation stage (pre-arranged in global memory
 //               in the same layout, f16) with one 1-D bulk copy per stage;
-//   warp 9      allocates TMEM and issues the MMAs (one thread), committing
+//   warp 17     allocates TMEM and issues the MMAs (one thread), committing
 //               each stage back to its producers;
 //   warps 0-3   after the last stage, read the accumulator out of TMEM
 //               (tcgen05.ld, one weight row per thread) and store f32 partial
@@ -43,11 +43,12 @@ constexpr int kTcM = 128;          // weight rows per tile (UMMA M)
 constexpr int kTcK = 64;           // k per pipeline stage
 constexpr int kTcStagesMax = 4;
 constexpr int kTcNMax = 128;       // tokens per tile (UMMA N)
-constexpr int kTcDequantWarps = 8;
+constexpr int kTcDequantWarps = 16;  // 512 threads: (tile row, quarter) -> 16 weights per stage
 constexpr int kTcThreads = (kTcDequantWarps + 2) * 32;
 constexpr int kTcABytes = kTcM * kTcK * 2;  // one f16 image of the weight tile: 16 KB
 constexpr int kTcMinTokens = 16;   // below this the GEMV path is used
 constexpr int kTcSmemBudget = 200 * 1024;
+constexpr int kTcPrefetch = 4;     // stages of raw weight bytes loaded ahead (registers)
 
 // Bytes of the activation stage (hi and lo images of N tokens x 64 k).
 __host__ __device__ inline int tc_b_bytes(int N) { return 2 * N * kTcK * 2; }
@@ -139,90 +140,136 @@ __device__ __forceinline__ void zero_img8(uint8_t* img, int lo_off, int row, int
   *reinterpret_cast<uint4*>(p + lo_off) = make_uint4(0, 0, 0, 0);
 }
 
-// Dequantise this thread's 32 weights of stage `ks` (tile row r, half hf)
-// into the A image.  Values are those of dequantize_slice (inference.rs:
-// 1367-1458), f32 operations in the reference's order, then rounded to f16.
-__device__ __forceinline__ void tc_dequant(const WeightDev& w, int64_t R, int r, int hf, int ks, uint8_t* img) {
+// Raw bytes of one thread's 16 weights of a stage, loaded ahead of use.
+// Thread (tile row r, quarter qq): half hf = qq >> 1 of the unit pair or
+// plane pair, and bytes 8*(qq & 1) .. +7 of each 16-byte plane it reads.
+struct TcRaw {
+  uint2 a, b, c;   // Q4_K: qs bytes, header words 0-1, 2-3; Q6_K: ql lo, ql hi, qh;
+                   // Q8_0: codes 0-15 part, 16-31 part
+  uint32_t s, d;   // Q6_K: sub-scale word, d word; Q8_0: d word
+  bool live;
+};
+
+// Unit of tile row r's half `hf` in stage ks (Q4_K / Q6_K: 64-weight
+// units, Q8_0: 32-weight blocks).
+__device__ __forceinline__ int tc_unit(int dt, int ks, int hf) {
+  if (dt == kQ8_0) return 2 * ks + hf;
+  if (dt == kQ6_K) return 4 * (ks >> 2) + 2 * ((ks & 3) >> 1) + hf;
+  return ks;
+}
+
+__device__ __forceinline__ uint2 ldg_nc64(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ TcRaw tc_load(const WeightDev& w, int64_t R, int qq, int ks) {
   const TileLayout& L = w.L;
   const int dt = L.dtype;
-  // unit of this thread and its k offsets within the stage
-  int u;
-  if (dt == kQ8_0) u = 2 * ks + hf;
-  else if (dt == kQ6_K) u = 4 * (ks >> 2) + 2 * ((ks & 3) >> 1) + hf;
-  else u = ks;
-  const bool live = R < (int64_t)L.G * 8 && u < L.U;
-  // k offsets (within the stage) of the four 8-element outputs
-  int kk[4];
-  if (dt == kQ8_0) { kk[0] = 32 * hf; kk[1] = 32 * hf + 8; kk[2] = 32 * hf + 16; kk[3] = 32 * hf + 24; }
-  else if (dt == kQ6_K) { kk[0] = 16 * hf; kk[1] = 16 * hf + 8; kk[2] = 32 + 16 * hf; kk[3] = 40 + 16 * hf; }
-  else { kk[0] = 16 * hf; kk[1] = 16 * hf + 8; kk[2] = 32 + 16 * hf; kk[3] = 40 + 16 * hf; }
-  if (!live) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) zero_img8(img, kTcABytes, r, kk[j]);
-    return;
-  }
+  const int hf = qq >> 1, e8 = 8 * (qq & 1);
+  const int u = tc_unit(dt, ks, hf);
+  TcRaw x;
+  x.live = R < (int64_t)L.G * 8 && u < L.U;
+  if (!x.live) return x;
   const int c = u / L.KC, ul = u - c * L.KC;
   const uint8_t* rc = w.base + (((R >> 3) * L.C + c) * 8 + (R & 7)) * (int64_t)L.rc;
-  float v[4][8];
   if (dt == kQ4_K) {
-    const uint4 q = ldg_nc128(rc + 16 * (hf * L.KC + ul));
+    x.a = ldg_nc64(rc + 16 * (hf * L.KC + ul) + e8);
     const uint4 hb = ldg_nc128(rc + L.o_aux + 16 * (ul >> 2));
-    const uint32_t sel = ul & 3;
+    x.b = make_uint2(hb.x, hb.y);
+    x.c = make_uint2(hb.z, hb.w);
+  } else if (dt == kQ6_K) {
+    x.a = ldg_nc64(rc + 16 * ul + e8);
+    x.b = ldg_nc64(rc + 16 * (L.KC + ul) + e8);
+    x.c = ldg_nc64(rc + 16 * (2 * L.KC + ul) + e8);
+    x.s = ldg_nc32(rc + L.o_aux + 4 * ul);
+    x.d = ldg_nc32(rc + L.o_aux2 + 4 * (ul >> 3));
+  } else {
+    x.a = ldg_nc64(rc + 16 * ul + e8);
+    x.b = ldg_nc64(rc + 16 * (L.KC + ul) + e8);
+    x.d = ldg_nc32(rc + L.o_aux + 4 * (ul >> 1));
+  }
+  return x;
+}
+
+// Exact float of a small non-negative integer held in the low bits of
+// `bits` (< 2^23): 2^23 + q is built by OR-ing q into the exponent pattern
+// of 2^23, then 2^23 is subtracted (full-rate ALU + FADD, no I2F).
+__device__ __forceinline__ float small_uint_f(uint32_t bits) {
+  return __uint_as_float(0x4B000000u | bits) - 8388608.0f;
+}
+
+// Dequantise one thread's 16 weights of stage `ks` (tile row r, quarter qq)
+// from its raw bytes into the A images (hi at img, lo at img + kTcABytes):
+// two runs of 8 consecutive k.  The block formats of dequantize_slice
+// (inference.rs:1367-1458); each value is d*sc*q - dmin*m with the products
+// d*sc, dmin*m in f32 as the reference forms them and the last step fused
+// (one rounding), which the hi/lo split then carries to ~2^-22.
+__device__ __forceinline__ void tc_convert(const TcRaw& x, int dt, int r, int qq, int ks, uint8_t* img) {
+  const int hf = qq >> 1, e8 = 8 * (qq & 1);
+  const int u = tc_unit(dt, ks, hf);
+  // k offsets (within the stage) of the two 8-element outputs
+  int k0, k1;
+  if (dt == kQ8_0) { k0 = 32 * hf + e8; k1 = 32 * hf + 16 + e8; }
+  else { k0 = 16 * hf + e8; k1 = 32 + 16 * hf + e8; }
+  if (!x.live) {
+    zero_img8(img, kTcABytes, r, k0);
+    zero_img8(img, kTcABytes, r, k1);
+    return;
+  }
+  float v0[8], v1[8];
+  if (dt == kQ4_K) {
+    const uint4 hb = make_uint4(x.b.x, x.b.y, x.c.x, x.c.y);
+    const uint32_t sel = u & 3;  // KC is a multiple of 8: u & 3 == ul & 3
     const uint32_t h = sel == 0 ? hb.x : sel == 1 ? hb.y : sel == 2 ? hb.z : hb.w;
     const uint32_t dd = __byte_perm(__byte_perm(hb.x, hb.y, 0x0073), __byte_perm(hb.z, hb.w, 0x0073), 0x5410);
     const float d = f16_bits_exact(dd & 0xffffu), dmin = f16_bits_exact(dd >> 16);
     const float d1 = __fmul_rn(d, (float)(h & 63u)), m1 = __fmul_rn(dmin, (float)((h >> 12) & 63u));
     const float d2 = __fmul_rn(d, (float)((h >> 6) & 63u)), m2 = __fmul_rn(dmin, (float)((h >> 18) & 63u));
-    const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+    const uint32_t wd[2] = {x.a.x, x.a.y};
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t b = (wd[i >> 2] >> (8 * (i & 3))) & 0xffu;
-      v[i >> 3][i & 7] = __fsub_rn(__fmul_rn(d1, (float)(b & 15u)), m1);
-      v[2 + (i >> 3)][i & 7] = __fsub_rn(__fmul_rn(d2, (float)(b >> 4)), m2);
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t b = wd[i >> 2] >> (8 * (i & 3));
+      v0[i] = fmaf(d1, small_uint_f(b & 15u), -m1);
+      v1[i] = fmaf(d2, small_uint_f((b >> 4) & 15u), -m2);
     }
   } else if (dt == kQ6_K) {
-    const uint4 qa = ldg_nc128(rc + 16 * ul);
-    const uint4 qb = ldg_nc128(rc + 16 * (L.KC + ul));
-    const uint4 qh = ldg_nc128(rc + 16 * (2 * L.KC + ul));
-    const uint32_t sw = ldg_nc32(rc + L.o_aux + 4 * ul);
-    const uint32_t dw = ldg_nc32(rc + L.o_aux2 + 4 * (ul >> 3));
-    const float d = f16_bits_exact(((ul >> 2) & 1) ? dw >> 16 : dw & 0xffffu);
+    // u & 7 == ul & 7 (KC a multiple of 8): the d of block ul >> 2 is half (ul >> 2) & 1 of the word
+    const float d = f16_bits_exact(((u >> 2) & 1) ? x.d >> 16 : x.d & 0xffffu);
     const int hi = (ks & 1);  // groups 2,3 (high nibbles) or 0,1 (low nibbles)
-    const float s0 = __fmul_rn(d, (float)(int8_t)((sw >> (8 * (2 * hi))) & 0xffu));
-    const float s1 = __fmul_rn(d, (float)(int8_t)((sw >> (8 * (2 * hi + 1))) & 0xffu));
-    const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wb[4] = {qb.x, qb.y, qb.z, qb.w};
-    const uint32_t wh[4] = {qh.x, qh.y, qh.z, qh.w};
+    const float s0 = __fmul_rn(d, (float)(int8_t)((x.s >> (8 * (2 * hi))) & 0xffu));
+    const float s1 = __fmul_rn(d, (float)(int8_t)((x.s >> (8 * (2 * hi + 1))) & 0xffu));
+    const uint32_t wa[2] = {x.a.x, x.a.y}, wb[2] = {x.b.x, x.b.y}, wh[2] = {x.c.x, x.c.y};
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       const int sh = 8 * (i & 3);
       const uint32_t a = (wa[i >> 2] >> sh) & 0xffu, b = (wb[i >> 2] >> sh) & 0xffu;
       const uint32_t hh = (wh[i >> 2] >> sh) & 0xffu;
-      int q0, q1;
+      uint32_t q0, q1;  // unsigned codes 0..63; the -32 offset is exact in f32
       if (hi) {
-        q0 = (int)((a >> 4) | (((hh >> 4) & 3u) << 4)) - 32;
-        q1 = (int)((b >> 4) | (((hh >> 6) & 3u) << 4)) - 32;
+        q0 = (a >> 4) | (((hh >> 4) & 3u) << 4);
+        q1 = (b >> 4) | (((hh >> 6) & 3u) << 4);
       } else {
-        q0 = (int)((a & 15u) | ((hh & 3u) << 4)) - 32;
-        q1 = (int)((b & 15u) | (((hh >> 2) & 3u) << 4)) - 32;
+        q0 = (a & 15u) | ((hh & 3u) << 4);
+        q1 = (b & 15u) | (((hh >> 2) & 3u) << 4);
       }
-      v[i >> 3][i & 7] = __fmul_rn(s0, (float)q0);
-      v[2 + (i >> 3)][i & 7] = __fmul_rn(s1, (float)q1);
+      v0[i] = s0 * (small_uint_f(q0) - 32.0f);
+      v1[i] = s1 * (small_uint_f(q1) - 32.0f);
     }
-  } else {  // Q8_0
-    const uint4 qa = ldg_nc128(rc + 16 * ul);
-    const uint4 qb = ldg_nc128(rc + 16 * (L.KC + ul));
-    const uint32_t dw = ldg_nc32(rc + L.o_aux + 4 * (ul >> 1));
-    const float d = f16_bits_exact((ul & 1) ? dw >> 16 : dw & 0xffffu);
-    const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wb[4] = {qb.x, qb.y, qb.z, qb.w};
+  } else {  // Q8_0: u & 1 == ul & 1 (KC even)
+    const float d = f16_bits_exact((u & 1) ? x.d >> 16 : x.d & 0xffffu);
+    const uint32_t wa[2] = {x.a.x, x.a.y}, wb[2] = {x.b.x, x.b.y};
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       const int sh = 8 * (i & 3);
-      v[i >> 3][i & 7] = __fmul_rn(d, (float)(int8_t)((wa[i >> 2] >> sh) & 0xffu));
-      v[2 + (i >> 3)][i & 7] = __fmul_rn(d, (float)(int8_t)((wb[i >> 2] >> sh) & 0xffu));
+      // int8 code c: (c ^ 0x80) = c + 128 as an unsigned byte
+      v0[i] = d * (small_uint_f(((wa[i >> 2] >> sh) & 0xffu) ^ 0x80u) - 128.0f);
+      v1[i] = d * (small_uint_f(((wb[i >> 2] >> sh) & 0xffu) ^ 0x80u) - 128.0f);
     }
   }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) st_img8(img, kTcABytes, r, kk[j], kTcM, v[j]);
+  st_img8(img, kTcABytes, r, k0, kTcM, v0);
+  st_img8(img, kTcABytes, r, k1, kTcM, v1);
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ TcArgs a) {
@@ -268,18 +315,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   if (warp < kTcDequantWarps) {
     // ---- weight producers ----
     const int d = threadIdx.x;
-    const int r = d & (kTcM - 1), hf = d >> 7;
+    const int r = d & (kTcM - 1), qq = d >> 7;
     const int64_t R = (int64_t)row0 + r;
-    for (int i = 0; i < nst; ++i) {
-      const int s = i % S;
-      if (i >= S && !mbar_wait_bounded(&empty[s], ((i / S) - 1) & 1)) {
-        *s_ok = 0;
-        break;
+    const int dt = a.w.L.dtype;
+    // raw bytes of the next kTcPrefetch stages are in flight in registers
+    // while the current one is converted
+    TcRaw raw[kTcPrefetch];
+#pragma unroll
+    for (int j = 0; j < kTcPrefetch; ++j)
+      if (j < nst) raw[j] = tc_load(a.w, R, qq, ks0 + j);
+    for (int i0 = 0; i0 < nst; i0 += kTcPrefetch) {
+#pragma unroll
+      for (int j = 0; j < kTcPrefetch; ++j) {
+        const int i = i0 + j;
+        if (i >= nst || !*s_ok) break;
+        const int s = i % S;
+        if (i >= S && !mbar_wait_bounded(&empty[s], ((i / S) - 1) & 1)) {
+          *s_ok = 0;
+          break;
+        }
+        tc_convert(raw[j], dt, r, qq, ks0 + i, As + (size_t)s * 2 * kTcABytes);
+        if (i + kTcPrefetch < nst) raw[j] = tc_load(a.w, R, qq, ks0 + i + kTcPrefetch);
+        fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[s]);
       }
-      tc_dequant(a.w, R, r, hf, ks0 + i, As + (size_t)s * 2 * kTcABytes);
-      fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[s]);
     }
   } else if (warp == kTcDequantWarps) {
     // ---- activation producer ----

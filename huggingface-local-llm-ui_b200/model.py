@@ -146,7 +146,7 @@ class StandardNativeEngine:
         check(lib().b2q_clear_state(self._h))
         self.current_pos = 0
 
-    def generate_greedy(self, prompt, max_tokens: int, prefill_chunk: int = 64) -> list[int]:
+    def generate_greedy(self, prompt, max_tokens: int, prefill_chunk: int = 128) -> list[int]:
         """Chunked prefill, then greedy decode of `max_tokens` tokens."""
         prompt = list(prompt)
         if not prompt:

@@ -53,8 +53,9 @@ def test_gqa_ratios(engine, orc, pkg, gqa):
 
 
 def test_long_prompt_chunks_and_splits(engine, orc, pkg):
-    """A prompt longer than one forward chunk (64) and than one attention
-    split (128 keys) exercises the chunked prefill and the split merge."""
+    """A prompt longer than two forward chunks (128 tokens each, the last one
+    ragged) and than one attention split (64 keys) exercises the chunked
+    prefill and the split merge."""
     dev, ref = _pair(engine, orc, pkg, dict(TOY, n_layers=1), seed=7, max_seq=512)
     rng = np.random.default_rng(0)
     toks = rng.integers(0, TOY["n_vocab"], 300).tolist()
