@@ -177,10 +177,10 @@ def build_model(pkg, engine, cfg, seed, rank, size, tp_id, max_seq, dist="bench"
 
 
 def step_algorithmic_bytes(cfg, rank: int, world: int, ctx: int) -> int:
-    """Bytes one single-token step must read on `rank`: every weight row it
-    owns (all matvec weights of every layer and the output head; one row of
-    token_embd), the norms, and the f16 K/V rows of its KV heads for `ctx`
-    cached tokens."""
+    """Bytes one single-token step must read on `rank`: the part of every
+    matvec weight it owns (its rows, or for attn_output / ffn_down its
+    columns) and of the output head, one row of token_embd, the norms, and
+    the f16 K/V rows of its KV heads for `ctx` cached tokens."""
     from hf_llm_b200 import ggml, model, synth
     total = 0
     for name, t, dims, _ in synth.llama_specs(cfg, model.q4_k_m_types()):
@@ -192,7 +192,8 @@ def step_algorithmic_bytes(cfg, rank: int, world: int, ctx: int) -> int:
             total += ggml.row_bytes(t, k)
             continue
         b, e = model.tp_shard_rows(cfg, name, n, rank, world)
-        total += (e - b) * ggml.row_bytes(t, k)
+        cb, ce = model.tp_shard_cols(cfg, name, k, rank, world)
+        total += (e - b) * ggml.row_bytes(t, ce - cb)
     total += cfg["n_layers"] * 2 * (cfg["n_kv_heads"] // world) * cfg["head_dim"] * 2 * ctx
     return total
 
@@ -205,7 +206,8 @@ def prefill_matmul_params(cfg, rank: int, world: int) -> int:
     for name, t, dims, _ in synth.llama_specs(cfg, model.q4_k_m_types()):
         if len(dims) == 2 and name.startswith("blk."):
             b, e = model.tp_shard_rows(cfg, name, dims[0], rank, world)
-            total += (e - b) * dims[1]
+            cb, ce = model.tp_shard_cols(cfg, name, dims[1], rank, world)
+            total += (e - b) * (ce - cb)
     return total
 
 

@@ -58,6 +58,7 @@ SIGNATURES = [
     ("b2q_model_set_tensor_rows", _I, [_VP, C.c_char_p, _I, C.POINTER(_I64), _I, _I64, _I64, _VP, _SZ]),
     ("b2q_model_shard_rows", _I, [_VP, C.c_char_p, _I64, C.POINTER(_I64), C.POINTER(_I64)]),
     ("b2q_tp_shard_rows", _I, [C.POINTER(ModelConfig), C.c_char_p, _I64, C.POINTER(_I64), C.POINTER(_I64)]),
+    ("b2q_tp_shard_cols", _I, [C.POINTER(ModelConfig), C.c_char_p, _I64, C.POINTER(_I64), C.POINTER(_I64)]),
     ("b2q_model_finalize", _I, [_VP]),
     ("b2q_forward", _I, [_VP, _U32P, _I, _I, _FP, _U32P]),
     ("b2q_forward_dev", _I, [_VP, _VP, _I, _I, _VP, _VP, _VP]),

@@ -113,16 +113,23 @@ struct DecodeArgs {
   uint32_t* argmax;       // model's argmax word
   uint32_t* argmax2;      // optional caller's copy
   // Tensor parallelism: this is rank `rank` of `tp` (tp = 1 on one GPU).  H,
-  // KV are this rank's heads; the vectors every rank needs whole live in
-  // every rank's memory, and xg[p], attng[p], hg[p], logitsg[p], candg[p]
-  // point at rank p's copy (peer memory over NVLink for p != rank): each
-  // epilogue stores its slice into all of them.
+  // KV are this rank's heads, Fl its SwiGLU rows.  Attention and the SwiGLU
+  // output stay local; attn_output and ffn_down hold this rank's columns
+  // (the K split), so their epilogues store partial sums of every row into
+  // each rank's slot partg[p][(set * tp + rank) * E + row] (set 0: O, 1:
+  // down), and every rank forms the residual x + sum_p partial_p in rank
+  // order while staging the next RMSNorm.  logitsg[p], candg[p] are rank
+  // p's copies of the vocabulary slices and argmax candidates.  Pointers for
+  // p != rank are peer memory over NVLink.
   int tp, rank;
   int Hg;                 // query heads over all ranks
-  int o_off, f_off, v_off, h_off;  // first global row (head) of this rank's slices
-  float* xg[kMaxTp];      // [E] residual stream
-  float* attng[kMaxTp];   // [Hg * 128] attention output
-  float* hg[kMaxTp];      // [F] SwiGLU output
+  int Fl;                 // this rank's SwiGLU rows
+  int v_off;              // first vocabulary row of this rank's head slice
+  float* xg[kMaxTp];      // [E] residual stream (this rank's own copy at xg[rank])
+  float* xalt;            // [E] second residual buffer (tp > 1: the updates alternate)
+  float* attng[kMaxTp];   // [H * 128] attention output of this rank's heads (local)
+  float* hg[kMaxTp];      // [Fl] SwiGLU output of this rank's rows (local)
+  float* partg[kMaxTp];   // [2][tp][E] partial O / down sums from every rank
   float* logitsg[kMaxTp]; // [V]
   int2* candg[kMaxTp];    // [tp * grid] per-CTA argmax candidates (value bits, global row)
   unsigned long long* xflagg[kMaxTp];  // [kMaxTp] per-source-rank barrier epochs
@@ -307,8 +314,12 @@ __host__ __device__ __forceinline__ size_t xq_smem_bytes(int kpad) { return (gem
 // CTA exactly (consumer thread i plays threads i and i + 512), so the values
 // are the same bits.  Quantisation: 8 lanes per block (xq_store_chunk8),
 // warp w takes blocks 4w..4w+3, then 4w+64.. .
+// `part` (tensor parallelism): np partial-sum rows of length dim, added to
+// x in order (x + part[0] + part[1] + ...) as the new residual; CTA b then
+// writes elements [b*dim/grid, (b+1)*dim/grid) of it to `xw`.
 __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, int dim, float eps, const XQ& q,
-                                              float* xs, float* red, int tl = -1, int tb = 0) {
+                                              float* xs, float* red, int tl = -1, int tb = 0,
+                                              const float* part = nullptr, int np = 0, float* xw = nullptr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = q.kpad >> 6;
   float sa = 0.0f, sb = 0.0f;
@@ -319,6 +330,15 @@ __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, in
       const int ea = e0 + 1024 * i + tid, eb = ea + 512;
       va[i] = ea < dim ? __ldcg(x + ea) : 0.0f;
       vb[i] = eb < dim ? __ldcg(x + eb) : 0.0f;
+    }
+    for (int p = 0; p < np; ++p) {
+      const float* pp = part + (size_t)p * dim;
+#pragma unroll
+      for (int i = 0; i < kStageBatch; ++i) {
+        const int ea = e0 + 1024 * i + tid, eb = ea + 512;
+        if (ea < dim) va[i] += __ldcg(pp + ea);
+        if (eb < dim) vb[i] += __ldcg(pp + eb);
+      }
     }
     if (e0 == 0) {  // norm weights towards L1 while x is in flight (one 128-byte line per thread)
       const int e = tid * 32;
@@ -340,6 +360,10 @@ __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, in
   }
   consumer_sync();
   B2Q_FTRACE(tl, tb + 1);
+  if (xw != nullptr) {
+    const int e0 = (int)((int64_t)dim * blockIdx.x / gridDim.x), e1 = (int)((int64_t)dim * (blockIdx.x + 1) / gridDim.x);
+    for (int e = e0 + tid; e < e1; e += kGemvConsumerWarps * 32) xw[e] = xs[e];
+  }
   const float tot = warp_sum(red[lane]);
   const float inv = 1.0f / sqrtf(tot / (float)dim + eps);
   B2Q_FTRACE(tl, tb + 2);
@@ -826,8 +850,7 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
       const int i = gt + kAttnThreads * r;
       if (i < G * HD) {
         const float v = O[r] * (1.0f / fmaxf(Ls[r], 1e-12f));
-        const int o = (a.h_off + g * G + i / HD) * HD + i % HD;
-        for (int p = 0; p < a.tp; ++p) a.attng[p][o] = v;
+        a.attng[a.rank][(g * G + i / HD) * HD + i % HD] = v;  // this rank's heads, local
       }
     }
     if (gt == 0) a.sync->attn_cnt[g] = 0u;
@@ -943,16 +966,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       for (int it = blockIdx.x; it < a.KV * nz; it += gridDim.x)
         attn_item<G>(a, Ly, it / nz, it % nz, nz, T, &attn_bar[0], attn_uses, &attn_last[0], l);
       B2Q_TRACE(tslot + 2);
-      xgrid_sync(a, bar, nbar, nxbar, okp);  // the O projection needs every rank's heads
+      grid_sync(bar, a.lbase, nbar, okp);  // the O projection reads this rank's heads
       continue;
     }
     const CtaPhase& ph = tab[head ? 4 * a.n_layers : 4 * l + (k == 0 ? 0 : k - 1)];
+    // residual buffers under tensor parallelism: the update after O reads
+    // xg[rank] and writes xalt, the update after down reads xalt and writes
+    // xg[rank]; one GPU adds into x in the epilogues instead
+    const bool tpk = a.tp > 1;
+    const bool after_down = tpk && (head || (k == 0 && l > 0));
+    const bool after_o = tpk && k == 3;
     if (ph.gb < ph.ge) {
-      const bool add = k == 2 || k == 4;
+      const bool proj = k == 2 || k == 4;  // O / down: partial sums under tensor parallelism
+      const bool add = proj && !tpk;
       const int row0 = ph.gb * 8, nrows = min(ph.ge * 8, ph.n) - row0;
       const int rows = (ph.ge - ph.gb) * 8;
-      // global row of local row 0 (O/down: x rows, gate/up: h rows, head: vocab)
-      const int grow0 = row0 + (add ? a.o_off : k == 3 ? a.f_off : head ? a.v_off : 0);
+      // global row of local row 0 (head: vocabulary rows of this rank)
+      const int grow0 = row0 + (head ? a.v_off : 0);
       // residual rows of this CTA: copied (L2 -> shared, asynchronously)
       // behind the accumulators while the input is staged
       float* resid = racc + 2 * rows;
@@ -964,15 +994,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       // stage the input: rmsnorm(x) for QKV, gate/up and the head; attn; h
       XQ q;
       if (k == 2) {
-        q = smem_xq(xs, round_up_int(a.Hg * kHeadDim, 256));
-        stage_plain(a.attng[a.rank], a.Hg * kHeadDim, q);
+        q = smem_xq(xs, round_up_int(a.H * kHeadDim, 256));
+        stage_plain(a.attng[a.rank], a.H * kHeadDim, q);
       } else if (k == 4) {
-        q = smem_xq(xs, round_up_int(a.F, 256));
-        stage_plain(a.hg[a.rank], a.F, q);
+        q = smem_xq(xs, round_up_int(a.Fl, 256));
+        stage_plain(a.hg[a.rank], a.Fl, q);
       } else {
         q = smem_xq(xs, kp_e);
         const float* nw = head ? a.out_norm : (k == 0 ? a.layers[l].attn_norm : a.layers[l].ffn_norm);
-        stage_rmsnorm(x, nw, a.E, a.eps, q, xcopy, red, l, k == 0 ? 0 : 4);
+        if (after_down)
+          stage_rmsnorm(a.xalt, nw, a.E, a.eps, q, xcopy, red, l, k == 0 ? 0 : 4,
+                        a.partg[a.rank] + (size_t)a.tp * a.E, a.tp, head ? nullptr : x);
+        else if (after_o)
+          stage_rmsnorm(x, nw, a.E, a.eps, q, xcopy, red, l, 4, a.partg[a.rank], a.tp, a.xalt);
+        else
+          stage_rmsnorm(x, nw, a.E, a.eps, q, xcopy, red, l, k == 0 ? 0 : 4);
       }
       B2Q_TRACE(tslot + 1);
       B2Q_FTRACE(l, 21 + k);
@@ -991,8 +1027,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
             a.qkv[ph.ycol + row0 + r] = v;
             continue;
           }
-          const float out = pair ? silu_f(v) * dec_racc(racc, rows, nw, r, 1) : add ? resid[r] + v : v;
-          float* const* yg = head ? a.logitsg : pair ? a.hg : a.xg;
+          if (pair) {  // SwiGLU rows of this rank, local
+            a.hg[a.rank][row0 + r] = silu_f(v) * dec_racc(racc, rows, nw, r, 1);
+            continue;
+          }
+          if (proj && tpk) {  // partial sums of every row, into every rank's slot for this rank
+            const size_t o = (size_t)((k == 2 ? 0 : 1) * a.tp + a.rank) * a.E + row0 + r;
+            for (int p = 0; p < a.tp; ++p) a.partg[p][o] = v;
+            continue;
+          }
+          const float out = add ? resid[r] + v : v;
+          float* const* yg = head ? a.logitsg : a.xg;
           for (int p = 0; p < a.tp; ++p) yg[p][grow0 + r] = out;
           if (head && v > best) { best = v; idx = grow0 + r; }
         }
@@ -1008,8 +1053,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
 #endif
     }
     if (head) break;
-    if (k == 0) grid_sync(bar, a.lbase, nbar, okp);  // attention is local to the rank
-    else xgrid_sync(a, bar, nbar, nxbar, okp);
+    // all ranks meet after the K-split projections (O, down); the other
+    // phases only need this rank's CTAs
+    if (k == 2 || k == 4) xgrid_sync(a, bar, nbar, nxbar, okp);
+    else grid_sync(bar, a.lbase, nbar, okp);
   }
   warp_argmax(best, idx);
   if (lane == 0) { s_bv[warp] = best; s_bi[warp] = idx; }

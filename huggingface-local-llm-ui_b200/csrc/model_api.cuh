@@ -81,6 +81,15 @@ b2q_status b2q_tp_shard_rows(const b2q_model_config* cfg, const char* name, int6
   return B2Q_OK;
 }
 
+b2q_status b2q_tp_shard_cols(const b2q_model_config* cfg, const char* name, int64_t k, int64_t* b, int64_t* e) {
+  if (!cfg || !name || !b || !e) return set_error(B2Q_EINVAL, "b2q_tp_shard_cols: NULL argument");
+  if (cfg->tp_size < 1 || cfg->tp_rank < 0 || cfg->tp_rank >= cfg->tp_size)
+    return set_error(B2Q_EINVAL, "b2q_tp_shard_cols: tp_rank %d of tp_size %d", cfg->tp_rank, cfg->tp_size);
+  int layer = -1;
+  col_range_cfg(*cfg, role_of(name, &layer), k, b, e);
+  return B2Q_OK;
+}
+
 b2q_status b2q_model_shard_rows(b2q_model* M, const char* name, int64_t n, int64_t* b, int64_t* e) {
   if (!M || !name || !b || !e) return set_error(B2Q_EINVAL, "b2q_model_shard_rows: NULL argument");
   return b2q_tp_shard_rows(&M->c, name, n, b, e);
@@ -128,10 +137,27 @@ static b2q_status set_tensor_impl(b2q_model* M, const char* name, int dtype, con
                        (long long)sb, (long long)se);
     if (!gemv_supported(dtype))
       return set_error(B2Q_EUNSUP, "tensor %s: GGML type %d has no GEMV kernel", name, dtype);
-    M->eng->mu.unlock();
-    b2q_status s = b2q_upload_weight(M->eng, src + (sb - rb) * row_bytes, (size_t)((se - sb) * row_bytes),
-                                     dtype, se - sb, k, dst);
-    M->eng->mu.lock();
+    int64_t cb, ce;
+    col_range_cfg(c, role, k, &cb, &ce);
+    b2q_status s;
+    if (cb == 0 && ce == k) {
+      M->eng->mu.unlock();
+      s = b2q_upload_weight(M->eng, src + (sb - rb) * row_bytes, (size_t)((se - sb) * row_bytes), dtype, se - sb,
+                            k, dst);
+      M->eng->mu.lock();
+    } else {
+      // this rank's columns: whole blocks of every row, gathered on the host
+      if (cb % bs || ce % bs || (ce - cb) % 64)
+        return set_error(B2Q_EUNSUP, "tensor %s: column split [%lld, %lld) is not block aligned", name,
+                         (long long)cb, (long long)ce);
+      const int64_t lb = (ce - cb) / bs * ts, off = cb / bs * ts;
+      std::vector<uint8_t> cols((size_t)((se - sb) * lb));
+      for (int64_t r = sb; r < se; ++r)
+        memcpy(cols.data() + (r - sb) * lb, src + (r - rb) * row_bytes + off, (size_t)lb);
+      M->eng->mu.unlock();
+      s = b2q_upload_weight(M->eng, cols.data(), cols.size(), dtype, se - sb, ce - cb, dst);
+      M->eng->mu.lock();
+    }
     if (s == B2Q_OK) {
       M->weight_bytes += (*dst)->gguf_bytes;
       M->have[name] = true;

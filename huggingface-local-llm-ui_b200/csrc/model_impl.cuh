@@ -113,11 +113,15 @@ static cudaLaunchConfig_t lcfg(dim3 g, dim3 b, size_t smem, cudaStream_t st, cud
 
 // Split the rows of an [n][...] tensor for tensor parallelism.
 //  attn_q / attn_k / attn_v: by KV head groups (whole heads per rank)
-//  attn_output, ffn_gate/up/down, output: contiguous row ranges
+//  ffn_gate/up, output: contiguous row ranges
+//  attn_output, ffn_down: every row (they are split by columns instead, see
+//  col_range_cfg), norms and token_embd: every row
+static bool col_split_role(const std::string& role) { return role == "attn_output" || role == "ffn_down"; }
+
 static void shard_range_cfg(const b2q_model_config& c, const std::string& role, int64_t n, int64_t* b,
                             int64_t* e) {
   const int r = c.tp_rank, P = c.tp_size;
-  if (P <= 1) {
+  if (P <= 1 || col_split_role(role)) {
     *b = 0;
     *e = n;
     return;
@@ -134,6 +138,24 @@ static void shard_range_cfg(const b2q_model_config& c, const std::string& role, 
 
 static void shard_range(const b2q_model* m, const std::string& role, int64_t n, int64_t* b, int64_t* e) {
   shard_range_cfg(m->c, role, n, b, e);
+}
+
+// Columns [b, e) of attn_output ([E][H*hd]: this rank's query heads) and
+// ffn_down ([E][F]: this rank's SwiGLU rows) that the rank keeps: the K
+// split that pairs with the head / row split of attention and gate/up, so
+// that attention output and SwiGLU output never leave the GPU.
+static void col_range_cfg(const b2q_model_config& c, const std::string& role, int64_t k, int64_t* b,
+                          int64_t* e) {
+  const int r = c.tp_rank, P = c.tp_size;
+  if (P <= 1 || !col_split_role(role)) {
+    *b = 0;
+    *e = k;
+    return;
+  }
+  const int64_t unit = role == "attn_output" ? c.head_dim : 1;
+  const int64_t per = k / unit / P;
+  *b = per * r * unit;
+  *e = per * (r + 1) * unit;
 }
 
 static std::string role_of(const std::string& name, int* layer) {
@@ -260,21 +282,17 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
       err = cudaLaunchKernelEx(&cfg2, attn_combine_kernel, (const float*)M->part, m, Hl, G,
                                (const int*)M->pos, c.max_seq, M->nsplit, aout, M->xq_a.x);
       if (err != cudaSuccess) return err;
-      if (P > 1) {
-        err = tp_allgather_rows(M->tp, M->attn_loc, M->attn, m, Hl * hd, st);
-        if (err != cudaSuccess) return err;
-        err = launch_quantize(e, M->attn, m, H * hd, M->xq_a, st, pdl);
-        if (err != cudaSuccess) return err;
-      }
+      // under tensor parallelism the attention output of this rank's heads
+      // stays local: attn_output holds the matching columns (K split)
     }
-    // o-projection + residual
+    // o-projection + residual (tensor parallelism: partial sums over this
+    // rank's heads, added across ranks in rank order)
     if (tc) {
       const int col0 = 0;
       const b2q_weight* wo = Lw.o;
-      err = P > 1 ? tc_matmul(e, M->attn, H * hd, m, H * hd, &wo, 1, kEpiStore, M->y_loc, (int)Lw.o->n, &col0, st, pdl)
+      err = P > 1 ? tc_matmul(e, M->attn_loc, Hl * hd, m, Hl * hd, &wo, 1, kEpiStore, M->y_loc, E, &col0, st, pdl)
                   : tc_matmul(e, M->attn, H * hd, m, H * hd, &wo, 1, kEpiAdd, M->x, E, &col0, st, pdl);
-      if (err == cudaSuccess && P > 1)
-        err = tp_allgather_add_rows(M->tp, M->y_loc, M->x, m, (int)Lw.o->n, E, st);
+      if (err == cudaSuccess && P > 1) err = tp_allreduce_add(M->tp, M->y_loc, M->x, m, E, st);
       if (err != cudaSuccess) return err;
     } else {
       GemvSeg sg;
@@ -284,9 +302,9 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
       sg.rows_out = (int)Lw.o->n;
       if (P > 1) {
         sg.y = M->y_loc;
-        sg.ldy = (int)Lw.o->n;
+        sg.ldy = E;
         err = run_gemv(e, &sg, 1, M->xq_a, m, kEpiStore, st, pdl);
-        if (err == cudaSuccess) err = tp_allgather_add_rows(M->tp, M->y_loc, M->x, m, (int)Lw.o->n, E, st);
+        if (err == cudaSuccess) err = tp_allreduce_add(M->tp, M->y_loc, M->x, m, E, st);
       } else {
         sg.y = M->x;
         sg.ldy = E;
@@ -328,22 +346,17 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
         err = launch_gemv(e, a, kEpiSwiglu, 1, st, pdl);
         if (err != cudaSuccess) return err;
       }
-      if (P > 1) {
-        err = tp_allgather_rows(M->tp, M->h_loc, M->hbuf, m, Fl, st);
-        if (err != cudaSuccess) return err;
-      }
-      if (!tc) err = launch_quantize(e, M->hbuf, m, c.n_ff, M->xq_f, st, pdl);
+      // under tensor parallelism the SwiGLU rows stay local: ffn_down holds the matching columns
+      if (!tc) err = launch_quantize(e, hout, m, Fl, M->xq_f, st, pdl);
       if (err != cudaSuccess) return err;
     }
     // down projection + residual
     if (tc) {
       const int col0 = 0;
       const b2q_weight* wd = Lw.down;
-      err = P > 1 ? tc_matmul(e, M->hbuf, c.n_ff, m, c.n_ff, &wd, 1, kEpiStore, M->y_loc, (int)Lw.down->n, &col0,
-                              st, pdl)
+      err = P > 1 ? tc_matmul(e, M->h_loc, Fl, m, Fl, &wd, 1, kEpiStore, M->y_loc, E, &col0, st, pdl)
                   : tc_matmul(e, M->hbuf, c.n_ff, m, c.n_ff, &wd, 1, kEpiAdd, M->x, E, &col0, st, pdl);
-      if (err == cudaSuccess && P > 1)
-        err = tp_allgather_add_rows(M->tp, M->y_loc, M->x, m, (int)Lw.down->n, E, st);
+      if (err == cudaSuccess && P > 1) err = tp_allreduce_add(M->tp, M->y_loc, M->x, m, E, st);
       if (err != cudaSuccess) return err;
     } else {
       GemvSeg sg;
@@ -353,10 +366,9 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
       sg.rows_out = (int)Lw.down->n;
       if (P > 1) {
         sg.y = M->y_loc;
-        sg.ldy = (int)Lw.down->n;
+        sg.ldy = E;
         err = run_gemv(e, &sg, 1, M->xq_f, m, kEpiStore, st, pdl);
-        if (err == cudaSuccess)
-          err = tp_allgather_add_rows(M->tp, M->y_loc, M->x, m, (int)Lw.down->n, E, st);
+        if (err == cudaSuccess) err = tp_allreduce_add(M->tp, M->y_loc, M->x, m, E, st);
       } else {
         sg.y = M->x;
         sg.ldy = E;
@@ -507,7 +519,7 @@ static size_t round128(size_t v) { return (v + 127) / 128 * 128; }
 // attng, hg, logitsg, candg, xbarg): one allocation, so that one IPC handle
 // maps it into the peers.
 struct XBlock {
-  size_t x, attn, h, logits, cand, bar, total;
+  size_t x, xalt, part, attn, h, logits, cand, bar, total;
 };
 static XBlock xblock_layout(int E, int Hhd, int F, int V, int tp, int grid) {
   auto al = [](size_t v) { return (v + 255) / 256 * 256; };
@@ -515,6 +527,10 @@ static XBlock xblock_layout(int E, int Hhd, int F, int V, int tp, int grid) {
   size_t o = 0;
   b.x = o;
   o += al((size_t)E * 4);
+  b.xalt = o;
+  o += al((size_t)E * 4);
+  b.part = o;  // [2][tp][E] partial O / down sums from every rank
+  o += al((size_t)2 * tp * E * 4);
   b.attn = o;
   o += al((size_t)Hhd * 4);
   b.h = o;
@@ -668,13 +684,13 @@ static cudaError_t setup_decode(b2q_model* M) {
   a.argmax = M->argmax;
   a.tp = P;
   a.rank = rk;
-  a.o_off = rk * (c.n_embd / P);
-  a.f_off = rk * M->F_loc;
+  a.Fl = M->F_loc;
   a.v_off = rk * M->V_loc;
-  a.h_off = rk * M->H_loc;
+  a.xalt = reinterpret_cast<float*>(static_cast<uint8_t*>(M->dec_xblock) + xl.xalt);
   for (int p = 0; p < P; ++p) {
     uint8_t* base = static_cast<uint8_t*>(M->dec_peer[p]);
     a.xg[p] = reinterpret_cast<float*>(base + xl.x);
+    a.partg[p] = reinterpret_cast<float*>(base + xl.part);
     a.attng[p] = reinterpret_cast<float*>(base + xl.attn);
     a.hg[p] = reinterpret_cast<float*>(base + xl.h);
     a.logitsg[p] = reinterpret_cast<float*>(base + xl.logits);
@@ -697,12 +713,12 @@ static cudaError_t launch_decode(b2q_model* M, const uint32_t* tok, int pos, uin
   a.token = tok;
   a.pos = pos;
   a.argmax2 = argmax2;
-  // every earlier launch passed 5L + 2 grid barriers (1 + L of them local
-  // only, 4L + 1 as the first level of an all-rank barrier) and 4L + 1
+  // every earlier launch passed 5L + 2 grid barriers (3L + 1 of them local
+  // only, 2L + 1 as the first level of an all-rank barrier) and 2L + 1
   // all-rank epochs
   const unsigned long long seq = M->dec_launches++, grid = (unsigned long long)M->eng->num_sms;
   a.lbase = seq * (5ull * a.n_layers + 2ull) * grid;
-  a.xepoch = seq * (4ull * a.n_layers + 1ull);
+  a.xepoch = seq * (2ull * a.n_layers + 1ull);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M->eng->num_sms);
   cfg.blockDim = dim3(kGemvThreads);

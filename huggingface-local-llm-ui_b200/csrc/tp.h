@@ -137,6 +137,29 @@ inline cudaError_t tp_allgather_rows(TpComm& t, const float* loc, float* full, i
   return tp_gather_core(t, loc, full, m, n_loc, 0, st);
 }
 
+// x[t][i] += part_0[t][i] + part_1[t][i] + ... (rank order) for a K-split
+// projection: every rank's partial sums [m][n] gathered to [P][m][n], then
+// summed in the same order on every rank, so all ranks hold the same x.
+__global__ void tp_sum_add_kernel(const float* __restrict__ stage, float* __restrict__ x, int P, int64_t cnt) {
+  pdl_wait();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < cnt; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = x[i];
+    for (int p = 0; p < P; ++p) v += stage[(int64_t)p * cnt + i];
+    x[i] = v;
+  }
+  pdl_launch_dependents();
+}
+
+inline cudaError_t tp_allreduce_add(TpComm& t, const float* part, float* x, int m, int n, cudaStream_t st) {
+  const size_t cnt = (size_t)m * n;
+  if (cnt * t.size > t.stage_cap) return cudaErrorInvalidValue;
+  nccl_result_t r = nccl().all_gather(part, t.stage, cnt, kNcclFloat32, t.comm, st);
+  if (r != 0) return cudaErrorUnknown;
+  const int blocks = (int)std::min<int64_t>(((int64_t)cnt + 255) / 256, 1024);
+  tp_sum_add_kernel<<<blocks, 256, 0, st>>>(t.stage, x, t.size, (int64_t)cnt);
+  return cudaGetLastError();
+}
+
 inline cudaError_t tp_allgather_add_rows(TpComm& t, const float* loc, float* x, int m, int n_loc,
                                          int n_full, cudaStream_t st) {
   (void)n_full;

@@ -33,6 +33,16 @@ def tp_shard_rows(cfg: dict, name: str, n: int, tp_rank: int, tp_size: int) -> t
     return b.value, e.value
 
 
+def tp_shard_cols(cfg: dict, name: str, k: int, tp_rank: int, tp_size: int) -> tuple[int, int]:
+    """Columns [begin, end) of tensor `name` ([...][k]) kept by `tp_rank` of
+    `tp_size` (b2q_tp_shard_cols; no device needed)."""
+    c = ModelConfig(cfg["n_layers"], cfg["n_embd"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"],
+                    cfg["n_ff"], cfg["n_vocab"], cfg["rms_eps"], cfg["rope_theta"], 8, tp_rank, tp_size, 0)
+    b, e = C.c_int64(), C.c_int64()
+    check(lib().b2q_tp_shard_cols(C.byref(c), name.encode(), k, C.byref(b), C.byref(e)))
+    return b.value, e.value
+
+
 def tp_unique_id() -> bytes:
     buf = (C.c_ubyte * 128)()
     check(lib().b2q_tp_unique_id(buf))

@@ -92,7 +92,9 @@ size_t b2q_weight_bytes(const b2q_weight* w);
 
 /* Replaces CudaEngine::matmul_batched (gpu.rs:557-589) and the kernels
  * matmul_{q4k,q6k,q8_0,...} it launched (gpu.rs:510-555):
- * y[t][r] = sum_c dequant(W)[r][c] * x[t][c], x [m][k], y [m][n], f32. */
+ * y[t][r] = sum_c dequant(W)[r][c] * x[t][c], x [m][k], y [m][n], f32.
+ * m < 16: the bandwidth-bound GEMV; m >= 16: the tensor-core GEMM
+ * (tcgen05, f16 hi/lo operand split, f32 accumulation). */
 b2q_status b2q_matmul(b2q_engine* eng, const b2q_weight* w, const float* x, float* y,
                       int m, int n, int k);
 b2q_status b2q_matmul_dev(b2q_engine* eng, const b2q_weight* w, const float* x_dev,
@@ -154,11 +156,11 @@ typedef struct {
   int tp_rank;       /* tensor-parallel rank of this process (0 for 1 GPU) */
   int tp_size;       /* tensor-parallel world size (1 for 1 GPU) */
   int no_graph;      /* single-token steps: 0 (default) one persistent kernel per
-                        token on one GPU (the captured graph under tensor
-                        parallelism or where the model does not fit it); 1 the
-                        per-layer kernels launched eagerly; 2 the captured CUDA
-                        graph of those kernels.  The three give bit-identical
-                        logits. */
+                        token, on one GPU or across the tensor-parallel ranks
+                        (the captured graph where the model does not fit it);
+                        1 the per-layer kernels launched eagerly; 2 the
+                        captured CUDA graph of those kernels.  The three give
+                        bit-identical logits. */
 } b2q_model_config;
 
 /* Unique id for NCCL communicator setup (ncclGetUniqueId); rank 0 creates
@@ -192,12 +194,23 @@ b2q_status b2q_model_shard_rows(b2q_model* m, const char* name, int64_t n,
 
 /* The same range from a configuration alone (cfg->tp_rank of cfg->tp_size),
    without a device: attn_q/k/v are split by whole heads (rank r owns KV heads
-   [r*KV/P, (r+1)*KV/P) and their query heads), attn_output, ffn_* and output
-   by contiguous rows; norms and token_embd are replicated.  Loader-side
-   counterpart of the reference's per-tensor placement in from_gguf
-   (inference.rs:2605-2616), which has no tensor parallelism. */
+   [r*KV/P, (r+1)*KV/P) and their query heads), ffn_gate/up and output by
+   contiguous rows; attn_output and ffn_down are split by columns instead
+   (b2q_tp_shard_cols), so every rank supplies all their rows; norms and
+   token_embd are replicated.  Loader-side counterpart of the reference's
+   per-tensor placement in from_gguf (inference.rs:2605-2616), which has no
+   tensor parallelism. */
 b2q_status b2q_tp_shard_rows(const b2q_model_config* cfg, const char* name, int64_t n,
                              int64_t* row_begin, int64_t* row_end);
+
+/* Columns [col_begin, col_end) of an [n][k] tensor this rank keeps: for
+   attn_output the columns of its query heads, for ffn_down those of its
+   ffn_gate/up rows (so attention and SwiGLU outputs stay on the rank and the
+   two projections produce partial sums that the ranks add in rank order);
+   [0, k) for every other tensor.  The library cuts the columns itself from
+   the full rows passed to b2q_model_set_tensor(_rows). */
+b2q_status b2q_tp_shard_cols(const b2q_model_config* cfg, const char* name, int64_t k,
+                             int64_t* col_begin, int64_t* col_end);
 
 /* Validate that every tensor is present, allocate the KV cache and build
  * the decode graphs. */

@@ -1,6 +1,9 @@
-"""Tensor parallelism across 2 GPUs of one box (row-sharded weights, KV
-heads split per GPU, NCCL all-gathers): logits of a prompt and of greedy
-decode steps must equal the one-GPU path bit for bit.  Runs
+"""Tensor parallelism across 2 GPUs of one box (KV heads and their query
+heads split per GPU, gate/up and the output head by rows, attn_output and
+ffn_down by the matching columns, partial sums added across ranks): the
+persistent step and the captured graph give the same logits bit for bit, and
+both stay within rel-L2 1e-3 (the decode tolerance) of the one-GPU path.
+Runs
 tests/tp_worker.py under torch.distributed.run; skipped with fewer than two
 visible GPUs."""
 from __future__ import annotations
@@ -35,4 +38,5 @@ def test_tp2_matches_single_gpu(tmp_path):
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=dict(os.environ))
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     verdict = json.loads(out.read_text())
-    assert verdict["bit_identical"], verdict
+    assert verdict["persistent_eq_graph"], verdict
+    assert verdict["matches_one_gpu"], verdict

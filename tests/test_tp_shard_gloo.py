@@ -1,11 +1,14 @@
 """Tensor-parallel host logic on CPU, as world_size-2 gloo ranks.
 
-Each rank asks the library for its row ranges (b2q_tp_shard_rows, no device),
-computes its rows of every weight's matvec with the oracle, and the ranks
-all-gather the slices with torch.distributed -- the exchange the device path
-performs with NCCL after each row-sharded matvec.  Rank 0 checks that the
-ranges tile every tensor exactly (heads kept whole, KV groups aligned with
-their query heads) and that the gathered product equals the unsharded one.
+Each rank asks the library for its row and column ranges (b2q_tp_shard_rows,
+b2q_tp_shard_cols; no device) and computes its part of every weight's matvec
+with the oracle: its rows for the row-split tensors, partial sums over its
+columns for attn_output and ffn_down.  The ranks all-gather the parts with
+torch.distributed -- the exchanges the device path performs.  Rank 0 checks
+that the ranges tile every tensor exactly (heads kept whole, KV groups
+aligned with their query heads, attn_output columns = the rank's query heads,
+ffn_down columns = its ffn_gate/up rows), that the gathered rows equal the
+unsharded product and that the partial sums add up to it.
 """
 from __future__ import annotations
 
@@ -40,19 +43,22 @@ def _worker(rank: int, world: int, port: int) -> None:
         orc = load_oracle()
         from hf_llm_b200 import model, synth
         specs = synth.llama_specs(CFG, model.q4_k_m_types())
-        x = synth.activation(CFG["n_embd"], 3)
         mine = {}
         for spec in specs:
             name, dtype, dims, _ = spec
             if len(dims) != 2:
                 continue
             n, k = dims
+            x = synth.activation(k, 3)
             b, e = model.tp_shard_rows(CFG, name, n, rank, world)
-            if k != CFG["n_embd"] or name == "token_embd.weight":
-                mine[name] = (b, e, None)
+            cb, ce = model.tp_shard_cols(CFG, name, k, rank, world)
+            if name == "token_embd.weight":
+                mine[name] = (b, e, cb, ce, None)
                 continue
             raw = synth.llama_tensor(spec, 5, b, e)  # this rank's rows only
-            mine[name] = (b, e, orc.matmul_f64(raw, dtype, e - b, k, x)[0])
+            w = orc.dequantize(raw.reshape(-1), dtype, (e - b) * k).reshape(e - b, k).astype(np.float64)
+            part = w[:, cb:ce] @ x[0, cb:ce].astype(np.float64)  # rows, or a partial sum over columns
+            mine[name] = (b, e, cb, ce, part)
         gathered = [None] * world
         dist.all_gather_object(gathered, mine)
         if rank == 0:
@@ -63,26 +69,40 @@ def _worker(rank: int, world: int, port: int) -> None:
                 n, k = dims
                 parts = [g[name] for g in gathered]
                 if name == "token_embd.weight":
-                    assert all(p[:2] == (0, n) for p in parts), name  # replicated
+                    assert all(p[:4] == (0, n, 0, k) for p in parts), name  # replicated
                     continue
-                # contiguous, ordered, exact tiling of [0, n)
+                x = synth.activation(k, 3)
+                full = orc.matmul_f64(synth.llama_tensor(spec, 5), dtype, n, k, x)[0]
+                role = name.split(".")[2] if name.startswith("blk.") else name
+                if role in ("attn_output", "ffn_down"):
+                    # every row on every rank; contiguous, ordered, exact tiling of the columns
+                    assert all(p[:2] == (0, n) for p in parts), name
+                    assert parts[0][2] == 0 and parts[-1][3] == k, name
+                    for a, c in zip(parts, parts[1:]):
+                        assert a[3] == c[2], name
+                    total = sum(p[4] for p in parts)
+                    assert np.allclose(total, full, rtol=1e-12, atol=1e-12 * np.abs(full).max()), name
+                    continue
+                # contiguous, ordered, exact tiling of [0, n), all columns
+                assert all(p[2:4] == (0, k) for p in parts), name
                 assert parts[0][0] == 0 and parts[-1][1] == n, name
                 for a, c in zip(parts, parts[1:]):
                     assert a[1] == c[0], name
-                if name.startswith("blk.0.attn_") and name.split(".")[2] in ("attn_q", "attn_k", "attn_v"):
+                if role in ("attn_q", "attn_k", "attn_v"):
                     hd = CFG["head_dim"]
                     assert all((p[1] - p[0]) % hd == 0 for p in parts), name  # whole heads
-                if parts[0][2] is not None:
-                    full = orc.matmul_f64(synth.llama_tensor(spec, 5), dtype, n, k, x)[0]
-                    cat = np.concatenate([p[2] for p in parts])
-                    assert np.array_equal(cat, full), name
+                cat = np.concatenate([p[4] for p in parts])
+                assert np.allclose(cat, full, rtol=1e-12, atol=1e-12 * np.abs(full).max()), name
             # q heads of rank r are exactly the query heads of its KV heads
             G = CFG["n_heads"] // CFG["n_kv_heads"]
             hd = CFG["head_dim"]
             for r, g in enumerate(gathered):
-                qb, qe, _ = g["blk.0.attn_q.weight"]
-                kb, ke, _ = g["blk.0.attn_k.weight"]
+                qb, qe = g["blk.0.attn_q.weight"][:2]
+                kb, ke = g["blk.0.attn_k.weight"][:2]
                 assert (qb // hd, qe // hd) == (G * (kb // hd), G * (ke // hd)), r
+                # attn_output's columns are this rank's query heads, ffn_down's its gate/up rows
+                assert g["blk.0.attn_output.weight"][2:4] == (qb, qe), r
+                assert g["blk.0.ffn_down.weight"][2:4] == g["blk.0.ffn_gate.weight"][:2], r
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -1,10 +1,14 @@
 """Two-rank tensor-parallel decode on GPUs (launched by tests/test_gpu_tp.py
-through torch.distributed.run): every rank builds its row shards of a
-Llama-shaped model, the ranks run a prompt and greedy decode steps, and rank
-0 compares each step's logits with a one-GPU eager model of the same weights.
-The per-row arithmetic, the per-head attention and the gathers do not depend
-on the sharding, so the logits must agree bit for bit.  Writes a JSON
-verdict to --out."""
+through torch.distributed.run): every rank builds its shards of a
+Llama-shaped model twice (persistent single-token kernel, captured per-kernel
+graph), the ranks run a prompt and greedy decode steps, and rank 0 compares
+each step's logits:
+  * persistent vs graph under tensor parallelism: bit for bit (the same
+    per-rank partial sums, added across ranks in rank order);
+  * tensor parallel vs a one-GPU eager model of the same weights: rel-L2
+    <= 1e-3, the decode path's tolerance (attn_output and ffn_down are split
+    by columns, so their sums are formed in another order; measured ~1e-4).
+Writes a JSON verdict to --out."""
 from __future__ import annotations
 
 import argparse
@@ -37,34 +41,46 @@ def main() -> int:
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     cfg = dict(model.LLAMA3_8B, n_layers=args.layers, n_vocab=32000)
     eng = CudaEngine(local)
-    obj = [model.tp_unique_id() if rank == 0 else None]
-    dist.broadcast_object_list(obj, src=0)
     specs = synth.llama_specs(cfg, model.q4_k_m_types())
-    m = model.StandardNativeEngine(eng, cfg, max_seq=160, tp_rank=rank, tp_size=world, tp_id=obj[0])
-    for spec in specs:
-        name, t, dims, _ = spec
-        if len(dims) == 1:
-            m.set_tensor(name, t, dims, synth.llama_tensor(spec, 9, dist="unit"))
-            continue
-        b, e = m.shard_rows(name, dims[0])
-        m.set_tensor(name, t, dims, synth.llama_tensor(spec, 9, b, e, dist="unit"), b, e)
-    m.finalize()
+
+    def build(decode):
+        obj = [model.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        mm = model.StandardNativeEngine(eng, cfg, max_seq=160, tp_rank=rank, tp_size=world, tp_id=obj[0],
+                                        decode=decode)
+        for spec in specs:
+            name, t, dims, _ = spec
+            if len(dims) == 1:
+                mm.set_tensor(name, t, dims, synth.llama_tensor(spec, 9, dist="unit"))
+                continue
+            b, e = mm.shard_rows(name, dims[0])
+            mm.set_tensor(name, t, dims, synth.llama_tensor(spec, 9, b, e, dist="unit"), b, e)
+        mm.finalize()
+        return mm
+
+    m = build("persistent")
+    mg = build("graph")
     ref = None
     if rank == 0:
         full = synth.llama_tensors(cfg, model.q4_k_m_types(), 9, dist="unit")
         ref = model.StandardNativeEngine.from_tensors(eng, cfg, full, max_seq=160, decode="eager")
     rng = np.random.default_rng(4)
-    prompt = rng.integers(0, cfg["n_vocab"], 70).tolist()  # > one forward chunk (64)
-    steps, same, pos = [], True, 0
+    # 140 tokens: a 128-token chunk (tensor cores) and a 12-token chunk (GEMV)
+    prompt = rng.integers(0, cfg["n_vocab"], 140).tolist()
+    steps, same, close, pos = [], True, True, 0
     tok_list = [prompt]
     for s in range(6):
         toks = tok_list[-1]
         lt = m.forward(toks, pos)
+        lg = mg.forward(toks, pos)
         if rank == 0:
             lr = ref.forward(toks, pos)
-            eq = bool(np.array_equal(lt.view(np.uint32), lr.view(np.uint32)))
+            eq = bool(np.array_equal(lt.view(np.uint32), lg.view(np.uint32)))
+            rl = float(np.linalg.norm(lt.astype(np.float64) - lr) / max(np.linalg.norm(lr.astype(np.float64)), 1e-30))
             same &= eq
-            steps.append({"pos": pos, "n": len(toks), "bit_identical": eq,
+            close &= rl <= 1e-3
+            steps.append({"pos": pos, "n": len(toks), "persistent_eq_graph": eq, "rel_l2_vs_one_gpu": rl,
+                          "same_argmax": int(np.argmax(lt)) == int(np.argmax(lr)),
                           "max_abs_diff": float(np.max(np.abs(lt - lr)))})
             nxt = int(np.argmax(lr))
         else:
@@ -75,8 +91,10 @@ def main() -> int:
         tok_list.append([o[0]])
     dist.barrier()
     if rank == 0:
-        Path(args.out).write_text(json.dumps({"world": world, "bit_identical": same, "steps": steps}))
+        Path(args.out).write_text(json.dumps({"world": world, "persistent_eq_graph": same,
+                                              "matches_one_gpu": close, "steps": steps}))
     m.close()
+    mg.close()
     if ref is not None:
         ref.close()
     dist.barrier()
