@@ -237,6 +237,7 @@ GEMV_SHAPES = {  # key: (ggml type, n, k, copies rotated to exceed L2)
     "q4k_4096x4096": (12, 4096, 4096, 48), "q4k_1024x4096": (12, 1024, 4096, 96),
     "q6k_128256x4096": (14, 128256, 4096, 2), "q6k_4096x14336": (14, 4096, 14336, 16),
     "q8_0_4096x4096": (8, 4096, 4096, 48),
+    "q5k_14336x4096": (13, 14336, 4096, 20), "q4_0_4096x4096": (2, 4096, 4096, 48),
 }
 
 

@@ -37,17 +37,28 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile libb2q.so if a source is newer than it.  Safe when several
+    processes (tensor-parallel ranks) call it at once: they serialise on a
+    lock file, the first one compiles, the others find it up to date."""
     if not force and up_to_date():
         return LIB
-    nvcc = os.environ.get("NVCC", "nvcc")
-    tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc, *NVCC_FLAGS, "-o", str(tmp), str(CSRC / "b2q_api.cu"), "-ldl"]
-    if verbose:
-        print(" ".join(cmd), file=sys.stderr)
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if r.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
-    os.replace(tmp, LIB)
+    import fcntl
+    with open(LIB.with_suffix(".so.lock"), "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            if not force and up_to_date():
+                return LIB
+            nvcc = os.environ.get("NVCC", "nvcc")
+            tmp = LIB.with_suffix(f".so.tmp{os.getpid()}")
+            cmd = [nvcc, *NVCC_FLAGS, "-o", str(tmp), str(CSRC / "b2q_api.cu"), "-ldl"]
+            if verbose:
+                print(" ".join(cmd), file=sys.stderr)
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+            os.replace(tmp, LIB)
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
     return LIB
 
 

@@ -36,7 +36,9 @@ b2q_status cuda_error(cudaError_t e, const char* what) {
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-bool gemv_supported(int dtype) { return dtype == kQ4_K || dtype == kQ6_K || dtype == kQ8_0; }
+bool gemv_supported(int dtype) {
+  return dtype == kQ4_K || dtype == kQ6_K || dtype == kQ8_0 || dtype == kQ5_K || dtype == kQ4_0;
+}
 
 int dtype_block(int t) {
   switch (t) {
@@ -405,6 +407,10 @@ b2q_status b2q_upload_weight(b2q_engine* e, const void* bytes, size_t len, int d
       repack_q4k_kernel<<<blocks, 256, 0, e->stream>>>(r8, v.L, base);
     else if (dtype == kQ6_K)
       repack_q6k_kernel<<<blocks, 256, 0, e->stream>>>(r8, v.L, base);
+    else if (dtype == kQ5_K)
+      repack_q5k_kernel<<<blocks, 256, 0, e->stream>>>(r8, v.L, base);
+    else if (dtype == kQ4_0)
+      repack_q40_kernel<<<blocks, 256, 0, e->stream>>>(r8, v.L, base);
     else
       repack_q80_kernel<<<blocks, 256, 0, e->stream>>>(r8, v.L, base);
     launch_counted(e, 1);

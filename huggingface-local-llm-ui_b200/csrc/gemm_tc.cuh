@@ -144,16 +144,16 @@ __device__ __forceinline__ void zero_img8(uint8_t* img, int lo_off, int row, int
 // Thread (tile row r, quarter qq): half hf = qq >> 1 of the unit pair or
 // plane pair, and bytes 8*(qq & 1) .. +7 of each 16-byte plane it reads.
 struct TcRaw {
-  uint2 a, b, c;   // Q4_K: qs bytes, header words 0-1, 2-3; Q6_K: ql lo, ql hi, qh;
-                   // Q8_0: codes 0-15 part, 16-31 part
-  uint32_t s, d;   // Q6_K: sub-scale word, d word; Q8_0: d word
+  uint2 a, b, c;   // Q4_K / Q5_K: qs bytes, header words 0-1, 2-3; Q6_K: ql lo, ql hi, qh;
+                   // Q8_0: codes 0-15 part, 16-31 part; Q4_0: qs bytes
+  uint32_t s, d;   // Q6_K: sub-scale word, d word; Q8_0 / Q4_0: d word; Q5_K: fifth-bit words
   bool live;
 };
 
 // Unit of tile row r's half `hf` in stage ks (Q4_K / Q6_K: 64-weight
 // units, Q8_0: 32-weight blocks).
 __device__ __forceinline__ int tc_unit(int dt, int ks, int hf) {
-  if (dt == kQ8_0) return 2 * ks + hf;
+  if (dt == kQ8_0 || dt == kQ4_0) return 2 * ks + hf;
   if (dt == kQ6_K) return 4 * (ks >> 2) + 2 * ((ks & 3) >> 1) + hf;
   return ks;
 }
@@ -174,11 +174,19 @@ __device__ __forceinline__ TcRaw tc_load(const WeightDev& w, int64_t R, int qq, 
   if (!x.live) return x;
   const int c = u / L.KC, ul = u - c * L.KC;
   const uint8_t* rc = w.base + (((R >> 3) * L.C + c) * 8 + (R & 7)) * (int64_t)L.rc;
-  if (dt == kQ4_K) {
+  if (dt == kQ4_K || dt == kQ5_K) {
     x.a = ldg_nc64(rc + 16 * (hf * L.KC + ul) + e8);
-    const uint4 hb = ldg_nc128(rc + L.o_aux + 16 * (ul >> 2));
+    const uint4 hb = ldg_nc128(rc + (dt == kQ5_K ? L.o_aux2 : L.o_aux) + 16 * (ul >> 2));
     x.b = make_uint2(hb.x, hb.y);
     x.c = make_uint2(hb.z, hb.w);
+    if (dt == kQ5_K) {
+      const uint2 m = ldg_nc64(rc + L.o_aux + 8 * ul);
+      x.s = m.x;
+      x.d = m.y;
+    }
+  } else if (dt == kQ4_0) {
+    x.a = ldg_nc64(rc + 16 * ul + e8);
+    x.d = ldg_nc32(rc + L.o_aux + 4 * (ul >> 1));
   } else if (dt == kQ6_K) {
     x.a = ldg_nc64(rc + 16 * ul + e8);
     x.b = ldg_nc64(rc + 16 * (L.KC + ul) + e8);
@@ -211,7 +219,7 @@ __device__ __forceinline__ void tc_convert(const TcRaw& x, int dt, int r, int qq
   const int u = tc_unit(dt, ks, hf);
   // k offsets (within the stage) of the two 8-element outputs
   int k0, k1;
-  if (dt == kQ8_0) { k0 = 32 * hf + e8; k1 = 32 * hf + 16 + e8; }
+  if (dt == kQ8_0 || dt == kQ4_0) { k0 = 32 * hf + e8; k1 = 32 * hf + 16 + e8; }
   else { k0 = 16 * hf + e8; k1 = 32 + 16 * hf + e8; }
   if (!x.live) {
     zero_img8(img, kTcABytes, r, k0);
@@ -219,7 +227,7 @@ __device__ __forceinline__ void tc_convert(const TcRaw& x, int dt, int r, int qq
     return;
   }
   float v0[8], v1[8];
-  if (dt == kQ4_K) {
+  if (dt == kQ4_K || dt == kQ5_K) {
     const uint4 hb = make_uint4(x.b.x, x.b.y, x.c.x, x.c.y);
     const uint32_t sel = u & 3;  // KC is a multiple of 8: u & 3 == ul & 3
     const uint32_t h = sel == 0 ? hb.x : sel == 1 ? hb.y : sel == 2 ? hb.z : hb.w;
@@ -228,11 +236,16 @@ __device__ __forceinline__ void tc_convert(const TcRaw& x, int dt, int r, int qq
     const float d1 = __fmul_rn(d, (float)(h & 63u)), m1 = __fmul_rn(dmin, (float)((h >> 12) & 63u));
     const float d2 = __fmul_rn(d, (float)((h >> 6) & 63u)), m2 = __fmul_rn(dmin, (float)((h >> 18) & 63u));
     const uint32_t wd[2] = {x.a.x, x.a.y};
+    const bool q5 = dt == kQ5_K;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const uint32_t b = wd[i >> 2] >> (8 * (i & 3));
-      v0[i] = fmaf(d1, small_uint_f(b & 15u), -m1);
-      v1[i] = fmaf(d2, small_uint_f((b >> 4) & 15u), -m2);
+      // Q5_K: fifth bit of element l of each sub-block at bit 8*(l & 3) + (l >> 2)
+      const int l = 16 * hf + e8 + i;
+      const uint32_t sh = 8 * (l & 3) + (l >> 2);
+      const uint32_t b5a = q5 ? ((x.s >> sh) & 1u) << 4 : 0u, b5b = q5 ? ((x.d >> sh) & 1u) << 4 : 0u;
+      v0[i] = fmaf(d1, small_uint_f((b & 15u) | b5a), -m1);
+      v1[i] = fmaf(d2, small_uint_f(((b >> 4) & 15u) | b5b), -m2);
     }
   } else if (dt == kQ6_K) {
     // u & 7 == ul & 7 (KC a multiple of 8): the d of block ul >> 2 is half (ul >> 2) & 1 of the word
@@ -256,6 +269,15 @@ __device__ __forceinline__ void tc_convert(const TcRaw& x, int dt, int r, int qq
       }
       v0[i] = s0 * (small_uint_f(q0) - 32.0f);
       v1[i] = s1 * (small_uint_f(q1) - 32.0f);
+    }
+  } else if (dt == kQ4_0) {  // u & 1 == ul & 1 (KC even)
+    const float d = f16_bits_exact((u & 1) ? x.d >> 16 : x.d & 0xffffu);
+    const uint32_t wd[2] = {x.a.x, x.a.y};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t b = wd[i >> 2] >> (8 * (i & 3));
+      v0[i] = d * (small_uint_f(b & 15u) - 8.0f);
+      v1[i] = d * (small_uint_f((b >> 4) & 15u) - 8.0f);
     }
   } else {  // Q8_0: u & 1 == ul & 1 (KC even)
     const float d = f16_bits_exact((u & 1) ? x.d >> 16 : x.d & 0xffffu);

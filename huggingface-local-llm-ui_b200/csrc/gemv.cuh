@@ -174,6 +174,14 @@ __device__ __forceinline__ void xload_q80(XUnit& X, const SX& sx, int t, int u, 
   X.xs = sx.scale[t * (sx.kpad >> 6) + (u >> 1)];
 }
 
+// Q4_0 unit u = one 32-element block: the Q8_0 chunks, plus the sum of its
+// 32 activations (the -8 offset of the codes).
+__device__ __forceinline__ void xload_q40(XUnit& X, const SX& sx, int t, int u, int F) {
+  xload_q80(X, sx, t, u, F);
+  const int32_t* q16 = sx.s16 + t * (sx.kpad >> 4) + 4 * (u >> 1) + 2 * (u & 1);
+  X.s16 = make_int4(q16[0] + q16[1], 0, 0, 0);
+}
+
 // ---------------------------------------------------------------------------
 // Per-row unit kernels.  rc: row-chunk base of the row in shared memory;
 // ul: unit index within the chunk.  Return the row's contribution.
@@ -254,6 +262,72 @@ __device__ __forceinline__ float row_q6k(const uint8_t* rc, int KC, int o_aux, i
   const int i01 = sc0 * (s0[0] + s1[0] - X.s16.x) + sc1 * (s0[1] + s1[1] - X.s16.y);
   const int i23 = sc2 * (s0[2] + s1[2] - X.s16.z) + sc3 * (s0[3] + s1[3] - X.s16.w);
   return d * (X.xs2.x * (float)i01 + X.xs2.y * (float)i23);
+}
+
+// Q5_K: as Q4_K with the fifth bit of every code (dequantize_slice,
+// inference.rs:1418-1447): word j of a qs half holds elements 4j..4j+3 of
+// both sub-blocks; their fifth bits sit at bits 8i + j of the unit's two
+// bit words, moved to bit 4 of each byte with one shift and mask.  Codes are
+// 0..31 in both halves (no 16x trick), so both partial sums are in code units.
+template <int J>
+__device__ __forceinline__ uint32_t q5_bits(uint32_t m) {
+  return (J <= 4 ? (m << (4 - J)) : (m >> (J - 4))) & 0x10101010u;
+}
+
+#define B2Q_Q5K_WORD(J, W, IA, IB, XA, XB, YA, YB)                                  \
+  {                                                                                \
+    const uint32_t lo_ = ((W)&0x0F0F0F0Fu) | q5_bits<J>(mb.x);                     \
+    const uint32_t hi_ = (((W) >> 4) & 0x0F0F0F0Fu) | q5_bits<J>(mb.y);            \
+    IA = dp2a_lo_ss((XA), (int)lo_, IA);                                           \
+    IA = dp2a_hi_ss((XB), (int)lo_, IA);                                           \
+    IB = dp2a_lo_ss((YA), (int)hi_, IB);                                           \
+    IB = dp2a_hi_ss((YB), (int)hi_, IB);                                           \
+  }
+
+__device__ __forceinline__ float row_q5k(const uint8_t* rc, int KC, int o_aux, int o_aux2, int ul, int csel,
+                                         const XUnit& X) {
+  const uint4 a = lds128(rc + ul * 16);
+  const uint4 b = lds128(rc + (KC + ul) * 16);
+  const uint2 mb = *reinterpret_cast<const uint2*>(rc + o_aux + ul * 8);
+  const uint4 hb = lds128(rc + o_aux2 + (ul >> 2) * 16);
+  const uint32_t h = (csel & 2) ? ((csel & 1) ? hb.w : hb.z) : ((csel & 1) ? hb.y : hb.x);
+  const uint32_t dd = __byte_perm(__byte_perm(hb.x, hb.y, 0x0073), __byte_perm(hb.z, hb.w, 0x0073), 0x5410);
+  const float d = f16_bits_fast(dd & 0xffffu), dm = f16_bits_fast(dd >> 16);
+  int ia0 = 0, ia1 = 0, ib0 = 0, ib1 = 0;
+  B2Q_Q5K_WORD(0, a.x, ia0, ib0, X.v[0].x, X.v[0].y, X.v[4].x, X.v[4].y)
+  B2Q_Q5K_WORD(1, a.y, ia1, ib1, X.v[0].z, X.v[0].w, X.v[4].z, X.v[4].w)
+  B2Q_Q5K_WORD(2, a.z, ia0, ib0, X.v[1].x, X.v[1].y, X.v[5].x, X.v[5].y)
+  B2Q_Q5K_WORD(3, a.w, ia1, ib1, X.v[1].z, X.v[1].w, X.v[5].z, X.v[5].w)
+  B2Q_Q5K_WORD(4, b.x, ia0, ib0, X.v[2].x, X.v[2].y, X.v[6].x, X.v[6].y)
+  B2Q_Q5K_WORD(5, b.y, ia1, ib1, X.v[2].z, X.v[2].w, X.v[6].z, X.v[6].w)
+  B2Q_Q5K_WORD(6, b.z, ia0, ib0, X.v[3].x, X.v[3].y, X.v[7].x, X.v[7].y)
+  B2Q_Q5K_WORD(7, b.w, ia1, ib1, X.v[3].z, X.v[3].w, X.v[7].z, X.v[7].w)
+  // codes <= 31, |x| <= 16383, 32 per sub-block, scales <= 63: |isum| < 2^31
+  const int isum = (int)(h & 63u) * (ia0 + ia1) + (int)((h >> 6) & 63u) * (ib0 + ib1);
+  const int msum = (int)((h >> 12) & 63u) * X.s16.x + (int)((h >> 18) & 63u) * X.s16.y;
+  return X.xs * (d * (float)isum - dm * (float)msum);
+}
+#undef B2Q_Q5K_WORD
+
+// Q4_0: one block of 32 codes 0..15 with offset -8 (dequantize_slice,
+// inference.rs:1459-1469): element i in the low nibble of byte i, i + 16 in
+// the high nibble.
+__device__ __forceinline__ float row_q40(const uint8_t* rc, int o_aux, int ul, const XUnit& X) {
+  const uint4 a = lds128(rc + ul * 16);
+  const float d = f16_bits_fast(*reinterpret_cast<const uint16_t*>(rc + o_aux + ul * 2));
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+  int s0 = 0, s1 = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
+    const int4& xl = X.v[j >> 1];
+    const int4& xh = X.v[2 + (j >> 1)];
+    s0 = dp2a_lo_ss((j & 1) ? xl.z : xl.x, (int)lo, s0);
+    s1 = dp2a_hi_ss((j & 1) ? xl.w : xl.y, (int)lo, s1);
+    s0 = dp2a_lo_ss((j & 1) ? xh.z : xh.x, (int)hi, s0);
+    s1 = dp2a_hi_ss((j & 1) ? xh.w : xh.y, (int)hi, s1);
+  }
+  return d * (X.xs * (float)(s0 + s1 - 8 * X.s16.x));
 }
 
 // Q8_0: one block (32 weights).
@@ -381,8 +455,9 @@ __device__ __forceinline__ void consume_gemv(Ring& rg, const TileLayout& L, int 
       if (uok && ok) {
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
-          if (dt == kQ4_K) xload_q4k(X[t], sx, t, u, xp.f4);
+          if (dt == kQ4_K || dt == kQ5_K) xload_q4k(X[t], sx, t, u, xp.f4);
           else if (dt == kQ6_K) xload_q6k(X[t], sx, t, u, xp.f6a, xp.f6b);
+          else if (dt == kQ4_0) xload_q40(X[t], sx, t, u, xp.f8);
           else xload_q80(X[t], sx, t, u, xp.f8);
         }
       }
@@ -404,6 +479,8 @@ __device__ __forceinline__ void consume_gemv(Ring& rg, const TileLayout& L, int 
         for (int t = 0; t < MT; ++t) {
           if (dt == kQ4_K) part[i][t] = row_q4k(rc, L.KC, L.o_aux, ul, csel, X[t]);
           else if (dt == kQ6_K) part[i][t] = row_q6k(rc, L.KC, L.o_aux, L.o_aux2, ul, X[t]);
+          else if (dt == kQ5_K) part[i][t] = row_q5k(rc, L.KC, L.o_aux, L.o_aux2, ul, csel, X[t]);
+          else if (dt == kQ4_0) part[i][t] = row_q40(rc, L.o_aux, ul, X[t]);
           else part[i][t] = row_q80(rc, L.KC, L.o_aux, ul, X[t]);
         }
       }

@@ -563,6 +563,15 @@ static cudaError_t setup_decode(b2q_model* M) {
   // the split merge stages {max, sum} of every split of a head group in one tile
   if (2 * G * M->nsplit > kAttnTile * kHeadDim / 2) return cudaSuccess;
   const int grid = e->num_sms;
+  // the persistent kernel's consume loop takes Q4_K, Q6_K and Q8_0 rows;
+  // models with other weight types step through the captured graph
+  auto dec_type = [](const b2q_weight* w) { return w->dtype == kQ4_K || w->dtype == kQ6_K || w->dtype == kQ8_0; };
+  if (!dec_type(M->output)) return cudaSuccess;
+  for (int l = 0; l < c.n_layers; ++l) {
+    const LayerW& w = M->L[l];
+    for (const b2q_weight* x : {w.q, w.k, w.v, w.o, w.gate, w.up, w.down})
+      if (!dec_type(x)) return cudaSuccess;
+  }
   int stage_max = 0;
   std::vector<DecLayer> host((size_t)c.n_layers);
   std::vector<const DecPhase*> phases;

@@ -298,6 +298,11 @@ __global__ void embed_rows_kernel(const uint8_t* __restrict__ raw, int dtype, in
 //         [2 B x KC/4: d per block, padded to 16 B]
 //   Q8_0  [16 B x KC: codes 0..15] [16 B x KC: codes 16..31]
 //         [2 B x KC: d, padded to 16 B]
+//   Q5_K  as Q4_K, plus [8 B x KC: the fifth bits of the unit's two
+//         sub-blocks, two words; element 4j+i of a sub-block at bit 8i+j]
+//         before the header words: [16 x KC][16 x KC][8 x KC][4 x KC]
+//   Q4_0  (unit = one block of 32) [16 B x KC: the 16 nibble bytes]
+//         [2 B x KC: d, padded to 16 B]
 // Padding units (u >= U) and rows (>= n) are zero and never read.
 // ---------------------------------------------------------------------------
 struct TileLayout {
@@ -317,11 +322,12 @@ __host__ inline TileLayout make_tile_layout(int dtype, int64_t n, int64_t k) {
   L.dtype = dtype;
   L.n = (int)n;
   L.k = (int)k;
-  const int qk = dtype == kQ8_0 ? 32 : 256;
+  const bool b32 = dtype == kQ8_0 || dtype == kQ4_0;  // units are whole 32-element blocks
+  const int qk = b32 ? 32 : 256;
   L.nb = (int)(k / qk);
-  L.U = dtype == kQ8_0 ? L.nb : (int)(k / 64);
+  L.U = b32 ? L.nb : (int)(k / 64);
   L.C = (L.U + 63) / 64;
-  L.KC = round_up_int((L.U + L.C - 1) / L.C, dtype == kQ8_0 ? 16 : 8);
+  L.KC = round_up_int((L.U + L.C - 1) / L.C, b32 ? 16 : 8);
   L.G = (int)((n + 7) / 8);
   const int kc = L.KC;
   if (dtype == kQ4_K) {
@@ -332,6 +338,14 @@ __host__ inline TileLayout make_tile_layout(int dtype, int64_t n, int64_t k) {
     L.o_aux = 48 * kc;
     L.o_aux2 = 52 * kc;
     L.rc = 52 * kc + round_up_int(kc / 2, 16);
+  } else if (dtype == kQ5_K) {
+    L.o_aux = 32 * kc;   // fifth-bit words
+    L.o_aux2 = 40 * kc;  // header words
+    L.rc = 44 * kc;
+  } else if (dtype == kQ4_0) {
+    L.o_aux = 16 * kc;
+    L.o_aux2 = 0;
+    L.rc = 16 * kc + round_up_int(2 * kc, 16);
   } else {
     L.o_aux = 32 * kc;
     L.o_aux2 = 0;
@@ -398,6 +412,65 @@ __global__ void repack_q6k_kernel(const uint8_t* __restrict__ raw, TileLayout L,
     *reinterpret_cast<uint32_t*>(rcp + L.o_aux + 4 * ul) =
         (uint32_t)sc[0] | ((uint32_t)sc[2] << 8) | ((uint32_t)sc[4] << 16) | ((uint32_t)sc[6] << 24);
     if ((ul & 3) == 0) *reinterpret_cast<uint16_t*>(rcp + L.o_aux2 + 2 * (ul >> 2)) = (uint16_t)rd16(b + 208);
+  }
+}
+
+// Q4_K / Q5_K header word of unit cc of a block (scales at b + 4, d|dmin at b).
+__device__ __forceinline__ uint32_t kquant_header_word(const uint8_t* b, int cc) {
+  const uint8_t* s = b + 4;
+  const int j0 = 2 * cc, j1 = 2 * cc + 1;
+  uint32_t sc0, m0, sc1, m1;
+  if (j0 < 4) {
+    sc0 = s[j0] & 63; m0 = s[j0 + 4] & 63; sc1 = s[j1] & 63; m1 = s[j1 + 4] & 63;
+  } else {
+    sc0 = (s[j0 + 4] & 0x0F) | ((s[j0 - 4] >> 6) << 4);
+    m0 = (s[j0 + 4] >> 4) | ((s[j0] >> 6) << 4);
+    sc1 = (s[j1 + 4] & 0x0F) | ((s[j1 - 4] >> 6) << 4);
+    m1 = (s[j1 + 4] >> 4) | ((s[j1] >> 6) << 4);
+  }
+  const uint32_t dd = rd16(b) | (rd16(b + 2) << 16);
+  return sc0 | (sc1 << 6) | (m0 << 12) | (m1 << 18) | (((dd >> (8 * cc)) & 0xffu) << 24);
+}
+
+// Q5_K block: d @0, dmin @2, scales[12] @4, qh[32] @16, qs[128] @48
+// (dequantize_slice, inference.rs:1418-1447).
+__global__ void repack_q5k_kernel(const uint8_t* __restrict__ raw, TileLayout L, uint8_t* __restrict__ out) {
+  const int64_t total = (int64_t)L.n * L.U;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = idx / L.U;
+    const int u = (int)(idx % L.U);
+    const int c = u / L.KC, ul = u % L.KC;
+    const int blk = u >> 2, cc = u & 3;
+    const uint8_t* b = raw + (row * L.nb + blk) * 176;
+    uint8_t* rcp = tile_row_chunk(out, L, row, c);
+    const uint8_t* qs = b + 48 + 32 * cc;
+    for (int i = 0; i < 16; ++i) { rcp[16 * ul + i] = qs[i]; rcp[16 * (L.KC + ul) + i] = qs[16 + i]; }
+    const uint8_t* qh = b + 16;
+    uint32_t mlo = 0, mhi = 0;
+    for (int l = 0; l < 32; ++l) {
+      const uint32_t pos = 8 * (l & 3) + (l >> 2);
+      mlo |= ((uint32_t)(qh[l] >> (2 * cc)) & 1u) << pos;
+      mhi |= ((uint32_t)(qh[l] >> (2 * cc + 1)) & 1u) << pos;
+    }
+    *reinterpret_cast<uint2*>(rcp + L.o_aux + 8 * ul) = make_uint2(mlo, mhi);
+    *reinterpret_cast<uint32_t*>(rcp + L.o_aux2 + 4 * ul) = kquant_header_word(b, cc);
+  }
+}
+
+// Q4_0 block: d @0, qs[16] @2 (element i: low nibble, i + 16: high nibble)
+// (dequantize_slice, inference.rs:1459-1469).
+__global__ void repack_q40_kernel(const uint8_t* __restrict__ raw, TileLayout L, uint8_t* __restrict__ out) {
+  const int64_t total = (int64_t)L.n * L.U;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = idx / L.U;
+    const int u = (int)(idx % L.U);
+    const int c = u / L.KC, ul = u % L.KC;
+    const uint8_t* b = raw + (row * L.nb + u) * 18;
+    uint8_t* rcp = tile_row_chunk(out, L, row, c);
+    for (int i = 0; i < 16; ++i) rcp[16 * ul + i] = b[2 + i];
+    *reinterpret_cast<uint16_t*>(rcp + L.o_aux + 2 * ul) = (uint16_t)rd16(b);
   }
 }
 

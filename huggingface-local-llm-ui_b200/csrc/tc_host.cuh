@@ -90,7 +90,7 @@ cudaError_t tc_matmul(b2q_engine* e, const float* x, int ldx, int m, int k, cons
                       int epi, float* y, int ldy, const int* col0, cudaStream_t st, bool pdl) {
   if (m < 1 || nw < 1 || (epi == kEpiSwiglu && nw != 2)) return cudaErrorInvalidValue;
   for (int i = 0; i < nw; ++i)
-    if (ws[i]->k != k || !(ws[i]->dtype == kQ4_K || ws[i]->dtype == kQ6_K || ws[i]->dtype == kQ8_0))
+    if (ws[i]->k != k || !gemv_supported(ws[i]->dtype))
       return cudaErrorInvalidValue;
   TcScratch& t = e->tc;
   // scratch: image and scales for these tokens, partials for the largest weight

@@ -93,6 +93,11 @@ def _blocks_unit(rng: np.random.Generator, dtype: int, nblk: int, k: int) -> np.
         d = np.abs(rng.standard_normal(nblk, dtype=np.float32)) * np.float32(1.25) * sig / np.float32(
             37.0 * 18.5)
         out[:, 208:210] = _f16_bits(d).reshape(nblk, 1).view(np.uint8)
+    elif dtype == ggml.Q4_0:
+        # codes uniform 0..15 with offset -8: std of (q - 8) ~ 4.6
+        d = np.abs(rng.standard_normal(nblk, dtype=np.float32)) * np.float32(1.25) * sig / np.float32(4.6)
+        out[:, 0:2] = _f16_bits(d).reshape(nblk, 1).view(np.uint8)
+        out[:, 2:18] = _rand_bytes(rng, nblk * 16).reshape(nblk, 16)
     else:
         return _blocks(rng, dtype, nblk)
     return out

@@ -30,7 +30,7 @@ def _check(engine, orc, dtype, n, k, m, seed, dist="bench"):
     return err
 
 
-@pytest.mark.parametrize("dtype", [12, 14, 8])
+@pytest.mark.parametrize("dtype", [12, 14, 8, 13, 2])
 @pytest.mark.parametrize("m", [16, 17, 48, 100, 256, 300])
 def test_tc_matmul_tokens(engine, orc, pkg, dtype, m):
     _check(engine, orc, dtype, 520, 1024, m, seed=m)
@@ -42,11 +42,11 @@ def test_tc_matmul_model_shapes(engine, orc, pkg, dtype, n, k):
     _check(engine, orc, dtype, n, k, 64, seed=3)
 
 
-@pytest.mark.parametrize("dtype", [12, 14, 8])
+@pytest.mark.parametrize("dtype", [12, 14, 8, 13, 2])
 def test_tc_matmul_ragged_rows_and_k(engine, orc, pkg, dtype):
     # rows not a multiple of 128 (or of 8); k of an odd number of 64-element
-    # stages, with padding units in the tile layout (Q8_0: 34 units, KC 48)
-    k = 1088 if dtype == 8 else 1280
+    # stages, with padding units in the tile layout (Q8_0 / Q4_0: 34 units, KC 48)
+    k = 1088 if dtype in (8, 2) else 1280
     _check(engine, orc, dtype, 77, k, 33, seed=5)
     _check(engine, orc, dtype, 1, k, 16, seed=6)
 

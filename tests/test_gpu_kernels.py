@@ -97,10 +97,10 @@ def _check_matvec(engine, orc, pkg, dtype, n, k, m=1, seed=0, dist="bench"):
     return err
 
 
-@pytest.mark.parametrize("dtype", [12, 14, 8])
+@pytest.mark.parametrize("dtype", [12, 14, 8, 13, 2])
 @pytest.mark.parametrize("n,k", SHAPES_SMALL)
 def test_matvec_small_shapes(engine, orc, pkg, dtype, n, k):
-    if k % 256 and dtype != 8:
+    if k % 256 and dtype not in (8, 2):
         pytest.skip("K-quants need k % 256 == 0")
     _check_matvec(engine, orc, pkg, dtype, n, k)
 
@@ -119,13 +119,21 @@ def test_matvec_q6k_output_head(engine, orc, pkg):
 
 
 @pytest.mark.parametrize("m", [2, 3, 8, 11, 17])
-@pytest.mark.parametrize("dtype", [12, 14, 8])
+@pytest.mark.parametrize("dtype", [12, 14, 8, 13, 2])
 def test_matvec_multi_token(engine, orc, pkg, dtype, m):
     _check_matvec(engine, orc, pkg, dtype, 520, 1024, m=m, seed=m)
 
 
+@pytest.mark.parametrize("dtype,n,k", [(13, 4096, 4096), (13, 14336, 4096), (13, 4096, 14336), (2, 4096, 4096),
+                                       (2, 1024, 4096)])
+def test_matvec_q5k_q40_model_shapes(engine, orc, pkg, dtype, n, k):
+    """Q5_K and Q4_0 (the other types the reference's GPU engine loads,
+    gpu.rs:316-318) at Llama-3-8B shapes."""
+    _check_matvec(engine, orc, pkg, dtype, n, k, seed=11)
+
+
 def test_matvec_unit_distribution(engine, orc, pkg):
-    for dtype in (12, 14, 8):
+    for dtype in (12, 14, 8, 13, 2):
         _check_matvec(engine, orc, pkg, dtype, 1000, 4096, dist="unit")
 
 

@@ -203,3 +203,31 @@ def test_model_error_paths(engine, pkg):
     with pytest.raises(B2QError):
         incomplete.finalize()  # tensors missing
     engine.check_device_error()
+
+
+@pytest.mark.parametrize("kind", ["q5_k_m", "q4_0"])
+def test_model_q5k_and_q40_weights(engine, orc, pkg, kind):
+    """Models whose projections are Q5_K (a Q5_K_M-style mix) or Q4_0: the
+    prompt pass (tensor cores) and decode steps stay within the fp64
+    tolerance; single-token steps run the captured per-kernel graph (the
+    persistent kernel takes Q4_K/Q6_K/Q8_0 rows) and equal the eager steps."""
+    from hf_llm_b200 import ggml, model, synth
+    base = model.q4_k_m_types()
+    if kind == "q5_k_m":
+        types = {r: (ggml.Q5_K if t == ggml.Q4_K else t) for r, t in base.items()}
+    else:
+        types = {r: ggml.Q4_0 for r in base}
+    t = synth.llama_tensors(TOY, types, 31, dist="unit")
+    dev = model.StandardNativeEngine.from_tensors(engine, TOY, t, max_seq=96)
+    eag = model.StandardNativeEngine.from_tensors(engine, TOY, t, max_seq=96, decode="eager")
+    ref = orc.Model(TOY, t, kv_capacity=96)
+    toks = list(range(2, 42))
+    a, e = dev.forward(toks, 0), eag.forward(toks, 0)
+    b = ref.forward_f64(toks, 0, kv_f16=True)
+    assert rel_l2(a, b) <= TOL, rel_l2(a, b)
+    for step, tok in enumerate((5, 77, 999)):
+        a, e = dev.forward([tok], 40 + step), eag.forward([tok], 40 + step)
+        b = ref.forward_f64([tok], 40 + step, kv_f16=True)
+        assert np.array_equal(a.view(np.uint32), e.view(np.uint32)), step
+        assert rel_l2(a, b) <= TOL, (step, rel_l2(a, b))
+    engine.check_device_error()
