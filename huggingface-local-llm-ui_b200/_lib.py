@@ -63,6 +63,9 @@ SIGNATURES = [
     ("b2q_forward", _I, [_VP, _U32P, _I, _I, _FP, _U32P]),
     ("b2q_forward_dev", _I, [_VP, _VP, _I, _I, _VP, _VP, _VP]),
     ("b2q_clear_state", _I, [_VP]),
+    ("b2q_forward_sample", _I, [_VP, _U32P, _I, _I, _F, _F, C.POINTER(C.c_uint64), _U32P]),
+    ("b2q_sampler_state", C.c_uint64, [C.c_uint64]),
+    ("b2q_sample_dev", _I, [_VP, _VP, _I, _F, _F, C.POINTER(C.c_uint64), _U32P, _VP]),
     ("b2q_gguf_open", _I, [C.c_char_p, C.POINTER(_VP)]),
     ("b2q_gguf_close", _I, [_VP]),
     ("b2q_gguf_version", _I, [_VP]),

@@ -159,6 +159,49 @@ cudaError_t launch_gemv(b2q_engine* e, GemvArgs& a, int epi, int mt, cudaStream_
   return mt == 1 ? launch_gemv_t<1, kEpiAdd>(e, a, st, pdl) : launch_gemv_t<2, kEpiAdd>(e, a, st, pdl);
 }
 
+b2q_status sample_core(b2q_engine* e, const float* logits_dev, int n, float temperature, float top_p,
+                       uint64_t* rng_state, uint32_t* token, cudaStream_t st) {
+  if (n <= 0) return set_error(B2Q_EINVAL, "sample: no logits");
+  cudaError_t err = cudaSuccess;
+  if (!e->ws_sample_out) err = cudaMalloc(&e->ws_sample_out, 2 * sizeof(uint32_t));
+  if (err == cudaSuccess && e->ws_sample_cap < (size_t)n) {
+    if (e->ws_sample) cudaFree(e->ws_sample);
+    e->ws_sample = nullptr;
+    e->ws_sample_cap = 0;
+    err = cudaMalloc(&e->ws_sample, sizeof(float) * (size_t)n);
+    if (err == cudaSuccess) e->ws_sample_cap = (size_t)n;
+  }
+  if (err != cudaSuccess) return cuda_error(err, "sample: workspace");
+  uint32_t out[2] = {0u, 0u};
+  if (temperature <= 1e-5f) {  // greedy: first index of the maximum, no draw
+    launch_counted(e, 1);
+    argmax_kernel<<<1, 1024, 0, st>>>(logits_dev, n, e->ws_sample_out);
+  } else {
+    // the draw the reference's next_f32 makes, kept only if the sampler uses it
+    uint64_t x = *rng_state;
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    const float u = (float)(uint32_t)(x >> 40) / (float)(1u << 24);
+    launch_counted(e, 1);
+    sample_top_p_kernel<<<1, kSampleThreads, 0, st>>>(logits_dev, n, temperature, top_p, u, e->ws_sample,
+                                                       e->ws_sample_out);
+    err = cudaGetLastError();
+    if (err == cudaSuccess) err = cudaMemcpyAsync(out, e->ws_sample_out, sizeof out, cudaMemcpyDeviceToHost, st);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+    if (err != cudaSuccess) return cuda_error(err, "sample");
+    if (out[1]) *rng_state = x;
+    *token = out[0];
+    return B2Q_OK;
+  }
+  err = cudaGetLastError();
+  if (err == cudaSuccess) err = cudaMemcpyAsync(out, e->ws_sample_out, sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+  if (err != cudaSuccess) return cuda_error(err, "sample");
+  *token = out[0];
+  return B2Q_OK;
+}
+
 }  // namespace b2q
 #include "tc_host.cuh"
 namespace b2q {
@@ -308,6 +351,11 @@ static void ws_free(b2q_engine* e) {
   xq_free(&e->ws_xq);
   xq_free(&e->ws_hq);
   tc_free(e);
+  if (e->ws_sample) cudaFree(e->ws_sample);
+  if (e->ws_sample_out) cudaFree(e->ws_sample_out);
+  e->ws_sample = nullptr;
+  e->ws_sample_out = nullptr;
+  e->ws_sample_cap = 0;
   e->ws_x = e->ws_y = e->ws_h = nullptr;
   e->ws_x_cap = e->ws_y_cap = e->ws_h_cap = 0;
 }
@@ -757,6 +805,17 @@ int b2q_debug_decode_dbg(void* host, size_t bytes) {
   return cudaMemcpyFromSymbol(host, b2q::g_dec_dbg, std::min(bytes, sizeof(b2q::g_dec_dbg))) == cudaSuccess ? 0 : 1;
 }
 #endif
+
+uint64_t b2q_sampler_state(uint64_t seed) { return seed == 0 ? 0x853C49E6748FEA9Bull : seed; }
+
+b2q_status b2q_sample_dev(b2q_engine* e, const float* logits_dev, int n, float temperature, float top_p,
+                          uint64_t* rng_state, uint32_t* token, void* stream) {
+  if (!e || !logits_dev || !rng_state || !token) return set_error(B2Q_EINVAL, "b2q_sample_dev: NULL argument");
+  std::lock_guard<std::mutex> lk(e->mu);
+  cudaSetDevice(e->device);
+  return sample_core(e, logits_dev, n, temperature, top_p, rng_state, token,
+                     stream ? (cudaStream_t)stream : e->stream);
+}
 
 b2q_status b2q_check_device_error(b2q_engine* e) {
   if (!e) return set_error(B2Q_EINVAL, "engine is NULL");

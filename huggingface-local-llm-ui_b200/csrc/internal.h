@@ -12,6 +12,7 @@
 #include "layer.cuh"
 #include "decode.cuh"
 #include "gemm_tc.cuh"
+#include "sample.cuh"
 
 namespace b2q {
 
@@ -55,6 +56,9 @@ struct b2q_engine {
   size_t ws_x_cap = 0, ws_y_cap = 0, ws_h_cap = 0;
   b2q::XQBuf ws_xq, ws_hq;
   b2q::TcScratch tc;
+  float* ws_sample = nullptr;       // [n] candidate weights of the sampler
+  uint32_t* ws_sample_out = nullptr; // token, drew
+  size_t ws_sample_cap = 0;
 };
 
 struct b2q_weight {
@@ -81,4 +85,8 @@ cudaError_t launch_quantize(b2q_engine* e, const float* x, int m, int k, XQBuf& 
 cudaError_t tc_matmul(b2q_engine* e, const float* x, int ldx, int m, int k, const b2q_weight* const* ws,
                       int nw, int epi, float* y, int ldy, const int* col0, cudaStream_t st, bool pdl);
 void tc_free(b2q_engine* e);
+// Next token from logits_dev [n] (SelfMadeSampler::sample); *rng_state is
+// advanced when the sampler draws.  Synchronous on `st`.
+b2q_status sample_core(b2q_engine* e, const float* logits_dev, int n, float temperature, float top_p,
+                       uint64_t* rng_state, uint32_t* token, cudaStream_t st);
 }  // namespace b2q

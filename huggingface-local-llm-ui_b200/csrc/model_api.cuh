@@ -413,6 +413,17 @@ b2q_status b2q_forward(b2q_model* M, const uint32_t* tokens, int n, int start, f
   return B2Q_OK;
 }
 
+b2q_status b2q_forward_sample(b2q_model* M, const uint32_t* tokens, int n, int start, float temperature,
+                              float top_p, uint64_t* rng_state, uint32_t* token) {
+  if (!M || !tokens || !rng_state || !token) return set_error(B2Q_EINVAL, "b2q_forward_sample: NULL argument");
+  if (!M->finalized) return set_error(B2Q_EINVAL, "b2q_forward_sample: model not finalized");
+  std::lock_guard<std::mutex> lk(M->eng->mu);
+  cudaSetDevice(M->eng->device);
+  b2q_status s = forward_impl(M, tokens, false, n, start, M->st);
+  if (s != B2Q_OK) return s;
+  return sample_core(M->eng, M->last_logits, M->c.n_vocab, temperature, top_p, rng_state, token, M->st);
+}
+
 b2q_status b2q_clear_state(b2q_model* M) {
   // The KV cache is indexed by absolute position, so clearing only resets
   // what the caller considers the current position; entries past it are

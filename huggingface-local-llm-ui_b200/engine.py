@@ -152,6 +152,16 @@ class CudaEngine:
         return y
 
     # -- device-pointer forms (torch tensors or raw addresses) -------------
+    def sample_dev(self, logits_ptr: int, n: int, temperature: float, top_p: float, state: int,
+                   stream: int = 0) -> tuple[int, int]:
+        """SelfMadeSampler::sample (inference.rs:1619-1681) on device logits:
+        (token, new sampler state)."""
+        st = C.c_uint64(state)
+        out = C.c_uint32()
+        check(lib().b2q_sample_dev(self._h, logits_ptr, n, temperature, top_p, C.byref(st), C.byref(out),
+                                   stream or None))
+        return int(out.value), int(st.value)
+
     def matmul_dev(self, buf: CudaWeightBuffer, x_ptr: int, y_ptr: int, m: int, n: int, k: int,
                    stream: int = 0) -> None:
         check(lib().b2q_matmul_dev(self._h, buf.handle, x_ptr, y_ptr, m, n, k, stream or None))

@@ -152,6 +152,36 @@ class StandardNativeEngine:
         check(lib().b2q_forward_dev(self._h, tokens_ptr, n, start_pos, logits_ptr or None,
                                     argmax_ptr or None, stream or None))
 
+    def forward_sample(self, tokens, start_pos: int, temperature: float, top_p: float, state: int) -> tuple[int, int]:
+        """forward, then SelfMadeSampler::sample (inference.rs:1619-1681) on
+        the device: (next token, new sampler state)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        st = C.c_uint64(state)
+        out = C.c_uint32()
+        check(lib().b2q_forward_sample(self._h, t.ctypes.data_as(C.POINTER(C.c_uint32)), t.size, start_pos,
+                                       temperature, top_p, C.byref(st), C.byref(out)))
+        return int(out.value), int(st.value)
+
+    def generate(self, prompt, max_tokens: int, temperature: float = 0.7, top_p: float = 0.9,
+                 seed: int = 0) -> list[int]:
+        """Prompt pass, then `max_tokens` sampled tokens (LocalLlm's generate
+        loop over forward + SelfMadeSampler).  temperature <= 1e-5 is greedy."""
+        prompt = list(prompt)
+        if not prompt:
+            raise ValueError("no tokens to prefill")
+        state = int(lib().b2q_sampler_state(seed))
+        nxt = None
+        for off in range(0, len(prompt), 128):
+            chunk = prompt[off:off + 128]
+            nxt, state = self.forward_sample(chunk, self.current_pos, temperature, top_p, state)
+            self.current_pos += len(chunk)
+        out = []
+        for _ in range(max_tokens):
+            out.append(nxt)
+            nxt, state = self.forward_sample([nxt], self.current_pos, temperature, top_p, state)
+            self.current_pos += 1
+        return out
+
     def clear_state(self) -> None:
         check(lib().b2q_clear_state(self._h))
         self.current_pos = 0

@@ -231,6 +231,26 @@ b2q_status b2q_forward(b2q_model* m, const uint32_t* tokens, int n_tokens, int s
 b2q_status b2q_forward_dev(b2q_model* m, const uint32_t* tokens_dev, int n_tokens,
                            int start_pos, float* logits_dev, uint32_t* argmax_dev, void* stream);
 
+/* The forward followed by SelfMadeSampler::sample (inference.rs:1619-1681)
+ * on the device: temperature <= 1e-5 is the greedy first maximum; otherwise
+ * the candidates within 14 * temperature of the max logit, weighed
+ * exp((v - max) / temperature), the smallest set of largest weights whose
+ * mass reaches top_p of the total, and a draw from it.  *rng_state is the
+ * sampler's xorshift64 state (b2q_sampler_state(seed) to start), advanced
+ * by one draw when the sampler draws; the next token goes to *token.  The
+ * token equals the reference's except when the draw falls within rounding
+ * of a boundary between two candidates (device exp, tree sums).  Under
+ * tensor parallelism every rank calls it with the same state. */
+b2q_status b2q_forward_sample(b2q_model* m, const uint32_t* tokens, int n_tokens, int start_pos,
+                              float temperature, float top_p, uint64_t* rng_state, uint32_t* token);
+
+/* Initial sampler state of SelfMadeSampler::new(seed) (inference.rs:1601-1607). */
+uint64_t b2q_sampler_state(uint64_t seed);
+
+/* The sampling step alone, on logits already on the device ([n] f32). */
+b2q_status b2q_sample_dev(b2q_engine* eng, const float* logits_dev, int n, float temperature, float top_p,
+                          uint64_t* rng_state, uint32_t* token, void* stream);
+
 /* Replaces StandardNativeEngine::clear_state (inference.rs:2688-2693). */
 b2q_status b2q_clear_state(b2q_model* m);
 

@@ -395,3 +395,82 @@ int oracle_forward_f64(void* p, const uint32_t* tokens, int64_t seq_len, int64_t
   free(x); free(normed); free(q); free(kk); free(vv); free(attn); free(proj); free(gate); free(up);
   return rc;
 }
+
+/* ------------------------------------------------------------------------- */
+/* SelfMadeSampler (inference.rs:1600-1681), restated: xorshift64 state,      */
+/* greedy first-max at temperature <= 1e-5, else candidates within           */
+/* 14 * temperature of the max logit, p = exp((v - max) / T) summed in index */
+/* order, sorted by p descending (the reference's unstable sort leaves ties  */
+/* unordered; here ties go by index), the shortest prefix reaching           */
+/* top_p * sum, and r = u * min(cum, sum) walked through the prefix.         */
+/* Returns the token; *drew = 1 when the random number was consumed.        */
+/* ------------------------------------------------------------------------- */
+typedef struct { uint32_t id; float p; } OCand;
+
+static int ocand_cmp(const void* a, const void* b) {
+  const OCand* x = (const OCand*)a;
+  const OCand* y = (const OCand*)b;
+  if (x->p > y->p) return -1;
+  if (x->p < y->p) return 1;
+  return x->id < y->id ? -1 : x->id > y->id ? 1 : 0;
+}
+
+float oracle_xorshift_f32(uint64_t* state) {
+  uint64_t x = *state;
+  x ^= x << 13;
+  x ^= x >> 7;
+  x ^= x << 17;
+  *state = x;
+  return (float)(uint32_t)(x >> 40) / (float)(1u << 24);
+}
+
+uint32_t oracle_sample(const float* logits, int64_t n, float temperature, float top_p, uint64_t* state,
+                       int* drew) {
+  *drew = 0;
+  if (temperature <= 1e-5f) {
+    int64_t best = 0;
+    float bv = -INFINITY;
+    for (int64_t i = 0; i < n; i++)
+      if (logits[i] > bv) { bv = logits[i]; best = i; }
+    return (uint32_t)best;
+  }
+  const float inv_temp = 1.0f / temperature;
+  float max_logit = -INFINITY;
+  for (int64_t i = 0; i < n; i++)
+    if (logits[i] > max_logit) max_logit = logits[i];
+  const float cutoff = max_logit - 14.0f * temperature;
+  OCand* c = (OCand*)malloc(sizeof(OCand) * (size_t)(n > 0 ? n : 1));
+  int64_t nc = 0;
+  float sum_prob = 0.0f;
+  for (int64_t i = 0; i < n; i++) {
+    if (logits[i] >= cutoff) {
+      const float p = expf((logits[i] - max_logit) * inv_temp);
+      c[nc].id = (uint32_t)i;
+      c[nc].p = p;
+      nc++;
+      sum_prob += p;
+    }
+  }
+  if (nc == 0 || sum_prob <= 0.0f) {
+    free(c);
+    return 0;
+  }
+  qsort(c, (size_t)nc, sizeof(OCand), ocand_cmp);
+  const float target = sum_prob * top_p;
+  float cum = 0.0f;
+  int64_t keep = nc;
+  for (int64_t i = 0; i < nc; i++) {
+    cum += c[i].p;
+    if (cum >= target) { keep = i + 1; break; }
+  }
+  *drew = 1;
+  const float r = oracle_xorshift_f32(state) * (cum < sum_prob ? cum : sum_prob);
+  float acc = 0.0f;
+  uint32_t tok = c[0].id;
+  for (int64_t i = 0; i < keep; i++) {
+    acc += c[i].p;
+    if (r <= acc) { tok = c[i].id; break; }
+  }
+  free(c);
+  return tok;
+}

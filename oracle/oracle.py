@@ -59,8 +59,23 @@ def lib():
                                          C.c_int, f64p]
         L.oracle_rope_table.argtypes = [C.c_void_p, C.c_int]
         L.oracle_rope_table.restype = f32p
+        L.oracle_xorshift_f32.argtypes = [C.POINTER(C.c_uint64)]
+        L.oracle_xorshift_f32.restype = C.c_float
+        L.oracle_sample.argtypes = [f32p, C.c_int64, C.c_float, C.c_float, C.POINTER(C.c_uint64),
+                                    C.POINTER(C.c_int)]
+        L.oracle_sample.restype = C.c_uint32
         _lib = L
     return _lib
+
+
+def sample(logits: np.ndarray, temperature: float, top_p: float, state: int) -> tuple[int, int, bool]:
+    """SelfMadeSampler::sample (inference.rs:1619-1681): (token, new rng
+    state, whether the random number was drawn)."""
+    v = np.ascontiguousarray(logits, dtype=np.float32).reshape(-1)
+    st = C.c_uint64(state if state != 0 else 0x853C49E6748FEA9B)
+    drew = C.c_int(0)
+    tok = lib().oracle_sample(_p(v, C.c_float), v.size, temperature, top_p, C.byref(st), C.byref(drew))
+    return int(tok), int(st.value), bool(drew.value)
 
 
 def _p(a: np.ndarray, ct):
