@@ -22,6 +22,11 @@ class B2QError(RuntimeError):
         self.status = status
 
 
+class GdnConfig(C.Structure):
+    _fields_ = [("n_k_heads", C.c_int), ("n_v_heads", C.c_int), ("d_k", C.c_int), ("d_v", C.c_int),
+                ("conv_kernel", C.c_int), ("eps", C.c_float)]
+
+
 class ModelConfig(C.Structure):
     _fields_ = [("n_layers", C.c_int), ("n_embd", C.c_int), ("n_heads", C.c_int),
                 ("n_kv_heads", C.c_int), ("head_dim", C.c_int), ("n_ff", C.c_int),
@@ -66,6 +71,7 @@ SIGNATURES = [
     ("b2q_forward_sample", _I, [_VP, _U32P, _I, _I, _F, _F, C.POINTER(C.c_uint64), _U32P]),
     ("b2q_sampler_state", C.c_uint64, [C.c_uint64]),
     ("b2q_sample_dev", _I, [_VP, _VP, _I, _F, _F, C.POINTER(C.c_uint64), _U32P, _VP]),
+    ("b2q_gdn_step_dev", _I, [_VP, C.POINTER(GdnConfig), _I] + [_VP] * 12),
     ("b2q_gguf_open", _I, [C.c_char_p, C.POINTER(_VP)]),
     ("b2q_gguf_close", _I, [_VP]),
     ("b2q_gguf_version", _I, [_VP]),

@@ -351,6 +351,9 @@ static void ws_free(b2q_engine* e) {
   xq_free(&e->ws_xq);
   xq_free(&e->ws_hq);
   tc_free(e);
+  if (e->ws_gdn) cudaFree(e->ws_gdn);
+  e->ws_gdn = nullptr;
+  e->ws_gdn_cap = 0;
   if (e->ws_sample) cudaFree(e->ws_sample);
   if (e->ws_sample_out) cudaFree(e->ws_sample_out);
   e->ws_sample = nullptr;
@@ -805,6 +808,54 @@ int b2q_debug_decode_dbg(void* host, size_t bytes) {
   return cudaMemcpyFromSymbol(host, b2q::g_dec_dbg, std::min(bytes, sizeof(b2q::g_dec_dbg))) == cudaSuccess ? 0 : 1;
 }
 #endif
+
+b2q_status b2q_gdn_step_dev(b2q_engine* e, const b2q_gdn_config* cfg, int n_tokens, const float* qkv,
+                            const float* z, const float* alpha, const float* beta, const float* conv_w,
+                            const float* ssm_a, const float* dt_bias, const float* ssm_norm, float* conv_state,
+                            float* ssm_state, float* y, void* stream) {
+  if (!e || !cfg || !qkv || !z || !alpha || !beta || !conv_w || !ssm_a || !dt_bias || !ssm_norm || !conv_state ||
+      !ssm_state || !y)
+    return set_error(B2Q_EINVAL, "b2q_gdn_step_dev: NULL argument");
+  const b2q_gdn_config c = *cfg;
+  if (n_tokens <= 0) return set_error(B2Q_EINVAL, "b2q_gdn_step_dev: n_tokens must be positive");
+  if (c.d_k != 128) return set_error(B2Q_EUNSUP, "b2q_gdn_step_dev: d_k %d (128 is supported)", c.d_k);
+  if (c.d_v <= 0 || c.d_v > 512 || c.n_k_heads <= 0 || c.n_v_heads <= 0 || c.n_v_heads % c.n_k_heads ||
+      c.conv_kernel < 1)
+    return set_error(B2Q_EINVAL, "b2q_gdn_step_dev: bad shape (n_k %d, n_v %d, d_v %d, kernel %d)", c.n_k_heads,
+                     c.n_v_heads, c.d_v, c.conv_kernel);
+  if (reinterpret_cast<uintptr_t>(ssm_state) % 16)
+    return set_error(B2Q_EINVAL, "b2q_gdn_step_dev: ssm_state must be 16-byte aligned");
+  const int channels = 2 * c.n_k_heads * c.d_k + c.n_v_heads * c.d_v;
+  const int vdim = c.n_v_heads * c.d_v;
+  std::lock_guard<std::mutex> lk(e->mu);
+  cudaSetDevice(e->device);
+  cudaStream_t st = stream ? (cudaStream_t)stream : e->stream;
+  cudaError_t err = cudaSuccess;
+  if (e->ws_gdn_cap < (size_t)channels) {
+    if (e->ws_gdn) {
+      err = cudaStreamSynchronize(st);
+      cudaFree(e->ws_gdn);
+    }
+    e->ws_gdn = nullptr;
+    e->ws_gdn_cap = 0;
+    if (err == cudaSuccess) err = cudaMalloc(&e->ws_gdn, sizeof(float) * (size_t)channels);
+    if (err != cudaSuccess) return cuda_error(err, "b2q_gdn_step_dev: workspace");
+    e->ws_gdn_cap = (size_t)channels;
+  }
+  // the recurrence runs token by token
+  for (int t = 0; t < n_tokens && err == cudaSuccess; ++t) {
+    launch_counted(e, 2);
+    gdn_conv_kernel<<<(channels + 255) / 256, 256, 0, st>>>(qkv + (size_t)t * channels, conv_state, conv_w,
+                                                            channels, c.conv_kernel, e->ws_gdn);
+    gdn_head_kernel<<<c.n_v_heads, kGdnThreads, 0, st>>>(e->ws_gdn, ssm_state, z + (size_t)t * vdim,
+                                                          alpha + (size_t)t * c.n_v_heads,
+                                                          beta + (size_t)t * c.n_v_heads, ssm_a, dt_bias, ssm_norm,
+                                                          c.n_k_heads, c.d_k, c.d_v, c.eps, y + (size_t)t * vdim);
+    err = cudaGetLastError();
+  }
+  if (err != cudaSuccess) return cuda_error(err, "b2q_gdn_step_dev");
+  return B2Q_OK;
+}
 
 uint64_t b2q_sampler_state(uint64_t seed) { return seed == 0 ? 0x853C49E6748FEA9Bull : seed; }
 

@@ -13,6 +13,7 @@
 #include "decode.cuh"
 #include "gemm_tc.cuh"
 #include "sample.cuh"
+#include "gdn.cuh"
 
 namespace b2q {
 
@@ -56,6 +57,8 @@ struct b2q_engine {
   size_t ws_x_cap = 0, ws_y_cap = 0, ws_h_cap = 0;
   b2q::XQBuf ws_xq, ws_hq;
   b2q::TcScratch tc;
+  float* ws_gdn = nullptr;          // [channels] Gated DeltaNet convolution output
+  size_t ws_gdn_cap = 0;
   float* ws_sample = nullptr;       // [n] candidate weights of the sampler
   uint32_t* ws_sample_out = nullptr; // token, drew
   size_t ws_sample_cap = 0;

@@ -251,6 +251,32 @@ uint64_t b2q_sampler_state(uint64_t seed);
 b2q_status b2q_sample_dev(b2q_engine* eng, const float* logits_dev, int n, float temperature, float top_p,
                           uint64_t* rng_state, uint32_t* token, void* stream);
 
+/* ---- Gated DeltaNet state update (the reference's Qwen3.5 hybrid model) ---- */
+typedef struct {
+  int n_k_heads;   /* qwen35.ssm.group_count: q/k heads */
+  int n_v_heads;   /* qwen35.ssm.time_step_rank: value heads (a multiple of n_k_heads) */
+  int d_k;         /* qwen35.ssm.state_size (128) */
+  int d_v;         /* qwen35.ssm.inner_size / n_v_heads (<= 512) */
+  int conv_kernel; /* qwen35.ssm.conv_kernel */
+  float eps;       /* the model's RMS epsilon (also the L2-norm epsilon) */
+} b2q_gdn_config;
+
+/* The Gated DeltaNet mixer core of Qwen35Mixer::GatedDeltaNet
+ * (inference.rs:2281-2374, ssm_head_step_avx2 :1535-1583) for n_tokens
+ * tokens in order, on the device: causal convolution with state and SiLU
+ * over the attn_qkv output, L2 norm of q and k per head, the per-head state
+ * update S = g S + ((v - g S k) beta) k^T with o = S q / sqrt(d_k), then
+ * RMS norm * ssm_norm * silu(z).  Inputs per token: qkv [2 n_k d_k + n_v d_v],
+ * z [n_v d_v], alpha / beta [n_v] (the quad projection's outputs, token-major);
+ * weights conv_w [channels][conv_kernel], ssm_a / dt_bias [n_v], ssm_norm
+ * [d_v]; state conv_state [channels][conv_kernel - 1] and ssm_state
+ * [n_v][d_v][d_k] (16-byte aligned) are read and updated; y [n_tokens][n_v d_v].
+ * All device pointers; asynchronous on `stream`. */
+b2q_status b2q_gdn_step_dev(b2q_engine* eng, const b2q_gdn_config* cfg, int n_tokens, const float* qkv,
+                            const float* z, const float* alpha, const float* beta, const float* conv_w,
+                            const float* ssm_a, const float* dt_bias, const float* ssm_norm, float* conv_state,
+                            float* ssm_state, float* y, void* stream);
+
 /* Replaces StandardNativeEngine::clear_state (inference.rs:2688-2693). */
 b2q_status b2q_clear_state(b2q_model* m);
 

@@ -474,3 +474,74 @@ uint32_t oracle_sample(const float* logits, int64_t n, float temperature, float 
   free(c);
   return tok;
 }
+
+/* ------------------------------------------------------------------------- */
+/* Gated DeltaNet mixer core of Qwen35Mixer::GatedDeltaNet, restated         */
+/* (inference.rs:2296-2374 with ssm_head_step_avx2 :1535-1583, silu /        */
+/* sigmoid / softplus :1481-1499, l2_norm_inplace :1525-1532): causal        */
+/* convolution with state + SiLU, L2 norm of q and k per head, per value     */
+/* head the state update and output, RMS norm * ssm_norm * silu(z), token    */
+/* by token.  Dot products are plain sequential f32 sums (the reference's    */
+/* AVX2 lane order differs by rounding only).                                */
+/* ------------------------------------------------------------------------- */
+static float o_silu(float x) { return x / (1.0f + expf(-x)); }
+static float o_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+static float o_softplus(float x) { return x > 20.0f ? x : x < -20.0f ? expf(x) : logf(1.0f + expf(x)); }
+
+int oracle_gdn_step(int n_k, int n_v, int d_k, int d_v, int K, float eps, int n_tokens, const float* qkv,
+                    const float* z, const float* alpha, const float* beta, const float* conv_w,
+                    const float* ssm_a, const float* dt_bias, const float* ssm_norm, float* conv_state,
+                    float* S, float* y) {
+  const int q_dim = n_k * d_k, channels = 2 * q_dim + n_v * d_v, hist = K - 1, vdim = n_v * d_v;
+  const float scale = 1.0f / sqrtf((float)d_k);
+  float* c = (float*)malloc(sizeof(float) * (size_t)channels);
+  if (!c) return 1;
+  for (int t = 0; t < n_tokens; t++) {
+    const float* x = qkv + (size_t)t * channels;
+    for (int ch = 0; ch < channels; ch++) {
+      float* st = conv_state + (size_t)ch * hist;
+      const float* w = conv_w + (size_t)ch * K;
+      float acc = 0.0f;
+      for (int k = 0; k < hist; k++) acc += st[k] * w[k];
+      acc += x[ch] * w[hist];
+      c[ch] = o_silu(acc);
+      for (int k = 0; k + 1 < hist; k++) st[k] = st[k + 1];
+      if (hist > 0) st[hist - 1] = x[ch];
+    }
+    for (int h = 0; h < 2 * n_k; h++) {  /* q heads then k heads */
+      float* v = c + (size_t)h * d_k;
+      float ss = 0.0f;
+      for (int i = 0; i < d_k; i++) ss += v[i] * v[i];
+      const float inv = 1.0f / sqrtf(ss + eps);
+      for (int i = 0; i < d_k; i++) v[i] *= inv;
+    }
+    for (int vh = 0; vh < n_v; vh++) {
+      const int kh = vh % n_k;
+      const float* q = c + (size_t)kh * d_k;
+      const float* kk = c + (size_t)q_dim + (size_t)kh * d_k;
+      const float* vv = c + (size_t)2 * q_dim + (size_t)vh * d_v;
+      const float b = o_sigmoid(beta[(size_t)t * n_v + vh]);
+      const float g = expf(o_softplus(alpha[(size_t)t * n_v + vh] + dt_bias[vh]) * ssm_a[vh]);
+      float* out = y + (size_t)t * vdim + (size_t)vh * d_v;
+      for (int i = 0; i < d_v; i++) {
+        float* row = S + ((size_t)vh * d_v + i) * d_k;
+        float sk = 0.0f;
+        for (int j = 0; j < d_k; j++) sk += row[j] * kk[j];
+        const float d = (vv[i] - g * sk) * b;
+        float o = 0.0f;
+        for (int j = 0; j < d_k; j++) {
+          row[j] = fmaf(d, kk[j], g * row[j]);
+          o += row[j] * q[j];
+        }
+        out[i] = o * scale;
+      }
+      float ss = 0.0f;
+      for (int i = 0; i < d_v; i++) ss += out[i] * out[i];
+      const float inv = 1.0f / sqrtf(ss / (float)d_v + eps);
+      const float* zz = z + (size_t)t * vdim + (size_t)vh * d_v;
+      for (int i = 0; i < d_v; i++) out[i] = out[i] * inv * ssm_norm[i] * o_silu(zz[i]);
+    }
+  }
+  free(c);
+  return 0;
+}

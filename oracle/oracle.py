@@ -64,6 +64,7 @@ def lib():
         L.oracle_sample.argtypes = [f32p, C.c_int64, C.c_float, C.c_float, C.POINTER(C.c_uint64),
                                     C.POINTER(C.c_int)]
         L.oracle_sample.restype = C.c_uint32
+        L.oracle_gdn_step.argtypes = [C.c_int] * 5 + [C.c_float, C.c_int] + [f32p] * 11
         _lib = L
     return _lib
 
@@ -76,6 +77,24 @@ def sample(logits: np.ndarray, temperature: float, top_p: float, state: int) -> 
     drew = C.c_int(0)
     tok = lib().oracle_sample(_p(v, C.c_float), v.size, temperature, top_p, C.byref(st), C.byref(drew))
     return int(tok), int(st.value), bool(drew.value)
+
+
+def gdn_step(cfg: dict, qkv, z, alpha, beta, conv_w, ssm_a, dt_bias, ssm_norm, conv_state, ssm_state):
+    """Gated DeltaNet mixer core (inference.rs:2296-2374) over len(qkv) tokens:
+    returns (y, new conv_state, new ssm_state)."""
+    f = lambda a: np.ascontiguousarray(a, dtype=np.float32)
+    qkv, z, alpha, beta = f(qkv), f(z), f(alpha), f(beta)
+    cs, ss = f(conv_state).copy(), f(ssm_state).copy()
+    n_tokens = qkv.shape[0]
+    y = np.zeros((n_tokens, cfg["n_v_heads"] * cfg["d_v"]), np.float32)
+    args = [f(conv_w), f(ssm_a), f(dt_bias), f(ssm_norm)]
+    rc = lib().oracle_gdn_step(cfg["n_k_heads"], cfg["n_v_heads"], cfg["d_k"], cfg["d_v"], cfg["conv_kernel"],
+                               cfg["eps"], n_tokens, _p(qkv, C.c_float), _p(z, C.c_float), _p(alpha, C.c_float),
+                               _p(beta, C.c_float), *[_p(a, C.c_float) for a in args], _p(cs, C.c_float),
+                               _p(ss, C.c_float), _p(y, C.c_float))
+    if rc != 0:
+        raise MemoryError("oracle_gdn_step")
+    return y, cs, ss
 
 
 def _p(a: np.ndarray, ct):
