@@ -42,7 +42,7 @@ namespace b2q {
 constexpr int kTcM = 128;          // weight rows per tile (UMMA M)
 constexpr int kTcK = 64;           // k per pipeline stage
 constexpr int kTcStagesMax = 4;
-constexpr int kTcNMax = 128;       // tokens per tile (UMMA N)
+constexpr int kTcNMax = 256;       // tokens per tile (UMMA N)
 constexpr int kTcDequantWarps = 16;  // 512 threads: (tile row, quarter) -> 16 weights per stage
 constexpr int kTcThreads = (kTcDequantWarps + 2) * 32;
 constexpr int kTcABytes = kTcM * kTcK * 2;  // one f16 image of the weight tile: 16 KB

@@ -23,7 +23,7 @@ struct LayerW {
   __half *kc = nullptr, *vc = nullptr;
 };
 
-constexpr int kPrefillChunk = 128;  // tokens per forward pass of a long prompt (one tensor-core N tile)
+constexpr int kPrefillChunk = 256;  // tokens per forward pass of a long prompt (one tensor-core N tile)
 
 }  // namespace b2q
 

@@ -8,7 +8,7 @@ struct TcPlan {
   int N, tiles, mpad, KS, rowtiles, splits;
 };
 
-// Token tiles of at most 128 (balanced), k-stages of 64, and a split-K
+// Token tiles of at most 256 (balanced), k-stages of 64, and a split-K
 // factor of one split per 16 stages (at most 8).  The split depends on k
 // only, so every output element is summed in the same order whatever the
 // number of rows (a tensor-parallel shard gives the same bits as the whole

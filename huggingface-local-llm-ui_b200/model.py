@@ -171,8 +171,8 @@ class StandardNativeEngine:
             raise ValueError("no tokens to prefill")
         state = int(lib().b2q_sampler_state(seed))
         nxt = None
-        for off in range(0, len(prompt), 128):
-            chunk = prompt[off:off + 128]
+        for off in range(0, len(prompt), 256):
+            chunk = prompt[off:off + 256]
             nxt, state = self.forward_sample(chunk, self.current_pos, temperature, top_p, state)
             self.current_pos += len(chunk)
         out = []
@@ -186,7 +186,7 @@ class StandardNativeEngine:
         check(lib().b2q_clear_state(self._h))
         self.current_pos = 0
 
-    def generate_greedy(self, prompt, max_tokens: int, prefill_chunk: int = 128) -> list[int]:
+    def generate_greedy(self, prompt, max_tokens: int, prefill_chunk: int = 256) -> list[int]:
         """Chunked prefill, then greedy decode of `max_tokens` tokens."""
         prompt = list(prompt)
         if not prompt:

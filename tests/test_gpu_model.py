@@ -53,7 +53,7 @@ def test_gqa_ratios(engine, orc, pkg, gqa):
 
 
 def test_long_prompt_chunks_and_splits(engine, orc, pkg):
-    """A prompt longer than two forward chunks (128 tokens each, the last one
+    """A prompt longer than one forward chunk (256 tokens; the second one
     ragged) and than one attention split (64 keys) exercises the chunked
     prefill and the split merge."""
     dev, ref = _pair(engine, orc, pkg, dict(TOY, n_layers=1), seed=7, max_seq=512)

@@ -46,7 +46,7 @@ def main() -> int:
     def build(decode):
         obj = [model.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
-        mm = model.StandardNativeEngine(eng, cfg, max_seq=160, tp_rank=rank, tp_size=world, tp_id=obj[0],
+        mm = model.StandardNativeEngine(eng, cfg, max_seq=300, tp_rank=rank, tp_size=world, tp_id=obj[0],
                                         decode=decode)
         for spec in specs:
             name, t, dims, _ = spec
@@ -63,10 +63,10 @@ def main() -> int:
     ref = None
     if rank == 0:
         full = synth.llama_tensors(cfg, model.q4_k_m_types(), 9, dist="unit")
-        ref = model.StandardNativeEngine.from_tensors(eng, cfg, full, max_seq=160, decode="eager")
+        ref = model.StandardNativeEngine.from_tensors(eng, cfg, full, max_seq=300, decode="eager")
     rng = np.random.default_rng(4)
-    # 140 tokens: a 128-token chunk (tensor cores) and a 12-token chunk (GEMV)
-    prompt = rng.integers(0, cfg["n_vocab"], 140).tolist()
+    # 270 tokens: a 256-token chunk (tensor cores) and a 14-token chunk (GEMV)
+    prompt = rng.integers(0, cfg["n_vocab"], 270).tolist()
     steps, same, close, pos = [], True, True, 0
     tok_list = [prompt]
     for s in range(6):
