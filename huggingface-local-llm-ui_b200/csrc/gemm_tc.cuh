@@ -164,9 +164,10 @@ __device__ __forceinline__ uint2 ldg_nc64(const void* p) {
   return v;
 }
 
+template <int DT>
 __device__ __forceinline__ TcRaw tc_load(const WeightDev& w, int64_t R, int qq, int ks) {
   const TileLayout& L = w.L;
-  const int dt = L.dtype;
+  constexpr int dt = DT;
   const int hf = qq >> 1, e8 = 8 * (qq & 1);
   const int u = tc_unit(dt, ks, hf);
   TcRaw x;
@@ -214,7 +215,9 @@ __device__ __forceinline__ float small_uint_f(uint32_t bits) {
 // (inference.rs:1367-1458); each value is d*sc*q - dmin*m with the products
 // d*sc, dmin*m in f32 as the reference forms them and the last step fused
 // (one rounding), which the hi/lo split then carries to ~2^-22.
-__device__ __forceinline__ void tc_convert(const TcRaw& x, int dt, int r, int qq, int ks, uint8_t* img) {
+template <int DT>
+__device__ __forceinline__ void tc_convert(const TcRaw& x, int r, int qq, int ks, uint8_t* img) {
+  constexpr int dt = DT;
   const int hf = qq >> 1, e8 = 8 * (qq & 1);
   const int u = tc_unit(dt, ks, hf);
   // k offsets (within the stage) of the two 8-element outputs
@@ -294,6 +297,37 @@ __device__ __forceinline__ void tc_convert(const TcRaw& x, int dt, int r, int qq
   st_img8(img, kTcABytes, r, k1, kTcM, v1);
 }
 
+// The dequantising warps' loop: raw bytes of the next kTcPrefetch stages are
+// in flight in registers while the current one is converted.
+template <int DT>
+__device__ __forceinline__ void tc_produce(const TcArgs& a, int row0, int ks0, int nst, int S, uint8_t* As,
+                                           uint64_t* empty, uint64_t* a_full, volatile int* s_ok) {
+  const int d = threadIdx.x, lane = threadIdx.x & 31;
+  const int r = d & (kTcM - 1), qq = d >> 7;
+  const int64_t R = (int64_t)row0 + r;
+  TcRaw raw[kTcPrefetch];
+#pragma unroll
+  for (int j = 0; j < kTcPrefetch; ++j)
+    if (j < nst) raw[j] = tc_load<DT>(a.w, R, qq, ks0 + j);
+  for (int i0 = 0; i0 < nst; i0 += kTcPrefetch) {
+#pragma unroll
+    for (int j = 0; j < kTcPrefetch; ++j) {
+      const int i = i0 + j;
+      if (i >= nst || !*s_ok) break;
+      const int s = i % S;
+      if (i >= S && !mbar_wait_bounded(&empty[s], ((i / S) - 1) & 1)) {
+        *s_ok = 0;
+        break;
+      }
+      tc_convert<DT>(raw[j], r, qq, ks0 + i, As + (size_t)s * 2 * kTcABytes);
+      if (i + kTcPrefetch < nst) raw[j] = tc_load<DT>(a.w, R, qq, ks0 + i + kTcPrefetch);
+      fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[s]);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ TcArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t a_full[kTcStagesMax], b_full[kTcStagesMax], empty[kTcStagesMax], done_bar;
@@ -335,33 +369,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   const uint32_t tmem = tmem_base;
 
   if (warp < kTcDequantWarps) {
-    // ---- weight producers ----
-    const int d = threadIdx.x;
-    const int r = d & (kTcM - 1), qq = d >> 7;
-    const int64_t R = (int64_t)row0 + r;
-    const int dt = a.w.L.dtype;
-    // raw bytes of the next kTcPrefetch stages are in flight in registers
-    // while the current one is converted
-    TcRaw raw[kTcPrefetch];
-#pragma unroll
-    for (int j = 0; j < kTcPrefetch; ++j)
-      if (j < nst) raw[j] = tc_load(a.w, R, qq, ks0 + j);
-    for (int i0 = 0; i0 < nst; i0 += kTcPrefetch) {
-#pragma unroll
-      for (int j = 0; j < kTcPrefetch; ++j) {
-        const int i = i0 + j;
-        if (i >= nst || !*s_ok) break;
-        const int s = i % S;
-        if (i >= S && !mbar_wait_bounded(&empty[s], ((i / S) - 1) & 1)) {
-          *s_ok = 0;
-          break;
-        }
-        tc_convert(raw[j], dt, r, qq, ks0 + i, As + (size_t)s * 2 * kTcABytes);
-        if (i + kTcPrefetch < nst) raw[j] = tc_load(a.w, R, qq, ks0 + i + kTcPrefetch);
-        fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[s]);
-      }
+    // ---- weight producers (one instantiation per GGML type) ----
+    switch (a.w.L.dtype) {
+      case kQ4_K: tc_produce<kQ4_K>(a, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
+      case kQ6_K: tc_produce<kQ6_K>(a, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
+      case kQ8_0: tc_produce<kQ8_0>(a, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
+      case kQ5_K: tc_produce<kQ5_K>(a, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
+      default: tc_produce<kQ4_0>(a, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
     }
   } else if (warp == kTcDequantWarps) {
     // ---- activation producer ----
