@@ -484,49 +484,56 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 
 // X f32 [m][ldx] (k valid columns) -> f16 stage images [token tile][k-stage]
 // [hi, lo][N * 64] (zero beyond m and k) and the per-token inverse scales
-// inv[t] = 2^(e-14), amax(x_t) = f * 2^e, f in [0.5, 1).  One block of 8
-// warps per 8 tokens.
+// inv[t] = 2^(e-14), amax(x_t) = f * 2^e, f in [0.5, 1).  One block per token
+// (padding tokens write zeros): the row is read twice, coalesced (float4 when
+// the rows are 16-byte aligned), for its maximum and for the image.
 __global__ void tc_act_kernel(const float* __restrict__ x, int ldx, int m, int k, int KS, int N,
                               __half* __restrict__ img, float* __restrict__ inv) {
   pdl_wait();
-  __shared__ float s_scale[8];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tb = blockIdx.x * 8;  // first token of this block
-  {
-    const int t = tb + warp;
-    float mx = 0.0f;
-    if (t < m)
-      for (int i = lane; i < k; i += 32) mx = fmaxf(mx, fabsf(x[(size_t)t * ldx + i]));
-    mx = warp_max(mx);
-    float sc = 1.0f, iv = 1.0f;
-    if (mx > 0.0f && mx <= 3.0e38f) {
-      int e;
-      frexpf(mx, &e);
-      sc = ldexpf(1.0f, 14 - e);
-      iv = ldexpf(1.0f, e - 14);
-    }
-    if (lane == 0) {
-      s_scale[warp] = sc;
-      if (t < m) inv[t] = iv;
+  __shared__ float red[32];
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool live = t < m;
+  const float* xr = x + (size_t)(live ? t : 0) * ldx;
+  const bool v4 = ((reinterpret_cast<uintptr_t>(x) | ((size_t)ldx * 4)) & 15) == 0;
+  float mx = 0.0f;
+  if (live) {
+    if (v4) {
+      for (int i = 4 * threadIdx.x; i < k; i += 4 * blockDim.x) {
+        const float4 q = *reinterpret_cast<const float4*>(xr + i);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w))));
+      }
+    } else {
+      for (int i = threadIdx.x; i < k; i += blockDim.x) mx = fmaxf(mx, fabsf(xr[i]));
     }
   }
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
   __syncthreads();
-  // chunks of 8 k per token: (stage ks, k8 index 0..7); thread -> (token tb + (id & 7), chunk id >> 3)
-  const int nch = KS * 8;
-  const int tile = tb / N, tt0 = tb - tile * N;
-  for (int id = threadIdx.x; id < nch * 8; id += blockDim.x) {
-    const int tr = id & 7, ch = id >> 3;
-    const int t = tb + tr;
-    const int ks = ch >> 3, kk = (ch & 7) * 8;
-    const int k0 = ks * kTcK + kk;
+  mx = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+  mx = warp_max(mx);
+  float sc = 1.0f, iv = 1.0f;
+  if (mx > 0.0f && mx <= 3.0e38f) {
+    int e;
+    frexpf(mx, &e);
+    sc = ldexpf(1.0f, 14 - e);
+    iv = ldexpf(1.0f, e - 14);
+  }
+  if (threadIdx.x == 0 && live) inv[t] = iv;
+  const int tile = t / N, tt = t - tile * N;
+  // chunks of 8 k: (stage ks, k8 index 0..7)
+  for (int ch = threadIdx.x; ch < KS * 8; ch += blockDim.x) {
+    const int ks = ch >> 3, kk = (ch & 7) * 8, k0 = ks * kTcK + kk;
     float v[8];
+    if (live && v4 && k0 + 8 <= k) {
+      const float4 a = *reinterpret_cast<const float4*>(xr + k0), b = *reinterpret_cast<const float4*>(xr + k0 + 4);
+      v[0] = a.x * sc; v[1] = a.y * sc; v[2] = a.z * sc; v[3] = a.w * sc;
+      v[4] = b.x * sc; v[5] = b.y * sc; v[6] = b.z * sc; v[7] = b.w * sc;
+    } else {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int kx = k0 + e;
-      v[e] = (t < m && kx < k) ? x[(size_t)t * ldx + kx] * s_scale[tr] : 0.0f;
+      for (int e = 0; e < 8; ++e) v[e] = (live && k0 + e < k) ? xr[k0 + e] * sc : 0.0f;
     }
     uint8_t* stage = reinterpret_cast<uint8_t*>(img) + ((size_t)tile * KS + ks) * (size_t)tc_b_bytes(N);
-    st_img8(stage, N * kTcK * 2, tt0 + tr, kk, N, v);
+    st_img8(stage, N * kTcK * 2, tt, kk, N, v);
   }
   pdl_launch_dependents();
 }

@@ -110,7 +110,7 @@ cudaError_t tc_matmul(b2q_engine* e, const float* x, int ldx, int m, int k, cons
   {
     launch_counted(e, 1);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p0.mpad / 8);
+    cfg.gridDim = dim3(p0.mpad);
     cfg.blockDim = dim3(256);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
