@@ -83,15 +83,23 @@ __host__ __device__ inline uint32_t umma_idesc_f16(int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
 }
 
+constexpr int kTcMaxSegs = 3;
+
+// Up to kTcMaxSegs weights with the same k (q, k, v) in one launch: segment
+// i owns row tiles [rt[i], rt[i+1]) of gridDim.x and columns [c0[i], c0[i] +
+// n of weight i) of the partial sums.
 struct TcArgs {
-  WeightDev w;
+  WeightDev w[kTcMaxSegs];
+  int rt[kTcMaxSegs + 1];
+  int c0[kTcMaxSegs];
+  int nseg;
   const __half* xh;    // activation images [token tile][k-stage][N * 64]
   int KS;              // k-stages of the whole row (kpad / 64)
   int N;               // tokens per tile (multiple of 16, <= 256)
   int m;               // valid tokens
-  int n;               // valid rows
+  int ncol;            // columns of the partial sums (all segments)
   int splits;          // split-K factor (gridDim.z)
-  float* part;         // [split][mpad][n] partial sums (scaled activations)
+  float* part;         // [split][mpad][ncol] partial sums (scaled activations)
   int mpad;            // token tiles * N
   int stages;          // pipeline depth (<= kTcStagesMax)
 };
@@ -300,7 +308,7 @@ __device__ __forceinline__ void tc_convert(const TcRaw& x, int r, int qq, int ks
 // The dequantising warps' loop: raw bytes of the next kTcPrefetch stages are
 // in flight in registers while the current one is converted.
 template <int DT>
-__device__ __forceinline__ void tc_produce(const TcArgs& a, int row0, int ks0, int nst, int S, uint8_t* As,
+__device__ __forceinline__ void tc_produce(const WeightDev& w, int row0, int ks0, int nst, int S, uint8_t* As,
                                            uint64_t* empty, uint64_t* a_full, volatile int* s_ok) {
   const int d = threadIdx.x, lane = threadIdx.x & 31;
   const int r = d & (kTcM - 1), qq = d >> 7;
@@ -308,7 +316,7 @@ __device__ __forceinline__ void tc_produce(const TcArgs& a, int row0, int ks0, i
   TcRaw raw[kTcPrefetch];
 #pragma unroll
   for (int j = 0; j < kTcPrefetch; ++j)
-    if (j < nst) raw[j] = tc_load<DT>(a.w, R, qq, ks0 + j);
+    if (j < nst) raw[j] = tc_load<DT>(w, R, qq, ks0 + j);
   for (int i0 = 0; i0 < nst; i0 += kTcPrefetch) {
 #pragma unroll
     for (int j = 0; j < kTcPrefetch; ++j) {
@@ -320,7 +328,7 @@ __device__ __forceinline__ void tc_produce(const TcArgs& a, int row0, int ks0, i
         break;
       }
       tc_convert<DT>(raw[j], r, qq, ks0 + i, As + (size_t)s * 2 * kTcABytes);
-      if (i + kTcPrefetch < nst) raw[j] = tc_load<DT>(a.w, R, qq, ks0 + i + kTcPrefetch);
+      if (i + kTcPrefetch < nst) raw[j] = tc_load<DT>(w, R, qq, ks0 + i + kTcPrefetch);
       fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[s]);
@@ -340,7 +348,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   const int bb = tc_b_bytes(N);
   uint8_t* As = smem;                                 // per stage: hi, lo weight images
   uint8_t* Bs = smem + (size_t)S * 2 * kTcABytes;     // per stage: hi, lo activation images
-  const int row0 = blockIdx.x * kTcM;
+  int sg = 0;
+#pragma unroll
+  for (int q = 1; q < kTcMaxSegs; ++q)
+    if (q < a.nseg && (int)blockIdx.x >= a.rt[q]) sg = q;
+  const WeightDev& W = a.w[sg];
+  const int row0 = ((int)blockIdx.x - a.rt[sg]) * kTcM;
   const int tile = blockIdx.y;
   const int z = blockIdx.z;
   const int ks0 = (int)((int64_t)a.KS * z / a.splits), ks1 = (int)((int64_t)a.KS * (z + 1) / a.splits);
@@ -370,12 +383,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 
   if (warp < kTcDequantWarps) {
     // ---- weight producers (one instantiation per GGML type) ----
-    switch (a.w.L.dtype) {
-      case kQ4_K: tc_produce<kQ4_K>(a, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
-      case kQ6_K: tc_produce<kQ6_K>(a, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
-      case kQ8_0: tc_produce<kQ8_0>(a, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
-      case kQ5_K: tc_produce<kQ5_K>(a, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
-      default: tc_produce<kQ4_0>(a, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
+    switch (W.L.dtype) {
+      case kQ4_K: tc_produce<kQ4_K>(W, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
+      case kQ6_K: tc_produce<kQ6_K>(W, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
+      case kQ8_0: tc_produce<kQ8_0>(W, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
+      case kQ5_K: tc_produce<kQ5_K>(W, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
+      default: tc_produce<kQ4_0>(W, row0, ks0, nst, S, As, empty, a_full, s_ok); break;
     }
   } else if (warp == kTcDequantWarps) {
     // ---- activation producer ----
@@ -451,7 +464,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       const int r = warp * 32 + lane;
       const int64_t R = (int64_t)row0 + r;
       const int t0 = tile * N;
-      float* outp = a.part + ((size_t)z * a.mpad) * a.n;
+      float* outp = a.part + ((size_t)z * a.mpad) * a.ncol + a.c0[sg];
+      const int64_t nrow = W.L.n;
       for (int c0 = 0; c0 < N; c0 += 16) {
         uint32_t v[16];
         asm volatile(
@@ -462,11 +476,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
               "=r"(v[15])
             : "r"(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (R < a.n) {
+        if (R < nrow) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int t = t0 + c0 + j;
-            if (t < a.m) outp[(size_t)t * a.n + R] = __uint_as_float(v[j]);
+            if (t < a.m) outp[(size_t)t * a.ncol + R] = __uint_as_float(v[j]);
           }
         }
       }
@@ -538,21 +552,21 @@ __global__ void tc_act_kernel(const float* __restrict__ x, int ldx, int m, int k
   pdl_launch_dependents();
 }
 
-// y[t][col0 + r] = epi(inv[t] * sum_s part[s][t][r]) for t < m, r < n.
-// EPI kEpiStore / kEpiAdd (y +=) / kEpiSwiglu (part2 = up partials:
-// silu(g) * u).
+// y[t][col0 + r] = epi(inv[t] * sum_s part[s][t][r]) for t < m, r < n;
+// partial rows have stride ldp.  EPI kEpiStore / kEpiAdd (y +=) /
+// kEpiSwiglu (part2 = up partials: silu(g) * u).
 template <int EPI>
 __global__ void tc_reduce_kernel(const float* __restrict__ part, const float* __restrict__ part2, int splits,
-                                 int mpad, int m, int n, const float* __restrict__ inv, float* __restrict__ y,
-                                 int ldy, int col0) {
+                                 int mpad, int m, int n, int ldp, const float* __restrict__ inv,
+                                 float* __restrict__ y, int ldy, int col0) {
   pdl_wait();
   const int64_t total = (int64_t)m * n;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int t = (int)(i / n), r = (int)(i - (int64_t)t * n);
     float g = 0.0f, u = 0.0f;
     for (int s = 0; s < splits; ++s) {
-      g += part[((size_t)s * mpad + t) * n + r];
-      if (EPI == kEpiSwiglu) u += part2[((size_t)s * mpad + t) * n + r];
+      g += part[((size_t)s * mpad + t) * ldp + r];
+      if (EPI == kEpiSwiglu) u += part2[((size_t)s * mpad + t) * ldp + r];
     }
     g *= inv[t];
     float* yp = y + (size_t)t * ldy + col0 + r;

@@ -27,9 +27,8 @@ struct XQBuf {
 struct TcScratch {
   __half* img = nullptr;   // f16 activation images
   float* inv = nullptr;    // per-token inverse scales
-  float* part = nullptr;   // split-K partials
-  float* part2 = nullptr;  // partials of the up projection (SwiGLU)
-  size_t img_cap = 0, inv_cap = 0, part_cap = 0, part2_cap = 0;  // bytes
+  float* part = nullptr;   // split-K partials (the weights of one launch side by side)
+  size_t img_cap = 0, inv_cap = 0, part_cap = 0;  // bytes
 };
 
 b2q_status set_error(b2q_status st, const char* fmt, ...);

@@ -43,20 +43,30 @@ void tc_free(b2q_engine* e) {
   if (t.img) cudaFree(t.img);
   if (t.inv) cudaFree(t.inv);
   if (t.part) cudaFree(t.part);
-  if (t.part2) cudaFree(t.part2);
   t = TcScratch{};
 }
 
-static cudaError_t tc_launch_gemm(b2q_engine* e, const b2q_weight* w, const TcPlan& p, int m, float* part,
-                                  cudaStream_t st, bool pdl) {
-  if (p.N < 16 || p.N > kTcNMax || p.N % 16 != 0) return cudaErrorInvalidValue;
+// One launch over the weights ws[0..nw) (same k): weight i's rows go to
+// columns c0[i].. of partial sums with ncol columns.
+static cudaError_t tc_launch_gemm(b2q_engine* e, const b2q_weight* const* ws, const int* c0, int nw,
+                                  const TcPlan& p, int m, float* part, int ncol, cudaStream_t st) {
+  if (p.N < 16 || p.N > kTcNMax || p.N % 16 != 0 || nw < 1 || nw > kTcMaxSegs) return cudaErrorInvalidValue;
   TcArgs a;
-  a.w = w->view;
+  memset(&a, 0, sizeof a);
+  a.nseg = nw;
+  int rt = 0;
+  for (int i = 0; i < nw; ++i) {
+    a.w[i] = ws[i]->view;
+    a.rt[i] = rt;
+    a.c0[i] = c0[i];
+    rt += (int)((ws[i]->n + kTcM - 1) / kTcM);
+  }
+  a.rt[nw] = rt;
   a.xh = e->tc.img;
   a.KS = p.KS;
   a.N = p.N;
   a.m = m;
-  a.n = (int)w->n;
+  a.ncol = ncol;
   a.splits = p.splits;
   a.part = part;
   a.mpad = p.mpad;
@@ -66,22 +76,21 @@ static cudaError_t tc_launch_gemm(b2q_engine* e, const b2q_weight* w, const TcPl
   cudaError_t err = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.rowtiles, p.tiles, p.splits);
+  cfg.gridDim = dim3(rt, p.tiles, p.splits);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  (void)pdl;  // the kernel reads the image from its first instruction: no early launch
   launch_counted(e, 1);
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, a);
 }
 
 template <int EPI>
-static cudaError_t tc_launch_reduce(b2q_engine* e, const TcPlan& p, int m, int n, float* y, int ldy, int col0,
-                                    cudaStream_t st) {
+static cudaError_t tc_launch_reduce(b2q_engine* e, const TcPlan& p, int m, int n, int ldp, const float* part2,
+                                    float* y, int ldy, int col0, cudaStream_t st) {
   const int64_t total = (int64_t)m * n;
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)e->num_sms * 8);
   launch_counted(e, 1);
-  tc_reduce_kernel<EPI><<<blocks, 256, 0, st>>>(e->tc.part, e->tc.part2, p.splits, p.mpad, m, n, e->tc.inv, y,
+  tc_reduce_kernel<EPI><<<blocks, 256, 0, st>>>(e->tc.part, part2, p.splits, p.mpad, m, n, ldp, e->tc.inv, y,
                                                 ldy, col0);
   return cudaGetLastError();
 }
@@ -90,27 +99,30 @@ cudaError_t tc_matmul(b2q_engine* e, const float* x, int ldx, int m, int k, cons
                       int epi, float* y, int ldy, const int* col0, cudaStream_t st, bool pdl) {
   if (m < 1 || nw < 1 || (epi == kEpiSwiglu && nw != 2)) return cudaErrorInvalidValue;
   for (int i = 0; i < nw; ++i)
-    if (ws[i]->k != k || !gemv_supported(ws[i]->dtype))
-      return cudaErrorInvalidValue;
+    if (ws[i]->k != k || !gemv_supported(ws[i]->dtype)) return cudaErrorInvalidValue;
   TcScratch& t = e->tc;
-  // scratch: image and scales for these tokens, partials for the largest weight
-  const TcPlan p0 = tc_plan(m, ws[0]->n, k, e->num_sms);
-  size_t part_need = 0;
+  const TcPlan p = tc_plan(m, ws[0]->n, k, e->num_sms);  // tiles, stages and splits depend on m and k only
+  // weights whose outputs are adjacent columns (q | k | v), and the gate/up
+  // pair, run as one launch; partial sums of all of them side by side
+  bool fused = nw <= kTcMaxSegs;
+  int64_t ncol = 0;
   for (int i = 0; i < nw; ++i) {
-    const TcPlan p = tc_plan(m, ws[i]->n, k, e->num_sms);
-    part_need = std::max(part_need, (size_t)p.splits * p.mpad * ws[i]->n * sizeof(float));
+    if (epi != kEpiSwiglu && col0[i] != col0[0] + ncol) fused = false;
+    ncol += ws[i]->n;
   }
+  size_t part_need = 0;
+  if (fused) part_need = (size_t)p.splits * p.mpad * ncol * sizeof(float);
+  else
+    for (int i = 0; i < nw; ++i) part_need = std::max(part_need, (size_t)p.splits * p.mpad * ws[i]->n * sizeof(float));
   cudaError_t err = tc_grow(reinterpret_cast<void**>(&t.img), &t.img_cap,
-                            (size_t)p0.tiles * p0.KS * tc_b_bytes(p0.N), st);
-  if (err == cudaSuccess) err = tc_grow(reinterpret_cast<void**>(&t.inv), &t.inv_cap, (size_t)p0.mpad * 4, st);
+                            (size_t)p.tiles * p.KS * tc_b_bytes(p.N), st);
+  if (err == cudaSuccess) err = tc_grow(reinterpret_cast<void**>(&t.inv), &t.inv_cap, (size_t)p.mpad * 4, st);
   if (err == cudaSuccess) err = tc_grow(reinterpret_cast<void**>(&t.part), &t.part_cap, part_need, st);
-  if (err == cudaSuccess && epi == kEpiSwiglu)
-    err = tc_grow(reinterpret_cast<void**>(&t.part2), &t.part2_cap, part_need, st);
   if (err != cudaSuccess) return err;
   {
     launch_counted(e, 1);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p0.mpad);
+    cfg.gridDim = dim3(p.mpad);
     cfg.blockDim = dim3(256);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -118,22 +130,29 @@ cudaError_t tc_matmul(b2q_engine* e, const float* x, int ldx, int m, int k, cons
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    err = cudaLaunchKernelEx(&cfg, tc_act_kernel, x, ldx, m, k, p0.KS, p0.N, t.img, t.inv);
+    err = cudaLaunchKernelEx(&cfg, tc_act_kernel, x, ldx, m, k, p.KS, p.N, t.img, t.inv);
     if (err != cudaSuccess) return err;
   }
-  if (epi == kEpiSwiglu) {
-    const TcPlan p = tc_plan(m, ws[0]->n, k, e->num_sms);
-    err = tc_launch_gemm(e, ws[0], p, m, t.part, st, pdl);
-    if (err == cudaSuccess) err = tc_launch_gemm(e, ws[1], p, m, t.part2, st, pdl);
-    if (err == cudaSuccess) err = tc_launch_reduce<kEpiSwiglu>(e, p, m, (int)ws[0]->n, y, ldy, col0[0], st);
-    return err;
+  if (fused) {
+    int c[kTcMaxSegs];
+    int64_t o = 0;
+    for (int i = 0; i < nw; ++i) {
+      c[i] = (int)o;
+      o += ws[i]->n;
+    }
+    err = tc_launch_gemm(e, ws, c, nw, p, m, t.part, (int)ncol, st);
+    if (err != cudaSuccess) return err;
+    if (epi == kEpiSwiglu)
+      return tc_launch_reduce<kEpiSwiglu>(e, p, m, (int)ws[0]->n, (int)ncol, t.part + ws[0]->n, y, ldy, col0[0], st);
+    if (epi == kEpiAdd) return tc_launch_reduce<kEpiAdd>(e, p, m, (int)ncol, (int)ncol, nullptr, y, ldy, col0[0], st);
+    return tc_launch_reduce<kEpiStore>(e, p, m, (int)ncol, (int)ncol, nullptr, y, ldy, col0[0], st);
   }
   for (int i = 0; i < nw && err == cudaSuccess; ++i) {
-    const TcPlan p = tc_plan(m, ws[i]->n, k, e->num_sms);
-    err = tc_launch_gemm(e, ws[i], p, m, t.part, st, pdl);
+    const int z0 = 0, n = (int)ws[i]->n;
+    err = tc_launch_gemm(e, &ws[i], &z0, 1, p, m, t.part, n, st);
     if (err != cudaSuccess) break;
-    err = epi == kEpiAdd ? tc_launch_reduce<kEpiAdd>(e, p, m, (int)ws[i]->n, y, ldy, col0[i], st)
-                         : tc_launch_reduce<kEpiStore>(e, p, m, (int)ws[i]->n, y, ldy, col0[i], st);
+    err = epi == kEpiAdd ? tc_launch_reduce<kEpiAdd>(e, p, m, n, n, nullptr, y, ldy, col0[i], st)
+                         : tc_launch_reduce<kEpiStore>(e, p, m, n, n, nullptr, y, ldy, col0[i], st);
   }
   return err;
 }
