@@ -222,7 +222,9 @@ __device__ __forceinline__ float small_uint_f(uint32_t bits) {
 // two runs of 8 consecutive k.  The block formats of dequantize_slice
 // (inference.rs:1367-1458); each value is d*sc*q - dmin*m with the products
 // d*sc, dmin*m in f32 as the reference forms them and the last step fused
-// (one rounding), which the hi/lo split then carries to ~2^-22.
+// (one rounding), which the hi/lo split then carries to ~2^-22.  Integer
+// fields become floats by exponent-pattern arithmetic (small_uint_f), the
+// f16 scales by the hardware conversion (exact for finite values).
 template <int DT>
 __device__ __forceinline__ void tc_convert(const TcRaw& x, int r, int qq, int ks, uint8_t* img) {
   constexpr int dt = DT;
@@ -243,9 +245,9 @@ __device__ __forceinline__ void tc_convert(const TcRaw& x, int r, int qq, int ks
     const uint32_t sel = u & 3;  // KC is a multiple of 8: u & 3 == ul & 3
     const uint32_t h = sel == 0 ? hb.x : sel == 1 ? hb.y : sel == 2 ? hb.z : hb.w;
     const uint32_t dd = __byte_perm(__byte_perm(hb.x, hb.y, 0x0073), __byte_perm(hb.z, hb.w, 0x0073), 0x5410);
-    const float d = f16_bits_exact(dd & 0xffffu), dmin = f16_bits_exact(dd >> 16);
-    const float d1 = __fmul_rn(d, (float)(h & 63u)), m1 = __fmul_rn(dmin, (float)((h >> 12) & 63u));
-    const float d2 = __fmul_rn(d, (float)((h >> 6) & 63u)), m2 = __fmul_rn(dmin, (float)((h >> 18) & 63u));
+    const float d = f16_bits_fast(dd & 0xffffu), dmin = f16_bits_fast(dd >> 16);
+    const float d1 = d * small_uint_f(h & 63u), m1 = dmin * small_uint_f((h >> 12) & 63u);
+    const float d2 = d * small_uint_f((h >> 6) & 63u), m2 = dmin * small_uint_f((h >> 18) & 63u);
     const uint32_t wd[2] = {x.a.x, x.a.y};
     const bool q5 = dt == kQ5_K;
 #pragma unroll
@@ -260,10 +262,10 @@ __device__ __forceinline__ void tc_convert(const TcRaw& x, int r, int qq, int ks
     }
   } else if (dt == kQ6_K) {
     // u & 7 == ul & 7 (KC a multiple of 8): the d of block ul >> 2 is half (ul >> 2) & 1 of the word
-    const float d = f16_bits_exact(((u >> 2) & 1) ? x.d >> 16 : x.d & 0xffffu);
+    const float d = f16_bits_fast(((u >> 2) & 1) ? x.d >> 16 : x.d & 0xffffu);
     const int hi = (ks & 1);  // groups 2,3 (high nibbles) or 0,1 (low nibbles)
-    const float s0 = __fmul_rn(d, (float)(int8_t)((x.s >> (8 * (2 * hi))) & 0xffu));
-    const float s1 = __fmul_rn(d, (float)(int8_t)((x.s >> (8 * (2 * hi + 1))) & 0xffu));
+    const float s0 = d * (small_uint_f(((x.s >> (8 * (2 * hi))) & 0xffu) ^ 0x80u) - 128.0f);
+    const float s1 = d * (small_uint_f(((x.s >> (8 * (2 * hi + 1))) & 0xffu) ^ 0x80u) - 128.0f);
     const uint32_t wa[2] = {x.a.x, x.a.y}, wb[2] = {x.b.x, x.b.y}, wh[2] = {x.c.x, x.c.y};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -282,7 +284,7 @@ __device__ __forceinline__ void tc_convert(const TcRaw& x, int r, int qq, int ks
       v1[i] = s1 * (small_uint_f(q1) - 32.0f);
     }
   } else if (dt == kQ4_0) {  // u & 1 == ul & 1 (KC even)
-    const float d = f16_bits_exact((u & 1) ? x.d >> 16 : x.d & 0xffffu);
+    const float d = f16_bits_fast((u & 1) ? x.d >> 16 : x.d & 0xffffu);
     const uint32_t wd[2] = {x.a.x, x.a.y};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -291,7 +293,7 @@ __device__ __forceinline__ void tc_convert(const TcRaw& x, int r, int qq, int ks
       v1[i] = d * (small_uint_f((b >> 4) & 15u) - 8.0f);
     }
   } else {  // Q8_0: u & 1 == ul & 1 (KC even)
-    const float d = f16_bits_exact((u & 1) ? x.d >> 16 : x.d & 0xffffu);
+    const float d = f16_bits_fast((u & 1) ? x.d >> 16 : x.d & 0xffffu);
     const uint32_t wa[2] = {x.a.x, x.a.y}, wb[2] = {x.b.x, x.b.y};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
