@@ -88,6 +88,7 @@ SIGNATURES = [
     ("b2q_gguf_llama_config", _I, [_VP, C.c_char_p, C.POINTER(ModelConfig)]),
     ("b2q_model_load_gguf", _I, [_VP, _VP]),
     ("b2q_model_weight_bytes", _SZ, [_VP]),
+    ("b2q_model_step_path", _I, [_VP]),
     ("b2q_model_destroy", _I, [_VP]),
     ("b2q_time_gemv", _I, [_VP, C.POINTER(_VP), _I, _VP, _I, _I, _VP, C.POINTER(C.c_float)]),
     ("b2q_kernel_launch_count", C.c_uint64, [_VP]),

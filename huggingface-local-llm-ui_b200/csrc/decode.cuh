@@ -150,6 +150,8 @@ __host__ __device__ __forceinline__ RcGeom rc_geom(int dtype, int kc) {
   RcGeom g;
   if (dtype == kQ4_K) { g.o_aux = 32 * kc; g.o_aux2 = 0; g.rc = 36 * kc; }
   else if (dtype == kQ6_K) { g.o_aux = 48 * kc; g.o_aux2 = 52 * kc; g.rc = 52 * kc + round_up_int(kc / 2, 16); }
+  else if (dtype == kQ5_K) { g.o_aux = 32 * kc; g.o_aux2 = 40 * kc; g.rc = 44 * kc; }
+  else if (dtype == kQ4_0) { g.o_aux = 16 * kc; g.o_aux2 = 0; g.rc = 16 * kc + round_up_int(2 * kc, 16); }
   else { g.o_aux = 32 * kc; g.o_aux2 = 0; g.rc = 32 * kc + round_up_int(2 * kc, 16); }
   return g;
 }
@@ -560,8 +562,11 @@ struct Consumer {
   int ro = 0;  // next read offset
 };
 
-// The stage loop (DT: the GGML type, or -1 to read it from the phase; one
-// runtime-typed copy keeps the kernel within its registers).  Software-pipelined: the warp
+// The stage loop (DT: the GGML type, or < 0 to read it from the phase; one
+// runtime-typed copy keeps the kernel within its registers).  DT == -1
+// takes Q4_K, Q6_K and Q8_0 rows (the Q4_K_M / Q6_K / Q8_0 models); DT ==
+// -2 adds Q5_K and Q4_0, in a separate kernel instance, so that the common
+// loop carries no branch for them.  Software-pipelined: the warp
 // reductions and accumulator updates of stage j are issued after the dot
 // products of stage j + 1 have started, in the same straight-line block, so
 // the shuffle latency overlaps integer work.
@@ -574,6 +579,7 @@ __device__ __forceinline__ void consume_loop(Consumer& cs, const CtaPhase& ph, b
   const int nr = ph.dtype_nr >> 8;
   const int KC = ph.KC, C = ph.C, U = ph.U;
   const int dt = DT >= 0 ? DT : (ph.dtype_nr & 0xff);  // uniform over the CTA
+  constexpr bool kAll = DT == -2;
   const RcGeom geo = rc_geom(dt, KC);
   const int tb = 8 * geo.rc;
   const int rows = (ge - gb) * 8;
@@ -593,8 +599,9 @@ __device__ __forceinline__ void consume_loop(Consumer& cs, const CtaPhase& ph, b
       const int u = c * KC + ul;
       uok = ul < KC && u < U;
       if (uok && ok) {
-        if (dt == kQ4_K) xload_q4k(X, sx, 0, u, xp.f4);
+        if (dt == kQ4_K || (kAll && dt == kQ5_K)) xload_q4k(X, sx, 0, u, xp.f4);
         else if (dt == kQ6_K) xload_q6k(X, sx, 0, u, xp.f6a, xp.f6b);
+        else if (kAll && dt == kQ4_0) xload_q40(X, sx, 0, u, xp.f8);
         else xload_q80(X, sx, 0, u, xp.f8);
       }
     }
@@ -622,6 +629,12 @@ __device__ __forceinline__ void consume_loop(Consumer& cs, const CtaPhase& ph, b
     } else if (dt == kQ6_K) {
       p0 = row_q6k(rc, KC, geo.o_aux, geo.o_aux2, ul, X);
       p1 = row_q6k(rc2, KC, geo.o_aux, geo.o_aux2, ul, X);
+    } else if (kAll && dt == kQ5_K) {
+      p0 = row_q5k(rc, KC, geo.o_aux, geo.o_aux2, ul, csel, X);
+      p1 = row_q5k(rc2, KC, geo.o_aux, geo.o_aux2, ul, csel, X);
+    } else if (kAll && dt == kQ4_0) {
+      p0 = row_q40(rc, geo.o_aux, ul, X);
+      p1 = row_q40(rc2, geo.o_aux, ul, X);
     } else {
       p0 = row_q80(rc, KC, geo.o_aux, ul, X);
       p1 = row_q80(rc2, KC, geo.o_aux, ul, X);
@@ -655,6 +668,7 @@ __device__ __forceinline__ void consume_loop(Consumer& cs, const CtaPhase& ph, b
   }
 }
 
+template <bool kAllTypes>
 __device__ __forceinline__ void consume_phase(Consumer& cs, const CtaPhase& ph, bool pair, const SX& sx, bool& ok,
                                               float* racc, int tph = -1) {
   long long wsum = 0;
@@ -665,7 +679,7 @@ __device__ __forceinline__ void consume_phase(Consumer& cs, const CtaPhase& ph, 
   const int nw = pair ? 2 : 1;
   for (int i = threadIdx.x; i < 2 * nw * rows; i += kGemvConsumerWarps * 32) racc[i] = 0.0f;
   consumer_sync();
-  consume_loop<-1>(cs, ph, pair, sx, ok, racc, wsum);
+  consume_loop<kAllTypes ? -2 : -1>(cs, ph, pair, sx, ok, racc, wsum);
 #ifdef B2Q_DECODE_TRACE
   if (threadIdx.x == 0 && tph >= 0 && tph < 160 && blockIdx.x < 160) {
     g_dec_wait[(blockIdx.x * 160 + tph) * 2] = wsum;
@@ -879,7 +893,9 @@ __device__ __forceinline__ void warp_argmax(float& best, int& idx) {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int G>
+// G: query heads per KV head; kAllTypes: the stage loop also takes Q5_K and
+// Q4_0 rows.
+template <int G, bool kAllTypes>
 __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t full_bar[kRingSlots], empty_bar[kRingSlots];
@@ -1013,7 +1029,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       B2Q_TRACE(tslot + 1);
       B2Q_FTRACE(l, 21 + k);
       const bool pair = k == 3;
-      consume_phase(cs, ph, pair, smem_sx(q), ok, racc, head ? 4 * a.n_layers : 4 * l + (k == 0 ? 0 : k - 1));
+      consume_phase<kAllTypes>(cs, ph, pair, smem_sx(q), ok, racc, head ? 4 * a.n_layers : 4 * l + (k == 0 ? 0 : k - 1));
       // epilogue
       if (add) {
         asm volatile("cp.async.wait_all;" ::: "memory");

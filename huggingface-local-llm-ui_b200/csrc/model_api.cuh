@@ -449,6 +449,11 @@ b2q_status b2q_clear_state(b2q_model* M) {
 
 size_t b2q_model_weight_bytes(const b2q_model* M) { return M ? M->weight_bytes : 0; }
 
+int b2q_model_step_path(const b2q_model* M) {
+  if (!M || !M->finalized) return -1;
+  return M->dec_on ? 0 : M->graph ? 2 : 1;
+}
+
 b2q_status b2q_model_destroy(b2q_model* M) {
   if (!M) return B2Q_OK;
   cudaSetDevice(M->eng->device);

@@ -78,6 +78,7 @@ struct b2q_model {
   b2q::DecodeArgs dec{};
   size_t dec_smem = 0;
   int dec_G = 0;
+  bool dec_all = false;  // the persistent kernel instance that also takes Q5_K / Q4_0 rows
   bool dec_on = false;
   bool finalized = false;
   std::map<std::string, bool> have;
@@ -501,14 +502,18 @@ static CtaPhase cta_phase(const DecPhase& ph, int b) {
 }
 
 template <int G>
-static void* decode_kernel_for() { return reinterpret_cast<void*>(decode_kernel<G>); }
+static void* decode_kernel_for(bool all) {
+  return all ? reinterpret_cast<void*>(decode_kernel<G, true>) : reinterpret_cast<void*>(decode_kernel<G, false>);
+}
 
-static void* decode_kernel_ptr(int G, size_t* attn_smem) {
+// all: the model has Q5_K or Q4_0 weights (the kernel instance whose stage
+// loop takes every supported type)
+static void* decode_kernel_ptr(int G, bool all, size_t* attn_smem) {
   switch (G) {
-    case 1: *attn_smem = sizeof(AttnTile<1>); return decode_kernel_for<1>();
-    case 2: *attn_smem = sizeof(AttnTile<2>); return decode_kernel_for<2>();
-    case 4: *attn_smem = sizeof(AttnTile<4>); return decode_kernel_for<4>();
-    case 8: *attn_smem = sizeof(AttnTile<8>); return decode_kernel_for<8>();
+    case 1: *attn_smem = sizeof(AttnTile<1>); return decode_kernel_for<1>(all);
+    case 2: *attn_smem = sizeof(AttnTile<2>); return decode_kernel_for<2>(all);
+    case 4: *attn_smem = sizeof(AttnTile<4>); return decode_kernel_for<4>(all);
+    case 8: *attn_smem = sizeof(AttnTile<8>); return decode_kernel_for<8>(all);
     default: return nullptr;
   }
 }
@@ -557,21 +562,29 @@ static cudaError_t setup_decode(b2q_model* M) {
   const int P = c.tp_size, rk = c.tp_rank;
   if (M->KV_loc > 64 || P > kMaxTp) return cudaSuccess;
   const int H = M->H_loc, KV = M->KV_loc, G = H / KV, hd = c.head_dim;
+  // the persistent kernel's stage loop takes Q4_K, Q6_K and Q8_0 rows, and
+  // in a second instance also Q5_K and Q4_0; models with other weight types
+  // step through the captured graph
+  bool all = false;
+  {
+    auto common = [](const b2q_weight* w) { return w->dtype == kQ4_K || w->dtype == kQ6_K || w->dtype == kQ8_0; };
+    auto other = [](const b2q_weight* w) { return w->dtype == kQ5_K || w->dtype == kQ4_0; };
+    std::vector<const b2q_weight*> ws{M->output};
+    for (int l = 0; l < c.n_layers; ++l) {
+      const LayerW& w = M->L[l];
+      ws.insert(ws.end(), {w.q, w.k, w.v, w.o, w.gate, w.up, w.down});
+    }
+    for (const b2q_weight* w : ws) {
+      if (other(w)) all = true;
+      else if (!common(w)) return cudaSuccess;
+    }
+  }
   size_t attn_one = 0;
-  void* kern = decode_kernel_ptr(G, &attn_one);
+  void* kern = decode_kernel_ptr(G, all, &attn_one);
   if (!kern) return cudaSuccess;
   // the split merge stages {max, sum} of every split of a head group in one tile
   if (2 * G * M->nsplit > kAttnTile * kHeadDim / 2) return cudaSuccess;
   const int grid = e->num_sms;
-  // the persistent kernel's consume loop takes Q4_K, Q6_K and Q8_0 rows;
-  // models with other weight types step through the captured graph
-  auto dec_type = [](const b2q_weight* w) { return w->dtype == kQ4_K || w->dtype == kQ6_K || w->dtype == kQ8_0; };
-  if (!dec_type(M->output)) return cudaSuccess;
-  for (int l = 0; l < c.n_layers; ++l) {
-    const LayerW& w = M->L[l];
-    for (const b2q_weight* x : {w.q, w.k, w.v, w.o, w.gate, w.up, w.down})
-      if (!dec_type(x)) return cudaSuccess;
-  }
   int stage_max = 0;
   std::vector<DecLayer> host((size_t)c.n_layers);
   std::vector<const DecPhase*> phases;
@@ -712,6 +725,7 @@ static cudaError_t setup_decode(b2q_model* M) {
   a.racc_bytes = (int)racc;
   M->dec_smem = smem;
   M->dec_G = G;
+  M->dec_all = all;
   M->dec_on = true;
   return cudaSuccess;
 }
@@ -739,11 +753,17 @@ static cudaError_t launch_decode(b2q_model* M, const uint32_t* tok, int pos, uin
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   launch_counted(M->eng, 1);
+  if (M->dec_all) switch (M->dec_G) {
+      case 1: return cudaLaunchKernelEx(&cfg, decode_kernel<1, true>, a);
+      case 2: return cudaLaunchKernelEx(&cfg, decode_kernel<2, true>, a);
+      case 4: return cudaLaunchKernelEx(&cfg, decode_kernel<4, true>, a);
+      default: return cudaLaunchKernelEx(&cfg, decode_kernel<8, true>, a);
+    }
   switch (M->dec_G) {
-    case 1: return cudaLaunchKernelEx(&cfg, decode_kernel<1>, a);
-    case 2: return cudaLaunchKernelEx(&cfg, decode_kernel<2>, a);
-    case 4: return cudaLaunchKernelEx(&cfg, decode_kernel<4>, a);
-    default: return cudaLaunchKernelEx(&cfg, decode_kernel<8>, a);
+    case 1: return cudaLaunchKernelEx(&cfg, decode_kernel<1, false>, a);
+    case 2: return cudaLaunchKernelEx(&cfg, decode_kernel<2, false>, a);
+    case 4: return cudaLaunchKernelEx(&cfg, decode_kernel<4, false>, a);
+    default: return cudaLaunchKernelEx(&cfg, decode_kernel<8, false>, a);
   }
 }
 

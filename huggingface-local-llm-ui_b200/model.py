@@ -131,6 +131,11 @@ class StandardNativeEngine:
     def weight_bytes(self) -> int:
         return int(lib().b2q_model_weight_bytes(self._h))
 
+    @property
+    def step_path(self) -> str:
+        """How single-token steps run: "persistent", "eager" or "graph"."""
+        return {0: "persistent", 1: "eager", 2: "graph"}.get(int(lib().b2q_model_step_path(self._h)), "none")
+
     # -- inference --------------------------------------------------------
     def forward(self, tokens, start_pos: int) -> np.ndarray:
         """Logits [n_vocab] of the last position (inference.rs:2695-2860)."""

@@ -339,6 +339,11 @@ b2q_status b2q_model_load_gguf(b2q_model* m, const b2q_gguf* g);
 /* Device bytes held by the model's weights on this rank. */
 size_t b2q_model_weight_bytes(const b2q_model* m);
 
+/* How a finalized model runs a single-token step: 0 = the persistent decode
+ * kernel, 1 = eager per-kernel launches, 2 = the captured per-kernel graph
+ * (-1 before b2q_model_finalize). */
+int b2q_model_step_path(const b2q_model* m);
+
 b2q_status b2q_model_destroy(b2q_model* m);
 
 /* Kernel timing for benchmarks: quantise x (device, [k] f32) once, then

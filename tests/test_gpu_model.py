@@ -209,8 +209,8 @@ def test_model_error_paths(engine, pkg):
 def test_model_q5k_and_q40_weights(engine, orc, pkg, kind):
     """Models whose projections are Q5_K (a Q5_K_M-style mix) or Q4_0: the
     prompt pass (tensor cores) and decode steps stay within the fp64
-    tolerance; single-token steps run the captured per-kernel graph (the
-    persistent kernel takes Q4_K/Q6_K/Q8_0 rows) and equal the eager steps."""
+    tolerance; single-token steps run the persistent kernel and equal the
+    eager per-kernel steps bit for bit."""
     from hf_llm_b200 import ggml, model, synth
     base = model.q4_k_m_types()
     if kind == "q5_k_m":
@@ -221,6 +221,7 @@ def test_model_q5k_and_q40_weights(engine, orc, pkg, kind):
     dev = model.StandardNativeEngine.from_tensors(engine, TOY, t, max_seq=96)
     eag = model.StandardNativeEngine.from_tensors(engine, TOY, t, max_seq=96, decode="eager")
     ref = orc.Model(TOY, t, kv_capacity=96)
+    assert dev.step_path == "persistent" and eag.step_path == "eager"
     toks = list(range(2, 42))
     a, e = dev.forward(toks, 0), eag.forward(toks, 0)
     b = ref.forward_f64(toks, 0, kv_f16=True)
