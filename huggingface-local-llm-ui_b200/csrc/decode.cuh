@@ -81,13 +81,11 @@ struct CtaPhase {
   int ycol;       // first output column
 };
 
-// Synchronisation words (zeroed at set-up; every complete launch returns
-// them to zero).
+// Synchronisation words (zeroed at set-up).
 struct DecSync {
   unsigned long long bar;  // grid barrier arrivals (monotonic)
   unsigned int head_cnt;   // CTAs done with their argmax candidate
   unsigned int pad;
-  unsigned int attn_cnt[64];  // per KV head: attention splits finished
 };
 
 struct DecodeArgs {
@@ -110,6 +108,24 @@ struct DecodeArgs {
   float* part;            // [H][nsplit][kPartStride] attention split partials
   int nsplit;
   DecSync* sync;
+  // [n_layers][KV] attention splits finished per layer and KV head (the
+  // last split to finish merges and returns the word to zero; the next use
+  // is the same layer of the next launch)
+  unsigned int* attn_cnt;
+  // One GPU (tp == 1): the vectors that cross CTAs between phases -- the
+  // residual x, q/k/v and the attention output -- are stored tagged, value |
+  // tag << 32 in one 8-byte store, with tag = tag0 + 5 * layer + hand-off
+  // (0: x into QKV, 1: q/k/v, 2: attention output, 3: x into gate/up).  A
+  // reader that sees the tag sees the value, so no release fence sits
+  // between a phase's last store and the barrier in front of the next
+  // phase: that barrier is a relaxed gate that only keeps readers from
+  // polling early, and each reader polls (bounded) for the tag.  The SwiGLU
+  // output h, the attention partials and the argmax candidates keep
+  // plain stores behind release/acquire synchronisation.
+  unsigned long long* xll;     // [E]
+  unsigned long long* qkvll;   // [(H + 2 KV) * 128]
+  unsigned long long* attnll;  // [H * 128]
+  uint32_t tag0;
   uint32_t* argmax;       // model's argmax word
   uint32_t* argmax2;      // optional caller's copy
   // Tensor parallelism: this is rank `rank` of `tp` (tp = 1 on one GPU).  H,
@@ -210,21 +226,63 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
   return v;
 }
 
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
+
+// Tagged hand-offs (one GPU, see DecodeArgs): value | tag << 32, one
+// single-copy-atomic 8-byte store.
+__device__ __forceinline__ void ll_store(unsigned long long* p, float v, uint32_t tag) {
+  const unsigned long long w = (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+// Polls p until it carries `tag` (out of line: the rare path).  Bounded: a
+// timeout raises the device error word and clears *s_ok, after which this
+// CTA polls no more (the value is then whatever was read).
+__device__ __noinline__ unsigned long long ll_poll(const unsigned long long* p, uint32_t tag, volatile int* s_ok) {
+  unsigned long long v = ld_relaxed_u64(p);
+  if (!*s_ok) return v;
+  const long long t0 = clock64();
+  while ((uint32_t)(v >> 32) != tag) {
+    __nanosleep(32);
+    v = ld_relaxed_u64(p);
+    if (clock64() - t0 > kSpinLimitCycles) {
+      atomicExch(&g_b2q_device_error, 5);
+      *s_ok = 0;
+      break;
+    }
+  }
+  return v;
+}
+
+// The value of `first` (an earlier load of p) once p carries `tag`.
+__device__ __forceinline__ float ll_value(const unsigned long long* p, unsigned long long first, uint32_t tag,
+                                          volatile int* s_ok) {
+  const unsigned long long v = (uint32_t)(first >> 32) == tag ? first : ll_poll(p, tag, s_ok);
+  return __uint_as_float((uint32_t)v);
+}
+
 // Barrier over the consumer warps of every CTA of this GPU.  The counter
 // only grows: barrier number k of a launch completes at base + (k + 1) *
 // gridDim.x arrivals (base: the count every earlier launch left).  The
-// arrival is a release reduction that does not wait for a reply.  `s_ok`
-// (shared) turns 0 when this CTA's wait gave up; later waits are skipped.
+// arrival is a release reduction that does not wait for a reply; `relaxed`
+// (a gate in front of tagged hand-offs): a relaxed reduction and relaxed
+// polling, no fence.  `s_ok` (shared) turns 0 when this CTA's wait gave up;
+// later waits are skipped.
 __device__ __forceinline__ void grid_sync(unsigned long long* bar, unsigned long long base, int& k,
-                                          volatile int* s_ok, bool sys = false) {
+                                          volatile int* s_ok, bool sys = false, bool relaxed = false) {
   consumer_sync();
   if (threadIdx.x == 0 && *s_ok) {
     // sys: the release also orders this CTA's stores into peer memory
     if (sys) asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
+    else if (relaxed) asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
     else asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
     const unsigned long long target = base + (unsigned long long)(k + 1) * gridDim.x;
     const long long t0 = clock64();
-    while (ld_acquire_u64(bar) < target) {
+    while ((relaxed ? ld_relaxed_u64(bar) : ld_acquire_u64(bar)) < target) {
       if (clock64() - t0 > kSpinLimitCycles) {
         atomicExch(&g_b2q_device_error, 5);
         *s_ok = 0;
@@ -256,8 +314,8 @@ __device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsign
 // parallel, so the cost does not grow with the number of ranks.  One GPU:
 // the grid barrier alone.
 __device__ __forceinline__ void xgrid_sync(const DecodeArgs& a, unsigned long long* bar, int& k, int& kx,
-                                           volatile int* s_ok) {
-  grid_sync(bar, a.lbase, k, s_ok, a.tp > 1);
+                                           volatile int* s_ok, bool relaxed = false) {
+  grid_sync(bar, a.lbase, k, s_ok, a.tp > 1, relaxed && a.tp == 1);
   if (a.tp == 1) return;
   const unsigned long long epoch = a.xepoch + (unsigned long long)(++kx);
   const int p = threadIdx.x;
@@ -319,19 +377,38 @@ __host__ __device__ __forceinline__ size_t xq_smem_bytes(int kpad) { return (gem
 // `part` (tensor parallelism): np partial-sum rows of length dim, added to
 // x in order (x + part[0] + part[1] + ...) as the new residual; CTA b then
 // writes elements [b*dim/grid, (b+1)*dim/grid) of it to `xw`.
+// `xll` (one GPU): x is read from the tagged copy instead, polling for `tag`.
 __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, int dim, float eps, const XQ& q,
                                               float* xs, float* red, int tl = -1, int tb = 0,
-                                              const float* part = nullptr, int np = 0, float* xw = nullptr) {
+                                              const float* part = nullptr, int np = 0, float* xw = nullptr,
+                                              const unsigned long long* xll = nullptr, uint32_t tag = 0,
+                                              volatile int* s_ok = nullptr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = q.kpad >> 6;
   float sa = 0.0f, sb = 0.0f;
   for (int e0 = 0; e0 < dim; e0 += 1024 * kStageBatch) {
     float va[kStageBatch], vb[kStageBatch];
+    if (xll != nullptr) {  // every load of the batch in flight, then the tags
+      unsigned long long ua[kStageBatch], ub[kStageBatch];
 #pragma unroll
-    for (int i = 0; i < kStageBatch; ++i) {
-      const int ea = e0 + 1024 * i + tid, eb = ea + 512;
-      va[i] = ea < dim ? __ldcg(x + ea) : 0.0f;
-      vb[i] = eb < dim ? __ldcg(x + eb) : 0.0f;
+      for (int i = 0; i < kStageBatch; ++i) {
+        const int ea = e0 + 1024 * i + tid, eb = ea + 512;
+        ua[i] = ea < dim ? ld_relaxed_u64(xll + ea) : 0ull;
+        ub[i] = eb < dim ? ld_relaxed_u64(xll + eb) : 0ull;
+      }
+#pragma unroll
+      for (int i = 0; i < kStageBatch; ++i) {
+        const int ea = e0 + 1024 * i + tid, eb = ea + 512;
+        va[i] = ea < dim ? ll_value(xll + ea, ua[i], tag, s_ok) : 0.0f;
+        vb[i] = eb < dim ? ll_value(xll + eb, ub[i], tag, s_ok) : 0.0f;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kStageBatch; ++i) {
+        const int ea = e0 + 1024 * i + tid, eb = ea + 512;
+        va[i] = ea < dim ? __ldcg(x + ea) : 0.0f;
+        vb[i] = eb < dim ? __ldcg(x + eb) : 0.0f;
+      }
     }
     for (int p = 0; p < np; ++p) {
       const float* pp = part + (size_t)p * dim;
@@ -412,6 +489,46 @@ __device__ __forceinline__ void stage_plain(const float* src, int dim, const XQ&
         if (e + i >= dim) v[i] = 0.0f;
       xq_store_chunk8(v, lane, 0, j, j < nb, q);
     }
+  }
+  consumer_sync();
+}
+
+// Plain quantisation of a tagged vector (one GPU): its elements are read with
+// coalesced 8-byte loads (polling for `tag`) into `xs` (shared memory, dim
+// floats, rounded up to 8), then quantised from there -- the values of
+// stage_plain.
+__device__ __forceinline__ void stage_plain_ll(const unsigned long long* src, int dim, const XQ& q, float* xs,
+                                               uint32_t tag, volatile int* s_ok) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nb = q.kpad >> 6;
+  constexpr int kB = 2 * kStageBatch;  // loads in flight per thread
+  for (int e0 = 0; e0 < dim; e0 += 512 * kB) {
+    unsigned long long u[kB];
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      const int e = e0 + 512 * i + tid;
+      u[i] = e < dim ? ld_relaxed_u64(src + e) : 0ull;
+    }
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      const int e = e0 + 512 * i + tid;
+      if (e < dim) xs[e] = ll_value(src + e, u[i], tag, s_ok);
+    }
+  }
+  consumer_sync();
+  for (int jq = 4 * warp; jq < nb; jq += 4 * kGemvConsumerWarps) {
+    const int j = jq + (lane >> 3), e = j * 64 + (lane & 7) * 8;
+    float v[8];
+    if (e < dim) {
+      const float4 x0 = *reinterpret_cast<const float4*>(xs + e), x1 = *reinterpret_cast<const float4*>(xs + e + 4);
+      const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = e + i < dim ? xv[i] : 0.0f;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+    xq_store_chunk8(v, lane, 0, j, true, q);
   }
   consumer_sync();
 }
@@ -711,7 +828,8 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 template <int G>
 __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& Ly, int g, int z, int nz,
-                                          AttnTile<G>& T, uint64_t* bar, int& uses, int* s_last, int tl) {
+                                          AttnTile<G>& T, uint64_t* bar, int& uses, int* s_last, int tl,
+                                          volatile int* s_ok) {
   constexpr int HD = kHeadDim, HALF = kHeadDim / 2;
   const int gt = threadIdx.x;  // 0..511
   const int pos = a.pos, cap = a.max_seq;
@@ -733,30 +851,59 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
   // indices per thread, all loads issued first.
   const int qn = G * HALF, nwork = qn + (last ? HALF + HD : 0);
   float x0[2], x1[2], c[2], sv[2];
+  int o0[2], o1[2];  // offsets of the thread's inputs in q|k|v (-1: none)
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int w = gt + kAttnThreads * r;
-    x0[r] = x1[r] = c[r] = sv[r] = 0.0f;
+    c[r] = sv[r] = 0.0f;
+    o0[r] = o1[r] = -1;
     if (w < qn) {
       const int hh = w / HALF, j = w % HALF, h = g * G + hh;
-      x0[r] = __ldcg(row + h * HD + j);
-      x1[r] = __ldcg(row + h * HD + HALF + j);
+      o0[r] = h * HD + j;
+      o1[r] = o0[r] + HALF;
       c[r] = cs[j];
       sv[r] = sn[j];
-      if (Ly.qb != nullptr) { x0[r] += Ly.qb[h * HD + j]; x1[r] += Ly.qb[h * HD + HALF + j]; }
     } else if (w < qn + HALF && w < nwork) {
       const int j = w - qn;
-      const float* kr = row + (H + g) * HD;
-      x0[r] = __ldcg(kr + j);
-      x1[r] = __ldcg(kr + HALF + j);
+      o0[r] = (H + g) * HD + j;
+      o1[r] = o0[r] + HALF;
       c[r] = cs[j];
       sv[r] = sn[j];
-      if (Ly.kb != nullptr) { x0[r] += Ly.kb[g * HD + j]; x1[r] += Ly.kb[g * HD + HALF + j]; }
     } else if (w < nwork) {
-      const int j = w - qn - HALF;
-      x0[r] = __ldcg(row + (H + KV) * HD + g * HD + j);
-      if (Ly.vb != nullptr) x0[r] += Ly.vb[g * HD + j];
+      o0[r] = (H + KV) * HD + g * HD + (w - qn - HALF);
     }
+  }
+  if (a.tp == 1) {  // tagged q|k|v
+    const uint32_t tq = a.tag0 + (uint32_t)(5 * tl + 1);
+    unsigned long long u0[2], u1[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      u0[r] = o0[r] >= 0 ? ld_relaxed_u64(a.qkvll + o0[r]) : 0ull;
+      u1[r] = o1[r] >= 0 ? ld_relaxed_u64(a.qkvll + o1[r]) : 0ull;
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      x0[r] = o0[r] >= 0 ? ll_value(a.qkvll + o0[r], u0[r], tq, s_ok) : 0.0f;
+      x1[r] = o1[r] >= 0 ? ll_value(a.qkvll + o1[r], u1[r], tq, s_ok) : 0.0f;
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      x0[r] = o0[r] >= 0 ? __ldcg(row + o0[r]) : 0.0f;
+      x1[r] = o1[r] >= 0 ? __ldcg(row + o1[r]) : 0.0f;
+    }
+  }
+  // optional biases: q rows h*HD + j, k rows (H + g)*HD + j, v rows
+  // (H + KV + g)*HD + j of q|k|v map to offset o - {0, H*HD, (H+KV)*HD} of
+  // the layer's q, k, v bias vectors
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    if (o0[r] < 0) continue;
+    const float* b = o0[r] < H * HD ? Ly.qb : o0[r] < (H + KV) * HD ? Ly.kb : Ly.vb;
+    if (b == nullptr) continue;
+    const int bo = o0[r] < H * HD ? o0[r] : o0[r] < (H + KV) * HD ? o0[r] - H * HD : o0[r] - (H + KV) * HD;
+    x0[r] += b[bo];
+    if (o1[r] >= 0) x1[r] += b[bo + HALF];
   }
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
@@ -794,7 +941,7 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
   B2Q_FTRACE(tl, 12);
   if (gt == 0) {
     __threadfence();
-    const unsigned int old = atomicAdd(&a.sync->attn_cnt[g], 1u);
+    const unsigned int old = atomicAdd(&a.attn_cnt[tl * KV + g], 1u);
     *s_last = old == (unsigned int)(nz - 1);
   }
   consumer_sync();
@@ -864,10 +1011,12 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
       const int i = gt + kAttnThreads * r;
       if (i < G * HD) {
         const float v = O[r] * (1.0f / fmaxf(Ls[r], 1e-12f));
-        a.attng[a.rank][(g * G + i / HD) * HD + i % HD] = v;  // this rank's heads, local
+        const int oi = (g * G + i / HD) * HD + i % HD;  // this rank's heads, local
+        if (a.tp == 1) ll_store(a.attnll + oi, v, a.tag0 + (uint32_t)(5 * tl + 2));
+        else a.attng[a.rank][oi] = v;
       }
     }
-    if (gt == 0) a.sync->attn_cnt[g] = 0u;
+    if (gt == 0) a.attn_cnt[tl * KV + g] = 0u;
     B2Q_FTRACE(tl, 14);
   }
   consumer_sync();  // the tile and s_last are reused by the next item
@@ -941,9 +1090,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
   unsigned long long* bar = &a.sync->bar;
   int nbar = 0, nxbar = 0;  // this-GPU and all-rank barriers passed
   float* const x = a.xg[a.rank];
+  const bool ll = a.tp == 1;  // tagged hand-offs (DecodeArgs)
+  const int kp_e = round_up_int(a.E, 256);
+  float* xcopy = reinterpret_cast<float*>(xs + xq_smem_bytes(kp_e));
 
   // this CTA's phase table, and the token embedding (embed_rows_kernel's
-  // values) spread over the grid
+  // values): spread over the grid; one GPU: every CTA dequantises the row
+  // into shared memory and stores its slice of x, tagged
   {
     const int4* src = reinterpret_cast<const int4*>(a.ctab + (size_t)blockIdx.x * a.nph);
     int4* dst = reinterpret_cast<int4*>(tab);
@@ -952,15 +1105,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
     if (tok >= (uint32_t)a.V) tok = 0;
     const uint8_t* rowp = a.tok_raw + (int64_t)tok * a.tok_row_bytes;
     const int64_t slots = dequant_slots(a.tok_dtype, a.E);
-    for (int64_t sl = (int64_t)blockIdx.x * 512 + threadIdx.x; sl < slots; sl += (int64_t)gridDim.x * 512)
-      dequant_slot(rowp, a.tok_dtype, sl, x);
+    if (ll) {
+      for (int64_t sl = threadIdx.x; sl < slots; sl += kGemvConsumerWarps * 32)
+        dequant_slot(rowp, a.tok_dtype, sl, xcopy);
+      consumer_sync();
+      const int e0 = (int)((int64_t)a.E * blockIdx.x / gridDim.x), e1 = (int)((int64_t)a.E * (blockIdx.x + 1) / gridDim.x);
+      for (int e = e0 + threadIdx.x; e < e1; e += kGemvConsumerWarps * 32) ll_store(a.xll + e, xcopy[e], a.tag0);
+    } else {
+      for (int64_t sl = (int64_t)blockIdx.x * 512 + threadIdx.x; sl < slots; sl += (int64_t)gridDim.x * 512)
+        dequant_slot(rowp, a.tok_dtype, sl, x);
+    }
   }
-  grid_sync(bar, a.lbase, nbar, okp);
+  grid_sync(bar, a.lbase, nbar, okp, false, ll);
 
   const int nz = a.pos / kAttnTile + 1;
   int attn_uses = 0;  // completed phases of the attention mbarrier
-  const int kp_e = round_up_int(a.E, 256);
-  float* xcopy = reinterpret_cast<float*>(xs + xq_smem_bytes(kp_e));
   float best = -INFINITY;
   int idx = 0x7fffffff;
   // steps: per layer QKV, attention, O, gate/up, down; then the head
@@ -980,9 +1139,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       const DecLayer& Ly = a.layers[l];
       AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(xs);
       for (int it = blockIdx.x; it < a.KV * nz; it += gridDim.x)
-        attn_item<G>(a, Ly, it / nz, it % nz, nz, T, &attn_bar[0], attn_uses, &attn_last[0], l);
+        attn_item<G>(a, Ly, it / nz, it % nz, nz, T, &attn_bar[0], attn_uses, &attn_last[0], l, okp);
       B2Q_TRACE(tslot + 2);
-      grid_sync(bar, a.lbase, nbar, okp);  // the O projection reads this rank's heads
+      grid_sync(bar, a.lbase, nbar, okp, false, ll);  // the O projection reads this rank's heads
       continue;
     }
     const CtaPhase& ph = tab[head ? 4 * a.n_layers : 4 * l + (k == 0 ? 0 : k - 1)];
@@ -999,19 +1158,27 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       const int rows = (ph.ge - ph.gb) * 8;
       // global row of local row 0 (head: vocabulary rows of this rank)
       const int grow0 = row0 + (head ? a.v_off : 0);
-      // residual rows of this CTA: copied (L2 -> shared, asynchronously)
-      // behind the accumulators while the input is staged
-      float* resid = racc + 2 * rows;
+      // residual rows of this CTA (one GPU, tagged): copied (L2 -> shared,
+      // asynchronously) behind the accumulators while the input is staged;
+      // the epilogue checks each tag (and polls x for it if the copy was
+      // early, which only a CTA that staged no input of the previous phase
+      // can meet)
+      unsigned long long* resid = reinterpret_cast<unsigned long long*>(racc + 2 * rows);
       if (add)
-        for (int r4 = threadIdx.x; 4 * r4 < nrows; r4 += kGemvConsumerWarps * 32)
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(resid + 4 * r4)),
-                       "l"(x + grow0 + 4 * r4)
+        for (int r2 = threadIdx.x; 2 * r2 < nrows; r2 += kGemvConsumerWarps * 32)
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(resid + 2 * r2)),
+                       "l"(a.xll + grow0 + 2 * r2)
                        : "memory");
       // stage the input: rmsnorm(x) for QKV, gate/up and the head; attn; h
       XQ q;
       if (k == 2) {
-        q = smem_xq(xs, round_up_int(a.H * kHeadDim, 256));
-        stage_plain(a.attng[a.rank], a.H * kHeadDim, q);
+        const int kp_a = round_up_int(a.H * kHeadDim, 256);
+        q = smem_xq(xs, kp_a);
+        if (ll)
+          stage_plain_ll(a.attnll, a.H * kHeadDim, q, reinterpret_cast<float*>(xs + xq_smem_bytes(kp_a)),
+                         a.tag0 + (uint32_t)(5 * l + 2), okp);
+        else
+          stage_plain(a.attng[a.rank], a.H * kHeadDim, q);
       } else if (k == 4) {
         q = smem_xq(xs, round_up_int(a.Fl, 256));
         stage_plain(a.hg[a.rank], a.Fl, q);
@@ -1024,7 +1191,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
         else if (after_o)
           stage_rmsnorm(x, nw, a.E, a.eps, q, xcopy, red, l, 4, a.partg[a.rank], a.tp, a.xalt);
         else
-          stage_rmsnorm(x, nw, a.E, a.eps, q, xcopy, red, l, k == 0 ? 0 : 4);
+          stage_rmsnorm(x, nw, a.E, a.eps, q, xcopy, red, l, k == 0 ? 0 : 4, nullptr, 0, nullptr,
+                        ll ? a.xll : nullptr, a.tag0 + (uint32_t)(5 * l + (k == 0 ? 0 : 3)), okp);
       }
       B2Q_TRACE(tslot + 1);
       B2Q_FTRACE(l, 21 + k);
@@ -1040,7 +1208,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
         for (int r = threadIdx.x; r < nrows; r += kGemvConsumerWarps * 32) {
           const float v = dec_racc(racc, rows, nw, r, 0);
           if (k == 0 && !head) {  // q/k/v: this rank's heads, local
-            a.qkv[ph.ycol + row0 + r] = v;
+            if (ll) ll_store(a.qkvll + ph.ycol + row0 + r, v, a.tag0 + (uint32_t)(5 * l + 1));
+            else a.qkv[ph.ycol + row0 + r] = v;
             continue;
           }
           if (pair) {  // SwiGLU rows of this rank, local
@@ -1052,9 +1221,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
             for (int p = 0; p < a.tp; ++p) a.partg[p][o] = v;
             continue;
           }
-          const float out = add ? resid[r] + v : v;
+          if (add) {  // one GPU: x += v, tagged for the next phase (gate/up, or the next layer's QKV)
+            const float xr = ll_value(a.xll + grow0 + r, resid[r], a.tag0 + (uint32_t)(5 * l + (k == 2 ? 0 : 3)), okp);
+            ll_store(a.xll + grow0 + r, xr + v, a.tag0 + (uint32_t)(k == 2 ? 5 * l + 3 : 5 * (l + 1)));
+            continue;
+          }
           float* const* yg = head ? a.logitsg : a.xg;
-          for (int p = 0; p < a.tp; ++p) yg[p][grow0 + r] = out;
+          for (int p = 0; p < a.tp; ++p) yg[p][grow0 + r] = v;
           if (head && v > best) { best = v; idx = grow0 + r; }
         }
       }
@@ -1071,8 +1244,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
     if (head) break;
     // all ranks meet after the K-split projections (O, down); the other
     // phases only need this rank's CTAs
-    if (k == 2 || k == 4) xgrid_sync(a, bar, nbar, nxbar, okp);
-    else grid_sync(bar, a.lbase, nbar, okp);
+    // (one GPU: gates in front of tagged data, except h after gate/up)
+    if (k == 2 || k == 4) xgrid_sync(a, bar, nbar, nxbar, okp, true);
+    else grid_sync(bar, a.lbase, nbar, okp, false, ll && k != 3);
   }
   warp_argmax(best, idx);
   if (lane == 0) { s_bv[warp] = best; s_bi[warp] = idx; }

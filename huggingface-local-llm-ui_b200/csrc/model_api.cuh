@@ -436,6 +436,8 @@ b2q_status b2q_clear_state(b2q_model* M) {
     cudaSetDevice(M->eng->device);
     // (all ranks of a tensor-parallel model call it together)
     cudaError_t err = cudaMemsetAsync(M->dec_sync, 0, sizeof(b2q::DecSync), M->st);
+    if (err == cudaSuccess)
+      err = cudaMemsetAsync(M->dec_attn_cnt, 0, sizeof(unsigned int) * M->c.n_layers * M->KV_loc, M->st);
     const b2q::XBlock xl = b2q::xblock_layout(M->c.n_embd, M->c.n_heads * M->c.head_dim, M->c.n_ff,
                                               M->c.n_vocab, M->c.tp_size, M->eng->num_sms);
     if (err == cudaSuccess)
@@ -472,7 +474,8 @@ b2q_status b2q_model_destroy(b2q_model* M) {
   b2q_weight_free(M->output);
   void* ps[] = {M->tok_raw, M->output_norm, M->x, M->qkv, M->attn, M->attn_loc, M->hbuf, M->h_loc,
                 M->y_loc, M->logits, M->logits_loc, M->part, M->tokens, M->argmax, M->pos, M->xn,
-                M->rope_cos, M->rope_sin, M->dec_layers, M->dec_tab, M->dec_sync, M->dec_xblock};
+                M->rope_cos, M->rope_sin, M->dec_layers, M->dec_tab, M->dec_sync, M->dec_xblock,
+                M->dec_attn_cnt, M->dec_ll};
   for (int p = 0; p < b2q::kMaxTp; ++p)
     if (M->dec_peer[p] && p != M->c.tp_rank) cudaIpcCloseMemHandle(M->dec_peer[p]);
   for (void* p : ps)

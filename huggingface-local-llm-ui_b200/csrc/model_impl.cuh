@@ -75,6 +75,9 @@ struct b2q_model {
   uint64_t dec_launches = 0;
   const float* last_logits = nullptr;       // where the last forward left its logits
   b2q::DecSync* dec_sync = nullptr;
+  unsigned int* dec_attn_cnt = nullptr;      // [n_layers][KV_loc] attention split arrivals
+  unsigned long long* dec_ll = nullptr;      // one GPU: tagged x | q|k|v | attention output
+  uint64_t dec_tags = 0;                     // tagged hand-offs issued (never reset: tags stay unique)
   b2q::DecodeArgs dec{};
   size_t dec_smem = 0;
   int dec_G = 0;
@@ -558,7 +561,7 @@ static cudaError_t setup_decode(b2q_model* M) {
   const b2q_model_config& c = M->c;
   b2q_engine* e = M->eng;
   M->dec_on = false;
-  // KV heads within the arrival counters; ranks within the peer tables
+  // at most 64 KV heads per rank; ranks within the peer tables
   const int P = c.tp_size, rk = c.tp_rank;
   if (M->KV_loc > 64 || P > kMaxTp) return cudaSuccess;
   const int H = M->H_loc, KV = M->KV_loc, G = H / KV, hd = c.head_dim;
@@ -627,7 +630,8 @@ static cudaError_t setup_decode(b2q_model* M) {
       tab[(size_t)b * nph + p] = r;
       // accumulators [2][nw][rows]; O and down also keep their residual rows
       const bool add = p < 4 * c.n_layers && (p % 4 == kPhO || p % 4 == kPhDown);
-      const size_t per_row = phases[(size_t)p]->pair ? 4 : add ? 3 : 2;
+      // (the residual rows are tagged 8-byte words)
+      const size_t per_row = phases[(size_t)p]->pair ? 4 : add ? 4 : 2;
       racc = std::max(racc, per_row * (r.ge - r.gb) * 8 * sizeof(float));
     }
   racc = round128(racc);
@@ -636,7 +640,12 @@ static cudaError_t setup_decode(b2q_model* M) {
   const int kp_e = round_up_int(c.n_embd, 256);
   const int kpmax = std::max({kp_e, round_up_int(H * hd, 256), round_up_int(c.n_ff, 256)});
   const size_t tile = round128(attn_one);
-  size_t stage = std::max(xq_smem_bytes(kpmax), xq_smem_bytes(kp_e) + (size_t)4 * c.n_embd);
+  // staging: the largest quantised input; the RMSNorm copy of x behind the
+  // quantised x; the float copy of the tagged attention output behind the
+  // quantised attention output (one GPU)
+  const int kp_a = round_up_int(H * hd, 256);
+  size_t stage = std::max({xq_smem_bytes(kpmax), xq_smem_bytes(kp_e) + (size_t)4 * c.n_embd,
+                           xq_smem_bytes(kp_a) + (size_t)4 * round_up_int(H * hd, 8)});
   if (stage + racc < tile) stage = tile - racc;
   stage = round128(stage);
   const size_t tabb = round128((size_t)nph * sizeof(CtaPhase));
@@ -660,6 +669,11 @@ static cudaError_t setup_decode(b2q_model* M) {
   if (err == cudaSuccess)
     err = cudaMemcpy(M->dec_tab, tab.data(), tab.size() * sizeof(CtaPhase), cudaMemcpyHostToDevice);
   if (err == cudaSuccess) err = dalloc(&M->dec_sync, 1);
+  if (err == cudaSuccess) err = dalloc(&M->dec_attn_cnt, (size_t)c.n_layers * KV);
+  // tagged vectors (one GPU): x (rounded up to even: the residual copy reads
+  // pairs), q|k|v, attention output
+  const size_t ll_x = (size_t)round_up_int(c.n_embd, 2), ll_qkv = (size_t)(H + 2 * KV) * hd, ll_attn = (size_t)H * hd;
+  if (err == cudaSuccess && P == 1) err = dalloc(&M->dec_ll, ll_x + ll_qkv + ll_attn);
   const XBlock xl = xblock_layout(c.n_embd, c.n_heads * hd, c.n_ff, c.n_vocab, P, grid);
   if (err == cudaSuccess) err = dalloc(reinterpret_cast<uint8_t**>(&M->dec_xblock), xl.total);
   if (err != cudaSuccess) return err;
@@ -703,6 +717,12 @@ static cudaError_t setup_decode(b2q_model* M) {
   a.part = M->part;
   a.nsplit = M->nsplit;
   a.sync = M->dec_sync;
+  a.attn_cnt = M->dec_attn_cnt;
+  if (P == 1) {
+    a.xll = M->dec_ll;
+    a.qkvll = M->dec_ll + ll_x;
+    a.attnll = M->dec_ll + ll_x + ll_qkv;
+  }
   a.argmax = M->argmax;
   a.tp = P;
   a.rank = rk;
@@ -740,6 +760,10 @@ static cudaError_t launch_decode(b2q_model* M, const uint32_t* tok, int pos, uin
   // only, 2L + 1 as the first level of an all-rank barrier) and 2L + 1
   // all-rank epochs
   const unsigned long long seq = M->dec_launches++, grid = (unsigned long long)M->eng->num_sms;
+  // tags of this launch: 5 per layer plus the head's input (wrap-around is
+  // harmless: every launch rewrites every tagged element)
+  a.tag0 = (uint32_t)(M->dec_tags + 1);
+  M->dec_tags += 5ull * a.n_layers + 5ull;
   a.lbase = seq * (5ull * a.n_layers + 2ull) * grid;
   a.xepoch = seq * (2ull * a.n_layers + 1ull);
   cudaLaunchConfig_t cfg = {};
