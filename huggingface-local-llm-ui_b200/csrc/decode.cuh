@@ -239,30 +239,38 @@ __device__ __forceinline__ void ll_store(unsigned long long* p, float v, uint32_
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
-// Polls p until it carries `tag` (out of line: the rare path).  Bounded: a
+// Polls (rare: the value was stored but not yet visible) are bounded by a
+// count; each one is an L2 round trip, so the limit is seconds.
+constexpr int kLLPollLimit = 1 << 22;
+
+// The value of `first` (an earlier load of p) once p carries `tag`.  A
 // timeout raises the device error word and clears *s_ok, after which this
 // CTA polls no more (the value is then whatever was read).
-__device__ __noinline__ unsigned long long ll_poll(const unsigned long long* p, uint32_t tag, volatile int* s_ok) {
-  unsigned long long v = ld_relaxed_u64(p);
-  if (!*s_ok) return v;
-  const long long t0 = clock64();
-  while ((uint32_t)(v >> 32) != tag) {
-    __nanosleep(32);
-    v = ld_relaxed_u64(p);
-    if (clock64() - t0 > kSpinLimitCycles) {
-      atomicExch(&g_b2q_device_error, 5);
-      *s_ok = 0;
-      break;
-    }
-  }
-  return v;
-}
-
-// The value of `first` (an earlier load of p) once p carries `tag`.
 __device__ __forceinline__ float ll_value(const unsigned long long* p, unsigned long long first, uint32_t tag,
                                           volatile int* s_ok) {
-  const unsigned long long v = (uint32_t)(first >> 32) == tag ? first : ll_poll(p, tag, s_ok);
+  unsigned long long v = first;
+  if ((uint32_t)(v >> 32) != tag) {
+    for (int it = 0; (uint32_t)(v >> 32) != tag && it < kLLPollLimit && *s_ok; ++it) {
+      __nanosleep(32);
+      v = ld_relaxed_u64(p);
+    }
+    if ((uint32_t)(v >> 32) != tag && *s_ok) {
+      atomicExch(&g_b2q_device_error, 5);
+      *s_ok = 0;
+    }
+  }
   return __uint_as_float((uint32_t)v);
+}
+
+// consumer_sync that also returns whether `v` was true on any consumer thread
+__device__ __forceinline__ bool consumer_sync_or(bool v) {
+  unsigned r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 512, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((unsigned)v)
+      : "memory");
+  return r != 0;
 }
 
 // Barrier over the consumer warps of every CTA of this GPU.  The counter
@@ -386,21 +394,22 @@ __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, in
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = q.kpad >> 6;
   float sa = 0.0f, sb = 0.0f;
+  uint32_t bad = 0u;  // nonzero: some tagged element read here was not yet visible
   for (int e0 = 0; e0 < dim; e0 += 1024 * kStageBatch) {
     float va[kStageBatch], vb[kStageBatch];
-    if (xll != nullptr) {  // every load of the batch in flight, then the tags
+    if (xll != nullptr) {  // every load of the batch in flight; the tags are checked in bulk below
       unsigned long long ua[kStageBatch], ub[kStageBatch];
 #pragma unroll
       for (int i = 0; i < kStageBatch; ++i) {
         const int ea = e0 + 1024 * i + tid, eb = ea + 512;
-        ua[i] = ea < dim ? ld_relaxed_u64(xll + ea) : 0ull;
-        ub[i] = eb < dim ? ld_relaxed_u64(xll + eb) : 0ull;
+        ua[i] = ea < dim ? ld_relaxed_u64(xll + ea) : (unsigned long long)tag << 32;
+        ub[i] = eb < dim ? ld_relaxed_u64(xll + eb) : (unsigned long long)tag << 32;
       }
 #pragma unroll
       for (int i = 0; i < kStageBatch; ++i) {
-        const int ea = e0 + 1024 * i + tid, eb = ea + 512;
-        va[i] = ea < dim ? ll_value(xll + ea, ua[i], tag, s_ok) : 0.0f;
-        vb[i] = eb < dim ? ll_value(xll + eb, ub[i], tag, s_ok) : 0.0f;
+        bad |= ((uint32_t)(ua[i] >> 32) ^ tag) | ((uint32_t)(ub[i] >> 32) ^ tag);
+        va[i] = __uint_as_float((uint32_t)ua[i]);
+        vb[i] = __uint_as_float((uint32_t)ub[i]);
       }
     } else {
 #pragma unroll
@@ -437,7 +446,32 @@ __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, in
     red[warp] = sa;
     red[warp + 16] = sb;
   }
-  consumer_sync();
+  if (consumer_sync_or(bad != 0u)) {
+    // rare: read x again, polling for the tag, and redo the sums in the same order
+    sa = sb = 0.0f;
+    for (int e0 = 0; e0 < dim; e0 += 1024 * kStageBatch)
+#pragma unroll
+      for (int i = 0; i < kStageBatch; ++i) {
+        const int ea = e0 + 1024 * i + tid, eb = ea + 512;
+        if (ea < dim) {
+          const float v = ll_value(xll + ea, ld_relaxed_u64(xll + ea), tag, s_ok);
+          sa = fmaf(v, v, sa);
+          xs[ea] = v;
+        }
+        if (eb < dim) {
+          const float v = ll_value(xll + eb, ld_relaxed_u64(xll + eb), tag, s_ok);
+          sb = fmaf(v, v, sb);
+          xs[eb] = v;
+        }
+      }
+    sa = warp_sum(sa);
+    sb = warp_sum(sb);
+    if (lane == 0) {
+      red[warp] = sa;
+      red[warp + 16] = sb;
+    }
+    consumer_sync();
+  }
   B2Q_FTRACE(tl, tb + 1);
   if (xw != nullptr) {
     const int e0 = (int)((int64_t)dim * blockIdx.x / gridDim.x), e1 = (int)((int64_t)dim * (blockIdx.x + 1) / gridDim.x);
@@ -502,20 +536,25 @@ __device__ __forceinline__ void stage_plain_ll(const unsigned long long* src, in
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = q.kpad >> 6;
   constexpr int kB = 2 * kStageBatch;  // loads in flight per thread
+  uint32_t bad = 0u;
   for (int e0 = 0; e0 < dim; e0 += 512 * kB) {
     unsigned long long u[kB];
 #pragma unroll
     for (int i = 0; i < kB; ++i) {
       const int e = e0 + 512 * i + tid;
-      u[i] = e < dim ? ld_relaxed_u64(src + e) : 0ull;
+      u[i] = e < dim ? ld_relaxed_u64(src + e) : (unsigned long long)tag << 32;
     }
 #pragma unroll
     for (int i = 0; i < kB; ++i) {
       const int e = e0 + 512 * i + tid;
-      if (e < dim) xs[e] = ll_value(src + e, u[i], tag, s_ok);
+      bad |= (uint32_t)(u[i] >> 32) ^ tag;
+      if (e < dim) xs[e] = __uint_as_float((uint32_t)u[i]);
     }
   }
-  consumer_sync();
+  if (consumer_sync_or(bad != 0u)) {  // rare: read again, polling for the tag
+    for (int e = tid; e < dim; e += 512) xs[e] = ll_value(src + e, ld_relaxed_u64(src + e), tag, s_ok);
+    consumer_sync();
+  }
   for (int jq = 4 * warp; jq < nb; jq += 4 * kGemvConsumerWarps) {
     const int j = jq + (lane >> 3), e = j * 64 + (lane & 7) * 8;
     float v[8];
