@@ -30,8 +30,11 @@
 //    microseconds.
 // Every value is computed with the same operations in the same order as the
 // per-kernel path (layer.cuh, gemv.cuh), so the logits are bit-identical to
-// it.  Cross-CTA data (x, qkv, attn, h, attention partials) is read with
-// L2-coherent loads (ld.global.cg) after the barriers.  Every wait is bounded
+// it.  Cross-CTA data is read from L2 after the barriers: on one GPU x, q|k|v
+// and the attention output as tagged 8-byte words (value and hand-off tag in
+// one store, see DecodeArgs), behind relaxed barriers; h, the attention
+// partials and, under tensor parallelism, everything else with L2-coherent
+// loads (ld.global.cg) behind release/acquire barriers.  Every wait is bounded
 // (kSpinLimitCycles); a CTA whose wait gave up raises the device error word
 // and skips its remaining barrier waits, so the kernel always ends.
 #pragma once
