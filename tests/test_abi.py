@@ -78,3 +78,34 @@ def test_ggml_type_table(pkg):
         ggml.from_u32(4)
     with pytest.raises(ValueError):
         ggml.row_bytes(ggml.Q4_K, 100)
+
+
+def test_header_is_plain_c_and_links_from_c(pkg, tmp_path):
+    """The boundary is for foreign-function callers (Rust extern "C", cgo,
+    ctypes): the header must compile as strict C99, and a C program must link
+    against the library and call it (version string; init without a device
+    or on a bad device id returns a status and an error message)."""
+    import shutil
+    import subprocess
+    from hf_llm_b200 import build
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    lib = build.build()
+    src = tmp_path / "abi.c"
+    src.write_text(
+        '#include <stdio.h>\n#include "b2q.h"\n'
+        "int main(void) {\n"
+        "  b2q_engine* e = NULL;\n"
+        "  b2q_status s = b2q_init(-1, &e);\n"
+        '  printf("%s|%d|%d|%s\\n", b2q_version(), (int)s, e == NULL, b2q_last_error());\n'
+        "  return s == B2Q_OK;\n"
+        "}\n")
+    exe = tmp_path / "abi"
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", f"-I{HEADER.parent}",
+                    str(src), "-o", str(exe), f"-L{lib.parent}", "-lb2q", f"-Wl,-rpath,{lib.parent}"],
+                   check=True, capture_output=True, text=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    version, status, null_out, err = r.stdout.strip().split("|", 3)
+    assert version.startswith("b2q") and int(status) != 0 and null_out == "1" and err
