@@ -93,6 +93,9 @@ SIGNATURES = [
     ("b2q_time_gemv", _I, [_VP, C.POINTER(_VP), _I, _VP, _I, _I, _VP, C.POINTER(C.c_float)]),
     ("b2q_kernel_launch_count", C.c_uint64, [_VP]),
     ("b2q_check_device_error", _I, [_VP]),
+    ("b2q_set_wait_limit_cycles", _I, [_VP, C.c_longlong]),
+    ("b2q_model_debug_desync", _I, [_VP]),
+    ("b2q_set_tp_init_timeout_ms", _I, [_I]),
 ]
 
 _lib = None

@@ -868,6 +868,17 @@ b2q_status b2q_sample_dev(b2q_engine* e, const float* logits_dev, int n, float t
                      stream ? (cudaStream_t)stream : e->stream);
 }
 
+b2q_status b2q_set_wait_limit_cycles(b2q_engine* e, long long cycles) {
+  if (!e) return set_error(B2Q_EINVAL, "engine is NULL");
+  if (cycles <= 0) cycles = kSpinLimitCycles;
+  std::lock_guard<std::mutex> lk(e->mu);
+  cudaSetDevice(e->device);
+  cudaError_t err = cudaStreamSynchronize(e->stream);
+  if (err == cudaSuccess) err = cudaMemcpyToSymbol(g_b2q_wait_limit, &cycles, sizeof cycles);
+  if (err != cudaSuccess) return cuda_error(err, "b2q_set_wait_limit_cycles");
+  return B2Q_OK;
+}
+
 b2q_status b2q_check_device_error(b2q_engine* e) {
   if (!e) return set_error(B2Q_EINVAL, "engine is NULL");
   cudaSetDevice(e->device);

@@ -8,12 +8,19 @@
 #define B2Q_FULL 0xffffffffu
 
 // Device error word: set by a kernel whose bounded wait gave up
-// (B2Q_ETIMEOUT = 5).  Read and cleared by b2q_check_device_error().
+// (B2Q_ETIMEOUT = 5).  Read and cleared by b2q_check_device_error() and by
+// the blocking forward entry points.
 // libb2q is a single translation unit (b2q_api.cu includes the rest).
 __device__ int g_b2q_device_error = 0;
 
-// Upper bound for any spin on an mbarrier, in SM clock cycles (~1-2 s).
+// Upper bound for any spin (an mbarrier, a grid or all-rank barrier, a
+// tagged hand-off), in SM clock cycles: 4e9 (~2 s at 1.965 GHz) unless the
+// host lowers it with b2q_set_wait_limit_cycles().  Read only on the slow
+// path of a wait, so the common case costs no load.
 constexpr long long kSpinLimitCycles = 4000000000ll;
+__device__ long long g_b2q_wait_limit = kSpinLimitCycles;
+
+__device__ __forceinline__ long long wait_limit() { return *(volatile long long*)&g_b2q_wait_limit; }
 
 // ---------------------------------------------------------------------------
 // Global loads.  Weights are read once per token and never reused by the
@@ -144,12 +151,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait: returns false (and raises the device error word) if the
-// phase did not complete within kSpinLimitCycles.
+// phase did not complete within the wait limit (g_b2q_wait_limit cycles).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;  // the common case: no clock reads
-  const long long t0 = clock64();
+  const long long t0 = clock64(), lim = wait_limit();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kSpinLimitCycles) {
+    if (clock64() - t0 > lim) {
       atomicExch(&g_b2q_device_error, 5);
       return false;
     }

@@ -35,7 +35,7 @@
 // one store, see DecodeArgs), behind relaxed barriers; h, the attention
 // partials and, under tensor parallelism, everything else with L2-coherent
 // loads (ld.global.cg) behind release/acquire barriers.  Every wait is bounded
-// (kSpinLimitCycles); a CTA whose wait gave up raises the device error word
+// (g_b2q_wait_limit cycles); a CTA whose wait gave up raises the device error word
 // and skips its remaining barrier waits, so the kernel always ends.
 #pragma once
 
@@ -242,10 +242,6 @@ __device__ __forceinline__ void ll_store(unsigned long long* p, float v, uint32_
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
-// Polls (rare: the value was stored but not yet visible) are bounded by a
-// count; each one is an L2 round trip, so the limit is seconds.
-constexpr int kLLPollLimit = 1 << 22;
-
 // The value of `first` (an earlier load of p) once p carries `tag`.  A
 // timeout raises the device error word and clears *s_ok, after which this
 // CTA polls no more (the value is then whatever was read).
@@ -253,7 +249,10 @@ __device__ __forceinline__ float ll_value(const unsigned long long* p, unsigned 
                                           volatile int* s_ok) {
   unsigned long long v = first;
   if ((uint32_t)(v >> 32) != tag) {
-    for (int it = 0; (uint32_t)(v >> 32) != tag && it < kLLPollLimit && *s_ok; ++it) {
+    // polls (rare: the value was stored but not yet visible) are bounded by
+    // the wait limit in clock cycles
+    const long long t0 = clock64(), lim = wait_limit();
+    while ((uint32_t)(v >> 32) != tag && *s_ok && clock64() - t0 <= lim) {
       __nanosleep(32);
       v = ld_relaxed_u64(p);
     }
@@ -292,9 +291,9 @@ __device__ __forceinline__ void grid_sync(unsigned long long* bar, unsigned long
     else if (relaxed) asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
     else asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
     const unsigned long long target = base + (unsigned long long)(k + 1) * gridDim.x;
-    const long long t0 = clock64();
+    const long long t0 = clock64(), lim = wait_limit();
     while ((relaxed ? ld_relaxed_u64(bar) : ld_acquire_u64(bar)) < target) {
-      if (clock64() - t0 > kSpinLimitCycles) {
+      if (clock64() - t0 > lim) {
         atomicExch(&g_b2q_device_error, 5);
         *s_ok = 0;
         break;
@@ -333,9 +332,9 @@ __device__ __forceinline__ void xgrid_sync(const DecodeArgs& a, unsigned long lo
   if (p < a.tp && p != a.rank && *s_ok) {
     if (blockIdx.x == 0) st_release_sys_u64(a.xflagg[p] + a.rank, epoch);
     const unsigned long long* slot = a.xflagg[a.rank] + p;
-    const long long t0 = clock64();
+    const long long t0 = clock64(), lim = wait_limit();
     while (ld_acquire_sys_u64(slot) < epoch) {
-      if (clock64() - t0 > kSpinLimitCycles) {
+      if (clock64() - t0 > lim) {
         atomicExch(&g_b2q_device_error, 5);
         *s_ok = 0;
         break;

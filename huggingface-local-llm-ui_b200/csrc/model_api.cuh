@@ -13,6 +13,12 @@ b2q_status b2q_tp_unique_id(unsigned char out[128]) {
   return tp_unique_id(out);
 }
 
+b2q_status b2q_set_tp_init_timeout_ms(int ms) {
+  if (ms <= 0) return set_error(B2Q_EINVAL, "b2q_set_tp_init_timeout_ms: %d ms", ms);
+  tp_timeout_ms() = ms;
+  return B2Q_OK;
+}
+
 b2q_status b2q_model_create(b2q_engine* e, const b2q_model_config* cfg, const unsigned char* tp_id,
                             b2q_model** out) {
   if (!e || !cfg || !out) return set_error(B2Q_EINVAL, "b2q_model_create: NULL argument");
@@ -294,6 +300,7 @@ b2q_status b2q_model_finalize(b2q_model* M) {
   if (err == cudaSuccess) err = xq_alloc(&M->xq_a, mm, H * hd);
   if (err == cudaSuccess) err = xq_alloc(&M->xq_f, mm, c.n_ff);
   if (err == cudaSuccess) err = cudaMallocHost(&M->h_tok, sizeof(uint32_t) * mm);
+  if (err == cudaSuccess) err = cudaMallocHost(&M->h_err, sizeof(int));
   if (err != cudaSuccess) return cuda_error(err, "b2q_model_finalize: allocation");
   // RoPE tables: freq = 1/theta^(2j/hd) in f32 powf, angle in f32, f32 cos/sin
   // (inference.rs:2538-2549), for positions 0..8191
@@ -339,7 +346,14 @@ static b2q_status forward_impl(b2q_model* M, const uint32_t* tokens, bool tok_on
     for (int i = 0; i < n; ++i)
       if (tokens[i] >= (uint32_t)c.n_vocab)
         return set_error(B2Q_EINVAL, "forward: token id %u >= vocab %d", tokens[i], c.n_vocab);
-  cudaError_t err = cudaSuccess;
+  // Under stream capture a single-token step takes the per-kernel path: the
+  // persistent kernel's barrier bases and hand-off tags are host counters
+  // baked into each launch's arguments, so a replayed launch would reuse
+  // them (stale tags would pass, barrier targets would not match).
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaError_t err = cudaStreamIsCapturing(st, &cap);
+  if (err != cudaSuccess) return cuda_error(err, "forward: cudaStreamIsCapturing");
+  const bool capturing = cap != cudaStreamCaptureStatusNone;
   for (int off = 0; off < n && err == cudaSuccess; off += M->mmax) {
     const int m = std::min(M->mmax, n - off);
     const uint32_t* src = tokens + off;
@@ -350,7 +364,7 @@ static b2q_status forward_impl(b2q_model* M, const uint32_t* tokens, bool tok_on
       if (err != cudaSuccess) break;
       src = M->tokens + M->mmax;
     }
-    if (m == 1 && M->dec_on) {
+    if (m == 1 && M->dec_on && !capturing) {
       // one persistent kernel for the whole step (validates the id itself)
       err = launch_decode(M, src, start + off, argmax_dev, st);
       M->last_logits = M->dec_logits;
@@ -362,7 +376,7 @@ static b2q_status forward_impl(b2q_model* M, const uint32_t* tokens, bool tok_on
     set_step_kernel<<<1, 64, 0, st>>>(M->pos, start + off, M->tokens, src, m, c.n_vocab);
     err = cudaGetLastError();
     if (err != cudaSuccess) break;
-    if (m == 1 && M->graph) {
+    if (m == 1 && M->graph && !capturing) {
       err = cudaGraphLaunch(M->graph, st);
       M->eng->launches.fetch_add(M->graph_kernels);
     } else {
@@ -395,6 +409,51 @@ b2q_status b2q_forward_dev(b2q_model* M, const uint32_t* tokens_dev, int n, int 
   return B2Q_OK;
 }
 
+// Re-arm the persistent kernel's synchronisation state: the grid-barrier
+// counter, the attention split counters, this rank's all-rank epoch slots and
+// the host's launch sequence (the barrier bases and epochs of the next launch
+// start from zero again).  A step whose bounded wait gave up leaves them
+// inconsistent.  Caller holds the engine lock; synchronous on M->st.
+static cudaError_t rearm_decode(b2q_model* M) {
+  if (!M->dec_sync) return cudaSuccess;
+  cudaError_t err = cudaMemsetAsync(M->dec_sync, 0, sizeof(b2q::DecSync), M->st);
+  if (err == cudaSuccess)
+    err = cudaMemsetAsync(M->dec_attn_cnt, 0, sizeof(unsigned int) * M->c.n_layers * M->KV_loc, M->st);
+  const b2q::XBlock xl = b2q::xblock_layout(M->c.n_embd, M->c.n_heads * M->c.head_dim, M->c.n_ff,
+                                            M->c.n_vocab, M->c.tp_size, M->eng->num_sms);
+  if (err == cudaSuccess)
+    err = cudaMemsetAsync(static_cast<uint8_t*>(M->dec_xblock) + xl.bar, 0, 8 * b2q::kMaxTp, M->st);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
+  M->dec_launches = 0;
+  return err;
+}
+
+// Queue the read-back of the device error word behind a blocking forward's
+// work on M->st (into pinned M->h_err; no extra synchronisation).
+static cudaError_t queue_error_readback(b2q_model* M) {
+  return cudaMemcpyFromSymbolAsync(M->h_err, g_b2q_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, M->st);
+}
+
+// After M->st has been synchronised: a nonzero device error word means a
+// bounded wait gave up during the step, so its outputs are not valid.  The
+// word is cleared and B2Q_ETIMEOUT returned.  On one GPU the persistent
+// kernel's synchronisation state is re-armed here, so the next step runs
+// normally; under tensor parallelism every rank must call b2q_clear_state
+// (together, followed by a host barrier across the ranks) before the next
+// step, since a rank cannot re-arm its peers' epoch slots on its own.
+static b2q_status forward_error_check(b2q_model* M, const char* what) {
+  const int v = *M->h_err;
+  if (v == 0) return B2Q_OK;
+  *M->h_err = 0;
+  const int zero = 0;
+  cudaError_t err = cudaMemcpyToSymbolAsync(g_b2q_device_error, &zero, sizeof zero, 0, cudaMemcpyHostToDevice, M->st);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
+  if (err == cudaSuccess && M->c.tp_size == 1) err = rearm_decode(M);
+  if (err != cudaSuccess) return cuda_error(err, what);
+  return set_error(B2Q_ETIMEOUT, "%s: a device-side bounded wait gave up (code %d); the step's outputs are invalid%s",
+                   what, v, M->c.tp_size > 1 ? "; every rank must call b2q_clear_state" : "");
+}
+
 b2q_status b2q_forward(b2q_model* M, const uint32_t* tokens, int n, int start, float* logits,
                        uint32_t* argmax) {
   if (!M || !tokens) return set_error(B2Q_EINVAL, "b2q_forward: NULL argument");
@@ -408,9 +467,10 @@ b2q_status b2q_forward(b2q_model* M, const uint32_t* tokens, int n, int start, f
     err = cudaMemcpyAsync(logits, M->last_logits, sizeof(float) * M->c.n_vocab, cudaMemcpyDeviceToHost, M->st);
   if (err == cudaSuccess && argmax)
     err = cudaMemcpyAsync(argmax, M->argmax, sizeof(uint32_t), cudaMemcpyDeviceToHost, M->st);
+  if (err == cudaSuccess) err = queue_error_readback(M);
   if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
   if (err != cudaSuccess) return cuda_error(err, "b2q_forward");
-  return B2Q_OK;
+  return forward_error_check(M, "b2q_forward");
 }
 
 b2q_status b2q_forward_sample(b2q_model* M, const uint32_t* tokens, int n, int start, float temperature,
@@ -421,7 +481,24 @@ b2q_status b2q_forward_sample(b2q_model* M, const uint32_t* tokens, int n, int s
   cudaSetDevice(M->eng->device);
   b2q_status s = forward_impl(M, tokens, false, n, start, M->st);
   if (s != B2Q_OK) return s;
-  return sample_core(M->eng, M->last_logits, M->c.n_vocab, temperature, top_p, rng_state, token, M->st);
+  cudaError_t err = queue_error_readback(M);
+  if (err != cudaSuccess) return cuda_error(err, "b2q_forward_sample");
+  // the sampler synchronises M->st, which also completes the read-back; a
+  // step whose wait gave up reports that instead of its (invalid) token
+  const uint64_t rng0 = *rng_state;
+  s = sample_core(M->eng, M->last_logits, M->c.n_vocab, temperature, top_p, rng_state, token, M->st);
+  if (s != B2Q_OK) return s;
+  s = forward_error_check(M, "b2q_forward_sample");
+  if (s != B2Q_OK) *rng_state = rng0;
+  return s;
+}
+
+b2q_status b2q_model_debug_desync(b2q_model* M) {
+  if (!M || !M->finalized) return set_error(B2Q_EINVAL, "b2q_model_debug_desync: model not finalized");
+  if (!M->dec_on) return set_error(B2Q_EUNSUP, "b2q_model_debug_desync: the model has no persistent decode step");
+  std::lock_guard<std::mutex> lk(M->eng->mu);
+  ++M->dec_launches;
+  return B2Q_OK;
 }
 
 b2q_status b2q_clear_state(b2q_model* M) {
@@ -430,20 +507,10 @@ b2q_status b2q_clear_state(b2q_model* M) {
   // never read (attention reads keys t < start + s + 1).
   if (!M) return set_error(B2Q_EINVAL, "b2q_clear_state: NULL model");
   if (M->dec_sync) {
-    // re-arm the persistent kernel's barrier words (a step that gave up on
-    // a wait can leave them inconsistent)
+    // (all ranks of a tensor-parallel model call it together)
     std::lock_guard<std::mutex> lk(M->eng->mu);
     cudaSetDevice(M->eng->device);
-    // (all ranks of a tensor-parallel model call it together)
-    cudaError_t err = cudaMemsetAsync(M->dec_sync, 0, sizeof(b2q::DecSync), M->st);
-    if (err == cudaSuccess)
-      err = cudaMemsetAsync(M->dec_attn_cnt, 0, sizeof(unsigned int) * M->c.n_layers * M->KV_loc, M->st);
-    const b2q::XBlock xl = b2q::xblock_layout(M->c.n_embd, M->c.n_heads * M->c.head_dim, M->c.n_ff,
-                                              M->c.n_vocab, M->c.tp_size, M->eng->num_sms);
-    if (err == cudaSuccess)
-      err = cudaMemsetAsync(static_cast<uint8_t*>(M->dec_xblock) + xl.bar, 0, 8 * b2q::kMaxTp, M->st);
-    if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
-    M->dec_launches = 0;
+    cudaError_t err = rearm_decode(M);
     if (err != cudaSuccess) return cuda_error(err, "b2q_clear_state");
   }
   return B2Q_OK;
@@ -484,6 +551,7 @@ b2q_status b2q_model_destroy(b2q_model* M) {
   xq_free(&M->xq_a);
   xq_free(&M->xq_f);
   if (M->h_tok) cudaFreeHost(M->h_tok);
+  if (M->h_err) cudaFreeHost(M->h_err);
   cudaStreamDestroy(M->st);
   delete M;
   return B2Q_OK;

@@ -61,8 +61,10 @@ struct b2q_model {
   b2q::XQBuf xq_e, xq_a, xq_f;
   int nsplit = 0;
   int mmax = b2q::kPrefillChunk;
-  // host staging (pinned) for b2q_forward's token ids
+  // host staging (pinned) for b2q_forward's token ids, and the device error
+  // word read back by the blocking forward entry points
   uint32_t* h_tok = nullptr;
+  int* h_err = nullptr;
   // decode graph (m = 1)
   cudaGraphExec_t graph = nullptr;
   uint64_t graph_kernels = 0;

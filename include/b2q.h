@@ -100,13 +100,18 @@ b2q_status b2q_matmul(b2q_engine* eng, const b2q_weight* w, const float* x, floa
 b2q_status b2q_matmul_dev(b2q_engine* eng, const b2q_weight* w, const float* x_dev,
                           float* y_dev, int m, int n, int k, void* stream);
 
-/* No counterpart in the reference.  y = W x like b2q_matmul_dev, for callers
- * that must not allocate device memory (a fixed memory pool, a real-time
- * path that cannot take an allocation's implicit synchronisation, a host
- * that owns the allocator): this entry point calls no cudaMalloc, cudaFree
- * or allocating library routine.  Its scratch (the quantised activations)
- * is a fixed array inside the library, about 0.6 MB per GPU that loads the
- * library, held until the process exits; calls with
+/* No counterpart in the reference.  y = W x for callers that must not
+ * allocate device memory (a fixed memory pool, a real-time path that cannot
+ * take an allocation's implicit synchronisation, a host that owns the
+ * allocator): this entry point calls no cudaMalloc, cudaFree or allocating
+ * library routine.  It always runs the GEMV path (the quantiser and the
+ * bandwidth-bound GEMV, in passes of one or two tokens), so below 16 tokens
+ * its output is bit-identical to b2q_matmul_dev's; from 16 tokens on,
+ * b2q_matmul_dev uses the tensor cores instead, and the two agree within
+ * the matvec tolerance (rel-L2 1e-3 of fp64) rather than bit for bit, while
+ * this call re-streams the weights once per pass.  Its scratch (the
+ * quantised activations) is a fixed array inside the library, about 0.6 MB
+ * per GPU that loads the library, held until the process exits; calls with
  * m * round_up(k, 256) > 262144 are rejected with B2Q_EINVAL.  The first call
  * on a device looks up the array's device address (cudaGetSymbolAddress);
  * make that first call before any stream capture.  Every call shares the
@@ -167,6 +172,14 @@ typedef struct {
  * it and the caller broadcasts the 128 bytes to the other ranks. */
 b2q_status b2q_tp_unique_id(unsigned char out[128]);
 
+/* Host-side bound (milliseconds, default 120000) of the NCCL communicator
+ * set-up in b2q_model_create under tensor parallelism, and of any NCCL call
+ * that answers "in progress".  Communicators are created non-blocking; when
+ * the other ranks do not join in time the set-up is aborted
+ * (ncclCommAbort) and b2q_model_create returns B2Q_ETIMEOUT instead of
+ * hanging.  No counterpart in the reference (it had no multi-GPU path). */
+b2q_status b2q_set_tp_init_timeout_ms(int ms);
+
 /* Replaces StandardNativeEngine::from_gguf (inference.rs:2513-2620):
  * create an empty model; tensors are then added by GGUF name. */
 b2q_status b2q_model_create(b2q_engine* eng, const b2q_model_config* cfg,
@@ -221,13 +234,24 @@ b2q_status b2q_model_finalize(b2q_model* m);
  * write the logits of the LAST position ([n_vocab] f32) to `logits` (host
  * pointer, may be NULL).  If `argmax` is non-NULL the greedy next token
  * (SelfMadeSampler at temperature <= 1e-5, inference.rs:1620-1630) is
- * written there too. */
+ * written there too.  Returns B2Q_ETIMEOUT (and clears the device error
+ * word) when a bounded device-side wait gave up during the step: its outputs
+ * are then invalid.  On one GPU the persistent kernel's synchronisation
+ * state is re-armed before returning, so the step can simply be repeated;
+ * under tensor parallelism every rank must call b2q_clear_state, followed by
+ * a host barrier across the ranks, first.  (The reference fell back to the
+ * CPU on any GPU failure, inference.rs:600-606; there is no fallback here.) */
 b2q_status b2q_forward(b2q_model* m, const uint32_t* tokens, int n_tokens, int start_pos,
                        float* logits, uint32_t* argmax);
 
 /* Device-pointer form: tokens_dev / logits_dev / argmax_dev are device
  * pointers (any may be NULL except tokens_dev); asynchronous on `stream`
- * (NULL: the model's own stream). */
+ * (NULL: the model's own stream).  It does not synchronise, so it cannot see
+ * a bounded wait that gave up: call b2q_check_device_error to learn that.
+ * Stream capture: when `stream` is capturing, a single-token step runs the
+ * per-kernel path (no persistent kernel, no nested graph), because the
+ * persistent kernel's barrier bases and hand-off tags are host counters
+ * baked into each launch and a replayed launch would reuse them. */
 b2q_status b2q_forward_dev(b2q_model* m, const uint32_t* tokens_dev, int n_tokens,
                            int start_pos, float* logits_dev, uint32_t* argmax_dev, void* stream);
 
@@ -277,8 +301,20 @@ b2q_status b2q_gdn_step_dev(b2q_engine* eng, const b2q_gdn_config* cfg, int n_to
                             const float* ssm_a, const float* dt_bias, const float* ssm_norm, float* conv_state,
                             float* ssm_state, float* y, void* stream);
 
-/* Replaces StandardNativeEngine::clear_state (inference.rs:2688-2693). */
+/* Replaces StandardNativeEngine::clear_state (inference.rs:2688-2693).
+ * Also re-arms the persistent decode kernel's barrier counters and all-rank
+ * epoch slots (tensor parallelism: every rank calls it, then the ranks meet
+ * at a host barrier before the next step). */
 b2q_status b2q_clear_state(b2q_model* m);
+
+/* Test hook, no counterpart in the reference: advances the model's
+ * persistent-kernel launch sequence on the host without launching, which is
+ * what a launch skipped by a peer looks like from this GPU: the next step's
+ * barrier targets lie beyond the arrivals it will see, so its bounded waits
+ * give up and the blocking forward returns B2Q_ETIMEOUT.  Used to test the
+ * failure path without faulting or hanging a GPU (lower the wait limit
+ * first with b2q_set_wait_limit_cycles). */
+b2q_status b2q_model_debug_desync(b2q_model* m);
 
 /* ---- GGUF files (GgufModelFile, inference.rs:235-510) ----
  * A read-only POSIX mapping of the file, parsed as GgufModelFile::open
@@ -361,6 +397,13 @@ uint64_t b2q_kernel_launch_count(b2q_engine* eng);
 /* Read and clear the device-side error word (B2Q_ETIMEOUT when a bounded
  * wait gave up); synchronises the engine's stream. */
 b2q_status b2q_check_device_error(b2q_engine* eng);
+
+/* Upper bound of every device-side wait of this engine's GPU (mbarriers,
+ * grid and all-rank barriers, tagged hand-offs), in SM clock cycles;
+ * cycles <= 0 restores the default 4e9 (~2 s).  A wait that reaches it sets
+ * the device error word and lets its kernel finish.  No counterpart in the
+ * reference, which had no device-side waits of its own. */
+b2q_status b2q_set_wait_limit_cycles(b2q_engine* eng, long long cycles);
 
 #ifdef __cplusplus
 }

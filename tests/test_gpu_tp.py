@@ -40,3 +40,26 @@ def test_tp2_matches_single_gpu(tmp_path):
     verdict = json.loads(out.read_text())
     assert verdict["persistent_eq_graph"], verdict
     assert verdict["matches_one_gpu"], verdict
+
+
+def test_tp2_rank_that_skips_a_step_times_out_and_recovers(tmp_path, pkg):
+    """Rank 1 skips one persistent single-token step: rank 0's bounded
+    all-rank barrier gives up (B2Q_ETIMEOUT, no hang), and after every rank
+    calls b2q_clear_state the step repeats on both ranks, equal to the
+    captured per-kernel graph bit for bit."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from hf_llm_b200._lib import ETIMEOUT
+    out = tmp_path / "skip.json"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           str(HERE / "tp_worker.py"), "--out", str(out), "--mode", "skip"]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    verdict = json.loads(out.read_text())
+    by_rank = {d["rank"]: d for d in verdict["ranks"]}
+    assert by_rank[0]["status"] == ETIMEOUT, verdict
+    assert by_rank[1]["status"] == 0, verdict
+    assert all(d["retry_eq_graph"] for d in verdict["ranks"]), verdict

@@ -28,6 +28,8 @@ def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
     ap.add_argument("--layers", type=int, default=2)
+    ap.add_argument("--mode", default="parity", choices=["parity", "skip"],
+                    help="parity: the checks above; skip: rank 1 skips one single-token step")
     args = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -60,6 +62,8 @@ def main() -> int:
 
     m = build("persistent")
     mg = build("graph")
+    if args.mode == "skip":
+        return skip_step(args, m, mg, rank, world, cfg, dist, torch)
     ref = None
     if rank == 0:
         full = synth.llama_tensors(cfg, model.q4_k_m_types(), 9, dist="unit")
@@ -97,6 +101,51 @@ def main() -> int:
     mg.close()
     if ref is not None:
         ref.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
+def skip_step(args, m, mg, rank, world, cfg, dist, torch) -> int:
+    """A rank that skips one single-token step (the host-side failure of a
+    peer): with a 10 ms wait limit, rank 0's persistent step gives up at its
+    first all-rank barrier and b2q_forward returns B2Q_ETIMEOUT; after every
+    rank calls b2q_clear_state and the ranks meet at a host barrier, the
+    same step runs on both ranks and equals the captured graph bit for bit."""
+    from hf_llm_b200._lib import B2QError, check, lib
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, cfg["n_vocab"], 40).tolist()
+    m.forward(prompt, 0)
+    lg = mg.forward(prompt, 0)
+    tok, pos = int(np.argmax(lg)), len(prompt)
+    m.forward([tok], pos)
+    lg = mg.forward([tok], pos)
+    tok, pos = int(np.argmax(lg)), pos + 1
+    torch.cuda.synchronize()
+    dist.barrier()
+    check(lib().b2q_set_wait_limit_cycles(m.engine.handle, 20_000_000))  # ~10 ms
+    status = 0
+    if rank == 0:
+        try:
+            m.forward([tok], pos)
+        except B2QError as e:
+            status = e.status
+    dist.barrier()
+    # every rank re-arms, then the ranks meet before the next step
+    m.clear_state()
+    torch.cuda.synchronize()
+    dist.barrier()
+    lt = m.forward([tok], pos)
+    lg = mg.forward([tok], pos)
+    same = bool(np.array_equal(lt.view(np.uint32), lg.view(np.uint32)))
+    check(lib().b2q_set_wait_limit_cycles(m.engine.handle, 0))
+    res = [None] * world
+    dist.all_gather_object(res, {"rank": rank, "status": status, "retry_eq_graph": same})
+    if rank == 0:
+        Path(args.out).write_text(json.dumps({"world": world, "ranks": res}))
+    dist.barrier()
+    m.close()
+    mg.close()
     dist.barrier()
     dist.destroy_process_group()
     return 0
