@@ -1,4 +1,5 @@
-"""Decode benchmark: Llama-3-8B-shaped Q4_K_M decoder, batch 1.
+"""Decode benchmark: Llama-3-8B-shaped Q4_K_M decoder at batch 1 (the headline),
+plus the Llama-3-70B-shaped decoder at an 8192-token context.
 
 Workload (the metric "decode tok/s at Llama-3-8B Q4_K_M shape; dequant-GEMV
 HBM GB/s vs 8 TB/s"): a random-init 32-layer Llama-3-8B-shaped decoder
@@ -8,21 +9,51 @@ Q4_K, f32 norms, f16 KV cache), weights drawn from the seeded benchmark
 distributions (synthetic: no checkpoints offline).  A 512-token random-id
 prompt is prefilled, then one step = one greedy decode token at batch 1.
 
-* value  -- decode tok/s with everything resident in HBM: each step replays
-            the captured decode graph; the next token id is the device argmax
-            of the previous step (no host round trip).  CUDA events on the
-            launching stream; weights (4.9 GB) far exceed L2.
-* e2e    -- the same through the host API b2q_forward: token id copied from
-            host, logits [128256] f32 copied back every step.
-* roofline -- the dominant kernel family, the dequant-GEMV: Q4_K at the FFN
-            gate shape 14336x4096 (33.1 MB per launch), launches timed with
-            CUDA events while rotating 24 weight copies (794 MB > L2).
-* cpu_baseline -- the reference's own CPU path (the oracle's restatement of
-            the AVX2/FMA Rayon matvec + Llama forward) on the host cores.
+* value    -- decode tok/s with everything resident in HBM: one step is one
+              launch of the persistent decode kernel (the whole single-token
+              forward); the next token id is the argmax that kernel writes on
+              the device (no host round trip).  CUDA events on the launching
+              stream, max over ranks.  After the host barrier and sync that
+              open the timed region, one untimed step runs first: its
+              all-rank barriers line the ranks' streams up on the device, so
+              host start skew stays out of every rank's events.  4.9 GB of
+              weights are read per step, far above L2 (126 MB).
+* e2e      -- the same through the host API b2q_forward: the token id copied
+              in from pinned host memory and the logits [128256] f32 copied
+              back every step; host wall clock, max over ranks.
+* roofline -- the dominant kernel, decode_kernel (the only kernel of a step):
+              algorithmic bytes of one step on this rank (the weight rows or
+              columns it owns, one token_embd row, the norms and the f16 K/V
+              rows of its KV heads at the mean timed context) / event time
+              per step; `traffic` from the committed ncu capture.
+* gemv_roofline / gemv_shapes -- the standalone GEMV per matvec config shape
+              (rank 0), weights rotated over copies larger than L2.
+* prefill  -- the 512-token prompt pass (tensor cores), its projection flops
+              against the measured bf16 peak.
+* tp_parity -- after the timed region, a fixed-seed 2-layer model of
+              Llama-3-8B widths (unit distribution) runs a 20-token prompt and
+              three single-token steps through the same path on the same
+              ranks; rank 0 compares the logits with the fp64 oracle
+              (rel-L2 <= 1e-3).
+* cpu_baseline -- the reference's CPU path (the oracle's restatement of the
+              AVX2/FMA Rayon matvec and the Llama forward), rank 0 at N = 1:
+              all host cores, and the reference governor's thread count
+              min(3/4 cores, cores - 2) (hardware.rs:157-166).
+* model_70b -- the Llama-3-70B-shaped decoder (80 layers, hidden 8192, 64/8
+              heads, FFN 28672, same quant mix, 44 GB): the f16 KV cache is
+              filled with seeded synthetic rows (b2q_model_fill_kv) up to the
+              8192-token context, then the same value / e2e / roofline.  Host
+              generation shortcut: one seeded layer's bytes are uploaded into
+              each of the 80 layers' own device buffers, so every step still
+              reads 44 GB of distinct device memory.
 
 --gpus N > 1 (launched under torchrun): tensor-parallel decode of the same
-model, weights row-sharded over N GPUs, NCCL all-gathers; strong scaling.
---impl reference: the reference's CPU path on the same workload (rank 0).
+model on N GPUs (KV heads, gate/up and the head by rows, attn_output and
+ffn_down by columns, partial sums exchanged over NVLink by the persistent
+kernel); the model is fixed, so scaling is strong.
+--impl reference: the reference's CPU path (the oracle restatement) on the
+same workload -- the same prompt ids, prefill length, warm-up and timed steps
+-- on rank 0 with all host cores.
 """
 from __future__ import annotations
 
@@ -100,6 +131,12 @@ def profile_traffic(name: str = "gemv_q4k_14336x4096.md") -> float | None:
     return None
 
 
+def governor_threads(cores: int) -> int:
+    """The reference's CPU thread count: min(3/4 cores, cores - 2), at least 1
+    (ResourceGovernor, hardware.rs:157-166)."""
+    return max(1, min(cores * 3 // 4, cores - 2))
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons during the timed region."""
 
@@ -154,24 +191,59 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def build_model(pkg, engine, cfg, seed, rank, size, tp_id, max_seq, dist="bench", decode="persistent"):
+def model_cfg(name: str, layers: int | None = None) -> dict:
+    from hf_llm_b200 import model
+    base = model.LLAMA3_70B if name == "70b" else model.LLAMA3_8B
+    return dict(base, n_layers=layers or base["n_layers"])
+
+
+def workload_config(name: str, cfg: dict, prefill: int, context: str | None = None) -> dict:
+    """The workload as both arms report it (no implementation keys)."""
+    c = {"workload": f"llama3-{name}-q4_k_m-decode", "layers": cfg["n_layers"], "hidden": cfg["n_embd"],
+         "heads": f"{cfg['n_heads']}/{cfg['n_kv_heads']}", "ffn": cfg["n_ff"], "vocab": cfg["n_vocab"],
+         "prefill": prefill, "batch": 1,
+         "l2": "inputs larger than L2: every step reads all weights (GBs) from memory"}
+    if context:
+        c["context"] = context
+    return c
+
+
+def build_model(engine, cfg, seed, rank, size, tp_id, max_seq, dist="bench", decode="persistent",
+                keep_host=False, share_layers=False):
+    """Upload this rank's shards of a synthetic Llama.  share_layers: every
+    layer gets the bytes of layer 0's tensors (generated once; each layer
+    still has its own device buffers)."""
     from hf_llm_b200 import model, synth
     m = model.StandardNativeEngine(engine, cfg, max_seq=max_seq, tp_rank=rank, tp_size=size, tp_id=tp_id,
                                    decode=decode)
     host = {}
-    for spec in synth.llama_specs(cfg, model.q4_k_m_types()):
+    cache = {}
+    specs = synth.llama_specs(cfg, model.q4_k_m_types())
+    by_name = {s[0]: s for s in specs}
+    for spec in specs:
         name, t, dims, _ = spec
+        src = spec
+        if share_layers and name.startswith("blk."):
+            role = name.split(".", 2)[2]
+            src = by_name[f"blk.0.{role}"]
         if len(dims) == 1:
-            arr = synth.llama_tensor(spec, seed, dist=dist)
+            arr = synth.llama_tensor(src, seed, dist=dist)
             m.set_tensor(name, t, dims, arr)
-            host[name] = (t, dims, arr)
+            if keep_host:
+                host[name] = (t, dims, arr)
             continue
         b, e = m.shard_rows(name, dims[0])
-        arr = synth.llama_tensor(spec, seed, b, e, dist=dist)
+        key = (src[0], b, e)
+        arr = cache.get(key) if share_layers else None
+        if arr is None:
+            arr = synth.llama_tensor(src, seed, b, e, dist=dist)
+            if share_layers and src[0].startswith("blk."):
+                cache[key] = arr
         m.set_tensor(name, t, dims, arr, b, e)
-        if size == 1:
+        if keep_host:
             host[name] = (t, dims, arr)
         del arr
+    cache.clear()
     m.finalize()
     return m, host
 
@@ -211,25 +283,36 @@ def prefill_matmul_params(cfg, rank: int, world: int) -> int:
     return total
 
 
-def cpu_decode_rate(orc, cfg, host, steps: int, warmup: int, threads: int) -> dict:
-    """The reference CPU path: decode tok/s of the same model (prefill 8
-    tokens, then `steps` timed greedy decode steps)."""
-    orc.set_threads(threads)
-    m = orc.Model(cfg, host, kv_capacity=8 + warmup + steps + 1)
-    rng = np.random.default_rng(7)
-    logits = m.forward_ref(rng.integers(0, cfg["n_vocab"], 8).tolist(), 0)
-    pos = 8
-    for _ in range(warmup):
-        logits = m.forward_ref([int(np.argmax(logits))], pos)
-        pos += 1
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        logits = m.forward_ref([int(np.argmax(logits))], pos)
-        pos += 1
-    dt = time.perf_counter() - t0
-    return {"value": steps / dt, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{steps} greedy decode steps after an 8-token prefill, full 32-layer model, "
-                      f"{threads} threads (OpenMP), quantised-x AVX2/FMA matvecs"}
+def prompt_ids(cfg, seed: int, n: int) -> np.ndarray:
+    """The benchmark prompt: n random token ids (both arms use these)."""
+    return np.random.default_rng(seed).integers(0, cfg["n_vocab"], n).astype(np.int32)
+
+
+def cpu_decode(orc, cfg, host, prompt, phases) -> list[dict]:
+    """The reference CPU path on one model at the benchmark's context: its
+    f32 KV cache holds len(prompt) - 1 positions of seeded synthetic rows (the
+    context the GPU arm reaches with its prompt pass; a 512-token CPU prompt
+    pass takes minutes), the last prompt token is run through the forward,
+    then for each (threads, warmup, steps) of `phases` untimed and timed
+    greedy steps."""
+    m = orc.Model(cfg, host, kv_capacity=len(prompt) + sum(w + s for _, w, s in phases) + 1)
+    m.fill_kv(len(prompt) - 1, seed=len(prompt))
+    orc.set_threads(phases[0][0])
+    logits = m.forward_ref([int(prompt[-1])], len(prompt) - 1)
+    pos = len(prompt)
+    out = []
+    for threads, warm, steps in phases:
+        orc.set_threads(threads)
+        for _ in range(warm):
+            logits = m.forward_ref([int(np.argmax(logits))], pos)
+            pos += 1
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            logits = m.forward_ref([int(np.argmax(logits))], pos)
+            pos += 1
+        dt = time.perf_counter() - t0
+        out.append({"value": steps / dt, "unit": "tok/s", "cores": threads, "kind": "port", "steps": steps})
+    return out
 
 
 GEMV_SHAPES = {  # key: (ggml type, n, k, copies rotated to exceed L2)
@@ -281,198 +364,196 @@ def run_gemv_only(args):
 
 
 def run_reference_arm(args):
+    """The reference's CPU path (oracle restatement) on the GPU arm's workload:
+    the same model, prompt ids, prefill, warm-up and timed steps."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    pkg = load_pkg()
+    load_pkg()
     orc = load_oracle()
     from hf_llm_b200 import model, synth
-    cfg = dict(model.LLAMA3_70B if args.model == "70b" else model.LLAMA3_8B)
+    cfg = model_cfg(args.model, args.layers)
     host = synth.llama_tensors(cfg, model.q4_k_m_types(), args.seed)
     threads = os.cpu_count() or 1
-    steps = max(1, min(args.steps, args.cpu_steps))
-    warm = max(0, min(args.warmup, 1))
-    r = cpu_decode_rate(orc, cfg, host, steps, warm, threads)
+    prompt = prompt_ids(cfg, args.seed, args.prefill)
+    r = cpu_decode(orc, cfg, host, prompt, [(threads, args.warmup, args.steps)])[0]
+    r["sample"] = (f"context of the GPU arm's {args.prefill}-token prompt (f32 KV cache filled with seeded "
+                   f"rows, the last prompt token run through the forward), {args.warmup} warm-up and "
+                   f"{args.steps} timed greedy decode steps, {threads} threads (OpenMP), quantised-x "
+                   f"AVX2/FMA matvecs, f32 KV cache as the reference keeps it")
     line = {"metric": f"decode tok/s at Llama-3-{args.model.upper()} Q4_K_M shape", "value": r["value"],
-            "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus, "steps": steps, "warmup": warm,
-            "ms_per_step": 1000.0 / r["value"], "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8/f32", "data": "synthetic",
-            "config": {"workload": f"llama3-{args.model}-q4_k_m-decode", "prefill": 8, "batch": 1},
+            "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / r["value"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8/f32", "data": "synthetic",
+            "config": workload_config(args.model, cfg, args.prefill),
             "cpu_baseline": r,
-            "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+            "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=128)
-    ap.add_argument("--warmup", type=int, default=8)
-    ap.add_argument("--impl", default="b2q", choices=["b2q", "reference"])
-    ap.add_argument("--prefill", type=int, default=512)
-    ap.add_argument("--seed", type=int, default=0x5EED)
-    ap.add_argument("--cpu-steps", type=int, default=6)
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--e2e-steps", type=int, default=64)
-    ap.add_argument("--model", default="8b", choices=["8b", "70b"],
-                    help="Llama-3-8B (the headline workload) or Llama-3-70B shape")
-    ap.add_argument("--layers", type=int, default=None,
-                    help="decoder layers (default: the model's; fewer only for kernel profiles on a small case)")
-    ap.add_argument("--decode", default="persistent", choices=["persistent", "graph", "eager"],
-                    help="single-token step: captured kernel graph, one persistent kernel, or eager")
-    ap.add_argument("--no-gemv-shapes", action="store_true", help="skip the per-shape GEMV timings")
-    ap.add_argument("--gemv-only", default=None,
-                    help="time one GEMV shape only (e.g. q4k_14336x4096), for kernel profiling")
-    ap.add_argument("--copies", type=int, default=24, help="weight copies rotated by --gemv-only")
-    ap.add_argument("--reps", type=int, default=20, help="rotations timed by --gemv-only")
-    args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
-    if args.impl == "reference":
-        return run_reference_arm(args)
-    if args.gemv_only:
-        return run_gemv_only(args)
-
+def timed_decode(m, tok, pos, steps, sp, stream, dist, dev, clk_dev):
+    """K timed single-token steps (device argmax feeds the next step), CUDA
+    events on `stream`, max over ranks.  Returns (ms, pos, clocks, library
+    kernel launches inside the timed region)."""
     import torch
-    pkg = load_pkg()
-    from hf_llm_b200 import build as bld
-    bld.build()
-    from hf_llm_b200 import model, synth
-    from hf_llm_b200.engine import CudaEngine
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        world = args.gpus if world == 1 else world
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
-        local = 0
-    dev = torch.device("cuda", local)
-    engine = CudaEngine(local)
-    tp_id = None
-    if world > 1:
-        obj = [model.tp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        tp_id = obj[0]
-
-    base = model.LLAMA3_70B if args.model == "70b" else model.LLAMA3_8B
-    cfg = dict(base, n_layers=args.layers or base["n_layers"])
-    max_seq = args.prefill + args.warmup + args.steps + args.e2e_steps + 8
-    t_load = time.perf_counter()
-    m, host = build_model(pkg, engine, cfg, args.seed, rank, world, tp_id, max_seq, decode=args.decode)
-    t_load = time.perf_counter() - t_load
-
-    stream = torch.cuda.Stream(device=dev)
-    sp = stream.cuda_stream
-    rng = np.random.default_rng(args.seed)
-    prompt = torch.tensor(rng.integers(0, cfg["n_vocab"], args.prefill).astype(np.int32), device=dev)
-    tok = torch.zeros(2, dtype=torch.int32, device=dev)
-    with torch.cuda.stream(stream):
-        m.forward_dev(prompt.data_ptr(), args.prefill, 0, 0, tok.data_ptr(), sp)
-    stream.synchronize()
-    pos = args.prefill
 
     def step(p):
-        # greedy: the argmax of this step is the input of the next one
         m.forward_dev(tok.data_ptr(), 1, p, 0, tok.data_ptr(), sp)
 
-    for _ in range(args.warmup):
-        step(pos)
-        pos += 1
     stream.synchronize()
     if dist:
         dist.barrier()
+    torch.cuda.synchronize(dev)
+    # untimed: its all-rank barriers align the ranks' streams on the device
+    step(pos)
+    pos += 1
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches0 = engine.kernel_launches()
-    with ClockSampler(local) as clk:
-        torch.cuda.synchronize(dev)
-        torch.cuda.nvtx.range_push("decode")
+    launches0 = m.engine.kernel_launches()
+    with ClockSampler(clk_dev) as clk:
         ev0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step(pos)
             pos += 1
         ev1.record(stream)
         ev1.synchronize()
-        torch.cuda.nvtx.range_pop()
-    launches = engine.kernel_launches() - launches0
+    launches = m.engine.kernel_launches() - launches0
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
     ms = ev0.elapsed_time(ev1)
     if dist:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    ms_step = ms / args.steps
-    value = args.steps / (ms / 1000.0)
+    return ms, pos, clk.summary(), launches
 
-    # ---- e2e through the host API (token id in, logits out, every step) ----
-    logits_host = np.empty(cfg["n_vocab"], np.float32)
-    nxt = int(tok[0].item())
+
+def timed_e2e(m, tok0, pos, steps, dist, dev):
+    """b2q_forward with host token ids and host logits every step; host wall
+    clock, max over ranks."""
+    import torch
+    nxt = tok0
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
-        logits_host = m.forward([nxt], pos)
-        nxt = int(np.argmax(logits_host))
+    for _ in range(steps):
+        logits = m.forward([nxt], pos)
+        nxt = int(np.argmax(logits))
         pos += 1
-    e2e_s = time.perf_counter() - t0
+    s = time.perf_counter() - t0
     if dist:
-        t = torch.tensor([e2e_s], device=dev)
+        t = torch.tensor([s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = {"value": args.e2e_steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4,
-           "d2h_bytes_per_step": 4 * cfg["n_vocab"],
-           "note": "b2q_forward with host token ids and host logits; host wall clock"}
+        s = float(t.item())
+    return s, pos
 
-    # ---- roofline of the dominant kernel ----
-    # persistent path: the decode kernel itself (the only kernel of a step);
-    # bytes = what one step must read (weights it owns + KV rows) per launch
+
+def tp_parity(engine, orc, rank, world, dist, seed=0x7A):
+    """Fixed-seed 2-layer model of Llama-3-8B widths (unit distribution) on
+    the same ranks and step path as the benchmark: a 20-token prompt and three
+    single-token steps, logits against the fp64 oracle on rank 0."""
+    from hf_llm_b200 import model, synth
+    cfg = model_cfg("8b", 2)
+    tp_id = None
+    if world > 1:
+        obj = [model.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        tp_id = obj[0]
+    m, _ = build_model(engine, cfg, seed, rank, world, tp_id, 64, dist="unit")
+    ref = None
+    if rank == 0:
+        full = synth.llama_tensors(cfg, model.q4_k_m_types(), seed, dist="unit")
+        ref = orc.Model(cfg, full, kv_capacity=64)
+    prompt = [int(v) for v in prompt_ids(cfg, seed, 20)]
+    errs, toks, pos = [], [prompt], 0
+    for s in range(4):
+        a = m.forward(toks[-1], pos)
+        nxt = 0
+        if rank == 0:
+            b = ref.forward_f64(toks[-1], pos, kv_f16=True)
+            errs.append(float(np.linalg.norm(a - b) / np.linalg.norm(b)))
+            nxt = int(np.argmax(b))
+        if dist:
+            o = [nxt]
+            dist.broadcast_object_list(o, src=0)
+            nxt = o[0]
+        pos += len(toks[-1])
+        toks.append([nxt])
+    path = m.step_path
+    m.close()
+    if rank != 0:
+        return None
+    return {"rel_l2": max(errs), "rel_l2_per_step": [round(e, 8) for e in errs], "tol": 1e-3,
+            "ok": bool(max(errs) <= 1e-3), "tp": world, "step_path": path,
+            "model": "Llama-3-8B widths, 2 layers, unit distribution; 20-token prompt + 3 single-token steps",
+            "oracle": "fp64 forward over the bit-exact dequantised weights, f16 KV"}
+
+
+def run_model(args, name, engine, rank, world, local, dist, dev, stream, orc):
+    """One model's decode measurements on this rank; returns the fields of
+    its bench block (rank 0) and the host tensors (N = 1, 8B only)."""
+    import torch
+    from hf_llm_b200 import model
+    cfg = model_cfg(name, args.layers)
+    is70 = name == "70b"
+    steps = args.steps
+    e2e_steps = args.e2e_steps_70b if is70 else args.e2e_steps
+    tp_id = None
+    if world > 1:
+        obj = [model.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        tp_id = obj[0]
+    max_seq = 8192 if is70 else args.prefill + args.warmup + steps + e2e_steps + 8
+    t_load = time.perf_counter()
+    m, host = build_model(engine, cfg, args.seed, rank, world, tp_id, max_seq, decode=args.decode,
+                          keep_host=(world == 1 and not is70 and not args.no_cpu), share_layers=is70)
+    t_load = time.perf_counter() - t_load
+    sp = stream.cuda_stream
+    tok = torch.zeros(2, dtype=torch.int32, device=dev)
+    prefill = None
+    if is70:
+        # an 8192-token context: seeded synthetic K/V rows up to the first step
+        pos = max_seq - (args.warmup + 1 + steps + e2e_steps + 1)
+        m.fill_kv(0, pos, seed=args.seed, scale=1.0)
+        tok.fill_(int(prompt_ids(cfg, args.seed, 1)[0]))
+    else:
+        prompt = torch.tensor(prompt_ids(cfg, args.seed, args.prefill), device=dev)
+        with torch.cuda.stream(stream):
+            m.forward_dev(prompt.data_ptr(), args.prefill, 0, 0, tok.data_ptr(), sp)
+        stream.synchronize()
+        pos = args.prefill
+    for _ in range(args.warmup):
+        m.forward_dev(tok.data_ptr(), 1, pos, 0, tok.data_ptr(), sp)
+        pos += 1
+    pos_t0 = pos + 1  # after the aligning step
+    ms, pos, clocks, launches = timed_decode(m, tok, pos, steps, sp, stream, dist, dev, local)
+    ms_step = ms / steps
+    value = steps / (ms / 1000.0)
+    e2e_s, pos = timed_e2e(m, int(tok[0].item()), pos, e2e_steps, dist, dev)
+    e2e = {"value": e2e_steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4,
+           "d2h_bytes_per_step": 4 * cfg["n_vocab"],
+           "note": "b2q_forward with host token ids and host logits; host wall clock, max over ranks"}
     peak, peak_kind = measured_peaks()
-    ctx = args.prefill + args.warmup + args.steps // 2
+    ctx = pos_t0 + steps // 2
     step_bytes = step_algorithmic_bytes(cfg, rank, world, ctx)
     step_gbs = step_bytes / (ms_step * 1e-3) / 1e9
     roof = None
     if m.decode_mode == "persistent":
+        traffic = None
+        if world == 1 and not is70 and cfg["n_layers"] == 32:
+            traffic = profile_traffic("decode_kernel_llama3_8b.md")
         roof = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(step_gbs / peak, 4),
-                "traffic": profile_traffic(f"decode_kernel_llama3_{args.model}.md") if world == 1 else None,
+                "frac": round(step_gbs / peak, 4), "traffic": traffic,
                 "kernel": "decode_kernel (persistent single-token step)",
                 "algorithmic_bytes_per_launch": int(step_bytes), "peak_kind": peak_kind,
-                "launch_us": round(ms_step * 1000, 2)}
-    # the standalone GEMV (Q4_K, FFN gate shape) and the other matvec shapes
-    gemv_roof = None
-    gemv_shapes = {}
-    if rank == 0:
-        keys = ["q4k_14336x4096"] if args.no_gemv_shapes else list(GEMV_SHAPES)
-        for key in keys:
-            ms_l, alg = time_gemv_shape(engine, synth, key, args.seed, dev, sp)
-            gemv_shapes[key] = {"us": round(ms_l * 1000, 3), "GBps": round(alg / (ms_l * 1e-3) / 1e9, 1),
-                                "bytes": alg}
-            if key == "q4k_14336x4096":
-                ach = alg / (ms_l * 1e-3) / 1e9
-                gemv_roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                             "frac": round(ach / peak, 4), "traffic": profile_traffic(),
-                             "kernel": "gemv_kernel (Q4_K, 14336x4096), one launch",
-                             "algorithmic_bytes_per_launch": alg, "peak_kind": peak_kind,
-                             "launch_us": round(ms_l * 1000, 3)}
-    if roof is None:
-        roof = gemv_roof
-
-    # ---- prompt pass (prefill) on the tensor cores: the same prompt again ----
-    prefill = None
-    if args.prefill >= 16:
+                "launch_us": round(ms_step * 1000, 2), "context": ctx}
+    if not is70 and args.prefill >= 16:
         reps = 3
         with torch.cuda.stream(stream):
             m.forward_dev(prompt.data_ptr(), args.prefill, 0, 0, tok.data_ptr(), sp)  # warm-up
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.synchronize()
         if dist:
             dist.barrier()
         e0.record(stream)
@@ -493,34 +574,141 @@ def main():
                    "frac_of_bf16_peak": round(tf / pk, 4) if pk else None,
                    "note": "whole prompt pass (norms, attention, f16 tensor-core projections); "
                            "flops = 2 x tokens x projection weights of the layers (head excluded)"}
+    decode_path = m.decode_mode
+    m.close()
+    block = {"value": round(value, 2), "ms_per_step": round(ms_step, 4), "steps": steps,
+             "roofline": roof, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
+             "decode_step": {"bytes_per_step_rank0": int(step_bytes), "GBps_rank0": round(step_gbs, 1)},
+             "config": workload_config(name, cfg, 0 if is70 else args.prefill,
+                                       f"{ctx} cached tokens (f16 KV rows: seeded synthetic fill)" if is70 else None),
+             "decode_path": decode_path, "load_s": round(t_load, 1)}
+    if prefill:
+        block["prefill"] = prefill
+    return block, host, cfg
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="b2q", choices=["b2q", "reference"])
+    ap.add_argument("--prefill", type=int, default=512)
+    ap.add_argument("--seed", type=int, default=0x5EED)
+    ap.add_argument("--cpu-steps", type=int, default=6, help="timed CPU-baseline steps per thread count")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--e2e-steps-70b", type=int, default=16)
+    ap.add_argument("--model", default="8b", choices=["8b", "70b"],
+                    help="headline model: Llama-3-8B (the metric's workload) or, for profiles, Llama-3-70B")
+    ap.add_argument("--no-70b", action="store_true", help="skip the Llama-3-70B block")
+    ap.add_argument("--no-parity", action="store_true", help="skip the tp_parity check")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decoder layers (default: the model's; fewer only for kernel profiles on a small case)")
+    ap.add_argument("--decode", default="persistent", choices=["persistent", "graph", "eager"],
+                    help="single-token step: one persistent kernel, the captured kernel graph, or eager")
+    ap.add_argument("--no-gemv-shapes", action="store_true", help="skip the per-shape GEMV timings")
+    ap.add_argument("--gemv-only", default=None,
+                    help="time one GEMV shape only (e.g. q4k_14336x4096), for kernel profiling")
+    ap.add_argument("--copies", type=int, default=24, help="weight copies rotated by --gemv-only")
+    ap.add_argument("--reps", type=int, default=20, help="rotations timed by --gemv-only")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    if args.gemv_only:
+        return run_gemv_only(args)
+
+    import torch
+    load_pkg()
+    from hf_llm_b200 import build as bld
+    bld.build()
+    from hf_llm_b200 import synth
+    from hf_llm_b200.engine import CudaEngine
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        world = args.gpus if world == 1 else world
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+        local = 0
+    dev = torch.device("cuda", local)
+    engine = CudaEngine(local)
+    stream = torch.cuda.Stream(device=dev)
+    sp = stream.cuda_stream
+    orc = load_oracle() if rank == 0 else None
+
+    head, host, cfg = run_model(args, args.model, engine, rank, world, local, dist, dev, stream, orc)
+
+    # the standalone GEMV (Q4_K, FFN gate shape) and the other matvec shapes
+    peak, peak_kind = measured_peaks()
+    gemv_roof = None
+    gemv_shapes = {}
+    if rank == 0:
+        keys = ["q4k_14336x4096"] if args.no_gemv_shapes else list(GEMV_SHAPES)
+        for key in keys:
+            ms_l, alg = time_gemv_shape(engine, synth, key, args.seed, dev, sp)
+            gemv_shapes[key] = {"us": round(ms_l * 1000, 3), "GBps": round(alg / (ms_l * 1e-3) / 1e9, 1),
+                                "bytes": alg}
+            if key == "q4k_14336x4096":
+                ach = alg / (ms_l * 1e-3) / 1e9
+                gemv_roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(ach / peak, 4), "traffic": profile_traffic(),
+                             "kernel": "gemv_kernel (Q4_K, 14336x4096), one launch",
+                             "algorithmic_bytes_per_launch": alg, "peak_kind": peak_kind,
+                             "launch_us": round(ms_l * 1000, 3)}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and host:
         try:
-            orc = load_oracle()
-            cpu = cpu_decode_rate(orc, cfg, host, args.cpu_steps, 1, os.cpu_count() or 1)
+            cores = os.cpu_count() or 1
+            gov = governor_threads(cores)
+            prompt = prompt_ids(cfg, args.seed, args.prefill)
+            r_gov, r_all = cpu_decode(orc, cfg, host, prompt, [(gov, 1, args.cpu_steps), (cores, 1, args.cpu_steps)])
+            cpu = dict(r_all)
+            cpu["sample"] = (f"context of the {args.prefill}-token prompt (f32 KV cache filled with seeded rows), "
+                             f"then {args.cpu_steps} timed greedy decode steps per thread count, full "
+                             f"{cfg['n_layers']}-layer model, quantised-x AVX2/FMA matvecs; value at all {cores} "
+                             f"host threads")
+            cpu["governor_threads"] = {"cores": gov, "value": r_gov["value"], "unit": "tok/s",
+                                       "rule": "min(3/4 cores, cores - 2), hardware.rs:157-166"}
         except Exception as ex:  # the baseline is reported, never required
             cpu = {"value": None, "error": str(ex)}
-    del host
+    host = None
+
+    parity = None
+    if not args.no_parity and args.decode == "persistent":
+        parity = tp_parity(engine, orc, rank, world, dist)
+
+    m70 = None
+    if not args.no_70b and args.model == "8b" and args.layers is None:
+        m70, _, _ = run_model(args, "70b", engine, rank, world, local, dist, dev, stream, orc)
 
     if rank == 0:
-        line = {"metric": f"decode tok/s at Llama-3-{args.model.upper()} Q4_K_M shape", "value": round(value, 2),
+        line = {"metric": f"decode tok/s at Llama-3-{args.model.upper()} Q4_K_M shape", "value": head["value"],
                 "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-                "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+                "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None,
                 "dtype": "int16xint8 dp2a, f32 accum", "data": "synthetic",
-                "config": {"workload": f"llama3-{args.model}-q4_k_m-decode", "layers": cfg["n_layers"],
-                           "hidden": cfg["n_embd"], "heads": f"{cfg['n_heads']}/{cfg['n_kv_heads']}",
-                           "ffn": cfg["n_ff"], "vocab": cfg["n_vocab"], "prefill": args.prefill,
-                           "batch": 1, "kv_cache": "f16", "tp": world, "decode": m.decode_mode,
-                           "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB read per step)"},
-                "decode_step": {"bytes_per_step_rank0": int(step_bytes), "GBps_rank0": round(step_gbs, 1)},
-                "roofline": roof, "gemv_roofline": gemv_roof, "gemv_shapes": gemv_shapes, "prefill": prefill,
-                "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": int(launches), "clocks": clk.summary(),
-                "load_s": round(t_load, 1)}
+                "config": head["config"],
+                "parallelism": f"tp{world}", "kv_cache": "f16", "decode_path": head["decode_path"],
+                "decode_step": head["decode_step"],
+                "roofline": head["roofline"], "gemv_roofline": gemv_roof, "gemv_shapes": gemv_shapes,
+                "prefill": head.get("prefill"), "cpu_baseline": cpu, "e2e": head["e2e"],
+                "tp_parity": parity, "model_70b": m70,
+                "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
+                "load_s": head["load_s"]}
         print(json.dumps(line), flush=True)
-    m.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

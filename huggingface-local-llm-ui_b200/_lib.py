@@ -95,6 +95,7 @@ SIGNATURES = [
     ("b2q_check_device_error", _I, [_VP]),
     ("b2q_set_wait_limit_cycles", _I, [_VP, C.c_longlong]),
     ("b2q_model_debug_desync", _I, [_VP]),
+    ("b2q_model_fill_kv", _I, [_VP, _I, _I, C.c_uint64, _F]),
     ("b2q_set_tp_init_timeout_ms", _I, [_I]),
 ]
 

@@ -182,7 +182,10 @@ __host__ __device__ __forceinline__ RcGeom rc_geom(int dtype, int kc) {
 // issued), read back with b2q_debug_decode_trace().
 // ---------------------------------------------------------------------------
 #ifdef B2Q_DECODE_TRACE
-constexpr int kTraceSlots = 512;
+#ifndef B2Q_TRACE_SLOTS
+#define B2Q_TRACE_SLOTS 512
+#endif
+constexpr int kTraceSlots = B2Q_TRACE_SLOTS;
 __device__ unsigned long long g_dec_trace[2 * 160 * kTraceSlots];
 __device__ __forceinline__ void dec_trace(int slot, bool producer) {
   unsigned long long t;
@@ -856,39 +859,47 @@ __device__ __forceinline__ float dec_racc(const float* racc, int rows, int nw, i
 }
 
 // ---------------------------------------------------------------------------
-// attention item (KV head g, split z) on the 16 consumer warps: the work of
-// rope_kv_kernel (for this head group) + attn_split_kernel + (last split of
-// head g to finish) attn_combine_kernel, with the same arithmetic.  The
-// split holding `pos` takes this token's k/v from registers (and appends
-// them to the cache); the other rows arrive by bulk copy.  Every global
-// load of a step is issued before any of them is used.
+// attention item (KV head g, group j of tpg consecutive key tiles) on the 16
+// consumer warps: the work of rope_kv_kernel (for this head group) +
+// attn_split_kernel + (last group of head g to finish) attn_combine_kernel,
+// with the same arithmetic.  The tiles of the group are folded one after the
+// other into a running softmax partial (AttnRun); the tile holding `pos`
+// takes this token's k/v from registers (which are also appended to the
+// cache), the other rows arrive by bulk copy.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 template <int G>
-__device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& Ly, int g, int z, int nz,
-                                          AttnTile<G>& T, uint64_t* bar, int& uses, int* s_last, int tl,
+__device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& Ly, int g, int j, int ng, int tpg,
+                                          int nz, AttnTile<G>& T, uint64_t* bar, int& uses, int* s_last, int tl,
                                           volatile int* s_ok) {
   constexpr int HD = kHeadDim, HALF = kHeadDim / 2;
+  constexpr int R = (G * HD + kAttnThreads - 1) / kAttnThreads;
   const int gt = threadIdx.x;  // 0..511
   const int pos = a.pos, cap = a.max_seq;
   const int H = a.H, KV = a.KV;
-  const int t_begin = z * kAttnTile;
-  const int nv = min(kAttnTile, pos + 1 - t_begin);
-  const bool last = z == nz - 1;
-  const int nload = last ? nv - 1 : nv;
-  if (gt == 0 && nload > 0) {
-    fence_proxy_async_smem();  // earlier generic accesses to this region come first
-    attn_tile_load(T, Ly.kc, Ly.vc, g, cap, t_begin, nload, bar);
-  }
+  const int z0 = j * tpg, z1 = min(nz, z0 + tpg);
+  const bool last = z1 == nz;  // this group holds the tile with the current token
+  // K/V rows of tile z by bulk copy; in the tile holding the current token
+  // that token's row comes from registers instead
+  auto load = [&](int z) {
+    const int nv = min(kAttnTile, pos + 1 - z * kAttnTile);
+    const int nload = z == nz - 1 ? nv - 1 : nv;
+    if (gt == 0 && nload > 0) {
+      fence_proxy_async_smem();  // earlier generic accesses to this region come first
+      attn_tile_load(T, Ly.kc, Ly.vc, g, cap, z * kAttnTile, nload, bar);
+    }
+    return nload;
+  };
+  int nload = load(z0);
   const int p_rope = pos < 8191 ? pos : 8191;
   const float* cs = a.rope_cos + (int64_t)p_rope * HALF;
   const float* sn = a.rope_sin + (int64_t)p_rope * HALF;
   const float* row = a.qkv;
   // work index w < G*64: one q pair; [G*64, G*64 + 64): a k pair of this
-  // token (last split); [G*64 + 64, G*64 + 192): a v value.  Up to two
+  // token (last group); [G*64 + 64, G*64 + 192): a v value.  Up to two
   // indices per thread, all loads issued first.
   const int qn = G * HALF, nwork = qn + (last ? HALF + HD : 0);
   float x0[2], x1[2], c[2], sv[2];
@@ -899,17 +910,17 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
     c[r] = sv[r] = 0.0f;
     o0[r] = o1[r] = -1;
     if (w < qn) {
-      const int hh = w / HALF, j = w % HALF, h = g * G + hh;
-      o0[r] = h * HD + j;
+      const int hh = w / HALF, jj = w % HALF, h = g * G + hh;
+      o0[r] = h * HD + jj;
       o1[r] = o0[r] + HALF;
-      c[r] = cs[j];
-      sv[r] = sn[j];
+      c[r] = cs[jj];
+      sv[r] = sn[jj];
     } else if (w < qn + HALF && w < nwork) {
-      const int j = w - qn;
-      o0[r] = (H + g) * HD + j;
+      const int jj = w - qn;
+      o0[r] = (H + g) * HD + jj;
       o1[r] = o0[r] + HALF;
-      c[r] = cs[j];
-      sv[r] = sn[j];
+      c[r] = cs[jj];
+      sv[r] = sn[jj];
     } else if (w < nwork) {
       o0[r] = (H + KV) * HD + g * HD + (w - qn - HALF);
     }
@@ -946,56 +957,82 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
     x0[r] += b[bo];
     if (o1[r] >= 0) x1[r] += b[bo + HALF];
   }
+  // rotated q into the tile; this token's rotated k and its v into the cache
+  // and into the tile that holds the token: directly if that is the group's
+  // first tile, else through T.kcur / T.vcur (copied in the tile loop)
+  const int nv_last = pos + 1 - (nz - 1) * kAttnTile;  // rows of the token's tile
+  __half* const krow = z0 == nz - 1 ? T.k + (nv_last - 1) * HD : T.kcur;
+  __half* const vrow = z0 == nz - 1 ? T.v + (nv_last - 1) * HD : T.vcur;
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int w = gt + kAttnThreads * r;
     if (w < qn) {
-      const int hh = w / HALF, j = w % HALF;
-      T.q[hh][j] = __fsub_rn(__fmul_rn(x0[r], c[r]), __fmul_rn(x1[r], sv[r]));
-      T.q[hh][HALF + j] = __fadd_rn(__fmul_rn(x1[r], c[r]), __fmul_rn(x0[r], sv[r]));
-    } else if (w < qn + HALF && w < nwork) {  // this token's k, rotated: into the tile and the cache
-      const int j = w - qn;
+      const int hh = w / HALF, jj = w % HALF;
+      T.q[hh][jj] = __fsub_rn(__fmul_rn(x0[r], c[r]), __fmul_rn(x1[r], sv[r]));
+      T.q[hh][HALF + jj] = __fadd_rn(__fmul_rn(x1[r], c[r]), __fmul_rn(x0[r], sv[r]));
+    } else if (w < qn + HALF && w < nwork) {
+      const int jj = w - qn;
       const __half y0 = __float2half_rn(__fsub_rn(__fmul_rn(x0[r], c[r]), __fmul_rn(x1[r], sv[r])));
       const __half y1 = __float2half_rn(__fadd_rn(__fmul_rn(x1[r], c[r]), __fmul_rn(x0[r], sv[r])));
       __half* dst = Ly.kc + ((int64_t)g * cap + pos) * HD;
-      dst[j] = y0;
-      dst[HALF + j] = y1;
-      T.k[(nv - 1) * HD + j] = y0;
-      T.k[(nv - 1) * HD + HALF + j] = y1;
+      dst[jj] = y0;
+      dst[HALF + jj] = y1;
+      krow[jj] = y0;
+      krow[HALF + jj] = y1;
     } else if (w < nwork) {
-      const int j = w - qn - HALF;
+      const int jj = w - qn - HALF;
       const __half hv = __float2half_rn(x0[r]);
-      Ly.vc[((int64_t)g * cap + pos) * HD + j] = hv;
-      T.v[(nv - 1) * HD + j] = hv;
+      Ly.vc[((int64_t)g * cap + pos) * HD + jj] = hv;
+      vrow[jj] = hv;
     }
   }
   B2Q_FTRACE(tl, 10);
-  if (nload > 0) {
-    mbar_wait_bounded(bar, (uint32_t)(uses & 1));  // a timeout is recorded in the device error word
-    ++uses;
+  AttnRun<R> run;
+  run.init();
+  for (int z = z0; z < z1; ++z) {
+    const int nv = min(kAttnTile, pos + 1 - z * kAttnTile);
+    if (z > z0) {
+      consumer_sync();  // the previous tile's shared-memory reads are done
+      nload = load(z);
+    }
+    if (z == nz - 1 && z > z0) {  // T.kcur / T.vcur were written before the sync above
+      if (gt < HD) {
+        T.k[(nv - 1) * HD + gt] = T.kcur[gt];
+        T.v[(nv - 1) * HD + gt] = T.vcur[gt];
+      }
+    }
+    if (nload > 0) {
+      mbar_wait_bounded(bar, (uint32_t)(uses & 1));  // a timeout is recorded in the device error word
+      ++uses;
+    }
+    consumer_sync();
+    attn_tile_compute_emit<G>(T, nv, a.scale, [] { consumer_sync(); },
+                              [&](int r, int, int, float mt, float lt, float ot) { run.fold(r, mt, lt, ot); });
   }
   B2Q_FTRACE(tl, 11);
-  consumer_sync();
-  attn_tile_compute<G>(T, nv, a.scale, a.part, g, z, a.nsplit, [] { consumer_sync(); });
-  // the last split of this KV head to finish merges all of them
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = gt + kAttnThreads * r;
+    if (i < G * HD) attn_store_partial(a.part, g, G, j, a.nsplit, i / HD, i % HD, run.m[r], run.l[r], run.o[r]);
+  }
+  // the last group of this KV head to finish merges all of them
   consumer_sync();
   B2Q_FTRACE(tl, 12);
   if (gt == 0) {
     __threadfence();
     const unsigned int old = atomicAdd(&a.attn_cnt[tl * KV + g], 1u);
-    *s_last = old == (unsigned int)(nz - 1);
+    *s_last = old == (unsigned int)(ng - 1);
   }
   consumer_sync();
   B2Q_FTRACE(tl, 13);
   if (*s_last) {
     // merge (attn_combine_kernel's arithmetic, same order): the partials of
-    // up to kZc splits per head are brought into the idle tile with bulk
-    // copies (one round trip), then reduced in split order
+    // up to kZc groups per head are brought into the idle tile with bulk
+    // copies (one round trip), then reduced in group order
     __threadfence();
     const int nsplit = a.nsplit;
     constexpr int kZc = (2 * kAttnTile * HD / 2) / (G * kPartStride);  // splits per chunk (T.k + T.v)
     float* pb = reinterpret_cast<float*>(T.k);                          // [G][zc][kPartStride]
-    constexpr int R = (G * HD + kAttnThreads - 1) / kAttnThreads;
     float M[R], Ls[R], O[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -1003,23 +1040,23 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
       Ls[r] = 0.0f;
       O[r] = 0.0f;
     }
-    if (nz > kZc) {  // long context: the maxima of every split first, 8 loads in flight
+    if (ng > kZc) {  // many groups: the maxima of every partial first, 8 loads in flight
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const int i = gt + kAttnThreads * r;
         if (i >= G * HD) continue;
         const float* ph = a.part + (int64_t)(g * G + i / HD) * nsplit * kPartStride;
-        for (int zz0 = 0; zz0 < nz; zz0 += 8) {
+        for (int zz0 = 0; zz0 < ng; zz0 += 8) {
           float mv[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) mv[u] = zz0 + u < nz ? __ldcg(ph + (zz0 + u) * kPartStride) : -INFINITY;
+          for (int u = 0; u < 8; ++u) mv[u] = zz0 + u < ng ? __ldcg(ph + (zz0 + u) * kPartStride) : -INFINITY;
 #pragma unroll
           for (int u = 0; u < 8; ++u) M[r] = fmaxf(M[r], mv[u]);
         }
       }
     }
-    for (int z0 = 0; z0 < nz; z0 += kZc) {
-      const int zn = min(kZc, nz - z0);
+    for (int z0 = 0; z0 < ng; z0 += kZc) {
+      const int zn = min(kZc, ng - z0);
       if (gt == 0) {
         asm volatile("fence.proxy.async.global;" ::: "memory");
         fence_proxy_async_smem();
@@ -1036,7 +1073,7 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
         if (i >= G * HD) continue;
         const int h = i / HD, d = i % HD;
         const float* ph = pb + h * zn * kPartStride;
-        if (nz <= kZc)  // one chunk holds every split: maxima from shared memory
+        if (ng <= kZc)  // one chunk holds every partial: maxima from shared memory
           for (int zz = 0; zz < zn; ++zz) M[r] = fmaxf(M[r], ph[zz * kPartStride]);
         for (int zz = 0; zz < zn; ++zz) {
           const float m = ph[zz * kPartStride];
@@ -1159,7 +1196,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
   }
   grid_sync(bar, a.lbase, nbar, okp, false, ll);
 
-  const int nz = a.pos / kAttnTile + 1;
+  const int nz = a.pos / kAttnTile + 1;  // key tiles of this step
+  const int tpg = attn_group_tiles(nz, a.KV, (int)gridDim.x), ng = (nz + tpg - 1) / tpg;
   int attn_uses = 0;  // completed phases of the attention mbarrier
   float best = -INFINITY;
   int idx = 0x7fffffff;
@@ -1179,8 +1217,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
     if (k == 1) {  // RoPE, KV append, attention
       const DecLayer& Ly = a.layers[l];
       AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(xs);
-      for (int it = blockIdx.x; it < a.KV * nz; it += gridDim.x)
-        attn_item<G>(a, Ly, it / nz, it % nz, nz, T, &attn_bar[0], attn_uses, &attn_last[0], l, okp);
+      for (int it = blockIdx.x; it < a.KV * ng; it += gridDim.x)
+        attn_item<G>(a, Ly, it / ng, it % ng, ng, tpg, nz, T, &attn_bar[0], attn_uses, &attn_last[0], l, okp);
       B2Q_TRACE(tslot + 2);
       grid_sync(bar, a.lbase, nbar, okp, false, ll);  // the O projection reads this rank's heads
       continue;

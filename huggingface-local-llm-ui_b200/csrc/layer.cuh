@@ -122,6 +122,8 @@ struct AttnTile {
   float q[G][kHeadDim];            // rotated queries
   float sp[G][kAttnTile];          // scores, then probabilities
   float m[G], l[G];                // softmax max and sum per head
+  __half kcur[kHeadDim];           // the current token's rotated k and its v (persistent
+  __half vcur[kHeadDim];           // kernel: copied into the tile that holds the token)
 };
 
 // Issue the bulk copies of K/V rows [t0, t0 + rows) of KV head g into the
@@ -135,13 +137,46 @@ __device__ __forceinline__ void attn_tile_load(AttnTile<G>& T, const __half* kc,
   bulk_g2s(T.v, vc + ((int64_t)g * cap + t0) * kHeadDim, bytes, bar);
 }
 
-// The split partial of one item on kAttnThreads threads; T.q and the first
-// `nv` rows of T.k / T.v are in place.  `sync` is the item's barrier.
-// Writes part[(h * nsplit + z) * kPartStride] = {max, sum, O[128]} for the G
-// heads of head group g (h = g*G + i).
-template <int G, class Sync>
-__device__ __forceinline__ void attn_tile_compute(AttnTile<G>& T, int nv, float scale, float* part, int g, int z,
-                                                  int nsplit, Sync sync) {
+// Key tiles per attention group.  A query's nz tiles of kAttnTile keys are
+// cut into groups of consecutive tiles, one work item per (KV head, group),
+// so that a single-token step has about `grid` items whatever the context:
+// at short contexts one tile per group, at 8192 keys and 8 KV heads eight.
+// The persistent kernel and the per-kernel path use the same grouping, so
+// their partials and merges are the same bits.
+__host__ __device__ __forceinline__ int attn_group_tiles(int nz, int KV, int grid) {
+  const int ng = max(1, grid / max(1, KV));
+  return (nz + ng - 1) / ng;
+}
+
+// Running softmax state of one attention group, for the (head, dim)
+// elements i = tid + kAttnThreads * r a thread owns: max, sum and the
+// unnormalised P*V of the tiles seen so far.  Folding tile partial (m_t, l_t,
+// O_t) in: M = max(m, m_t); l = l * e^(m - M) + l_t * e^(m_t - M); O likewise
+// (the first tile is taken as is, so a one-tile group is that tile's partial
+// bit for bit).
+template <int R>
+struct AttnRun {
+  float m[R], l[R], o[R];
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int r = 0; r < R; ++r) { m[r] = -INFINITY; l[r] = 0.0f; o[r] = 0.0f; }
+  }
+  __device__ __forceinline__ void fold(int r, float mt, float lt, float ot) {
+    if (m[r] == -INFINITY) { m[r] = mt; l[r] = lt; o[r] = ot; return; }
+    const float M = fmaxf(m[r], mt);
+    const float a = expf(m[r] - M), b = expf(mt - M);
+    l[r] = fmaf(lt, b, l[r] * a);
+    o[r] = fmaf(ot, b, o[r] * a);
+    m[r] = M;
+  }
+};
+
+// The softmax partial of one tile on kAttnThreads threads; T.q and the first
+// `nv` rows of T.k / T.v are in place.  `sync` is the item's barrier.  For
+// every (head, dim) element i = h * 128 + d of the G heads of head group g a
+// thread owns (i = tid + kAttnThreads * r), calls emit(r, h, d, max, sum, O).
+template <int G, class Sync, class Emit>
+__device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, int nv, float scale, Sync sync, Emit emit) {
   constexpr int HD = kHeadDim;
   const int tid = threadIdx.x & (kAttnThreads - 1), lane = threadIdx.x & 31, w = tid >> 5;
   // scores: thread (token t, eighth e) sums dims 8e..8e+7 and 64+8e..64+8e+7,
@@ -217,55 +252,84 @@ __device__ __forceinline__ void attn_tile_compute(AttnTile<G>& T, int nv, float 
   for (int h = 0; h < G; ++h)
     *reinterpret_cast<float2*>(o8 + (tg * G + h) * HD + 2 * dp) = make_float2(o[h][0], o[h][1]);
   sync();
-  for (int i = tid; i < G * HD; i += kAttnThreads) {
+  constexpr int R = (G * HD + kAttnThreads - 1) / kAttnThreads;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = tid + kAttnThreads * r;
+    if (i >= G * HD) break;
     const int h = i / HD, d = i % HD;
     float O = o8[h * HD + d];
 #pragma unroll
     for (int q = 1; q < 8; ++q) O += o8[(q * G + h) * HD + d];
-    float* pp = part + ((int64_t)(g * G + h) * nsplit + z) * kPartStride;
-    if (d == 0) { pp[0] = T.m[h]; pp[1] = T.l[h]; }
-    pp[2 + d] = O;
+    emit(r, h, d, T.m[h], T.l[h], O);
   }
+}
+
+// Write a group partial: part[(h * nsplit + j) * kPartStride] = {max, sum,
+// O[128]} for head h = g*G + (element's head).
+__device__ __forceinline__ void attn_store_partial(float* part, int g, int G, int j, int nsplit, int h, int d,
+                                                   float m, float l, float o) {
+  float* pp = part + ((int64_t)(g * G + h) * nsplit + j) * kPartStride;
+  if (d == 0) { pp[0] = m; pp[1] = l; }
+  pp[2 + d] = o;
 }
 
 // Per-kernel path: grid (KV, m, nsplit), kAttnThreads threads,
 // sizeof(AttnTile<G>) bytes of dynamic shared memory.  Query s sits at
 // position start+s and sees keys t < start+s+1 (causal); q was rotated in
-// place by rope_kv_kernel.
+// place by rope_kv_kernel.  Block (g, s, j) folds the key tiles of group j
+// (attn_group_tiles with `grid` = the SM count) into one partial.
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
     const float* __restrict__ qkv, int m, int H, int KV, const int* __restrict__ pos_dev, int cap,
     const __half* __restrict__ kc, const __half* __restrict__ vc, float scale, int nsplit,
-    float* __restrict__ part) {
+    float* __restrict__ part, int grid) {
   extern __shared__ __align__(128) uint8_t attn_smem[];
   __shared__ uint64_t bar;
   AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(attn_smem);
   pdl_wait();
   constexpr int HD = kHeadDim;
-  const int g = blockIdx.x, s = blockIdx.y, z = blockIdx.z;
+  constexpr int R = (G * HD + kAttnThreads - 1) / kAttnThreads;
+  const int g = blockIdx.x, s = blockIdx.y, j = blockIdx.z;
   const int start = *pos_dev;
   const int valid = min(start + s + 1, cap);
-  const int t_begin = z * kAttnTile;
+  const int nz = (valid + kAttnTile - 1) / kAttnTile;
+  const int tpg = attn_group_tiles(nz, KV, grid);
+  const int z0 = j * tpg, z1 = min(nz, z0 + tpg);
   float* ps = part + (int64_t)s * H * nsplit * kPartStride;
-  if (t_begin >= valid) {
+  if (z0 >= nz) {
     if (threadIdx.x < G) {
-      float* p = ps + ((int64_t)(g * G + threadIdx.x) * nsplit + z) * kPartStride;
+      float* p = ps + ((int64_t)(g * G + threadIdx.x) * nsplit + j) * kPartStride;
       p[0] = -INFINITY;
       p[1] = 0.0f;
     }
     return;
   }
-  const int nv = min(kAttnTile, valid - t_begin);
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
-    attn_tile_load(T, kc, vc, g, cap, t_begin, nv, &bar);
+    attn_tile_load(T, kc, vc, g, cap, z0 * kAttnTile, min(kAttnTile, valid - z0 * kAttnTile), &bar);
   }
   const int width = (H + 2 * KV) * HD;
   for (int i = threadIdx.x; i < G * HD; i += blockDim.x) T.q[i / HD][i % HD] = qkv[(int64_t)s * width + g * G * HD + i];
-  __syncthreads();
-  mbar_wait_bounded(&bar, 0);  // a timeout is recorded in the device error word
-  attn_tile_compute<G>(T, nv, scale, ps, g, z, nsplit, [] { __syncthreads(); });
+  AttnRun<R> run;
+  run.init();
+  for (int z = z0; z < z1; ++z) {
+    const int t_begin = z * kAttnTile, nv = min(kAttnTile, valid - t_begin);
+    __syncthreads();  // q in place / the previous tile's shared-memory reads are done
+    if (z > z0 && threadIdx.x == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      attn_tile_load(T, kc, vc, g, cap, t_begin, nv, &bar);
+    }
+    mbar_wait_bounded(&bar, (uint32_t)((z - z0) & 1));  // a timeout is recorded in the device error word
+    attn_tile_compute_emit<G>(T, nv, scale, [] { __syncthreads(); },
+                              [&](int r, int, int, float mt, float lt, float ot) { run.fold(r, mt, lt, ot); });
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = threadIdx.x + kAttnThreads * r;
+    if (i < G * HD) attn_store_partial(ps, g, G, j, nsplit, i / HD, i % HD, run.m[r], run.l[r], run.o[r]);
+  }
   pdl_launch_dependents();
 }
 
@@ -274,7 +338,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
 // for the o-projection.  grid (KV, m), G*128 threads (one per output dim).
 __global__ void attn_combine_kernel(const float* __restrict__ part, int m, int H, int G,
                                     const int* __restrict__ pos_dev, int cap, int nsplit,
-                                    float* __restrict__ out, XQ xq) {
+                                    float* __restrict__ out, XQ xq, int grid) {
   pdl_wait();
   constexpr int HD = kHeadDim;
   __shared__ float vals[8 * HD];
@@ -282,7 +346,9 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int m, int H
   const int h = g * G + threadIdx.x / HD, d = threadIdx.x % HD;
   const int start = *pos_dev;
   const int valid = min(start + s + 1, cap);
-  const int ns = min(nsplit, (valid + kAttnTile - 1) / kAttnTile);
+  const int nz = (valid + kAttnTile - 1) / kAttnTile;
+  const int tpg = attn_group_tiles(nz, H / G, grid);
+  const int ns = min(nsplit, (nz + tpg - 1) / tpg);  // groups
   const float* pp = part + ((int64_t)s * H + h) * nsplit * kPartStride;
   float M = -INFINITY;
   for (int z = 0; z < ns; ++z) M = fmaxf(M, pp[z * kPartStride]);
@@ -303,6 +369,28 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int m, int H
   if (warp < 2 * G)
     xq_store_block(vals[64 * warp + lane], vals[64 * warp + 32 + lane], lane, s, (col0 >> 6) + warp, xq);
   pdl_launch_dependents();
+}
+
+// Seeded synthetic KV rows (benchmark set-up: a long context without a
+// prompt pass).  Element e of the K (kv = 0) or V (kv = 1) row of global KV
+// head h at position t in layer l is u * scale, u in [-1, 1) from a 64-bit
+// mix (splitmix64 finaliser) of (seed, l, kv, h, t, e), rounded to f16; the
+// global head index makes a tensor-parallel rank's rows those of one GPU.
+// grid (positions, local KV heads), block kHeadDim.
+__global__ void kv_fill_kernel(__half* __restrict__ kc, __half* __restrict__ vc, int max_seq, int t0,
+                               int layer, int head0, uint64_t seed, float scale) {
+  const int t = t0 + (int)blockIdx.x, g = (int)blockIdx.y, e = (int)threadIdx.x;
+  const int64_t off = ((int64_t)g * max_seq + t) * kHeadDim + e;
+  for (int kv = 0; kv < 2; ++kv) {
+    uint64_t z = seed ^ ((uint64_t)layer << 48) ^ ((uint64_t)kv << 47) ^ ((uint64_t)(head0 + g) << 38) ^
+                 ((uint64_t)t << 8) ^ (uint64_t)e;
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    z ^= z >> 31;
+    const float u = (float)(z >> 40) * (1.0f / 8388608.0f) - 1.0f;  // 24 bits -> [-1, 1)
+    (kv ? vc : kc)[off] = __float2half_rn(u * scale);
+  }
 }
 
 // Step inputs written by a kernel (parameters are captured at launch), so

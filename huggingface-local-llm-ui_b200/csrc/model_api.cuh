@@ -493,6 +493,26 @@ b2q_status b2q_forward_sample(b2q_model* M, const uint32_t* tokens, int n, int s
   return s;
 }
 
+b2q_status b2q_model_fill_kv(b2q_model* M, int start, int n, uint64_t seed, float scale) {
+  if (!M || !M->finalized) return set_error(B2Q_EINVAL, "b2q_model_fill_kv: model not finalized");
+  if (start < 0 || n <= 0 || start + n > M->c.max_seq)
+    return set_error(B2Q_EINVAL, "b2q_model_fill_kv: positions [%d, %d) outside the KV capacity %d", start,
+                     start + n, M->c.max_seq);
+  std::lock_guard<std::mutex> lk(M->eng->mu);
+  cudaSetDevice(M->eng->device);
+  const int head0 = M->c.tp_rank * M->KV_loc;
+  cudaError_t err = cudaSuccess;
+  for (int l = 0; l < M->c.n_layers && err == cudaSuccess; ++l) {
+    launch_counted(M->eng, 1);
+    kv_fill_kernel<<<dim3(n, M->KV_loc), kHeadDim, 0, M->st>>>(M->L[l].kc, M->L[l].vc, M->c.max_seq, start, l,
+                                                               head0, seed, scale);
+    err = cudaGetLastError();
+  }
+  if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
+  if (err != cudaSuccess) return cuda_error(err, "b2q_model_fill_kv");
+  return B2Q_OK;
+}
+
 b2q_status b2q_model_debug_desync(b2q_model* M) {
   if (!M || !M->finalized) return set_error(B2Q_EINVAL, "b2q_model_debug_desync: model not finalized");
   if (!M->dec_on) return set_error(B2Q_EUNSUP, "b2q_model_debug_desync: the model has no persistent decode step");

@@ -269,24 +269,24 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
       if (G == 4)
         err = cudaLaunchKernelEx(&cfg, attn_split_kernel<4>, (const float*)M->qkv, m, Hl, KVl,
                                  (const int*)M->pos, c.max_seq, (const __half*)Lw.kc,
-                                 (const __half*)Lw.vc, scale, M->nsplit, M->part);
+                                 (const __half*)Lw.vc, scale, M->nsplit, M->part, e->num_sms);
       else if (G == 8)
         err = cudaLaunchKernelEx(&cfg, attn_split_kernel<8>, (const float*)M->qkv, m, Hl, KVl,
                                  (const int*)M->pos, c.max_seq, (const __half*)Lw.kc,
-                                 (const __half*)Lw.vc, scale, M->nsplit, M->part);
+                                 (const __half*)Lw.vc, scale, M->nsplit, M->part, e->num_sms);
       else if (G == 2)
         err = cudaLaunchKernelEx(&cfg, attn_split_kernel<2>, (const float*)M->qkv, m, Hl, KVl,
                                  (const int*)M->pos, c.max_seq, (const __half*)Lw.kc,
-                                 (const __half*)Lw.vc, scale, M->nsplit, M->part);
+                                 (const __half*)Lw.vc, scale, M->nsplit, M->part, e->num_sms);
       else
         err = cudaLaunchKernelEx(&cfg, attn_split_kernel<1>, (const float*)M->qkv, m, Hl, KVl,
                                  (const int*)M->pos, c.max_seq, (const __half*)Lw.kc,
-                                 (const __half*)Lw.vc, scale, M->nsplit, M->part);
+                                 (const __half*)Lw.vc, scale, M->nsplit, M->part, e->num_sms);
       if (err != cudaSuccess) return err;
       cudaLaunchConfig_t cfg2 = lcfg(dim3(KVl, m), dim3(G * kHeadDim), 0, st, attr, pdl);
       launch_counted(e, 1);
       err = cudaLaunchKernelEx(&cfg2, attn_combine_kernel, (const float*)M->part, m, Hl, G,
-                               (const int*)M->pos, c.max_seq, M->nsplit, aout, M->xq_a.x);
+                               (const int*)M->pos, c.max_seq, M->nsplit, aout, M->xq_a.x, e->num_sms);
       if (err != cudaSuccess) return err;
       // under tensor parallelism the attention output of this rank's heads
       // stays local: attn_output holds the matching columns (K split)

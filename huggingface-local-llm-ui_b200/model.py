@@ -187,6 +187,11 @@ class StandardNativeEngine:
             self.current_pos += 1
         return out
 
+    def fill_kv(self, start: int, n: int, seed: int = 0, scale: float = 1.0) -> None:
+        """Seeded synthetic K/V rows for positions [start, start + n) of every
+        layer (benchmark set-up for a long context; b2q_model_fill_kv)."""
+        check(lib().b2q_model_fill_kv(self._h, start, n, seed, scale))
+
     def clear_state(self) -> None:
         check(lib().b2q_clear_state(self._h))
         self.current_pos = 0

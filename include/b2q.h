@@ -307,6 +307,15 @@ b2q_status b2q_gdn_step_dev(b2q_engine* eng, const b2q_gdn_config* cfg, int n_to
  * at a host barrier before the next step). */
 b2q_status b2q_clear_state(b2q_model* m);
 
+/* Benchmark set-up, no counterpart in the reference: writes seeded synthetic
+ * K and V rows (uniform in [-scale, scale), rounded to f16) for positions
+ * [start, start + n) of every layer's KV cache, for this rank's KV heads, so
+ * that single-token steps can be timed at a long context without a prompt
+ * pass.  The values depend only on (seed, layer, K or V, global KV head,
+ * position, element), so tensor-parallel ranks hold the rows one GPU would.
+ * Synchronous. */
+b2q_status b2q_model_fill_kv(b2q_model* m, int start, int n, uint64_t seed, float scale);
+
 /* Test hook, no counterpart in the reference: advances the model's
  * persistent-kernel launch sequence on the host without launching, which is
  * what a launch skipped by a peer looks like from this GPU: the next step's

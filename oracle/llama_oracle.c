@@ -99,6 +99,28 @@ void oracle_clear_state(void* p) {
   for (int l = 0; l < m->c.n_layers; l++) { m->layers[l].len32 = 0; m->layers[l].len64 = 0; }
 }
 
+/* Timing set-up for the CPU baseline (not part of the reference): the f32
+ * reference-path KV cache of every layer holds `n` positions of seeded
+ * synthetic rows, uniform in [-1, 1), as after an n-token prompt, so that
+ * decode steps can be timed at that context without the prompt pass. */
+int oracle_fill_kv(void* p, int64_t n, uint64_t seed) {
+  OModel* m = (OModel*)p;
+  if (n < 0 || n > m->cap) return -1;
+  const int64_t row = (int64_t)m->c.n_kv_heads * m->c.head_dim;
+  for (int l = 0; l < m->c.n_layers; l++) {
+    OLayer* L = &m->layers[l];
+    uint64_t s = seed ^ ((uint64_t)(l + 1) * 0x9e3779b97f4a7c15ull);
+    for (int64_t i = 0; i < n * row; i++) {
+      s ^= s << 13; s ^= s >> 7; s ^= s << 17;
+      L->kc32[i] = (float)(s >> 40) * (1.0f / 8388608.0f) - 1.0f;
+      s ^= s << 13; s ^= s >> 7; s ^= s << 17;
+      L->vc32[i] = (float)(s >> 40) * (1.0f / 8388608.0f) - 1.0f;
+    }
+    L->len32 = n;
+  }
+  return 0;
+}
+
 const float* oracle_rope_table(void* p, int cos_not_sin) {
   OModel* m = (OModel*)p;
   return cos_not_sin ? m->rope_cos : m->rope_sin;

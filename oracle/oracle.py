@@ -52,6 +52,7 @@ def lib():
         L.oracle_model_create.restype = C.c_void_p
         L.oracle_model_free.argtypes = [C.c_void_p]
         L.oracle_clear_state.argtypes = [C.c_void_p]
+        L.oracle_fill_kv.argtypes = [C.c_void_p, C.c_int64, C.c_uint64]
         L.oracle_model_set.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int,
                                        C.c_int64, C.c_int64]
         L.oracle_forward_ref.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.c_int64, C.c_int64, f32p]
@@ -195,6 +196,12 @@ class Model:
 
     def clear_state(self):
         lib().oracle_clear_state(self._h)
+
+    def fill_kv(self, n: int, seed: int = 0) -> None:
+        """Timing set-up: n positions of seeded synthetic rows in the
+        reference path's f32 KV cache (decode steps then run at context n)."""
+        if lib().oracle_fill_kv(self._h, n, seed) != 0:
+            raise ValueError("oracle fill_kv: n exceeds the KV capacity")
 
     def forward_ref(self, tokens, start_pos: int) -> np.ndarray:
         t = np.ascontiguousarray(tokens, dtype=np.uint32)

@@ -179,3 +179,26 @@ def test_qkv_biases_vs_fp64(engine, orc, pkg, gqa):
     engine.check_device_error()
     for d in devs.values():
         d.close()
+
+
+def test_synthetic_kv_fill_steps_persistent_equals_eager(engine, pkg):
+    """b2q_model_fill_kv (the benchmark's long-context set-up): after the same
+    seeded fill of 8000 positions, persistent and per-kernel single-token
+    steps at positions 8000..8002 give the same logits bit for bit, and a
+    different seed gives different logits (the steps read the filled rows)."""
+    from hf_llm_b200 import model, synth
+    cfg = dict(LONG)
+    t = synth.llama_tensors(cfg, model.q4_k_m_types(), 53, dist="unit")
+    ms = {md: model.StandardNativeEngine.from_tensors(engine, cfg, t, max_seq=8192, decode=md)
+          for md in ("persistent", "eager")}
+    other = model.StandardNativeEngine.from_tensors(engine, cfg, t, max_seq=8192, decode="eager")
+    for m in ms.values():
+        m.fill_kv(0, 8000, seed=9, scale=0.5)
+    other.fill_kv(0, 8000, seed=10, scale=0.5)
+    for pos, tok in ((8000, 17), (8001, 300), (8002, 5)):
+        a, b = ms["persistent"].forward([tok], pos), ms["eager"].forward([tok], pos)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), pos
+        assert not np.array_equal(a, other.forward([tok], pos))
+    engine.check_device_error()
+    for m in list(ms.values()) + [other]:
+        m.close()

@@ -138,3 +138,20 @@ def test_bench_distribution_is_chaotic(orc, pkg):
     b = orc.Model(cfg, t, 64).forward_f64([5, 17, 300, 2, 99], 0, kv_f16=False)
     c = orc.Model(cfg, t, 64).forward_f64([5, 17, 300, 2, 99], 0, kv_f16=True)
     assert rel_l2(c, b) > 1e-3
+
+
+def test_fill_kv_sets_the_context(orc, pkg):
+    """The CPU-baseline timing set-up: n synthetic positions in the reference
+    path's KV cache; the next forward attends over them (its logits depend on
+    the filled rows) and n beyond the capacity is rejected."""
+    from hf_llm_b200 import model, synth
+    cfg = dict(n_layers=1, n_embd=256, n_heads=2, n_kv_heads=1, head_dim=128, n_ff=256, n_vocab=64,
+               rms_eps=1e-5, rope_theta=500000.0)
+    t = synth.llama_tensors(cfg, model.q4_k_m_types(), 3, dist="unit")
+    a, b = orc.Model(cfg, t, kv_capacity=40), orc.Model(cfg, t, kv_capacity=40)
+    a.fill_kv(32, seed=1)
+    b.fill_kv(32, seed=2)
+    la, lb = a.forward_ref([5], 32), b.forward_ref([5], 32)
+    assert np.all(np.isfinite(la)) and not np.array_equal(la, lb)
+    with pytest.raises(ValueError):
+        a.fill_kv(41)
