@@ -90,7 +90,7 @@ SIGNATURES = [
     ("b2q_model_weight_bytes", _SZ, [_VP]),
     ("b2q_model_step_path", _I, [_VP]),
     ("b2q_model_destroy", _I, [_VP]),
-    ("b2q_time_gemv", _I, [_VP, C.POINTER(_VP), _I, _VP, _I, _I, _VP, C.POINTER(C.c_float)]),
+    ("b2q_time_gemv", _I, [_VP, C.POINTER(_VP), _I, _VP, _I, _I, _VP, C.POINTER(C.c_float), _I]),
     ("b2q_kernel_launch_count", C.c_uint64, [_VP]),
     ("b2q_check_device_error", _I, [_VP]),
     ("b2q_set_wait_limit_cycles", _I, [_VP, C.c_longlong]),

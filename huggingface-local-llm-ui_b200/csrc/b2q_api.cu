@@ -716,7 +716,7 @@ b2q_status b2q_dequantize_dev(b2q_engine* e, const void* raw_dev, int dtype, int
 }
 
 b2q_status b2q_time_gemv(b2q_engine* e, const b2q_weight* const* ws, int count, const float* x_dev,
-                         int k, int reps, void* stream, float* avg_ms) {
+                         int k, int reps, void* stream, float* avg_ms, int chained) {
   if (!e || !ws || count <= 0 || !x_dev || reps <= 0 || !avg_ms)
     return set_error(B2Q_EINVAL, "b2q_time_gemv: bad argument");
   int64_t nmax = 0;
@@ -739,7 +739,10 @@ b2q_status b2q_time_gemv(b2q_engine* e, const b2q_weight* const* ws, int count, 
   for (int r = 0; r < reps && err == cudaSuccess; ++r)
     for (int i = 0; i < count && err == cudaSuccess; ++i) {
       GemvSeg sg = make_seg(ws[i], e->ws_y, (int)ws[i]->n);
-      err = run_gemv(e, &sg, 1, e->ws_xq, 1, kEpiStore, st, false);
+      // chained: programmatic dependent launch, as the per-kernel decode
+      // path launches its GEMVs (the next launch streams its weights while
+      // this one drains; it reads the activations only after this one ends)
+      err = run_gemv(e, &sg, 1, e->ws_xq, 1, kEpiStore, st, chained != 0);
     }
   cudaEventRecord(ev1, st);
   if (err == cudaSuccess) err = cudaEventSynchronize(ev1);

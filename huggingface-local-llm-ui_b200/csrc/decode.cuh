@@ -107,7 +107,6 @@ struct DecodeArgs {
   const float* rope_sin;
   const uint32_t* token;  // this step's token id (device)
   int pos;                // its position
-  float* qkv;             // [(H + 2 KV) * 128] this rank's heads
   float* part;            // [H][nsplit][kPartStride] attention split partials
   int nsplit;
   DecSync* sync;
@@ -115,40 +114,43 @@ struct DecodeArgs {
   // last split to finish merges and returns the word to zero; the next use
   // is the same layer of the next launch)
   unsigned int* attn_cnt;
-  // One GPU (tp == 1): the vectors that cross CTAs between phases -- the
-  // residual x, q/k/v and the attention output -- are stored tagged, value |
-  // tag << 32 in one 8-byte store, with tag = tag0 + 5 * layer + hand-off
-  // (0: x into QKV, 1: q/k/v, 2: attention output, 3: x into gate/up).  A
-  // reader that sees the tag sees the value, so no release fence sits
-  // between a phase's last store and the barrier in front of the next
-  // phase: that barrier is a relaxed gate that only keeps readers from
-  // polling early, and each reader polls (bounded) for the tag.  The SwiGLU
-  // output h, the attention partials and the argmax candidates keep
-  // plain stores behind release/acquire synchronisation.
+  // The vectors that cross CTAs between phases -- the residual x, q/k/v and
+  // the attention output -- are stored tagged, value | tag << 32 in one
+  // 8-byte store, with tag = tag0 + 5 * layer + hand-off (0: x into QKV, 1:
+  // q/k/v, 2: attention output, 3: x into gate/up).  A reader that sees the
+  // tag sees the value, so no release fence sits between a phase's last
+  // store and the barrier in front of the next phase: that barrier is a
+  // relaxed gate that only keeps readers from polling early, and each reader
+  // polls (bounded) for the tag.  The SwiGLU output h, the attention
+  // partials and the argmax candidates keep plain stores behind
+  // release/acquire synchronisation.
   unsigned long long* xll;     // [E]
-  unsigned long long* qkvll;   // [(H + 2 KV) * 128]
-  unsigned long long* attnll;  // [H * 128]
+  unsigned long long* qkvll;   // [(H + 2 KV) * 128] this rank's heads
+  unsigned long long* attnll;  // [H * 128] this rank's heads
   uint32_t tag0;
   uint32_t* argmax;       // model's argmax word
   uint32_t* argmax2;      // optional caller's copy
   // Tensor parallelism: this is rank `rank` of `tp` (tp = 1 on one GPU).  H,
   // KV are this rank's heads, Fl its SwiGLU rows.  Attention and the SwiGLU
   // output stay local; attn_output and ffn_down hold this rank's columns
-  // (the K split), so their epilogues store partial sums of every row into
-  // each rank's slot partg[p][(set * tp + rank) * E + row] (set 0: O, 1:
-  // down), and every rank forms the residual x + sum_p partial_p in rank
-  // order while staging the next RMSNorm.  logitsg[p], candg[p] are rank
-  // p's copies of the vocabulary slices and argmax candidates.  Pointers for
-  // p != rank are peer memory over NVLink.
+  // (the K split), so their epilogues produce partial sums of every row.  The
+  // CTA owning a row stores its partial, tagged (tag0 + 5 * layer + 2 for O,
+  // + 4 for down), into every rank's slot partll[p][(set * tp + rank) * E +
+  // row] (set 0: O, 1: down) over NVLink, then waits (bounded) for the other
+  // ranks' partials of the same row in its own slots and forms x + p_0 + p_1
+  // + ... in rank order -- the sum the per-kernel path forms after its NCCL
+  // all-gather -- so every rank holds the same residual and no per-layer
+  // all-rank barrier is needed: a slot is rewritten only after every rank
+  // has consumed its previous contents, which the data dependencies between
+  // layers guarantee.  logitsg[p], candg[p] are rank p's copies of the
+  // vocabulary slices and argmax candidates (one all-rank barrier per
+  // token, at the head).  Pointers for p != rank are peer memory over NVLink.
   int tp, rank;
   int Hg;                 // query heads over all ranks
   int Fl;                 // this rank's SwiGLU rows
   int v_off;              // first vocabulary row of this rank's head slice
-  float* xg[kMaxTp];      // [E] residual stream (this rank's own copy at xg[rank])
-  float* xalt;            // [E] second residual buffer (tp > 1: the updates alternate)
-  float* attng[kMaxTp];   // [H * 128] attention output of this rank's heads (local)
   float* hg[kMaxTp];      // [Fl] SwiGLU output of this rank's rows (local)
-  float* partg[kMaxTp];   // [2][tp][E] partial O / down sums from every rank
+  unsigned long long* partll[kMaxTp];  // [2][tp][E] tagged partial O / down sums from every rank
   float* logitsg[kMaxTp]; // [V]
   int2* candg[kMaxTp];    // [tp * grid] per-CTA argmax candidates (value bits, global row)
   unsigned long long* xflagg[kMaxTp];  // [kMaxTp] per-source-rank barrier epochs
@@ -258,6 +260,37 @@ __device__ __forceinline__ float ll_value(const unsigned long long* p, unsigned 
     while ((uint32_t)(v >> 32) != tag && *s_ok && clock64() - t0 <= lim) {
       __nanosleep(32);
       v = ld_relaxed_u64(p);
+    }
+    if ((uint32_t)(v >> 32) != tag && *s_ok) {
+      atomicExch(&g_b2q_device_error, 5);
+      *s_ok = 0;
+    }
+  }
+  return __uint_as_float((uint32_t)v);
+}
+
+// Tagged words crossing GPUs (tensor-parallel partial sums): system-scope
+// 8-byte stores into a peer's memory and loads of the words peers wrote here.
+__device__ __forceinline__ void ll_store_sys(unsigned long long* p, float v, uint32_t tag) {
+  const unsigned long long w = (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
+
+// ll_value for words written by other GPUs (bounded polling, system scope).
+__device__ __forceinline__ float ll_value_sys(const unsigned long long* p, unsigned long long first, uint32_t tag,
+                                              volatile int* s_ok) {
+  unsigned long long v = first;
+  if ((uint32_t)(v >> 32) != tag) {
+    const long long t0 = clock64(), lim = wait_limit();
+    while ((uint32_t)(v >> 32) != tag && *s_ok && clock64() - t0 <= lim) {
+      __nanosleep(64);
+      v = ld_relaxed_sys_u64(p);
     }
     if ((uint32_t)(v >> 32) != tag && *s_ok) {
       atomicExch(&g_b2q_device_error, 5);
@@ -386,23 +419,19 @@ __host__ __device__ __forceinline__ size_t xq_smem_bytes(int kpad) { return (gem
 // squares follows the reduction order of rmsnorm_quant_kernel's 1024-thread
 // CTA exactly (consumer thread i plays threads i and i + 512), so the values
 // are the same bits.  Quantisation: 8 lanes per block (xq_store_chunk8),
-// warp w takes blocks 4w..4w+3, then 4w+64.. .
-// `part` (tensor parallelism): np partial-sum rows of length dim, added to
-// x in order (x + part[0] + part[1] + ...) as the new residual; CTA b then
-// writes elements [b*dim/grid, (b+1)*dim/grid) of it to `xw`.
-// `xll` (one GPU): x is read from the tagged copy instead, polling for `tag`.
-__device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, int dim, float eps, const XQ& q,
-                                              float* xs, float* red, int tl = -1, int tb = 0,
-                                              const float* part = nullptr, int np = 0, float* xw = nullptr,
-                                              const unsigned long long* xll = nullptr, uint32_t tag = 0,
-                                              volatile int* s_ok = nullptr) {
+// warp w takes blocks 4w..4w+3, then 4w+64.. .  x is read from its tagged
+// copy `xll`, whose elements must carry `tag` (polled for, bounded, in the
+// rare case that some element is not yet visible).
+__device__ __forceinline__ void stage_rmsnorm(const unsigned long long* xll, const float* w, int dim, float eps,
+                                              const XQ& q, float* xs, float* red, int tl, int tb, uint32_t tag,
+                                              volatile int* s_ok) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = q.kpad >> 6;
   float sa = 0.0f, sb = 0.0f;
   uint32_t bad = 0u;  // nonzero: some tagged element read here was not yet visible
   for (int e0 = 0; e0 < dim; e0 += 1024 * kStageBatch) {
     float va[kStageBatch], vb[kStageBatch];
-    if (xll != nullptr) {  // every load of the batch in flight; the tags are checked in bulk below
+    {  // every load of the batch in flight; the tags are checked in bulk below
       unsigned long long ua[kStageBatch], ub[kStageBatch];
 #pragma unroll
       for (int i = 0; i < kStageBatch; ++i) {
@@ -415,22 +444,6 @@ __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, in
         bad |= ((uint32_t)(ua[i] >> 32) ^ tag) | ((uint32_t)(ub[i] >> 32) ^ tag);
         va[i] = __uint_as_float((uint32_t)ua[i]);
         vb[i] = __uint_as_float((uint32_t)ub[i]);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < kStageBatch; ++i) {
-        const int ea = e0 + 1024 * i + tid, eb = ea + 512;
-        va[i] = ea < dim ? __ldcg(x + ea) : 0.0f;
-        vb[i] = eb < dim ? __ldcg(x + eb) : 0.0f;
-      }
-    }
-    for (int p = 0; p < np; ++p) {
-      const float* pp = part + (size_t)p * dim;
-#pragma unroll
-      for (int i = 0; i < kStageBatch; ++i) {
-        const int ea = e0 + 1024 * i + tid, eb = ea + 512;
-        if (ea < dim) va[i] += __ldcg(pp + ea);
-        if (eb < dim) vb[i] += __ldcg(pp + eb);
       }
     }
     if (e0 == 0) {  // norm weights towards L1 while x is in flight (one 128-byte line per thread)
@@ -478,10 +491,6 @@ __device__ __forceinline__ void stage_rmsnorm(const float* x, const float* w, in
     consumer_sync();
   }
   B2Q_FTRACE(tl, tb + 1);
-  if (xw != nullptr) {
-    const int e0 = (int)((int64_t)dim * blockIdx.x / gridDim.x), e1 = (int)((int64_t)dim * (blockIdx.x + 1) / gridDim.x);
-    for (int e = e0 + tid; e < e1; e += kGemvConsumerWarps * 32) xw[e] = xs[e];
-  }
   const float tot = warp_sum(red[lane]);
   const float inv = 1.0f / sqrtf(tot / (float)dim + eps);
   B2Q_FTRACE(tl, tb + 2);
@@ -897,7 +906,6 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
   const int p_rope = pos < 8191 ? pos : 8191;
   const float* cs = a.rope_cos + (int64_t)p_rope * HALF;
   const float* sn = a.rope_sin + (int64_t)p_rope * HALF;
-  const float* row = a.qkv;
   // work index w < G*64: one q pair; [G*64, G*64 + 64): a k pair of this
   // token (last group); [G*64 + 64, G*64 + 192): a v value.  Up to two
   // indices per thread, all loads issued first.
@@ -925,7 +933,7 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
       o0[r] = (H + KV) * HD + g * HD + (w - qn - HALF);
     }
   }
-  if (a.tp == 1) {  // tagged q|k|v
+  {  // tagged q|k|v
     const uint32_t tq = a.tag0 + (uint32_t)(5 * tl + 1);
     unsigned long long u0[2], u1[2];
 #pragma unroll
@@ -937,12 +945,6 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
     for (int r = 0; r < 2; ++r) {
       x0[r] = o0[r] >= 0 ? ll_value(a.qkvll + o0[r], u0[r], tq, s_ok) : 0.0f;
       x1[r] = o1[r] >= 0 ? ll_value(a.qkvll + o1[r], u1[r], tq, s_ok) : 0.0f;
-    }
-  } else {
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      x0[r] = o0[r] >= 0 ? __ldcg(row + o0[r]) : 0.0f;
-      x1[r] = o1[r] >= 0 ? __ldcg(row + o1[r]) : 0.0f;
     }
   }
   // optional biases: q rows h*HD + j, k rows (H + g)*HD + j, v rows
@@ -1090,8 +1092,7 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
       if (i < G * HD) {
         const float v = O[r] * (1.0f / fmaxf(Ls[r], 1e-12f));
         const int oi = (g * G + i / HD) * HD + i % HD;  // this rank's heads, local
-        if (a.tp == 1) ll_store(a.attnll + oi, v, a.tag0 + (uint32_t)(5 * tl + 2));
-        else a.attng[a.rank][oi] = v;
+        ll_store(a.attnll + oi, v, a.tag0 + (uint32_t)(5 * tl + 2));
       }
     }
     if (gt == 0) a.attn_cnt[tl * KV + g] = 0u;
@@ -1167,14 +1168,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
   cs.R.cap = a.cap;
   unsigned long long* bar = &a.sync->bar;
   int nbar = 0, nxbar = 0;  // this-GPU and all-rank barriers passed
-  float* const x = a.xg[a.rank];
-  const bool ll = a.tp == 1;  // tagged hand-offs (DecodeArgs)
   const int kp_e = round_up_int(a.E, 256);
   float* xcopy = reinterpret_cast<float*>(xs + xq_smem_bytes(kp_e));
 
   // this CTA's phase table, and the token embedding (embed_rows_kernel's
-  // values): spread over the grid; one GPU: every CTA dequantises the row
-  // into shared memory and stores its slice of x, tagged
+  // values): every CTA dequantises the row into shared memory and stores its
+  // slice of x, tagged
   {
     const int4* src = reinterpret_cast<const int4*>(a.ctab + (size_t)blockIdx.x * a.nph);
     int4* dst = reinterpret_cast<int4*>(tab);
@@ -1183,18 +1182,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
     if (tok >= (uint32_t)a.V) tok = 0;
     const uint8_t* rowp = a.tok_raw + (int64_t)tok * a.tok_row_bytes;
     const int64_t slots = dequant_slots(a.tok_dtype, a.E);
-    if (ll) {
-      for (int64_t sl = threadIdx.x; sl < slots; sl += kGemvConsumerWarps * 32)
-        dequant_slot(rowp, a.tok_dtype, sl, xcopy);
-      consumer_sync();
-      const int e0 = (int)((int64_t)a.E * blockIdx.x / gridDim.x), e1 = (int)((int64_t)a.E * (blockIdx.x + 1) / gridDim.x);
-      for (int e = e0 + threadIdx.x; e < e1; e += kGemvConsumerWarps * 32) ll_store(a.xll + e, xcopy[e], a.tag0);
-    } else {
-      for (int64_t sl = (int64_t)blockIdx.x * 512 + threadIdx.x; sl < slots; sl += (int64_t)gridDim.x * 512)
-        dequant_slot(rowp, a.tok_dtype, sl, x);
-    }
+    for (int64_t sl = threadIdx.x; sl < slots; sl += kGemvConsumerWarps * 32) dequant_slot(rowp, a.tok_dtype, sl, xcopy);
+    consumer_sync();
+    const int e0 = (int)((int64_t)a.E * blockIdx.x / gridDim.x), e1 = (int)((int64_t)a.E * (blockIdx.x + 1) / gridDim.x);
+    for (int e = e0 + threadIdx.x; e < e1; e += kGemvConsumerWarps * 32) ll_store(a.xll + e, xcopy[e], a.tag0);
   }
-  grid_sync(bar, a.lbase, nbar, okp, false, ll);
+  grid_sync(bar, a.lbase, nbar, okp, false, true);
 
   const int nz = a.pos / kAttnTile + 1;  // key tiles of this step
   const int tpg = attn_group_tiles(nz, a.KV, (int)gridDim.x), ng = (nz + tpg - 1) / tpg;
@@ -1220,24 +1213,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       for (int it = blockIdx.x; it < a.KV * ng; it += gridDim.x)
         attn_item<G>(a, Ly, it / ng, it % ng, ng, tpg, nz, T, &attn_bar[0], attn_uses, &attn_last[0], l, okp);
       B2Q_TRACE(tslot + 2);
-      grid_sync(bar, a.lbase, nbar, okp, false, ll);  // the O projection reads this rank's heads
+      grid_sync(bar, a.lbase, nbar, okp, false, true);  // the O projection reads this rank's heads
       continue;
     }
     const CtaPhase& ph = tab[head ? 4 * a.n_layers : 4 * l + (k == 0 ? 0 : k - 1)];
-    // residual buffers under tensor parallelism: the update after O reads
-    // xg[rank] and writes xalt, the update after down reads xalt and writes
-    // xg[rank]; one GPU adds into x in the epilogues instead
-    const bool tpk = a.tp > 1;
-    const bool after_down = tpk && (head || (k == 0 && l > 0));
-    const bool after_o = tpk && k == 3;
     if (ph.gb < ph.ge) {
-      const bool proj = k == 2 || k == 4;  // O / down: partial sums under tensor parallelism
-      const bool add = proj && !tpk;
+      const bool add = k == 2 || k == 4;  // O / down: the residual update
       const int row0 = ph.gb * 8, nrows = min(ph.ge * 8, ph.n) - row0;
       const int rows = (ph.ge - ph.gb) * 8;
       // global row of local row 0 (head: vocabulary rows of this rank)
       const int grow0 = row0 + (head ? a.v_off : 0);
-      // residual rows of this CTA (one GPU, tagged): copied (L2 -> shared,
+      // residual rows of this CTA (tagged): copied (L2 -> shared,
       // asynchronously) behind the accumulators while the input is staged;
       // the epilogue checks each tag (and polls x for it if the copy was
       // early, which only a CTA that staged no input of the previous phase
@@ -1253,25 +1239,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
       if (k == 2) {
         const int kp_a = round_up_int(a.H * kHeadDim, 256);
         q = smem_xq(xs, kp_a);
-        if (ll)
-          stage_plain_ll(a.attnll, a.H * kHeadDim, q, reinterpret_cast<float*>(xs + xq_smem_bytes(kp_a)),
-                         a.tag0 + (uint32_t)(5 * l + 2), okp);
-        else
-          stage_plain(a.attng[a.rank], a.H * kHeadDim, q);
+        stage_plain_ll(a.attnll, a.H * kHeadDim, q, reinterpret_cast<float*>(xs + xq_smem_bytes(kp_a)),
+                       a.tag0 + (uint32_t)(5 * l + 2), okp);
       } else if (k == 4) {
         q = smem_xq(xs, round_up_int(a.Fl, 256));
         stage_plain(a.hg[a.rank], a.Fl, q);
       } else {
         q = smem_xq(xs, kp_e);
         const float* nw = head ? a.out_norm : (k == 0 ? a.layers[l].attn_norm : a.layers[l].ffn_norm);
-        if (after_down)
-          stage_rmsnorm(a.xalt, nw, a.E, a.eps, q, xcopy, red, l, k == 0 ? 0 : 4,
-                        a.partg[a.rank] + (size_t)a.tp * a.E, a.tp, head ? nullptr : x);
-        else if (after_o)
-          stage_rmsnorm(x, nw, a.E, a.eps, q, xcopy, red, l, 4, a.partg[a.rank], a.tp, a.xalt);
-        else
-          stage_rmsnorm(x, nw, a.E, a.eps, q, xcopy, red, l, k == 0 ? 0 : 4, nullptr, 0, nullptr,
-                        ll ? a.xll : nullptr, a.tag0 + (uint32_t)(5 * l + (k == 0 ? 0 : 3)), okp);
+        stage_rmsnorm(a.xll, nw, a.E, a.eps, q, xcopy, red, l, k == 0 ? 0 : 4,
+                      a.tag0 + (uint32_t)(5 * l + (k == 0 ? 0 : 3)), okp);
       }
       B2Q_TRACE(tslot + 1);
       B2Q_FTRACE(l, 21 + k);
@@ -1282,22 +1259,43 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
         asm volatile("cp.async.wait_all;" ::: "memory");
         consumer_sync();
       }
-      if (ok) {
+      if (ok && add && a.tp > 1) {
+        // x + p_0 + p_1 + ... (rank order), tagged for the next phase.  v is
+        // this rank's partial sum of a row (its columns of attn_output /
+        // ffn_down); it goes, tagged, into every rank's slot for this rank
+        // over NVLink, and the row's other partials arrive in this rank's
+        // slots the same way.  Three passes, the partials gathered through
+        // shared memory behind the accumulators and residual rows.
+        const uint32_t tp_tag = a.tag0 + (uint32_t)(5 * l + (k == 2 ? 2 : 4));
+        const size_t set = (size_t)(k == 2 ? 0 : 1) * a.tp;
+        float* pv = racc + 4 * rows;  // [tp][rows]
+        for (int r = threadIdx.x; r < nrows; r += kGemvConsumerWarps * 32) {
+          const float v = dec_racc(racc, rows, 1, r, 0);
+          for (int p = 0; p < a.tp; ++p) ll_store_sys(a.partll[p] + (set + a.rank) * a.E + grow0 + r, v, tp_tag);
+          pv[a.rank * rows + r] = v;
+        }
+        for (int i = threadIdx.x; i < a.tp * nrows; i += kGemvConsumerWarps * 32) {
+          const int p = i / nrows, r = i - p * nrows;
+          if (p == a.rank) continue;
+          const unsigned long long* w = a.partll[a.rank] + (set + p) * a.E + grow0 + r;
+          pv[p * rows + r] = ll_value_sys(w, ld_relaxed_sys_u64(w), tp_tag, okp);
+        }
+        consumer_sync();
+        for (int r = threadIdx.x; r < nrows; r += kGemvConsumerWarps * 32) {
+          float sum = ll_value(a.xll + grow0 + r, resid[r], a.tag0 + (uint32_t)(5 * l + (k == 2 ? 0 : 3)), okp);
+          for (int p = 0; p < a.tp; ++p) sum += pv[p * rows + r];
+          ll_store(a.xll + grow0 + r, sum, a.tag0 + (uint32_t)(k == 2 ? 5 * l + 3 : 5 * (l + 1)));
+        }
+      } else if (ok) {
         const int nw = pair ? 2 : 1;
         for (int r = threadIdx.x; r < nrows; r += kGemvConsumerWarps * 32) {
           const float v = dec_racc(racc, rows, nw, r, 0);
           if (k == 0 && !head) {  // q/k/v: this rank's heads, local
-            if (ll) ll_store(a.qkvll + ph.ycol + row0 + r, v, a.tag0 + (uint32_t)(5 * l + 1));
-            else a.qkv[ph.ycol + row0 + r] = v;
+            ll_store(a.qkvll + ph.ycol + row0 + r, v, a.tag0 + (uint32_t)(5 * l + 1));
             continue;
           }
           if (pair) {  // SwiGLU rows of this rank, local
             a.hg[a.rank][row0 + r] = silu_f(v) * dec_racc(racc, rows, nw, r, 1);
-            continue;
-          }
-          if (proj && tpk) {  // partial sums of every row, into every rank's slot for this rank
-            const size_t o = (size_t)((k == 2 ? 0 : 1) * a.tp + a.rank) * a.E + row0 + r;
-            for (int p = 0; p < a.tp; ++p) a.partg[p][o] = v;
             continue;
           }
           if (add) {  // one GPU: x += v, tagged for the next phase (gate/up, or the next layer's QKV)
@@ -1305,9 +1303,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
             ll_store(a.xll + grow0 + r, xr + v, a.tag0 + (uint32_t)(k == 2 ? 5 * l + 3 : 5 * (l + 1)));
             continue;
           }
-          float* const* yg = head ? a.logitsg : a.xg;
-          for (int p = 0; p < a.tp; ++p) yg[p][grow0 + r] = v;
-          if (head && v > best) { best = v; idx = grow0 + r; }
+          // the head: this rank's vocabulary slice into every rank's logits
+          for (int p = 0; p < a.tp; ++p) a.logitsg[p][grow0 + r] = v;
+          if (v > best) { best = v; idx = grow0 + r; }
         }
       }
       B2Q_TRACE(tslot + 2);
@@ -1321,11 +1319,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
 #endif
     }
     if (head) break;
-    // all ranks meet after the K-split projections (O, down); the other
-    // phases only need this rank's CTAs
-    // (one GPU: gates in front of tagged data, except h after gate/up)
-    if (k == 2 || k == 4) xgrid_sync(a, bar, nbar, nxbar, okp, true);
-    else grid_sync(bar, a.lbase, nbar, okp, false, ll && k != 3);
+    // gates in front of tagged data (relaxed), except h after gate/up
+    grid_sync(bar, a.lbase, nbar, okp, false, k != 3);
   }
   warp_argmax(best, idx);
   if (lane == 0) { s_bv[warp] = best; s_bi[warp] = idx; }

@@ -423,6 +423,12 @@ static cudaError_t rearm_decode(b2q_model* M) {
                                             M->c.n_vocab, M->c.tp_size, M->eng->num_sms);
   if (err == cudaSuccess)
     err = cudaMemsetAsync(static_cast<uint8_t*>(M->dec_xblock) + xl.bar, 0, 8 * b2q::kMaxTp, M->st);
+  // every tagged word back to tag 0 (never a live tag): the tags of the next
+  // launches restart from the launch sequence, on every rank alike
+  if (err == cudaSuccess) err = cudaMemsetAsync(M->dec_ll, 0, sizeof(unsigned long long) * M->dec_ll_words, M->st);
+  if (err == cudaSuccess)
+    err = cudaMemsetAsync(static_cast<uint8_t*>(M->dec_xblock) + xl.part, 0,
+                          sizeof(unsigned long long) * 2 * (size_t)M->c.tp_size * M->c.n_embd, M->st);
   if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
   M->dec_launches = 0;
   return err;

@@ -78,8 +78,8 @@ struct b2q_model {
   const float* last_logits = nullptr;       // where the last forward left its logits
   b2q::DecSync* dec_sync = nullptr;
   unsigned int* dec_attn_cnt = nullptr;      // [n_layers][KV_loc] attention split arrivals
-  unsigned long long* dec_ll = nullptr;      // one GPU: tagged x | q|k|v | attention output
-  uint64_t dec_tags = 0;                     // tagged hand-offs issued (never reset: tags stay unique)
+  unsigned long long* dec_ll = nullptr;      // tagged x | q|k|v | attention output
+  size_t dec_ll_words = 0;
   b2q::DecodeArgs dec{};
   size_t dec_smem = 0;
   int dec_G = 0;
@@ -529,20 +529,15 @@ static size_t round128(size_t v) { return (v + 127) / 128 * 128; }
 // attng, hg, logitsg, candg, xbarg): one allocation, so that one IPC handle
 // maps it into the peers.
 struct XBlock {
-  size_t x, xalt, part, attn, h, logits, cand, bar, total;
+  size_t part, h, logits, cand, bar, total;
 };
 static XBlock xblock_layout(int E, int Hhd, int F, int V, int tp, int grid) {
+  (void)Hhd;
   auto al = [](size_t v) { return (v + 255) / 256 * 256; };
   XBlock b;
   size_t o = 0;
-  b.x = o;
-  o += al((size_t)E * 4);
-  b.xalt = o;
-  o += al((size_t)E * 4);
-  b.part = o;  // [2][tp][E] partial O / down sums from every rank
-  o += al((size_t)2 * tp * E * 4);
-  b.attn = o;
-  o += al((size_t)Hhd * 4);
+  b.part = o;  // [2][tp][E] tagged partial O / down sums from every rank (8 bytes each)
+  o += al((size_t)2 * tp * E * 8);
   b.h = o;
   o += al((size_t)F * 4);
   b.logits = o;
@@ -556,8 +551,8 @@ static XBlock xblock_layout(int E, int Hhd, int F, int V, int tp, int grid) {
 }
 
 // Builds the persistent decode plan.  Leaves dec_on false (single-token
-// steps then use the captured graph) when the model does not fit it:
-// tensor parallelism, an unsupported head grouping, or too little shared
+// steps then use the captured graph) when the model does not fit it: more
+// ranks than kMaxTp, an unsupported head grouping, or too little shared
 // memory for two pipeline stages.
 static cudaError_t setup_decode(b2q_model* M) {
   const b2q_model_config& c = M->c;
@@ -632,8 +627,9 @@ static cudaError_t setup_decode(b2q_model* M) {
       tab[(size_t)b * nph + p] = r;
       // accumulators [2][nw][rows]; O and down also keep their residual rows
       const bool add = p < 4 * c.n_layers && (p % 4 == kPhO || p % 4 == kPhDown);
-      // (the residual rows are tagged 8-byte words)
-      const size_t per_row = phases[(size_t)p]->pair ? 4 : add ? 4 : 2;
+      // (the residual rows are tagged 8-byte words; under tensor parallelism
+      // every rank's partial of each row follows them)
+      const size_t per_row = phases[(size_t)p]->pair ? 4 : add ? 4 + (size_t)P : 2;
       racc = std::max(racc, per_row * (r.ge - r.gb) * 8 * sizeof(float));
     }
   racc = round128(racc);
@@ -672,10 +668,11 @@ static cudaError_t setup_decode(b2q_model* M) {
     err = cudaMemcpy(M->dec_tab, tab.data(), tab.size() * sizeof(CtaPhase), cudaMemcpyHostToDevice);
   if (err == cudaSuccess) err = dalloc(&M->dec_sync, 1);
   if (err == cudaSuccess) err = dalloc(&M->dec_attn_cnt, (size_t)c.n_layers * KV);
-  // tagged vectors (one GPU): x (rounded up to even: the residual copy reads
-  // pairs), q|k|v, attention output
+  // tagged vectors: x (rounded up to even: the residual copy reads pairs),
+  // q|k|v and the attention output of this rank's heads
   const size_t ll_x = (size_t)round_up_int(c.n_embd, 2), ll_qkv = (size_t)(H + 2 * KV) * hd, ll_attn = (size_t)H * hd;
-  if (err == cudaSuccess && P == 1) err = dalloc(&M->dec_ll, ll_x + ll_qkv + ll_attn);
+  if (err == cudaSuccess) err = dalloc(&M->dec_ll, ll_x + ll_qkv + ll_attn);
+  M->dec_ll_words = ll_x + ll_qkv + ll_attn;
   const XBlock xl = xblock_layout(c.n_embd, c.n_heads * hd, c.n_ff, c.n_vocab, P, grid);
   if (err == cudaSuccess) err = dalloc(reinterpret_cast<uint8_t**>(&M->dec_xblock), xl.total);
   if (err != cudaSuccess) return err;
@@ -715,27 +712,21 @@ static cudaError_t setup_decode(b2q_model* M) {
   a.tok_row_bytes = M->tok_row_bytes;
   a.rope_cos = M->rope_cos;
   a.rope_sin = M->rope_sin;
-  a.qkv = M->qkv;
   a.part = M->part;
   a.nsplit = M->nsplit;
   a.sync = M->dec_sync;
   a.attn_cnt = M->dec_attn_cnt;
-  if (P == 1) {
-    a.xll = M->dec_ll;
-    a.qkvll = M->dec_ll + ll_x;
-    a.attnll = M->dec_ll + ll_x + ll_qkv;
-  }
+  a.xll = M->dec_ll;
+  a.qkvll = M->dec_ll + ll_x;
+  a.attnll = M->dec_ll + ll_x + ll_qkv;
   a.argmax = M->argmax;
   a.tp = P;
   a.rank = rk;
   a.Fl = M->F_loc;
   a.v_off = rk * M->V_loc;
-  a.xalt = reinterpret_cast<float*>(static_cast<uint8_t*>(M->dec_xblock) + xl.xalt);
   for (int p = 0; p < P; ++p) {
     uint8_t* base = static_cast<uint8_t*>(M->dec_peer[p]);
-    a.xg[p] = reinterpret_cast<float*>(base + xl.x);
-    a.partg[p] = reinterpret_cast<float*>(base + xl.part);
-    a.attng[p] = reinterpret_cast<float*>(base + xl.attn);
+    a.partll[p] = reinterpret_cast<unsigned long long*>(base + xl.part);
     a.hg[p] = reinterpret_cast<float*>(base + xl.h);
     a.logitsg[p] = reinterpret_cast<float*>(base + xl.logits);
     a.candg[p] = reinterpret_cast<int2*>(base + xl.cand);
@@ -758,16 +749,16 @@ static cudaError_t launch_decode(b2q_model* M, const uint32_t* tok, int pos, uin
   a.token = tok;
   a.pos = pos;
   a.argmax2 = argmax2;
-  // every earlier launch passed 5L + 2 grid barriers (3L + 1 of them local
-  // only, 2L + 1 as the first level of an all-rank barrier) and 2L + 1
-  // all-rank epochs
+  // every earlier launch passed 5L + 2 grid barriers (the last one the
+  // first level of the head's all-rank barrier) and one all-rank epoch
   const unsigned long long seq = M->dec_launches++, grid = (unsigned long long)M->eng->num_sms;
-  // tags of this launch: 5 per layer plus the head's input (wrap-around is
-  // harmless: every launch rewrites every tagged element)
-  a.tag0 = (uint32_t)(M->dec_tags + 1);
-  M->dec_tags += 5ull * a.n_layers + 5ull;
+  // tags of this launch: 5 per layer plus the head's input, counted from
+  // the launch sequence, so the ranks of a tensor-parallel model agree on
+  // them; re-arming clears every tagged word and restarts the sequence
+  // (wrap-around is harmless: every launch rewrites every tagged element)
+  a.tag0 = (uint32_t)(1ull + seq * (5ull * a.n_layers + 5ull));
   a.lbase = seq * (5ull * a.n_layers + 2ull) * grid;
-  a.xepoch = seq * (2ull * a.n_layers + 1ull);
+  a.xepoch = seq;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M->eng->num_sms);
   cfg.blockDim = dim3(kGemvThreads);

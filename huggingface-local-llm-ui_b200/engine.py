@@ -180,12 +180,13 @@ class CudaEngine:
     def dequantize_dev(self, raw_ptr: int, dtype: int, n_elems: int, out_ptr: int, stream: int = 0) -> None:
         check(lib().b2q_dequantize_dev(self._h, raw_ptr, dtype, n_elems, out_ptr, stream or None))
 
-    def time_gemv(self, bufs, x_ptr: int, k: int, reps: int, stream: int = 0) -> float:
-        """Average device milliseconds of one GEMV launch, rotating `bufs`."""
+    def time_gemv(self, bufs, x_ptr: int, k: int, reps: int, stream: int = 0, chained: bool = False) -> float:
+        """Average device milliseconds of one GEMV launch, rotating `bufs`;
+        chained: each launch a programmatic dependent launch of the last."""
         cnt = len(bufs)
         ws = (C.c_void_p * cnt)(*[b.handle.value for b in bufs])
         ms = C.c_float()
-        check(lib().b2q_time_gemv(self._h, ws, cnt, x_ptr, k, reps, stream or None, C.byref(ms)))
+        check(lib().b2q_time_gemv(self._h, ws, cnt, x_ptr, k, reps, stream or None, C.byref(ms), int(chained)))
         return float(ms.value)
 
     def kernel_launches(self) -> int:

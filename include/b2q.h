@@ -395,9 +395,13 @@ b2q_status b2q_model_destroy(b2q_model* m);
  * launch the GEMV of each of the `count` weights (same k) `reps` times in
  * turn on `stream`, writing y to scratch, and return the average device
  * time of one GEMV launch in *avg_ms (CUDA events on `stream`).  Rotating
- * through weights that together exceed the L2 cache times HBM streaming. */
+ * through weights that together exceed the L2 cache times HBM streaming.
+ * chained != 0: each launch is a programmatic dependent launch of the
+ * previous one, as the per-kernel decode path chains its GEMVs, so a
+ * launch's weight stream starts while the previous launch drains; 0: plain
+ * back-to-back launches (each launch's ring fill exposed). */
 b2q_status b2q_time_gemv(b2q_engine* eng, const b2q_weight* const* ws, int count,
-                         const float* x_dev, int k, int reps, void* stream, float* avg_ms);
+                         const float* x_dev, int k, int reps, void* stream, float* avg_ms, int chained);
 
 /* Launch statistics: number of library kernels launched so far on this
  * engine (graph replays count every kernel node). */
