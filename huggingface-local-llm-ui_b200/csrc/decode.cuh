@@ -158,6 +158,7 @@ struct DecodeArgs {
   // counter and the epochs only grow)
   unsigned long long lbase, xepoch;
   // shared memory: [ring cap][staging stage_bytes][accumulators racc_bytes][phase table]
+  int attn_dbuf;  // the staging + accumulator regions hold a second K/V tile buffer
   int cap;
   int stage_bytes;
   int racc_bytes;
@@ -882,8 +883,8 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 template <int G>
 __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& Ly, int g, int j, int ng, int tpg,
-                                          int nz, AttnTile<G>& T, uint64_t* bar, int& uses, int* s_last, int tl,
-                                          volatile int* s_ok) {
+                                          int nz, AttnTile<G>& T, __half* kb2, uint64_t* bar, int& uses,
+                                          uint64_t* bar2, int& uses2, int* s_last, int tl, volatile int* s_ok) {
   constexpr int HD = kHeadDim, HALF = kHeadDim / 2;
   constexpr int R = (G * HD + kAttnThreads - 1) / kAttnThreads;
   const int gt = threadIdx.x;  // 0..511
@@ -891,18 +892,26 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
   const int H = a.H, KV = a.KV;
   const int z0 = j * tpg, z1 = min(nz, z0 + tpg);
   const bool last = z1 == nz;  // this group holds the tile with the current token
-  // K/V rows of tile z by bulk copy; in the tile holding the current token
-  // that token's row comes from registers instead
-  auto load = [&](int z) {
+  // K/V rows of tile z by bulk copy into buffer b (0: T.k / T.v, 1: the
+  // second buffer kb2, when the region holds one: the group's tiles are then
+  // double-buffered, tile z + 1 in flight while tile z is computed); in the
+  // tile holding the current token that token's row comes from registers
+  // (compiled in for eight query heads per KV head only, the widths whose
+  // staging region holds the second buffer; the other instances keep their
+  // registers)
+  const bool dbuf = G >= 8 && kb2 != nullptr;
+  auto kbuf = [&](int b) { return b ? kb2 : T.k; };
+  auto vbuf = [&](int b) { return b ? kb2 + kAttnTile * HD : T.v; };
+  auto load = [&](int z, int b) {
     const int nv = min(kAttnTile, pos + 1 - z * kAttnTile);
     const int nload = z == nz - 1 ? nv - 1 : nv;
     if (gt == 0 && nload > 0) {
       fence_proxy_async_smem();  // earlier generic accesses to this region come first
-      attn_tile_load(T, Ly.kc, Ly.vc, g, cap, z * kAttnTile, nload, bar);
+      attn_rows_load(kbuf(b), vbuf(b), Ly.kc, Ly.vc, g, cap, z * kAttnTile, nload, b ? bar2 : bar);
     }
     return nload;
   };
-  int nload = load(z0);
+  int nl[2] = {load(z0, 0), 0};
   const int p_rope = pos < 8191 ? pos : 8191;
   const float* cs = a.rope_cos + (int64_t)p_rope * HALF;
   const float* sn = a.rope_sin + (int64_t)p_rope * HALF;
@@ -993,22 +1002,24 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
   run.init();
   for (int z = z0; z < z1; ++z) {
     const int nv = min(kAttnTile, pos + 1 - z * kAttnTile);
+    const int b = dbuf ? (z - z0) & 1 : 0;
     if (z > z0) {
       consumer_sync();  // the previous tile's shared-memory reads are done
-      nload = load(z);
+      if (!dbuf) nl[0] = load(z, 0);
     }
+    if (dbuf && z + 1 < z1) nl[b ^ 1] = load(z + 1, b ^ 1);  // into the buffer tile z - 1 has left
     if (z == nz - 1 && z > z0) {  // T.kcur / T.vcur were written before the sync above
       if (gt < HD) {
-        T.k[(nv - 1) * HD + gt] = T.kcur[gt];
-        T.v[(nv - 1) * HD + gt] = T.vcur[gt];
+        kbuf(b)[(nv - 1) * HD + gt] = T.kcur[gt];
+        vbuf(b)[(nv - 1) * HD + gt] = T.vcur[gt];
       }
     }
-    if (nload > 0) {
-      mbar_wait_bounded(bar, (uint32_t)(uses & 1));  // a timeout is recorded in the device error word
-      ++uses;
+    if (nl[b] > 0) {  // a timeout is recorded in the device error word
+      if (b) mbar_wait_bounded(bar2, (uint32_t)(uses2++ & 1));
+      else mbar_wait_bounded(bar, (uint32_t)(uses++ & 1));
     }
     consumer_sync();
-    attn_tile_compute_emit<G>(T, nv, a.scale, [] { consumer_sync(); },
+    attn_tile_compute_emit<G>(T, kbuf(b), vbuf(b), nv, a.scale, [] { consumer_sync(); },
                               [&](int r, int, int, float mt, float lt, float ot) { run.fold(r, mt, lt, ot); });
   }
   B2Q_FTRACE(tl, 11);
@@ -1191,7 +1202,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
 
   const int nz = a.pos / kAttnTile + 1;  // key tiles of this step
   const int tpg = attn_group_tiles(nz, a.KV, (int)gridDim.x), ng = (nz + tpg - 1) / tpg;
-  int attn_uses = 0;  // completed phases of the attention mbarrier
+  int attn_uses = 0, attn_uses2 = 0;  // completed phases of the two attention mbarriers
   float best = -INFINITY;
   int idx = 0x7fffffff;
   // steps: per layer QKV, attention, O, gate/up, down; then the head
@@ -1210,8 +1221,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
     if (k == 1) {  // RoPE, KV append, attention
       const DecLayer& Ly = a.layers[l];
       AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(xs);
+      __half* kb2 = a.attn_dbuf ? reinterpret_cast<__half*>(xs + (sizeof(AttnTile<G>) + 127) / 128 * 128) : nullptr;
       for (int it = blockIdx.x; it < a.KV * ng; it += gridDim.x)
-        attn_item<G>(a, Ly, it / ng, it % ng, ng, tpg, nz, T, &attn_bar[0], attn_uses, &attn_last[0], l, okp);
+        attn_item<G>(a, Ly, it / ng, it % ng, ng, tpg, nz, T, kb2, &attn_bar[0], attn_uses, &attn_bar[1],
+                     attn_uses2, &attn_last[0], l, okp);
       B2Q_TRACE(tslot + 2);
       grid_sync(bar, a.lbase, nbar, okp, false, true);  // the O projection reads this rank's heads
       continue;

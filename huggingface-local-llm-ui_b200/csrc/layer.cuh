@@ -126,15 +126,20 @@ struct AttnTile {
   __half vcur[kHeadDim];           // kernel: copied into the tile that holds the token)
 };
 
-// Issue the bulk copies of K/V rows [t0, t0 + rows) of KV head g into the
-// tile (one thread); completes on `bar` (expect_tx included).
+// Issue the bulk copies of K/V rows [t0, t0 + rows) of KV head g into kb /
+// vb (shared memory; one thread); completes on `bar` (expect_tx included).
+__device__ __forceinline__ void attn_rows_load(__half* kb, __half* vb, const __half* kc, const __half* vc, int g,
+                                               int cap, int t0, int rows, uint64_t* bar) {
+  const uint32_t bytes = (uint32_t)rows * kHeadDim * 2;
+  mbar_arrive_expect_tx(bar, 2 * bytes);
+  bulk_g2s(kb, kc + ((int64_t)g * cap + t0) * kHeadDim, bytes, bar);
+  bulk_g2s(vb, vc + ((int64_t)g * cap + t0) * kHeadDim, bytes, bar);
+}
+
 template <int G>
 __device__ __forceinline__ void attn_tile_load(AttnTile<G>& T, const __half* kc, const __half* vc, int g, int cap,
                                                int t0, int rows, uint64_t* bar) {
-  const uint32_t bytes = (uint32_t)rows * kHeadDim * 2;
-  mbar_arrive_expect_tx(bar, 2 * bytes);
-  bulk_g2s(T.k, kc + ((int64_t)g * cap + t0) * kHeadDim, bytes, bar);
-  bulk_g2s(T.v, vc + ((int64_t)g * cap + t0) * kHeadDim, bytes, bar);
+  attn_rows_load(T.k, T.v, kc, vc, g, cap, t0, rows, bar);
 }
 
 // Key tiles per attention group.  A query's nz tiles of kAttnTile keys are
@@ -172,11 +177,13 @@ struct AttnRun {
 };
 
 // The softmax partial of one tile on kAttnThreads threads; T.q and the first
-// `nv` rows of T.k / T.v are in place.  `sync` is the item's barrier.  For
+// `nv` rows of kb / vb (T.k / T.v, or a second tile buffer; vb must follow
+// kb directly) are in place.  `sync` is the item's barrier.  For
 // every (head, dim) element i = h * 128 + d of the G heads of head group g a
 // thread owns (i = tid + kAttnThreads * r), calls emit(r, h, d, max, sum, O).
 template <int G, class Sync, class Emit>
-__device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, int nv, float scale, Sync sync, Emit emit) {
+__device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, const __half* kb, const __half* vb, int nv,
+                                                       float scale, Sync sync, Emit emit) {
   constexpr int HD = kHeadDim;
   const int tid = threadIdx.x & (kAttnThreads - 1), lane = threadIdx.x & 31, w = tid >> 5;
   // scores: thread (token t, eighth e) sums dims 8e..8e+7 and 64+8e..64+8e+7,
@@ -190,7 +197,7 @@ __device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, int nv, f
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const int d0 = hf * 64 + 8 * e;
-        const uint4 pk = *reinterpret_cast<const uint4*>(T.k + t * HD + d0);
+        const uint4 pk = *reinterpret_cast<const uint4*>(kb + t * HD + d0);
         const __half2* h2 = reinterpret_cast<const __half2*>(&pk);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -238,7 +245,7 @@ __device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, int nv, f
   for (int j = 0; j < 8; ++j) {
     const int t = 8 * tg + j;
     if (t >= nv) break;
-    const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(T.v + t * HD + 2 * dp));
+    const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(vb + t * HD + 2 * dp));
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       const float ph = T.sp[h][t];
@@ -247,7 +254,7 @@ __device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, int nv, f
     }
   }
   sync();  // K and V are no longer read
-  float* o8 = reinterpret_cast<float*>(T.k);  // [8][G][HD] (spans K and V)
+  float* o8 = reinterpret_cast<float*>(const_cast<__half*>(kb));  // [8][G][HD] (spans K and V)
 #pragma unroll
   for (int h = 0; h < G; ++h)
     *reinterpret_cast<float2*>(o8 + (tg * G + h) * HD + 2 * dp) = make_float2(o[h][0], o[h][1]);
@@ -322,7 +329,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
       attn_tile_load(T, kc, vc, g, cap, t_begin, nv, &bar);
     }
     mbar_wait_bounded(&bar, (uint32_t)((z - z0) & 1));  // a timeout is recorded in the device error word
-    attn_tile_compute_emit<G>(T, nv, scale, [] { __syncthreads(); },
+    attn_tile_compute_emit<G>(T, T.k, T.v, nv, scale, [] { __syncthreads(); },
                               [&](int r, int, int, float mt, float lt, float ot) { run.fold(r, mt, lt, ot); });
   }
 #pragma unroll

@@ -736,6 +736,10 @@ static cudaError_t setup_decode(b2q_model* M) {
   a.cap = (int)cap;
   a.stage_bytes = (int)stage;
   a.racc_bytes = (int)racc;
+  // a second K/V tile buffer (long contexts: the tiles of an attention group
+  // double-buffered) where the staging and accumulator regions already hold
+  // it; never grown for it (the ring would shrink)
+  a.attn_dbuf = stage + racc >= round128(attn_one) + (size_t)2 * kAttnTile * kHeadDim * sizeof(__half) ? 1 : 0;
   M->dec_smem = smem;
   M->dec_G = G;
   M->dec_all = all;

@@ -125,8 +125,11 @@ inline b2q_status tp_unique_id(unsigned char out[128]) {
 }
 
 inline void tp_destroy(TpComm& t) {
-  NcclApi& a = nccl();
   if (t.comm) {
+    // (NCCL is loaded only when a communicator exists: a one-GPU model must
+    // not pull libnccl into the process, whose copy would then shadow the
+    // one a later import of torch brings)
+    NcclApi& a = nccl();
     // non-blocking communicator: finalize (flushes pending work), wait, destroy
     if (a.comm_finalize && nccl_done(t.comm, a.comm_finalize(t.comm)) == ncclSuccess)
       a.comm_destroy(t.comm);
