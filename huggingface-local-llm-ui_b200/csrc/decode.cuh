@@ -979,8 +979,8 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
     const int w = gt + kAttnThreads * r;
     if (w < qn) {
       const int hh = w / HALF, jj = w % HALF;
-      T.q[hh][jj] = __fsub_rn(__fmul_rn(x0[r], c[r]), __fmul_rn(x1[r], sv[r]));
-      T.q[hh][HALF + jj] = __fadd_rn(__fmul_rn(x1[r], c[r]), __fmul_rn(x0[r], sv[r]));
+      attn_set_q(T, hh, jj, __fsub_rn(__fmul_rn(x0[r], c[r]), __fmul_rn(x1[r], sv[r])));
+      attn_set_q(T, hh, HALF + jj, __fadd_rn(__fmul_rn(x1[r], c[r]), __fmul_rn(x0[r], sv[r])));
     } else if (w < qn + HALF && w < nwork) {
       const int jj = w - qn;
       const __half y0 = __float2half_rn(__fsub_rn(__fmul_rn(x0[r], c[r]), __fmul_rn(x1[r], sv[r])));

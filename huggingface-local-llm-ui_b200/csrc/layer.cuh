@@ -115,16 +115,66 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int m, int H, int KV, in
 // ---------------------------------------------------------------------------
 constexpr int kAttnThreads = 512;
 
+// The two products of a tile, q K^T and P V, run on the warp-level tensor
+// cores (mma.sync m16n8k16, f16 operands, f32 accumulation).  The f16 K and
+// V rows of the cache enter exactly; the f32 queries and probabilities are
+// carried as two f16 parts each, hi = f16(v) toward zero and lo = f16(v -
+// hi), as rows h (hi) and G + h (lo) of the A operand (A rows 2G..15, G < 8,
+// repeat rows 0..2G-1 and their products are dropped), so one MMA gives both
+// halves of each product; their sum carries the f32 operand to ~2^-22
+// relative.  The probabilities enter scaled by 2^15 (out of the f16
+// subnormal range; the P*V sums are scaled back exactly).  Queries must stay
+// below the f16 maximum, 65504, in magnitude.
+constexpr int kQImgStride = kHeadDim + 8;   // halves per query image row (ldmatrix rows on distinct banks)
+constexpr int kSpStride = kAttnTile + 4;    // floats per score row
+constexpr float kPScale = 32768.0f;
+
 template <int G>
 struct AttnTile {
-  __half k[kAttnTile * kHeadDim];  // rows t_begin.. of the split; K and V are
-  __half v[kAttnTile * kHeadDim];  // reused for the P*V partial sums
-  float q[G][kHeadDim];            // rotated queries
-  float sp[G][kAttnTile];          // scores, then probabilities
-  float m[G], l[G];                // softmax max and sum per head
-  __half kcur[kHeadDim];           // the current token's rotated k and its v (persistent
-  __half vcur[kHeadDim];           // kernel: copied into the tile that holds the token)
+  __half k[kAttnTile * kHeadDim];  // rows t_begin.. of the split (then the P*V output)
+  __half v[kAttnTile * kHeadDim];
+  __half qimg[2 * G * kQImgStride];  // rotated queries: hi rows 0..G-1, lo rows G..2G-1
+  float sp[G][kSpStride];            // scores; then the probabilities' hi (bytes 0..127) and lo
+                                     // (bytes 128..255) f16 parts, over each head's own row
+  float m[G], l[G];                  // softmax max and sum per head
+  __half kcur[kHeadDim];             // the current token's rotated k and its v (persistent
+  __half vcur[kHeadDim];             // kernel: copied into the tile that holds the token)
 };
+
+__device__ __forceinline__ __half f16_hi(float v) { return __float2half_rz(v); }
+__device__ __forceinline__ __half f16_lo(float v, __half hi) { return __float2half_rn(v - __half2float(hi)); }
+
+template <int G>
+__device__ __forceinline__ void attn_set_q(AttnTile<G>& T, int h, int d, float v) {
+  const __half hi = f16_hi(v);
+  T.qimg[h * kQImgStride + d] = hi;
+  T.qimg[(G + h) * kQImgStride + d] = f16_lo(v, hi);
+}
+
+// Image row (head h + G * part, part 0 hi / 1 lo) behind A-operand row r
+// (0..15) of an m16n8k16 product
+template <int G>
+__device__ __forceinline__ int attn_arow(int r) { return G == 8 ? r : r % (2 * G); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t& r0, uint32_t& r1, const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t& r0, uint32_t& r1, const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(smem_u32(p)));
+}
+// d += a * b, m16n8k16, f16 x f16 -> f32
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 
 // Issue the bulk copies of K/V rows [t0, t0 + rows) of KV head g into kb /
 // vb (shared memory; one thread); completes on `bar` (expect_tx included).
@@ -176,9 +226,9 @@ struct AttnRun {
   }
 };
 
-// The softmax partial of one tile on kAttnThreads threads; T.q and the first
-// `nv` rows of kb / vb (T.k / T.v, or a second tile buffer; vb must follow
-// kb directly) are in place.  `sync` is the item's barrier.  For
+// The softmax partial of one tile on kAttnThreads threads; the query image
+// and the first `nv` rows of kb / vb (T.k / T.v, or a second tile buffer; vb
+// must follow kb directly) are in place.  `sync` is the item's barrier.  For
 // every (head, dim) element i = h * 128 + d of the G heads of head group g a
 // thread owns (i = tid + kAttnThreads * r), calls emit(r, h, d, max, sum, O).
 template <int G, class Sync, class Emit>
@@ -186,43 +236,38 @@ __device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, const __h
                                                        float scale, Sync sync, Emit emit) {
   constexpr int HD = kHeadDim;
   const int tid = threadIdx.x & (kAttnThreads - 1), lane = threadIdx.x & 31, w = tid >> 5;
-  // scores: thread (token t, eighth e) sums dims 8e..8e+7 and 64+8e..64+8e+7,
-  // then the 8 lanes of a token add their partials (fixed butterfly)
-  {
-    const int t = tid >> 3, e = tid & 7;
-    float acc[G];
+  const int g = lane >> 2, t = lane & 3, l16 = lane & 15;
+  // the A-operand row (as head and part) and column half an ldmatrix.x4 lane
+  // addresses; the head a lane's D row g holds and the sum of its two parts
+  const int ar = attn_arow<G>((lane & 7) + ((lane >> 3) & 1) * 8), acol = (lane >> 4) * 8;
+  auto parts = [&](float hi_or_g, float g8) {
+    return G == 8 ? hi_or_g + g8 : hi_or_g + __shfl_xor_sync(B2Q_FULL, hi_or_g, 4 * G);
+  };
+  if (w < 8) {
+    // scores: warp w takes keys 8w..8w+7 over the 128 dims (8 k16 slices)
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-    for (int h = 0; h < G; ++h) acc[h] = 0.0f;
-    if (t < nv) {
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int d0 = hf * 64 + 8 * e;
-        const uint4 pk = *reinterpret_cast<const uint4*>(kb + t * HD + d0);
-        const __half2* h2 = reinterpret_cast<const __half2*>(&pk);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 kf = __half22float2(h2[i]);
-#pragma unroll
-          for (int h = 0; h < G; ++h) {
-            acc[h] = fmaf(T.q[h][d0 + 2 * i], kf.x, acc[h]);
-            acc[h] = fmaf(T.q[h][d0 + 2 * i + 1], kf.y, acc[h]);
-          }
-        }
-      }
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      uint32_t a[4], b0, b1;
+      ldsm_x4(a, T.qimg + ar * kQImgStride + 16 * ks + acol);
+      ldsm_x2(b0, b1, kb + (8 * w + (l16 & 7)) * HD + 16 * ks + (l16 >> 3) * 8);
+      mma_16816(d, a, b0, b1);
     }
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      acc[h] += __shfl_xor_sync(B2Q_FULL, acc[h], 1);
-      acc[h] += __shfl_xor_sync(B2Q_FULL, acc[h], 2);
-      acc[h] += __shfl_xor_sync(B2Q_FULL, acc[h], 4);
+    const float s0 = parts(d[0], d[2]), s1 = parts(d[1], d[3]);
+    if (g < G) {
+      T.sp[g][8 * w + 2 * t] = s0;
+      T.sp[g][8 * w + 2 * t + 1] = s1;
     }
-    if (e == 0) {
-#pragma unroll
-      for (int h = 0; h < G; ++h) T.sp[h][t] = acc[h];
-    }
+  } else if (nv < kAttnTile) {
+    // V rows past the tile's end hold stale shared memory: zero them, so that
+    // a zero probability never meets an inf or NaN there
+    uint32_t* vz = reinterpret_cast<uint32_t*>(const_cast<__half*>(vb) + nv * HD);
+    for (int i = tid - 256; i < (kAttnTile - nv) * HD / 2; i += kAttnThreads - 256) vz[i] = 0u;
   }
   sync();
-  // softmax: warp h takes head h; lane holds tokens lane, lane + 32
+  // softmax: warp h takes head h; lane holds tokens lane, lane + 32.  The
+  // probability parts overwrite the head's score row after the warp's
+  // reductions, so every lane has read its scores by then.
   if (w < G) {
     const int h = w, t0 = lane, t1 = lane + 32;
     const float s0 = t0 < nv ? T.sp[h][t0] * scale : -INFINITY;
@@ -231,33 +276,34 @@ __device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, const __h
     const float p0 = t0 < nv ? expf(s0 - mx) : 0.0f;
     const float p1 = t1 < nv ? expf(s1 - mx) : 0.0f;
     const float sum = warp_sum(p0 + p1);
-    T.sp[h][t0] = p0;
-    T.sp[h][t1] = p1;
+    __half* pr = reinterpret_cast<__half*>(T.sp[h]);
+    const __half h0 = f16_hi(p0 * kPScale), h1 = f16_hi(p1 * kPScale);
+    pr[t0] = h0;
+    pr[t1] = h1;
+    pr[kAttnTile + t0] = f16_lo(p0 * kPScale, h0);
+    pr[kAttnTile + t1] = f16_lo(p1 * kPScale, h1);
     if (lane == 0) { T.m[h] = mx; T.l[h] = sum; }
   }
   sync();
-  // P * V: thread (dims 2dp, 2dp+1; token eighth tg = tokens 8tg..8tg+7)
-  const int dp = tid & 63, tg = tid >> 6;
-  float o[G][2];
+  // P * V: warp w takes dims 8w..8w+7 over the 64 keys (4 k16 slices); the
+  // output [G][HD] goes over the K rows, no longer read
+  float* o = reinterpret_cast<float*>(const_cast<__half*>(kb));
+  {
+    const __half* pa = reinterpret_cast<const __half*>(T.sp[ar % G]) + (ar / G) * kAttnTile + acol;
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-  for (int h = 0; h < G; ++h) o[h][0] = o[h][1] = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int t = 8 * tg + j;
-    if (t >= nv) break;
-    const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(vb + t * HD + 2 * dp));
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float ph = T.sp[h][t];
-      o[h][0] = fmaf(ph, vf.x, o[h][0]);
-      o[h][1] = fmaf(ph, vf.y, o[h][1]);
+    for (int ks = 0; ks < kAttnTile / 16; ++ks) {
+      uint32_t a[4], b0, b1;
+      ldsm_x4(a, pa + 16 * ks);
+      ldsm_x2_t(b0, b1, vb + (16 * ks + l16) * HD + 8 * w);
+      mma_16816(d, a, b0, b1);
+    }
+    const float o0 = parts(d[0], d[2]), o1 = parts(d[1], d[3]);
+    if (g < G) {
+      o[g * HD + 8 * w + 2 * t] = o0 * (1.0f / kPScale);
+      o[g * HD + 8 * w + 2 * t + 1] = o1 * (1.0f / kPScale);
     }
   }
-  sync();  // K and V are no longer read
-  float* o8 = reinterpret_cast<float*>(const_cast<__half*>(kb));  // [8][G][HD] (spans K and V)
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-    *reinterpret_cast<float2*>(o8 + (tg * G + h) * HD + 2 * dp) = make_float2(o[h][0], o[h][1]);
   sync();
   constexpr int R = (G * HD + kAttnThreads - 1) / kAttnThreads;
 #pragma unroll
@@ -265,10 +311,7 @@ __device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, const __h
     const int i = tid + kAttnThreads * r;
     if (i >= G * HD) break;
     const int h = i / HD, d = i % HD;
-    float O = o8[h * HD + d];
-#pragma unroll
-    for (int q = 1; q < 8; ++q) O += o8[(q * G + h) * HD + d];
-    emit(r, h, d, T.m[h], T.l[h], O);
+    emit(r, h, d, T.m[h], T.l[h], o[h * HD + d]);
   }
 }
 
@@ -318,7 +361,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
     attn_tile_load(T, kc, vc, g, cap, z0 * kAttnTile, min(kAttnTile, valid - z0 * kAttnTile), &bar);
   }
   const int width = (H + 2 * KV) * HD;
-  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) T.q[i / HD][i % HD] = qkv[(int64_t)s * width + g * G * HD + i];
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) attn_set_q(T, i / HD, i % HD, qkv[(int64_t)s * width + g * G * HD + i]);
   AttnRun<R> run;
   run.init();
   for (int z = z0; z < z1; ++z) {
