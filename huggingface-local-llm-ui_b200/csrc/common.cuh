@@ -8,7 +8,8 @@
 #define B2Q_FULL 0xffffffffu
 
 // Device error word: set by a kernel whose bounded wait gave up
-// (B2Q_ETIMEOUT = 5).  Read and cleared by b2q_check_device_error() and by
+// (B2Q_ETIMEOUT = 5), or by the persistent decode kernel when its shared
+// memory is not laid out as planned (B2Q_ECUDA = 3).  Read and cleared by b2q_check_device_error() and by
 // the blocking forward entry points.
 // libb2q is a single translation unit (b2q_api.cu includes the rest).
 __device__ int g_b2q_device_error = 0;
@@ -172,6 +173,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
           smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Tiled 2-D TMA copy of the box at element coordinates (x, y) of the tensor
+// map at `tmap` (global memory) into shared memory at dst; completes on `bar`.
+// x times the element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
 

@@ -73,6 +73,8 @@ struct DecLayer {
   const float* vb;
   __half* kc;       // f16 KV cache [KV][max_seq][128]
   __half* vc;
+  const void* tmk;  // TMA descriptors of kc and vc (global memory)
+  const void* tmv;
 };
 
 // Consumer view of one phase for one CTA (32 bytes; table [grid][phases]).
@@ -157,8 +159,10 @@ struct DecodeArgs {
   // this launch's grid-barrier counter base and all-rank epoch base (the
   // counter and the epochs only grow)
   unsigned long long lbase, xepoch;
-  // shared memory: [ring cap][staging stage_bytes][accumulators racc_bytes][phase table]
+  // shared memory: [ring cap][staging stage_bytes][accumulators racc_bytes][phase table];
+  // the staging region starts on a 1024-byte boundary
   int attn_dbuf;  // the staging + accumulator regions hold a second K/V tile buffer
+  int* probe;     // set-up only: receives the shared-memory address of the dynamic region, nothing else runs
   int cap;
   int stage_bytes;
   int racc_bytes;
@@ -892,13 +896,14 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
   const int H = a.H, KV = a.KV;
   const int z0 = j * tpg, z1 = min(nz, z0 + tpg);
   const bool last = z1 == nz;  // this group holds the tile with the current token
-  // K/V rows of tile z by bulk copy into buffer b (0: T.k / T.v, 1: the
-  // second buffer kb2, when the region holds one: the group's tiles are then
-  // double-buffered, tile z + 1 in flight while tile z is computed); in the
-  // tile holding the current token that token's row comes from registers
-  // (compiled in for eight query heads per KV head only, the widths whose
+  // K/V tile z by TMA into buffer b (0: T.k / T.v, 1: the second buffer
+  // kb2, when the region holds one: the group's tiles are then
+  // double-buffered, tile z + 1 in flight while tile z is computed).  The
+  // current token's row is copied in from T.kcur / T.vcur once its tile has
+  // landed; a tile with no other row is not loaded.  (Double buffering is
+  // compiled in for eight query heads per KV head only, the widths whose
   // staging region holds the second buffer; the other instances keep their
-  // registers)
+  // registers.)
   const bool dbuf = G >= 8 && kb2 != nullptr;
   auto kbuf = [&](int b) { return b ? kb2 : T.k; };
   auto vbuf = [&](int b) { return b ? kb2 + kAttnTile * HD : T.v; };
@@ -907,7 +912,7 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
     const int nload = z == nz - 1 ? nv - 1 : nv;
     if (gt == 0 && nload > 0) {
       fence_proxy_async_smem();  // earlier generic accesses to this region come first
-      attn_rows_load(kbuf(b), vbuf(b), Ly.kc, Ly.vc, g, cap, z * kAttnTile, nload, b ? bar2 : bar);
+      attn_rows_load(kbuf(b), vbuf(b), Ly.tmk, Ly.tmv, g * cap + z * kAttnTile, b ? bar2 : bar);
     }
     return nload;
   };
@@ -916,13 +921,14 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
   const float* cs = a.rope_cos + (int64_t)p_rope * HALF;
   const float* sn = a.rope_sin + (int64_t)p_rope * HALF;
   // work index w < G*64: one q pair; [G*64, G*64 + 64): a k pair of this
-  // token (last group); [G*64 + 64, G*64 + 192): a v value.  Up to two
-  // indices per thread, all loads issued first.
+  // token (last group); [G*64 + 64, G*64 + 192): a v value.  RW indices per
+  // thread (one up to four query heads per KV head), all loads issued first.
+  constexpr int RW = (G * HALF + HALF + HD + kAttnThreads - 1) / kAttnThreads;
   const int qn = G * HALF, nwork = qn + (last ? HALF + HD : 0);
-  float x0[2], x1[2], c[2], sv[2];
-  int o0[2], o1[2];  // offsets of the thread's inputs in q|k|v (-1: none)
+  float x0[RW], x1[RW], c[RW], sv[RW];
+  int o0[RW], o1[RW];  // offsets of the thread's inputs in q|k|v (-1: none)
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
+  for (int r = 0; r < RW; ++r) {
     const int w = gt + kAttnThreads * r;
     c[r] = sv[r] = 0.0f;
     o0[r] = o1[r] = -1;
@@ -944,14 +950,14 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
   }
   {  // tagged q|k|v
     const uint32_t tq = a.tag0 + (uint32_t)(5 * tl + 1);
-    unsigned long long u0[2], u1[2];
+    unsigned long long u0[RW], u1[RW];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
+    for (int r = 0; r < RW; ++r) {
       u0[r] = o0[r] >= 0 ? ld_relaxed_u64(a.qkvll + o0[r]) : 0ull;
       u1[r] = o1[r] >= 0 ? ld_relaxed_u64(a.qkvll + o1[r]) : 0ull;
     }
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
+    for (int r = 0; r < RW; ++r) {
       x0[r] = o0[r] >= 0 ? ll_value(a.qkvll + o0[r], u0[r], tq, s_ok) : 0.0f;
       x1[r] = o1[r] >= 0 ? ll_value(a.qkvll + o1[r], u1[r], tq, s_ok) : 0.0f;
     }
@@ -960,7 +966,7 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
   // (H + KV + g)*HD + j of q|k|v map to offset o - {0, H*HD, (H+KV)*HD} of
   // the layer's q, k, v bias vectors
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
+  for (int r = 0; r < RW; ++r) {
     if (o0[r] < 0) continue;
     const float* b = o0[r] < H * HD ? Ly.qb : o0[r] < (H + KV) * HD ? Ly.kb : Ly.vb;
     if (b == nullptr) continue;
@@ -969,13 +975,11 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
     if (o1[r] >= 0) x1[r] += b[bo + HALF];
   }
   // rotated q into the tile; this token's rotated k and its v into the cache
-  // and into the tile that holds the token: directly if that is the group's
-  // first tile, else through T.kcur / T.vcur (copied in the tile loop)
-  const int nv_last = pos + 1 - (nz - 1) * kAttnTile;  // rows of the token's tile
-  __half* const krow = z0 == nz - 1 ? T.k + (nv_last - 1) * HD : T.kcur;
-  __half* const vrow = z0 == nz - 1 ? T.v + (nv_last - 1) * HD : T.vcur;
+  // and into T.kcur / T.vcur (copied into its tile in the tile loop)
+  __half* const krow = T.kcur;
+  __half* const vrow = T.vcur;
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
+  for (int r = 0; r < RW; ++r) {
     const int w = gt + kAttnThreads * r;
     if (w < qn) {
       const int hh = w / HALF, jj = w % HALF;
@@ -1008,15 +1012,16 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
       if (!dbuf) nl[0] = load(z, 0);
     }
     if (dbuf && z + 1 < z1) nl[b ^ 1] = load(z + 1, b ^ 1);  // into the buffer tile z - 1 has left
-    if (z == nz - 1 && z > z0) {  // T.kcur / T.vcur were written before the sync above
-      if (gt < HD) {
-        kbuf(b)[(nv - 1) * HD + gt] = T.kcur[gt];
-        vbuf(b)[(nv - 1) * HD + gt] = T.vcur[gt];
-      }
-    }
     if (nl[b] > 0) {  // a timeout is recorded in the device error word
       if (b) mbar_wait_bounded(bar2, (uint32_t)(uses2++ & 1));
       else mbar_wait_bounded(bar, (uint32_t)(uses++ & 1));
+    }
+    if (z == nz - 1) {  // the current token's row, over what the copy brought
+      if (z == z0) consumer_sync();  // T.kcur / T.vcur written above
+      if (gt < HD) {
+        kbuf(b)[kv_off(nv - 1, gt)] = T.kcur[gt];
+        vbuf(b)[kv_off(nv - 1, gt)] = T.vcur[gt];
+      }
     }
     consumer_sync();
     attn_tile_compute_emit<G>(T, kbuf(b), vbuf(b), nv, a.scale, [] { consumer_sync(); },
@@ -1137,6 +1142,10 @@ __device__ __forceinline__ void warp_argmax(float& best, int& idx) {
 template <int G, bool kAllTypes>
 __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
+  if (a.probe != nullptr) {  // layout query
+    if (blockIdx.x == 0 && threadIdx.x == 0) *a.probe = (int)smem_u32(smem);
+    return;
+  }
   __shared__ uint64_t full_bar[kRingSlots], empty_bar[kRingSlots];
   __shared__ int ring_qs[kRingSlots], ring_qe[kRingSlots];
   __shared__ float red[32];
@@ -1153,6 +1162,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
   uint8_t* xs = smem + a.cap;
   float* racc = reinterpret_cast<float*>(xs + a.stage_bytes);
   CtaPhase* tab = reinterpret_cast<CtaPhase*>(xs + a.stage_bytes + a.racc_bytes);
+  if ((smem_u32(xs) & 1023u) != 0u) {  // the layout the host planned (never expected to differ)
+    if (threadIdx.x == 0) atomicExch(&g_b2q_device_error, 3);
+    return;  // every CTA alike, before any exchange
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRingSlots; ++i) {
@@ -1220,8 +1233,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
     B2Q_FTRACE(l, 16 + k);
     if (k == 1) {  // RoPE, KV append, attention
       const DecLayer& Ly = a.layers[l];
-      AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(xs);
-      __half* kb2 = a.attn_dbuf ? reinterpret_cast<__half*>(xs + (sizeof(AttnTile<G>) + 127) / 128 * 128) : nullptr;
+      // [second K/V buffer (double buffering, eight query heads per KV head
+      // only)][AttnTile], from a 1024-byte boundary of the staging region
+      const bool dbuf = G >= 8 && a.attn_dbuf;
+      uint8_t* ab = xs;
+      __half* kb2 = dbuf ? reinterpret_cast<__half*>(ab) : nullptr;
+      AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(ab + (dbuf ? kAttnTileBytes : 0u));
       for (int it = blockIdx.x; it < a.KV * ng; it += gridDim.x)
         attn_item<G>(a, Ly, it / ng, it % ng, ng, tpg, nz, T, kb2, &attn_bar[0], attn_uses, &attn_bar[1],
                      attn_uses2, &attn_last[0], l, okp);

@@ -107,9 +107,8 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int m, int H, int KV, in
 // cached keys of a query are cut into splits of kAttnTile tokens; one item =
 // (KV head g, split z) on kAttnThreads threads computes, for the G query
 // heads of g, the split's softmax partial (max, sum, unnormalised P*V).  The
-// K and V rows of the split are brought into shared memory with two bulk
-// async copies (one round trip to HBM), then everything runs from shared
-// memory.  The same item code serves the per-kernel path
+// K and V rows of a tile are brought into shared memory by TMA (one round
+// trip to HBM), then everything runs from shared memory.  The same item code serves the per-kernel path
 // (attn_split_kernel) and the persistent decode kernel, so both give the
 // same bits.
 // ---------------------------------------------------------------------------
@@ -125,21 +124,46 @@ constexpr int kAttnThreads = 512;
 // relative.  The probabilities enter scaled by 2^15 (out of the f16
 // subnormal range; the P*V sums are scaled back exactly).  Queries must stay
 // below the f16 maximum, 65504, in magnitude.
-constexpr int kQImgStride = kHeadDim + 8;   // halves per query image row (ldmatrix rows on distinct banks)
-constexpr int kSpStride = kAttnTile + 4;    // floats per score row
+//
+// Shared-memory layouts, all chosen so that the eight 16-byte rows of every
+// ldmatrix phase sit on distinct banks:
+//  * K and V tiles arrive by TMA with the 128-byte swizzle: two boxes of
+//    64 rows x 64 dims (128 bytes) per tile, dims 0..63 then 64..127, and
+//    the 16-byte chunk c of row r of a box stored at chunk c ^ (r & 7)
+//    (kv_off); each tile buffer starts on a 1024-byte boundary, the period
+//    of the swizzle.
+//  * the query image [2G rows][128 dims] and the probability image (over
+//    the score rows) store the chunk c of image row i at c ^ (i & 7).
 constexpr float kPScale = 32768.0f;
+constexpr uint32_t kAttnTileBytes = 2u * kAttnTile * kHeadDim * 2u;  // K + V of one tile
+constexpr int kAttnAlignPad = 1024 - 16;  // worst-case padding of a tile buffer to 1024 bytes
 
 template <int G>
 struct AttnTile {
-  __half k[kAttnTile * kHeadDim];  // rows t_begin.. of the split (then the P*V output)
+  __half k[kAttnTile * kHeadDim];  // tile rows (kv_off layout), then the P*V output [G][128] f32
   __half v[kAttnTile * kHeadDim];
-  __half qimg[2 * G * kQImgStride];  // rotated queries: hi rows 0..G-1, lo rows G..2G-1
-  float sp[G][kSpStride];            // scores; then the probabilities' hi (bytes 0..127) and lo
-                                     // (bytes 128..255) f16 parts, over each head's own row
-  float m[G], l[G];                  // softmax max and sum per head
-  __half kcur[kHeadDim];             // the current token's rotated k and its v (persistent
-  __half vcur[kHeadDim];             // kernel: copied into the tile that holds the token)
+  __half qimg[2 * G * kHeadDim];   // rotated queries: hi rows 0..G-1, lo rows G..2G-1
+  float sp[G][kAttnTile];          // scores; then, over each head's own row, the probability
+                                   // image: hi parts in chunks 0..7, lo parts in chunks 8..15
+  float m[G], l[G];                // softmax max and sum per head
+  __half kcur[kHeadDim];           // the current token's rotated k and its v, copied into
+  __half vcur[kHeadDim];           // the tile that holds the token once its copy has landed
 };
+
+// element offset (halves) of row r, dim d in a K or V tile buffer
+__device__ __forceinline__ int kv_off(int r, int d) {
+  return (d >> 6) * (kAttnTile * 64) + r * 64 + ((d & 63) ^ ((r & 7) << 3));
+}
+// element offset of column c in an image row keyed i (halves; 128 per row)
+__device__ __forceinline__ int img_col(int i, int c) { return c ^ ((i & 7) << 3); }
+
+// the 1024-byte aligned address at or after p (shared memory); computed
+// where it is used (volatile: never hoisted into a long-lived register)
+__device__ __forceinline__ uint8_t* smem_align1024(uint8_t* p) {
+  uint32_t pad;
+  asm volatile("{\n\t.reg .u32 t;\n\tneg.s32 t, %1;\n\tand.b32 %0, t, 1023;\n\t}" : "=r"(pad) : "r"(smem_u32(p)));
+  return p + pad;
+}
 
 __device__ __forceinline__ __half f16_hi(float v) { return __float2half_rz(v); }
 __device__ __forceinline__ __half f16_lo(float v, __half hi) { return __float2half_rn(v - __half2float(hi)); }
@@ -147,8 +171,8 @@ __device__ __forceinline__ __half f16_lo(float v, __half hi) { return __float2ha
 template <int G>
 __device__ __forceinline__ void attn_set_q(AttnTile<G>& T, int h, int d, float v) {
   const __half hi = f16_hi(v);
-  T.qimg[h * kQImgStride + d] = hi;
-  T.qimg[(G + h) * kQImgStride + d] = f16_lo(v, hi);
+  T.qimg[h * kHeadDim + img_col(h, d)] = hi;
+  T.qimg[(G + h) * kHeadDim + img_col(G + h, d)] = f16_lo(v, hi);
 }
 
 // Image row (head h + G * part, part 0 hi / 1 lo) behind A-operand row r
@@ -156,16 +180,17 @@ __device__ __forceinline__ void attn_set_q(AttnTile<G>& T, int h, int d, float v
 template <int G>
 __device__ __forceinline__ int attn_arow(int r) { return G == 8 ? r : r % (2 * G); }
 
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+// ldmatrix from a shared-memory address (32-bit)
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
+               : "r"(addr));
 }
-__device__ __forceinline__ void ldsm_x2(uint32_t& r0, uint32_t& r1, const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(smem_u32(p)));
+__device__ __forceinline__ void ldsm_x2(uint32_t& r0, uint32_t& r1, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
-__device__ __forceinline__ void ldsm_x2_t(uint32_t& r0, uint32_t& r1, const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(smem_u32(p)));
+__device__ __forceinline__ void ldsm_x2_t(uint32_t& r0, uint32_t& r1, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
 // d += a * b, m16n8k16, f16 x f16 -> f32
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -176,20 +201,18 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Issue the bulk copies of K/V rows [t0, t0 + rows) of KV head g into kb /
-// vb (shared memory; one thread); completes on `bar` (expect_tx included).
-__device__ __forceinline__ void attn_rows_load(__half* kb, __half* vb, const __half* kc, const __half* vc, int g,
-                                               int cap, int t0, int rows, uint64_t* bar) {
-  const uint32_t bytes = (uint32_t)rows * kHeadDim * 2;
-  mbar_arrive_expect_tx(bar, 2 * bytes);
-  bulk_g2s(kb, kc + ((int64_t)g * cap + t0) * kHeadDim, bytes, bar);
-  bulk_g2s(vb, vc + ((int64_t)g * cap + t0) * kHeadDim, bytes, bar);
-}
-
-template <int G>
-__device__ __forceinline__ void attn_tile_load(AttnTile<G>& T, const __half* kc, const __half* vc, int g, int cap,
-                                               int t0, int rows, uint64_t* bar) {
-  attn_rows_load(T.k, T.v, kc, vc, g, cap, t0, rows, bar);
+// Issue the TMA copies of the K and V tile whose first cache row (KV head
+// times capacity plus token) is row0: four boxes of 64 rows x 64 dims into
+// kb / vb (1024-byte aligned shared memory; one thread); completes on `bar`
+// (expect_tx included).  Rows past the cache's end read as zeros; rows past
+// the valid tokens are read as they are and masked by the caller.
+__device__ __forceinline__ void attn_rows_load(__half* kb, __half* vb, const void* tmk, const void* tmv, int row0,
+                                               uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, kAttnTileBytes);
+  tma_load_2d(kb, tmk, 0, row0, bar);
+  tma_load_2d(kb + kAttnTile * 64, tmk, 64, row0, bar);
+  tma_load_2d(vb, tmv, 0, row0, bar);
+  tma_load_2d(vb + kAttnTile * 64, tmv, 64, row0, bar);
 }
 
 // Key tiles per attention group.  A query's nz tiles of kAttnTile keys are
@@ -227,30 +250,42 @@ struct AttnRun {
 };
 
 // The softmax partial of one tile on kAttnThreads threads; the query image
-// and the first `nv` rows of kb / vb (T.k / T.v, or a second tile buffer; vb
-// must follow kb directly) are in place.  `sync` is the item's barrier.  For
+// and the first `nv` rows of kb / vb (T.k / T.v, or a second tile buffer) are
+// in place.  `sync` is the item's barrier.  For
 // every (head, dim) element i = h * 128 + d of the G heads of head group g a
 // thread owns (i = tid + kAttnThreads * r), calls emit(r, h, d, max, sum, O).
 template <int G, class Sync, class Emit>
 __device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, const __half* kb, const __half* vb, int nv,
                                                        float scale, Sync sync, Emit emit) {
   constexpr int HD = kHeadDim;
-  const int tid = threadIdx.x & (kAttnThreads - 1), lane = threadIdx.x & 31, w = tid >> 5;
+  // the thread index through a volatile read: the per-lane operand addresses
+  // below are then formed here, per tile, and never hoisted by the compiler
+  // into registers held across a persistent kernel's other phases
+  uint32_t tix;
+  asm volatile("mov.u32 %0, %%tid.x;" : "=r"(tix));
+  const int tid = (int)tix & (kAttnThreads - 1), lane = tid & 31, w = tid >> 5;
   const int g = lane >> 2, t = lane & 3, l16 = lane & 15;
-  // the A-operand row (as head and part) and column half an ldmatrix.x4 lane
-  // addresses; the head a lane's D row g holds and the sum of its two parts
-  const int ar = attn_arow<G>((lane & 7) + ((lane >> 3) & 1) * 8), acol = (lane >> 4) * 8;
+  // the A-operand image row and column half (hb) an ldmatrix.x4 lane
+  // addresses; the head a lane's D row g holds and the sum of its two parts.
+  // Every swizzled chunk index below is (2 ks) ^ (lane constant), so each
+  // operand address is one per-lane base XOR / plus an immediate per slice.
+  const int ar = attn_arow<G>((lane & 7) + ((lane >> 3) & 1) * 8), hb = lane >> 4;
   auto parts = [&](float hi_or_g, float g8) {
     return G == 8 ? hi_or_g + g8 : hi_or_g + __shfl_xor_sync(B2Q_FULL, hi_or_g, 4 * G);
   };
   if (w < 8) {
     // scores: warp w takes keys 8w..8w+7 over the 128 dims (8 k16 slices)
+    // q image row ar: chunk 2 ks + hb at (2 ks) ^ (hb ^ (ar & 7)); K row
+    // 8w + (l16 & 7) of box ks / 4: chunk 2 (ks & 3) + (l16 >> 3) at
+    // (2 (ks & 3)) ^ ((l16 >> 3) ^ (l16 & 7))
+    const uint32_t qa = smem_u32(T.qimg) + ar * 256 + ((hb ^ (ar & 7)) << 4);
+    const uint32_t ka = smem_u32(kb) + (8 * w + (l16 & 7)) * 128 + ((((l16 >> 3) ^ l16) & 7) << 4);
     float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int ks = 0; ks < HD / 16; ++ks) {
       uint32_t a[4], b0, b1;
-      ldsm_x4(a, T.qimg + ar * kQImgStride + 16 * ks + acol);
-      ldsm_x2(b0, b1, kb + (8 * w + (l16 & 7)) * HD + 16 * ks + (l16 >> 3) * 8);
+      ldsm_x4(a, qa ^ (uint32_t)(ks << 5));
+      ldsm_x2(b0, b1, (ka ^ (uint32_t)((ks & 3) << 5)) + (ks >> 2) * (kAttnTile * 128));
       mma_16816(d, a, b0, b1);
     }
     const float s0 = parts(d[0], d[2]), s1 = parts(d[1], d[3]);
@@ -259,10 +294,15 @@ __device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, const __h
       T.sp[g][8 * w + 2 * t + 1] = s1;
     }
   } else if (nv < kAttnTile) {
-    // V rows past the tile's end hold stale shared memory: zero them, so that
-    // a zero probability never meets an inf or NaN there
-    uint32_t* vz = reinterpret_cast<uint32_t*>(const_cast<__half*>(vb) + nv * HD);
-    for (int i = tid - 256; i < (kAttnTile - nv) * HD / 2; i += kAttnThreads - 256) vz[i] = 0u;
+    // V rows past the valid tokens hold whatever the cache or an earlier
+    // tile left: zero them (rows nv.. of both boxes), so that a zero
+    // probability never meets an inf or NaN there
+    uint32_t* vz = reinterpret_cast<uint32_t*>(const_cast<__half*>(vb));
+    const int per = (kAttnTile - nv) * 32;  // words per box
+    for (int i = tid - 256; i < 2 * per; i += kAttnThreads - 256) {
+      const int bx = i >= per ? 1 : 0;
+      vz[bx * (kAttnTile * 32) + nv * 32 + (i - bx * per)] = 0u;
+    }
   }
   sync();
   // softmax: warp h takes head h; lane holds tokens lane, lane + 32.  The
@@ -278,10 +318,10 @@ __device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, const __h
     const float sum = warp_sum(p0 + p1);
     __half* pr = reinterpret_cast<__half*>(T.sp[h]);
     const __half h0 = f16_hi(p0 * kPScale), h1 = f16_hi(p1 * kPScale);
-    pr[t0] = h0;
-    pr[t1] = h1;
-    pr[kAttnTile + t0] = f16_lo(p0 * kPScale, h0);
-    pr[kAttnTile + t1] = f16_lo(p1 * kPScale, h1);
+    pr[img_col(h, t0)] = h0;
+    pr[img_col(h, t1)] = h1;
+    pr[img_col(G + h, kAttnTile + t0)] = f16_lo(p0 * kPScale, h0);
+    pr[img_col(G + h, kAttnTile + t1)] = f16_lo(p1 * kPScale, h1);
     if (lane == 0) { T.m[h] = mx; T.l[h] = sum; }
   }
   sync();
@@ -289,13 +329,17 @@ __device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, const __h
   // output [G][HD] goes over the K rows, no longer read
   float* o = reinterpret_cast<float*>(const_cast<__half*>(kb));
   {
-    const __half* pa = reinterpret_cast<const __half*>(T.sp[ar % G]) + (ar / G) * kAttnTile + acol;
+    // probability image row ar (score row ar % G): chunk 8 part + 2 ks + hb
+    // at (8 part) ^ (2 ks) ^ (hb ^ (ar & 7)); V rows 16 ks + l16, dims 8w..
+    // (box w / 8, chunk w & 7 at (w ^ l16) & 7)
+    const uint32_t pa = smem_u32(T.sp[ar % G]) + ((((ar / G) << 3) ^ (hb ^ (ar & 7))) << 4);
+    const uint32_t va = smem_u32(vb) + (w >> 3) * (kAttnTile * 128) + l16 * 128 + (((w ^ l16) & 7) << 4);
     float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int ks = 0; ks < kAttnTile / 16; ++ks) {
       uint32_t a[4], b0, b1;
-      ldsm_x4(a, pa + 16 * ks);
-      ldsm_x2_t(b0, b1, vb + (16 * ks + l16) * HD + 8 * w);
+      ldsm_x4(a, pa ^ (uint32_t)(ks << 5));
+      ldsm_x2_t(b0, b1, va + ks * (16 * 128));
       mma_16816(d, a, b0, b1);
     }
     const float o0 = parts(d[0], d[2]), o1 = parts(d[1], d[3]);
@@ -325,18 +369,18 @@ __device__ __forceinline__ void attn_store_partial(float* part, int g, int G, in
 }
 
 // Per-kernel path: grid (KV, m, nsplit), kAttnThreads threads,
-// sizeof(AttnTile<G>) bytes of dynamic shared memory.  Query s sits at
+// sizeof(AttnTile<G>) + kAttnAlignPad bytes of dynamic shared memory; tmk /
+// tmv are the TMA descriptors of the layer's K and V caches (global memory).  Query s sits at
 // position start+s and sees keys t < start+s+1 (causal); q was rotated in
 // place by rope_kv_kernel.  Block (g, s, j) folds the key tiles of group j
 // (attn_group_tiles with `grid` = the SM count) into one partial.
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
     const float* __restrict__ qkv, int m, int H, int KV, const int* __restrict__ pos_dev, int cap,
-    const __half* __restrict__ kc, const __half* __restrict__ vc, float scale, int nsplit,
-    float* __restrict__ part, int grid) {
+    const void* tmk, const void* tmv, float scale, int nsplit, float* __restrict__ part, int grid) {
   extern __shared__ __align__(128) uint8_t attn_smem[];
   __shared__ uint64_t bar;
-  AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(attn_smem);
+  AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(smem_align1024(attn_smem));
   pdl_wait();
   constexpr int HD = kHeadDim;
   constexpr int R = (G * HD + kAttnThreads - 1) / kAttnThreads;
@@ -358,7 +402,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
-    attn_tile_load(T, kc, vc, g, cap, z0 * kAttnTile, min(kAttnTile, valid - z0 * kAttnTile), &bar);
+    attn_rows_load(T.k, T.v, tmk, tmv, g * cap + z0 * kAttnTile, &bar);
   }
   const int width = (H + 2 * KV) * HD;
   for (int i = threadIdx.x; i < G * HD; i += blockDim.x) attn_set_q(T, i / HD, i % HD, qkv[(int64_t)s * width + g * G * HD + i]);
@@ -369,7 +413,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
     __syncthreads();  // q in place / the previous tile's shared-memory reads are done
     if (z > z0 && threadIdx.x == 0) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      attn_tile_load(T, kc, vc, g, cap, t_begin, nv, &bar);
+      attn_rows_load(T.k, T.v, tmk, tmv, g * cap + t_begin, &bar);
     }
     mbar_wait_bounded(&bar, (uint32_t)((z - z0) & 1));  // a timeout is recorded in the device error word
     attn_tile_compute_emit<G>(T, T.k, T.v, nv, scale, [] { __syncthreads(); },

@@ -282,6 +282,21 @@ b2q_status b2q_model_finalize(b2q_model* M) {
     err = dalloc(&M->L[l].kc, kv);
     if (err == cudaSuccess) err = dalloc(&M->L[l].vc, kv);
   }
+  if (err == cudaSuccess) {  // the caches' TMA descriptors
+    std::vector<CUtensorMap> maps((size_t)2 * c.n_layers);
+    for (int l = 0; l < c.n_layers; ++l)
+      for (int kv2 = 0; kv2 < 2; ++kv2)
+        if (!kv_tensor_map(&maps[(size_t)2 * l + kv2], kv2 ? M->L[l].vc : M->L[l].kc,
+                           (uint64_t)M->KV_loc * c.max_seq))
+          return set_error(B2Q_ECUDA, "cuTensorMapEncodeTiled failed for the KV cache of layer %d", l);
+    err = dalloc(&M->kv_maps, maps.size());
+    if (err == cudaSuccess)
+      err = cudaMemcpy(M->kv_maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice);
+    for (int l = 0; l < c.n_layers && err == cudaSuccess; ++l) {
+      M->L[l].tmk = M->kv_maps + 2 * l;
+      M->L[l].tmv = M->kv_maps + 2 * l + 1;
+    }
+  }
   if (err == cudaSuccess) err = dalloc(&M->x, (size_t)mm * E);
   if (err == cudaSuccess && mm >= kTcMinTokens) err = dalloc(&M->xn, (size_t)mm * E);
   if (err == cudaSuccess) err = dalloc(&M->qkv, (size_t)mm * (M->H_loc + 2 * M->KV_loc) * hd);
@@ -456,6 +471,9 @@ static b2q_status forward_error_check(b2q_model* M, const char* what) {
   if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
   if (err == cudaSuccess && M->c.tp_size == 1) err = rearm_decode(M);
   if (err != cudaSuccess) return cuda_error(err, what);
+  if (v == 3)
+    return set_error(B2Q_ECUDA, "%s: the decode kernel's shared-memory layout differs from the planned one; the "
+                     "step's outputs are invalid", what);
   return set_error(B2Q_ETIMEOUT, "%s: a device-side bounded wait gave up (code %d); the step's outputs are invalid%s",
                    what, v, M->c.tp_size > 1 ? "; every rank must call b2q_clear_state" : "");
 }
@@ -568,7 +586,7 @@ b2q_status b2q_model_destroy(b2q_model* M) {
   void* ps[] = {M->tok_raw, M->output_norm, M->x, M->qkv, M->attn, M->attn_loc, M->hbuf, M->h_loc,
                 M->y_loc, M->logits, M->logits_loc, M->part, M->tokens, M->argmax, M->pos, M->xn,
                 M->rope_cos, M->rope_sin, M->dec_layers, M->dec_tab, M->dec_sync, M->dec_xblock,
-                M->dec_attn_cnt, M->dec_ll};
+                M->dec_attn_cnt, M->dec_ll, M->kv_maps};
   for (int p = 0; p < b2q::kMaxTp; ++p)
     if (M->dec_peer[p] && p != M->c.tp_rank) cudaIpcCloseMemHandle(M->dec_peer[p]);
   for (void* p : ps)

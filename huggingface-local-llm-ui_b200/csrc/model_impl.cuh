@@ -10,6 +10,8 @@
 #include <string>
 #include <vector>
 
+#include <cuda.h>  // CUtensorMap and its enums (the encoder comes from the driver at run time)
+
 #include "internal.h"
 #include "tp.h"
 
@@ -21,7 +23,42 @@ struct LayerW {
   float *attn_norm = nullptr, *ffn_norm = nullptr;
   float *q_bias = nullptr, *k_bias = nullptr, *v_bias = nullptr;
   __half *kc = nullptr, *vc = nullptr;
+  const CUtensorMap *tmk = nullptr, *tmv = nullptr;  // TMA descriptors of kc / vc (device)
 };
+
+// cuTensorMapEncodeTiled, resolved through the runtime's driver entry point
+// (no link-time dependency on the driver library)
+typedef CUresult (*TmapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static TmapEncodeFn tmap_encoder() {
+  static TmapEncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<TmapEncodeFn>(p);
+  });
+  return fn;
+}
+
+// TMA descriptor of one KV cache, `rows` rows of kHeadDim f16: boxes of
+// kAttnTile rows x 64 dims (128 bytes) with the 128-byte swizzle, the layout
+// attn_rows_load and kv_off expect; rows past the end read as zeros.
+static bool kv_tensor_map(CUtensorMap* out, void* base, uint64_t rows) {
+  const TmapEncodeFn enc = tmap_encoder();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kHeadDim * sizeof(__half)};
+  const cuuint32_t box[2] = {64u, (cuuint32_t)kAttnTile};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return enc(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 constexpr int kPrefillChunk = 256;  // tokens per forward pass of a long prompt (one tensor-core N tile)
 
@@ -54,6 +91,7 @@ struct b2q_model {
   float* logits = nullptr;  // [V]
   float* logits_loc = nullptr;
   float* part = nullptr;    // attention split partials
+  CUtensorMap* kv_maps = nullptr;  // [n_layers][K, V] TMA descriptors of the KV caches
   uint32_t* tokens = nullptr;
   uint32_t* argmax = nullptr;
   int* pos = nullptr;
@@ -262,26 +300,26 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
     // attention (split over the cached tokens) + combine/quantise
     {
       float* aout = P > 1 ? M->attn_loc : M->attn;
-      const size_t tile = G == 4 ? sizeof(AttnTile<4>) : G == 8 ? sizeof(AttnTile<8>)
-                        : G == 2 ? sizeof(AttnTile<2>) : sizeof(AttnTile<1>);
+      const size_t tile = kAttnAlignPad + (G == 4 ? sizeof(AttnTile<4>) : G == 8 ? sizeof(AttnTile<8>)
+                                           : G == 2 ? sizeof(AttnTile<2>) : sizeof(AttnTile<1>));
       cudaLaunchConfig_t cfg = lcfg(dim3(KVl, m, M->nsplit), dim3(kAttnThreads), tile, st, attr, pdl);
       launch_counted(e, 1);
       if (G == 4)
         err = cudaLaunchKernelEx(&cfg, attn_split_kernel<4>, (const float*)M->qkv, m, Hl, KVl,
-                                 (const int*)M->pos, c.max_seq, (const __half*)Lw.kc,
-                                 (const __half*)Lw.vc, scale, M->nsplit, M->part, e->num_sms);
+                                 (const int*)M->pos, c.max_seq, (const void*)Lw.tmk,
+                                 (const void*)Lw.tmv, scale, M->nsplit, M->part, e->num_sms);
       else if (G == 8)
         err = cudaLaunchKernelEx(&cfg, attn_split_kernel<8>, (const float*)M->qkv, m, Hl, KVl,
-                                 (const int*)M->pos, c.max_seq, (const __half*)Lw.kc,
-                                 (const __half*)Lw.vc, scale, M->nsplit, M->part, e->num_sms);
+                                 (const int*)M->pos, c.max_seq, (const void*)Lw.tmk,
+                                 (const void*)Lw.tmv, scale, M->nsplit, M->part, e->num_sms);
       else if (G == 2)
         err = cudaLaunchKernelEx(&cfg, attn_split_kernel<2>, (const float*)M->qkv, m, Hl, KVl,
-                                 (const int*)M->pos, c.max_seq, (const __half*)Lw.kc,
-                                 (const __half*)Lw.vc, scale, M->nsplit, M->part, e->num_sms);
+                                 (const int*)M->pos, c.max_seq, (const void*)Lw.tmk,
+                                 (const void*)Lw.tmv, scale, M->nsplit, M->part, e->num_sms);
       else
         err = cudaLaunchKernelEx(&cfg, attn_split_kernel<1>, (const float*)M->qkv, m, Hl, KVl,
-                                 (const int*)M->pos, c.max_seq, (const __half*)Lw.kc,
-                                 (const __half*)Lw.vc, scale, M->nsplit, M->part, e->num_sms);
+                                 (const int*)M->pos, c.max_seq, (const void*)Lw.tmk,
+                                 (const void*)Lw.tmv, scale, M->nsplit, M->part, e->num_sms);
       if (err != cudaSuccess) return err;
       cudaLaunchConfig_t cfg2 = lcfg(dim3(KVl, m), dim3(G * kHeadDim), 0, st, attr, pdl);
       launch_counted(e, 1);
@@ -609,6 +647,8 @@ static cudaError_t setup_decode(b2q_model* M) {
     d.vb = w.v_bias;
     d.kc = w.kc;
     d.vc = w.vc;
+    d.tmk = w.tmk;
+    d.tmv = w.tmv;
   }
   DecodeArgs& a = M->dec;
   memset(&a, 0, sizeof a);
@@ -733,13 +773,35 @@ static cudaError_t setup_decode(b2q_model* M) {
     a.xflagg[p] = reinterpret_cast<unsigned long long*>(base + xl.bar);
   }
   M->dec_logits = a.logitsg[rk];
-  a.cap = (int)cap;
   a.stage_bytes = (int)stage;
   a.racc_bytes = (int)racc;
+  // where the kernel's dynamic shared memory starts (fixed per kernel: its
+  // static shared memory comes first); the ring ends where the staging
+  // region, and with it the attention tile buffers, start on a 1024-byte
+  // boundary (the ring gives up less than 1 KB)
+  {
+    int* d_base = nullptr;
+    err = cudaMalloc(&d_base, sizeof(int));
+    if (err != cudaSuccess) return err;
+    DecodeArgs q{};
+    q.probe = d_base;
+    void* qargs[] = {&q};
+    err = cudaLaunchKernel(kern, dim3(1), dim3(kGemvThreads), qargs, smem, M->st);
+    int base = 0;
+    if (err == cudaSuccess) err = cudaMemcpyAsync(&base, d_base, sizeof(int), cudaMemcpyDeviceToHost, M->st);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(M->st);
+    cudaFree(d_base);
+    if (err != cudaSuccess) return err;
+    a.cap = (int)(cap - (((size_t)base + cap) & 1023u));
+  }
   // a second K/V tile buffer (long contexts: the tiles of an attention group
   // double-buffered) where the staging and accumulator regions already hold
   // it; never grown for it (the ring would shrink)
-  a.attn_dbuf = stage + racc >= round128(attn_one) + (size_t)2 * kAttnTile * kHeadDim * sizeof(__half) ? 1 : 0;
+  a.attn_dbuf = stage + racc >= (size_t)kAttnTileBytes + attn_one ? 1 : 0;
+#ifdef B2Q_DECODE_TRACE
+  fprintf(stderr, "decode smem: ring %d stage %zu racc %zu table %zu attention tile %zu double buffer %d\n", a.cap,
+          stage, racc, tabb, attn_one, a.attn_dbuf);
+#endif
   M->dec_smem = smem;
   M->dec_G = G;
   M->dec_all = all;
