@@ -6,10 +6,13 @@ missing library or a failing call raises.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-LIB_PATH = HERE / "libb2q.so"
+# B2Q_CHECKS=1 selects the debug-bounds build (build.py --checks), the same
+# kernels with index and layout checks compiled in
+LIB_PATH = HERE / ("libb2q_checks.so" if os.environ.get("B2Q_CHECKS") == "1" else "libb2q.so")
 
 OK, EINVAL, ENOMEM, ECUDA, ENCCL, ETIMEOUT, EUNSUP = range(7)
 _STATUS_NAMES = {0: "B2Q_OK", 1: "B2Q_EINVAL", 2: "B2Q_ENOMEM", 3: "B2Q_ECUDA",
@@ -93,6 +96,8 @@ SIGNATURES = [
     ("b2q_time_gemv", _I, [_VP, C.POINTER(_VP), _I, _VP, _I, _I, _VP, C.POINTER(C.c_float), _I]),
     ("b2q_kernel_launch_count", C.c_uint64, [_VP]),
     ("b2q_check_device_error", _I, [_VP]),
+    ("b2q_debug_checks_enabled", _I, []),
+    ("b2q_debug_check_site", _I, [_VP, C.POINTER(_I)]),
     ("b2q_set_wait_limit_cycles", _I, [_VP, C.c_longlong]),
     ("b2q_model_debug_desync", _I, [_VP]),
     ("b2q_model_fill_kv", _I, [_VP, _I, _I, C.c_uint64, _F]),

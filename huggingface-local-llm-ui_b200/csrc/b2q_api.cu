@@ -891,7 +891,21 @@ b2q_status b2q_check_device_error(b2q_engine* e) {
   err = cudaMemcpyFromSymbol(&v, g_b2q_device_error, sizeof v);
   if (err == cudaSuccess) err = cudaMemcpyToSymbol(g_b2q_device_error, &zero, sizeof zero);
   if (err != cudaSuccess) return cuda_error(err, "check_device_error: symbol");
+  if (v == 3) return set_error(B2Q_ECUDA, "a device-side layout or bounds check failed (b2q_debug_check_site)");
   if (v != 0) return set_error((b2q_status)v, "a device-side bounded wait gave up (code %d)", v);
+  return B2Q_OK;
+}
+
+int b2q_debug_checks_enabled(void) { return kChecks ? 1 : 0; }
+
+b2q_status b2q_debug_check_site(b2q_engine* e, int* site) {
+  if (!e || !site) return set_error(B2Q_EINVAL, "b2q_debug_check_site: NULL argument");
+  cudaSetDevice(e->device);
+  cudaError_t err = cudaStreamSynchronize(e->stream);
+  int zero = 0;
+  if (err == cudaSuccess) err = cudaMemcpyFromSymbol(site, g_b2q_check_site, sizeof(int));
+  if (err == cudaSuccess) err = cudaMemcpyToSymbol(g_b2q_check_site, &zero, sizeof zero);
+  if (err != cudaSuccess) return cuda_error(err, "b2q_debug_check_site");
   return B2Q_OK;
 }
 

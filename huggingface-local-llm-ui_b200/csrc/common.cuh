@@ -14,6 +14,49 @@
 // libb2q is a single translation unit (b2q_api.cu includes the rest).
 __device__ int g_b2q_device_error = 0;
 
+// Debug-bounds build (compiled with -DB2Q_CHECKS; build.py --checks makes
+// libb2q_checks.so): index and layout checks in front of the accesses that
+// a wrong plan, layout or argument could send astray -- ring offsets, staged
+// input sizes, attention tile rows, tagged-vector and partial-sum indices,
+// tensor-core stage offsets, GEMV row groups, embedding rows.  A failed check
+// records its site (the first one wins) in g_b2q_check_site, sets the device
+// error word to B2Q_ECUDA (3) and skips the access it guards; the host reads
+// the site with b2q_debug_check_site().  Without the flag every check is the
+// constant true and compiles away.
+enum CheckSite : int {
+  kChkRing = 1,       // a ring stage lies inside the ring
+  kChkAttnRows = 2,   // an attention tile's first cache row
+  kChkAttnTok = 3,    // the current token's row inside its tile
+  kChkStage = 4,      // a phase input fits the staging region
+  kChkTag = 5,        // a tagged-vector index
+  kChkTpSlot = 6,     // a tensor-parallel partial-sum slot
+  kChkPart = 7,       // an attention partial index
+  kChkTcStage = 8,    // a tensor-core pipeline stage
+  kChkGemv = 9,       // a standalone GEMV's row groups and shared-memory plan
+};
+__device__ int g_b2q_check_site = 0;
+#ifdef B2Q_CHECKS
+constexpr bool kChecks = true;
+__device__ __noinline__ void b2q_check_fail(int site) {
+  atomicCAS(&g_b2q_check_site, 0, site);
+  atomicExch(&g_b2q_device_error, 3);
+}
+__device__ __forceinline__ bool b2q_check(bool ok, int site) {
+  if (!ok) b2q_check_fail(site);
+  return ok;
+}
+#else
+constexpr bool kChecks = false;
+__device__ __forceinline__ constexpr bool b2q_check(bool, int) { return true; }
+#endif
+
+// Bytes of dynamic shared memory this CTA was launched with.
+__device__ __forceinline__ uint32_t dyn_smem_bytes() {
+  uint32_t v;
+  asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(v));
+  return v;
+}
+
 // Upper bound for any spin (an mbarrier, a grid or all-rank barrier, a
 // tagged hand-off), in SM clock cycles: 4e9 (~2 s at 1.965 GHz) unless the
 // host lowers it with b2q_set_wait_limit_cycles().  Read only on the slow

@@ -784,6 +784,7 @@ __device__ __forceinline__ void consume_loop(Consumer& cs, const CtaPhase& ph, b
     int off = cs.ro;
     const int size = nt2 ? 2 * tb : tb;
     if (off + size > cs.R.cap) off = 0;
+    if (!b2q_check(off + size <= cs.R.cap, kChkRing)) ok = false;  // outputs withheld
     cs.ro = off + size;
     const int slot = cs.j & (kRingSlots - 1);
 #ifdef B2Q_DECODE_TRACE
@@ -909,7 +910,8 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
   auto vbuf = [&](int b) { return b ? kb2 + kAttnTile * HD : T.v; };
   auto load = [&](int z, int b) {
     const int nv = min(kAttnTile, pos + 1 - z * kAttnTile);
-    const int nload = z == nz - 1 ? nv - 1 : nv;
+    int nload = z == nz - 1 ? nv - 1 : nv;
+    if (!b2q_check(g >= 0 && g < KV && z >= 0 && z * kAttnTile < cap, kChkAttnRows)) nload = 0;  // (uniform)
     if (gt == 0 && nload > 0) {
       fence_proxy_async_smem();  // earlier generic accesses to this region come first
       attn_rows_load(kbuf(b), vbuf(b), Ly.tmk, Ly.tmv, g * cap + z * kAttnTile, b ? bar2 : bar);
@@ -1018,7 +1020,7 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
     }
     if (z == nz - 1) {  // the current token's row, over what the copy brought
       if (z == z0) consumer_sync();  // T.kcur / T.vcur written above
-      if (gt < HD) {
+      if (gt < HD && b2q_check(nv >= 1 && nv <= kAttnTile, kChkAttnTok)) {
         kbuf(b)[kv_off(nv - 1, gt)] = T.kcur[gt];
         vbuf(b)[kv_off(nv - 1, gt)] = T.vcur[gt];
       }
@@ -1108,7 +1110,7 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
       if (i < G * HD) {
         const float v = O[r] * (1.0f / fmaxf(Ls[r], 1e-12f));
         const int oi = (g * G + i / HD) * HD + i % HD;  // this rank's heads, local
-        ll_store(a.attnll + oi, v, a.tag0 + (uint32_t)(5 * tl + 2));
+        if (b2q_check(oi < a.H * HD, kChkTag)) ll_store(a.attnll + oi, v, a.tag0 + (uint32_t)(5 * tl + 2));
       }
     }
     if (gt == 0) a.attn_cnt[tl * KV + g] = 0u;
@@ -1166,6 +1168,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
     if (threadIdx.x == 0) atomicExch(&g_b2q_device_error, 3);
     return;  // every CTA alike, before any exchange
   }
+  if (kChecks && !b2q_check((size_t)a.cap + a.stage_bytes + a.racc_bytes + (size_t)a.nph * sizeof(CtaPhase) <=
+                                dyn_smem_bytes(),
+                            kChkStage))
+    return;  // (uniform, before any exchange)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRingSlots; ++i) {
@@ -1265,8 +1271,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
                        "l"(a.xll + grow0 + 2 * r2)
                        : "memory");
       // stage the input: rmsnorm(x) for QKV, gate/up and the head; attn; h
+      bool stage_ok = true;
+      if (kChecks) {
+        const size_t need = k == 2 ? xq_smem_bytes(round_up_int(a.H * kHeadDim, 256)) +
+                                         (size_t)4 * round_up_int(a.H * kHeadDim, 8)
+                            : k == 4 ? xq_smem_bytes(round_up_int(a.Fl, 256))
+                                     : xq_smem_bytes(kp_e) + (size_t)4 * a.E;
+        stage_ok = b2q_check(need <= (size_t)a.stage_bytes, kChkStage);
+        if (!stage_ok) ok = false;  // nothing staged, outputs withheld
+      }
       XQ q;
-      if (k == 2) {
+      if (!stage_ok) {
+        q = smem_xq(xs, kp_e);
+      } else if (k == 2) {
         const int kp_a = round_up_int(a.H * kHeadDim, 256);
         q = smem_xq(xs, kp_a);
         stage_plain_ll(a.attnll, a.H * kHeadDim, q, reinterpret_cast<float*>(xs + xq_smem_bytes(kp_a)),
@@ -1301,7 +1318,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
         float* pv = racc + 4 * rows;  // [tp][rows]
         for (int r = threadIdx.x; r < nrows; r += kGemvConsumerWarps * 32) {
           const float v = dec_racc(racc, rows, 1, r, 0);
-          for (int p = 0; p < a.tp; ++p) ll_store_sys(a.partll[p] + (set + a.rank) * a.E + grow0 + r, v, tp_tag);
+          if (b2q_check(grow0 + r < a.E && a.rank < a.tp, kChkTpSlot))
+            for (int p = 0; p < a.tp; ++p) ll_store_sys(a.partll[p] + (set + a.rank) * a.E + grow0 + r, v, tp_tag);
           pv[a.rank * rows + r] = v;
         }
         for (int i = threadIdx.x; i < a.tp * nrows; i += kGemvConsumerWarps * 32) {
@@ -1314,14 +1332,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
         for (int r = threadIdx.x; r < nrows; r += kGemvConsumerWarps * 32) {
           float sum = ll_value(a.xll + grow0 + r, resid[r], a.tag0 + (uint32_t)(5 * l + (k == 2 ? 0 : 3)), okp);
           for (int p = 0; p < a.tp; ++p) sum += pv[p * rows + r];
-          ll_store(a.xll + grow0 + r, sum, a.tag0 + (uint32_t)(k == 2 ? 5 * l + 3 : 5 * (l + 1)));
+          if (b2q_check(grow0 + r < a.E, kChkTag))
+            ll_store(a.xll + grow0 + r, sum, a.tag0 + (uint32_t)(k == 2 ? 5 * l + 3 : 5 * (l + 1)));
         }
       } else if (ok) {
         const int nw = pair ? 2 : 1;
         for (int r = threadIdx.x; r < nrows; r += kGemvConsumerWarps * 32) {
           const float v = dec_racc(racc, rows, nw, r, 0);
           if (k == 0 && !head) {  // q/k/v: this rank's heads, local
-            ll_store(a.qkvll + ph.ycol + row0 + r, v, a.tag0 + (uint32_t)(5 * l + 1));
+            if (b2q_check(ph.ycol + row0 + r < (a.H + 2 * a.KV) * kHeadDim, kChkTag))
+              ll_store(a.qkvll + ph.ycol + row0 + r, v, a.tag0 + (uint32_t)(5 * l + 1));
             continue;
           }
           if (pair) {  // SwiGLU rows of this rank, local
@@ -1330,7 +1350,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
           }
           if (add) {  // one GPU: x += v, tagged for the next phase (gate/up, or the next layer's QKV)
             const float xr = ll_value(a.xll + grow0 + r, resid[r], a.tag0 + (uint32_t)(5 * l + (k == 2 ? 0 : 3)), okp);
-            ll_store(a.xll + grow0 + r, xr + v, a.tag0 + (uint32_t)(k == 2 ? 5 * l + 3 : 5 * (l + 1)));
+            if (b2q_check(grow0 + r < a.E, kChkTag))
+              ll_store(a.xll + grow0 + r, xr + v, a.tag0 + (uint32_t)(k == 2 ? 5 * l + 3 : 5 * (l + 1)));
             continue;
           }
           // the head: this rank's vocabulary slice into every rank's logits

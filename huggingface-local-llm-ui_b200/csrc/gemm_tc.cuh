@@ -361,6 +361,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   const int ks0 = (int)((int64_t)a.KS * z / a.splits), ks1 = (int)((int64_t)a.KS * (z + 1) / a.splits);
   const int nst = ks1 - ks0;
   const int ncols = tc_tmem_cols(N);
+  if (kChecks && !b2q_check(S >= 1 && S <= kTcStagesMax && N >= 16 && N <= kTcNMax && (N & 15) == 0 &&
+                                (size_t)S * tc_stage_bytes(N) <= dyn_smem_bytes() && ks0 >= 0 && ks1 <= a.KS &&
+                                row0 >= 0,
+                            kChkTcStage))
+    return;  // (uniform over the CTA, before any barrier or TMEM allocation)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -548,6 +553,10 @@ __global__ void tc_act_kernel(const float* __restrict__ x, int ldx, int m, int k
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e] = (live && k0 + e < k) ? xr[k0 + e] * sc : 0.0f;
     }
+    // a NaN element contributes nothing (the quantised paths' rule, after
+    // quantize_row_q8_k); the maximum above already ignores it
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = v[e] != v[e] ? 0.0f : v[e];
     uint8_t* stage = reinterpret_cast<uint8_t*>(img) + ((size_t)tile * KS + ks) * (size_t)tc_b_bytes(N);
     st_img8(stage, N * kTcK * 2, tt, kk, N, v);
   }

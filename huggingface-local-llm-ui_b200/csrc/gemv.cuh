@@ -555,6 +555,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
   const int NS = a.ns;
 
   const int kp = a.kpad;
+  if (kChecks) {  // uniform over the CTA: every thread leaves before any barrier
+    const size_t need = gemv_x_bytes(kp, MT) + (size_t)NS * a.slot_bytes;
+    if (!b2q_check(ci >= 0 && ci < sg.ncta && 0 <= gb && gb <= ge && ge <= L.G && NS <= kGemvMaxStages &&
+                       need <= dyn_smem_bytes(),
+                   kChkGemv))
+      return;
+  }
   uint8_t* stages = smem + gemv_x_bytes(kp, MT);
   float* racc = reinterpret_cast<float*>(stages + (size_t)NS * a.slot_bytes);
   SX sx;

@@ -363,6 +363,7 @@ __device__ __forceinline__ void attn_tile_compute_emit(AttnTile<G>& T, const __h
 // O[128]} for head h = g*G + (element's head).
 __device__ __forceinline__ void attn_store_partial(float* part, int g, int G, int j, int nsplit, int h, int d,
                                                    float m, float l, float o) {
+  if (!b2q_check(h >= 0 && h < G && j >= 0 && j < nsplit && d >= 0 && d < kHeadDim, kChkPart)) return;
   float* pp = part + ((int64_t)(g * G + h) * nsplit + j) * kPartStride;
   if (d == 0) { pp[0] = m; pp[1] = l; }
   pp[2 + d] = o;
@@ -399,6 +400,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
     }
     return;
   }
+  if (kChecks && !b2q_check(g < KV && (z1 - 1) * kAttnTile < cap &&
+                                smem_u32(&T) + sizeof(AttnTile<G>) <= smem_u32(attn_smem) + dyn_smem_bytes(),
+                            kChkAttnRows))
+    return;  // (uniform over the CTA)
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();

@@ -46,14 +46,22 @@ __host__ __device__ inline int xswz(int pos) { return xswz_chunk(pos >> 6, (pos 
 // All 32 lanes call it.  The block maximum of |x| is a warp reduction of
 // the float bit patterns (for non-negative floats the integer order is the
 // float order), the quarter sums are integer reductions: single redux.sync
-// instructions, exact, so every ordering gives the same bits.  A NaN in the
-// block makes the maximum a NaN and the block quantises to zeros.
+// instructions, exact, so every ordering gives the same bits.  A NaN
+// element is left out of the maximum and quantises to 0 (the float to int
+// conversion maps NaN to 0), as quantize_row_q8_k treats it
+// (inference.rs:933-962: NaN never wins the |x| scan, and `NaN as i8` is 0).
 __device__ __forceinline__ int xq_quant(float v, float inv) {
   return max(-kXMax, min(kXMax, __float2int_rn(v * inv)));
 }
 
+// |v| as an ordered bit pattern, NaN as 0
+__device__ __forceinline__ uint32_t xq_abs_bits(float v) {
+  const uint32_t b = __float_as_uint(fabsf(v));
+  return b > 0x7F800000u ? 0u : b;
+}
+
 __device__ __forceinline__ void xq_store_block(float v0, float v1, int lane, int t, int j, const XQ& xq) {
-  const uint32_t mbits = __reduce_max_sync(B2Q_FULL, max(__float_as_uint(fabsf(v0)), __float_as_uint(fabsf(v1))));
+  const uint32_t mbits = __reduce_max_sync(B2Q_FULL, max(xq_abs_bits(v0), xq_abs_bits(v1)));
   const float amax = __uint_as_float(mbits);
   int q0 = 0, q1 = 0;
   float scale = 0.0f;
@@ -97,7 +105,7 @@ __device__ __forceinline__ void xq_store_chunk8(const float (&v)[8], int lane, i
                                                 const XQ& xq) {
   uint32_t mb = 0u;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(fabsf(v[i])));
+  for (int i = 0; i < 8; ++i) mb = max(mb, xq_abs_bits(v[i]));
   mb = max(mb, __shfl_xor_sync(B2Q_FULL, mb, 1));
   mb = max(mb, __shfl_xor_sync(B2Q_FULL, mb, 2));
   mb = max(mb, __shfl_xor_sync(B2Q_FULL, mb, 4));

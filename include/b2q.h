@@ -408,8 +408,23 @@ b2q_status b2q_time_gemv(b2q_engine* eng, const b2q_weight* const* ws, int count
 uint64_t b2q_kernel_launch_count(b2q_engine* eng);
 
 /* Read and clear the device-side error word (B2Q_ETIMEOUT when a bounded
- * wait gave up); synchronises the engine's stream. */
+ * wait gave up; B2Q_ECUDA when the persistent decode kernel found its shared
+ * memory laid out otherwise than planned, or, in the debug-bounds build, a
+ * bounds check failed); synchronises the engine's stream. */
 b2q_status b2q_check_device_error(b2q_engine* eng);
+
+/* Debug-bounds build (libb2q_checks.so, compiled with -DB2Q_CHECKS): 1 when
+ * this library has the kernels' index and layout checks compiled in, else 0.
+ * No counterpart in the reference (its kernels are a PTX image, gpu.rs:6,301);
+ * it stands in for a memory checker. */
+int b2q_debug_checks_enabled(void);
+
+/* Site of the first failed check since the last call (0: none; 1 ring stage,
+ * 2 attention tile rows, 3 current token row, 4 staged input size, 5
+ * tagged-vector index, 6 tensor-parallel slot, 7 attention partial index, 8
+ * tensor-core stage plan, 9 standalone GEMV plan), then cleared.  Always 0
+ * in the regular build.  Synchronises the engine's stream. */
+b2q_status b2q_debug_check_site(b2q_engine* eng, int* site);
 
 /* Upper bound of every device-side wait of this engine's GPU (mbarriers,
  * grid and all-rank barriers, tagged hand-offs), in SM clock cycles;

@@ -31,6 +31,19 @@ def test_library_builds_and_exports_all_symbols(pkg):
     assert declared_symbols() <= bound, declared_symbols() - bound
 
 
+def test_checks_build_exports_all_symbols(pkg):
+    """The debug-bounds twin (-DB2Q_CHECKS) has the same ABI and says so;
+    the regular library has its checks compiled out."""
+    from hf_llm_b200 import build
+    path = build.build(checks=True)
+    assert path.exists() and path != build.lib_path()
+    lib = C.CDLL(str(path))
+    missing = [s for s in sorted(declared_symbols()) if not hasattr(lib, s)]
+    assert not missing, f"declared but not exported: {missing}"
+    assert lib.b2q_debug_checks_enabled() == 1
+    assert C.CDLL(str(build.build())).b2q_debug_checks_enabled() == 0
+
+
 def test_kernels_compiled_for_sm100a(pkg):
     from hf_llm_b200 import build
     assert "arch=compute_100a,code=sm_100a" in " ".join(build.NVCC_FLAGS)

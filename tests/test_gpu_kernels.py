@@ -153,6 +153,29 @@ def test_matvec_zero_and_ragged_inputs(engine, orc, pkg):
     assert rel_l2(y, y64) <= TOL
 
 
+@pytest.mark.parametrize("dtype", [12, 14, 8])
+def test_matvec_nan_activation_elements(engine, orc, pkg, dtype):
+    """A NaN activation element contributes nothing and leaves the rest of
+    its block intact, as in quantize_row_q8_k (inference.rs:933-962: NaN
+    never wins the |x| scan, `NaN as i8` is 0): the matvec equals the
+    fp64 one over the activations with the NaN elements set to zero, for
+    one token, for several (GEMV) and for enough to take the tensor-core
+    path."""
+    from hf_llm_b200 import ggml, synth
+    n, k = 512, 4096
+    raw = synth.tensor_rows(dtype, n, k, 3, 21)
+    buf = engine.try_upload_weight(raw, dtype, n, k)
+    for m in (1, 5, 20):  # 20 tokens: the tensor-core path
+        x = np.concatenate([synth.activation(k, 30 + t) for t in range(m)], axis=0)
+        x[0, [3, 64, 65, 1000, 4095]] = np.nan  # blocks 0, 1, 15 and 63 keep their other elements
+        if m > 1:
+            x[m - 1, 128:192] = np.nan             # a whole block
+        y = engine.matmul_batched(buf, x, m, n, k)
+        assert np.isfinite(y).all()
+        y64 = orc.matmul_f64(raw, dtype, n, k, np.nan_to_num(x, nan=0.0))
+        assert rel_l2(y, y64) <= TOL, f"type {dtype} m={m}: rel-L2 {rel_l2(y, y64):.3g}"
+
+
 def test_matmul_group_same_input(engine, orc, pkg):
     """QKV-style group: outputs concatenated in order (gpu.rs:617-646)."""
     from hf_llm_b200 import ggml, synth
