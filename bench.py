@@ -28,6 +28,8 @@ prompt is prefilled, then one step = one greedy decode token at batch 1.
               per step; `traffic` from the committed ncu capture.
 * gemv_roofline / gemv_shapes -- the standalone GEMV per matvec config shape
               (rank 0), weights rotated over copies larger than L2.
+* output_head -- the Q6_K output head (128256 x 4096) row-sharded over the N
+              ranks: the GEMV of one rank's rows, max over ranks.
 * prefill  -- the 512-token prompt pass (tensor cores), its projection flops
               against the measured bf16 peak.
 * tp_parity -- after the timed region, a fixed-seed 2-layer model of
@@ -341,6 +343,38 @@ def time_gemv_shape(engine, synth, key, seed, dev, sp, copies=None, reps=None, c
     for b in bufs:
         b.free()
     return ms_l, alg
+
+
+def time_head_shard(engine, synth, world, rank, seed, dev, sp, dist, peak, peak_kind):
+    """The Q6_K output head (128256 x 4096) row-sharded over the ranks as the
+    model shards it: every rank times the GEMV of its rows (chained launches,
+    weight copies rotated past L2), max over ranks.  The logit slices are
+    then exchanged inside the persistent kernel's epilogue (each rank stores
+    its slice into every rank's logits over NVLink), not by a collective."""
+    import torch
+    t, n, k = 14, 128256, 4096
+    rows = -(-n // world)
+    rows = -(-rows // 8) * 8  # the model's V_loc: 8-row groups
+    r0 = min(n, rank * rows)
+    nl = max(8, min(rows, n - r0))
+    raw = synth.tensor_rows(t, n, k, seed, 901, r0, r0 + nl)
+    copies = max(2, -(-400_000_000 // raw.nbytes))
+    bufs = [engine.try_upload_weight(raw, t, nl, k) for _ in range(copies)]
+    x = torch.randn(k, device=dev)
+    engine.time_gemv(bufs, x.data_ptr(), k, 2, sp, True)
+    ms = engine.time_gemv(bufs, x.data_ptr(), k, max(4, 400 // copies), sp, True)
+    for b in bufs:
+        b.free()
+    alg = raw.nbytes + 4 * k + 4 * nl
+    if dist:
+        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    ach = alg / (ms * 1e-3) / 1e9
+    return {"rows_per_rank": nl, "us": round(ms * 1000, 3), "GBps_per_rank": round(ach, 1),
+            "GBps_all_ranks": round(ach * world, 1), "frac": round(ach / peak, 4), "peak_kind": peak_kind,
+            "note": "Q6_K 128256x4096 row-sharded; GEMV of one rank's rows, chained launches, max over ranks; "
+                    "the logit slices go to every rank by peer stores in the persistent kernel's epilogue"}
 
 
 def run_gemv_only(args):
@@ -678,6 +712,9 @@ def main():
                                                "achieved": round(alg / (ms_l * 1e-3) / 1e9, 1),
                                                "frac": round(alg / (ms_l * 1e-3) / 1e9 / peak, 4)}}
 
+    # the Q6_K output head, row-sharded over the ranks (every rank)
+    head_shard = time_head_shard(engine, synth, world, rank, args.seed, dev, sp, dist, peak, peak_kind)
+
     cpu = None
     if rank == 0 and world == 1 and host:
         try:
@@ -714,6 +751,7 @@ def main():
                 "parallelism": f"tp{world}", "kv_cache": "f16", "decode_path": head["decode_path"],
                 "decode_step": head["decode_step"],
                 "roofline": head["roofline"], "gemv_roofline": gemv_roof, "gemv_shapes": gemv_shapes,
+                "output_head": head_shard,
                 "prefill": head.get("prefill"), "cpu_baseline": cpu, "e2e": head["e2e"],
                 "tp_parity": parity, "model_70b": m70,
                 "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
