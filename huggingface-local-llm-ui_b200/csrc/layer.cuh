@@ -470,6 +470,191 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int m, int H
   pdl_launch_dependents();
 }
 
+// ---------------------------------------------------------------------------
+// Prompt-pass attention (m >= 16 queries, the tensor-core projection path):
+// one CTA of 4 warps takes 64 query rows -- 64 / G consecutive tokens times
+// the G query heads of KV head g, row r = token (r / G), head (r % G) -- and
+// runs over the key tiles up to its last token with a running softmax
+// (inference.rs:2782-2833 for each query: scores q.k * scale over the keys
+// t <= position, softmax, P.V, normalised by 1/max(sum, 1e-12)).  K and V
+// tiles arrive by TMA (the decode tiles' 128-byte-swizzled layout, two
+// buffers, the next tile in flight); the products run on mma.sync
+// m16n8k16 with the f32 queries and probabilities each split into f16 hi
+// and lo fragments (two MMAs per product, ~2^-22 relative) and the f16 K/V
+// entering exactly.  Warp w owns rows 16w..16w+15: its S tile (16 x 64) and
+// its output (16 x 128) stay in registers; the S accumulator fragments of
+// two adjacent key octets are the A fragment of the P.V k-slice.
+// grid (KV, ceil(m / (64 / G))), 128 threads, kAttnPrefillSmem bytes of
+// dynamic shared memory.
+// ---------------------------------------------------------------------------
+constexpr int kAttnPrefillSmem = 2 * (int)kAttnTileBytes + 1024;
+
+__device__ __forceinline__ void f16_split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half ha = f16_hi(a), hb = f16_hi(b);
+  const __half la = f16_lo(a, ha), lb = f16_lo(b, hb);
+  hi = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+  lo = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+}
+
+template <int G>
+__global__ void __launch_bounds__(128) attn_prefill_kernel(const float* __restrict__ qkv, int m, int H, int KV,
+                                                            const int* __restrict__ pos_dev, int cap,
+                                                            const void* tmk, const void* tmv, float scale,
+                                                            float* __restrict__ out) {
+  extern __shared__ __align__(128) uint8_t attn_smem[];
+  __shared__ uint64_t bars[2];
+  constexpr int HD = kHeadDim, QT = 64 / G;  // tokens per CTA
+  pdl_wait();
+  const int g = blockIdx.x, s0 = blockIdx.y * QT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, t = lane & 3;
+  const int start = *pos_dev;
+  const int s_last = min(m, s0 + QT) - 1;
+  const int nkeys = min(start + s_last + 1, cap);  // keys of the block's last query
+  const int ntiles = (nkeys + kAttnTile - 1) / kAttnTile;
+  uint8_t* base = smem_align1024(attn_smem);
+  __half* kb[2] = {reinterpret_cast<__half*>(base), reinterpret_cast<__half*>(base + kAttnTileBytes)};
+  if (kChecks && !b2q_check(g < KV && smem_u32(base) + 2 * kAttnTileBytes <= smem_u32(attn_smem) + dyn_smem_bytes(),
+                            kChkAttnRows))
+    return;  // (uniform over the CTA)
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+    attn_rows_load(kb[0], kb[0] + kAttnTile * HD, tmk, tmv, g * cap, &bars[0]);
+  }
+  // this thread's two rows (gq and gq + 8 of the warp's 16) and their query positions
+  const int width = (H + 2 * KV) * HD;
+  const int r0 = 16 * warp + gq, r1 = r0 + 8;
+  const int tok0 = s0 + r0 / G, tok1 = s0 + r1 / G;
+  const int qp0 = start + tok0, qp1 = start + tok1;
+  // Q fragments (hi, lo) for the 8 k16 slices of the 128 dims
+  uint32_t qh[8][4], ql[8][4];
+  {
+    const float* q0 = qkv + (int64_t)min(tok0, m - 1) * width + (g * G + r0 % G) * HD;
+    const float* q1 = qkv + (int64_t)min(tok1, m - 1) * width + (g * G + r1 % G) * HD;
+    const bool v0 = tok0 < m, v1 = tok1 < m;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      const int c = 16 * ks + 2 * t;
+      const float2 a = v0 ? *reinterpret_cast<const float2*>(q0 + c) : make_float2(0.f, 0.f);
+      const float2 b = v1 ? *reinterpret_cast<const float2*>(q1 + c) : make_float2(0.f, 0.f);
+      const float2 cc = v0 ? *reinterpret_cast<const float2*>(q0 + c + 8) : make_float2(0.f, 0.f);
+      const float2 d = v1 ? *reinterpret_cast<const float2*>(q1 + c + 8) : make_float2(0.f, 0.f);
+      f16_split2(a.x, a.y, qh[ks][0], ql[ks][0]);
+      f16_split2(b.x, b.y, qh[ks][1], ql[ks][1]);
+      f16_split2(cc.x, cc.y, qh[ks][2], ql[ks][2]);
+      f16_split2(d.x, d.y, qh[ks][3], ql[ks][3]);
+    }
+  }
+  __syncthreads();  // the barriers are initialised
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+  float mx0 = -INFINITY, mx1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  const int l16 = lane & 15;
+  for (int z = 0; z < ntiles; ++z) {
+    const int b = z & 1;
+    if (threadIdx.x == 0 && z + 1 < ntiles) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      attn_rows_load(kb[b ^ 1], kb[b ^ 1] + kAttnTile * HD, tmk, tmv, g * cap + (z + 1) * kAttnTile, &bars[b ^ 1]);
+    }
+    mbar_wait_bounded(&bars[b], (uint32_t)((z >> 1) & 1));  // a timeout is recorded in the device error word
+    const __half* K = kb[b];
+    const __half* V = kb[b] + kAttnTile * HD;
+    // S = Q K^T: 16 rows x 64 keys, 8 key octets
+    float sc[8][4];
+    const uint32_t ka = smem_u32(K) + (l16 & 7) * 128 + ((((l16 >> 3) ^ l16) & 7) << 4);
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+#pragma unroll
+      for (int ks = 0; ks < HD / 16; ++ks) {
+        uint32_t b0, b1;
+        ldsm_x2(b0, b1, ((ka + nt * 8 * 128) ^ (uint32_t)((ks & 3) << 5)) + (ks >> 2) * (kAttnTile * 128));
+        mma_16816(sc[nt], qh[ks], b0, b1);
+        mma_16816(sc[nt], ql[ks], b0, b1);
+      }
+    }
+    // scale, causal mask, running max
+    const int kp0 = z * kAttnTile;
+    float tm0 = -INFINITY, tm1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int kp = kp0 + 8 * nt + 2 * t + e;
+        sc[nt][e] = kp <= qp0 && kp < nkeys ? sc[nt][e] * scale : -INFINITY;
+        sc[nt][2 + e] = kp <= qp1 && kp < nkeys ? sc[nt][2 + e] * scale : -INFINITY;
+        tm0 = fmaxf(tm0, sc[nt][e]);
+        tm1 = fmaxf(tm1, sc[nt][2 + e]);
+      }
+    }
+    tm0 = fmaxf(tm0, __shfl_xor_sync(B2Q_FULL, tm0, 1));
+    tm0 = fmaxf(tm0, __shfl_xor_sync(B2Q_FULL, tm0, 2));
+    tm1 = fmaxf(tm1, __shfl_xor_sync(B2Q_FULL, tm1, 1));
+    tm1 = fmaxf(tm1, __shfl_xor_sync(B2Q_FULL, tm1, 2));
+    const float nm0 = fmaxf(mx0, tm0), nm1 = fmaxf(mx1, tm1);
+    // rows with no key yet keep m = -inf and contribute nothing
+    const float al0 = nm0 == -INFINITY ? 1.0f : expf(mx0 - nm0), al1 = nm1 == -INFINITY ? 1.0f : expf(mx1 - nm1);
+    mx0 = nm0;
+    mx1 = nm1;
+    l0 *= al0;
+    l1 *= al1;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= al0;
+      o[n][1] *= al0;
+      o[n][2] *= al1;
+      o[n][3] *= al1;
+    }
+    // P = exp(S - m) (scaled by 2^15 out of the f16 subnormal range) as A
+    // fragments of the 4 key slices, then O += P V
+#pragma unroll
+    for (int ks = 0; ks < kAttnTile / 16; ++ks) {
+      uint32_t ph[4], pl[4];
+      float p[2][4];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float sv = sc[2 * ks + hh][e];
+          const float pe = sv == -INFINITY ? 0.0f : expf(sv - (e < 2 ? nm0 : nm1));
+          p[hh][e] = pe;
+          if (e < 2) l0 += pe;
+          else l1 += pe;
+        }
+      f16_split2(p[0][0] * kPScale, p[0][1] * kPScale, ph[0], pl[0]);
+      f16_split2(p[0][2] * kPScale, p[0][3] * kPScale, ph[1], pl[1]);
+      f16_split2(p[1][0] * kPScale, p[1][1] * kPScale, ph[2], pl[2]);
+      f16_split2(p[1][2] * kPScale, p[1][3] * kPScale, ph[3], pl[3]);
+      const uint32_t va = smem_u32(V) + (16 * ks + l16) * 128;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        uint32_t b0, b1;
+        ldsm_x2_t(b0, b1, va + (n >> 3) * (kAttnTile * 128) + (((n ^ l16) & 7) << 4));
+        mma_16816(o[n], ph, b0, b1);
+        mma_16816(o[n], pl, b0, b1);
+      }
+    }
+    __syncthreads();  // buffer b is free for the tile after next
+  }
+  // row sums across the quad, normalise, store
+  l0 += __shfl_xor_sync(B2Q_FULL, l0, 1);
+  l0 += __shfl_xor_sync(B2Q_FULL, l0, 2);
+  l1 += __shfl_xor_sync(B2Q_FULL, l1, 1);
+  l1 += __shfl_xor_sync(B2Q_FULL, l1, 2);
+  const float i0 = (1.0f / kPScale) * (1.0f / fmaxf(l0, 1e-12f)), i1 = (1.0f / kPScale) * (1.0f / fmaxf(l1, 1e-12f));
+  float* o0 = out + (int64_t)tok0 * H * HD + (g * G + r0 % G) * HD;
+  float* o1 = out + (int64_t)tok1 * H * HD + (g * G + r1 % G) * HD;
+#pragma unroll
+  for (int n = 0; n < 16; ++n) {
+    const int d = 8 * n + 2 * t;
+    if (tok0 < m) *reinterpret_cast<float2*>(o0 + d) = make_float2(o[n][0] * i0, o[n][1] * i0);
+    if (tok1 < m) *reinterpret_cast<float2*>(o1 + d) = make_float2(o[n][2] * i1, o[n][3] * i1);
+  }
+  pdl_launch_dependents();
+}
+
 // Seeded synthetic KV rows (benchmark set-up: a long context without a
 // prompt pass).  Element e of the K (kv = 0) or V (kv = 1) row of global KV
 // head h at position t in layer l is u * scale, u in [-1, 1) from a 64-bit

@@ -297,8 +297,23 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
                                (const float*)Lw.v_bias);
       if (err != cudaSuccess) return err;
     }
-    // attention (split over the cached tokens) + combine/quantise
-    {
+    // attention: prompt chunks on the tensor-core path take the 64-row
+    // prompt kernel (its float output feeds the tensor-core O projection);
+    // fewer tokens take the split + combine/quantise kernels of the decode
+    // path (their quantised output feeds the GEMV)
+    if (tc) {
+      float* aout = P > 1 ? M->attn_loc : M->attn;
+      const int qt = 64 / G;
+      cudaLaunchConfig_t cfg = lcfg(dim3(KVl, (m + qt - 1) / qt), dim3(128), kAttnPrefillSmem, st, attr, pdl);
+      launch_counted(e, 1);
+      auto kern = G == 4 ? attn_prefill_kernel<4> : G == 8 ? attn_prefill_kernel<8>
+                : G == 2 ? attn_prefill_kernel<2> : attn_prefill_kernel<1>;
+      err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnPrefillSmem);
+      if (err == cudaSuccess)
+        err = cudaLaunchKernelEx(&cfg, kern, (const float*)M->qkv, m, Hl, KVl, (const int*)M->pos, c.max_seq,
+                                 (const void*)Lw.tmk, (const void*)Lw.tmv, scale, aout);
+      if (err != cudaSuccess) return err;
+    } else {
       float* aout = P > 1 ? M->attn_loc : M->attn;
       const size_t tile = kAttnAlignPad + (G == 4 ? sizeof(AttnTile<4>) : G == 8 ? sizeof(AttnTile<8>)
                                            : G == 2 ? sizeof(AttnTile<2>) : sizeof(AttnTile<1>));
