@@ -708,10 +708,34 @@ __device__ __noinline__ void decode_producer(const DecodeArgs& a, uint8_t* ring,
   P.pol = make_evict_first_policy();
   P.qs = qs;
   P.qe = qe;
+  // this CTA's attention work items (the consumers' grouping)
+  const int nz = a.pos / kAttnTile + 1;
+  const int tpg = attn_group_tiles(nz, a.KV, (int)gridDim.x), ng = (nz + tpg - 1) / tpg;
   for (int l = 0; l < a.n_layers; ++l) {
     const DecLayer& Ly = a.layers[l];
 #pragma unroll 1
     for (int p = 0; p < kDecPhases; ++p) {
+      if (p == 1 && tpg == 1) {
+        // short contexts (one key tile per attention item), once the layer's
+        // q/k/v weights are issued: the cached K/V tile of each of this
+        // CTA's attention items into L2, so the copy that opens the item
+        // finds it there (the K and the V rows of a 64-key tile are 16 KB
+        // each, contiguous; the current token's row is written by the item
+        // itself).  Measured +0.6 % at 512 keys (8B).  With several tiles
+        // per item (8192 keys, 70B) prefetching all of them cost 1 % and the
+        // first one alone 0.35 %: those groups copy each tile one ahead.
+        for (int it = blockIdx.x; it < a.KV * ng; it += gridDim.x) {
+          const int g = it / ng, zb = (it % ng) * tpg, ze = min(nz, zb + 1);
+          for (int z = zb; z < ze; ++z) {
+            const int rows = min(kAttnTile, a.max_seq - z * kAttnTile);  // inside this head's rows
+            if (rows <= 0) break;
+            const int64_t r0 = ((int64_t)g * a.max_seq + z * kAttnTile) * kHeadDim;
+            const uint32_t bytes = (uint32_t)rows * kHeadDim * 2;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(Ly.kc + r0), "r"(bytes) : "memory");
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(Ly.vc + r0), "r"(bytes) : "memory");
+          }
+        }
+      }
       if (!produce_phase(P, Ly.ph[p])) return;
       B2Q_PTRACE(l * kDecPhases + p);
       B2Q_DBG(true, l * kDecPhases + p, P.j, P.wo, P.oldest, 0);

@@ -21,7 +21,7 @@
 //               each stage back to its producers;
 //   warps 0-3   after the last stage, read the accumulator out of TMEM
 //               (tcgen05.ld, one weight row per thread) and store f32 partial
-//               sums [split][token][row] for gemm_reduce_kernel.
+//               sums [split][token][row] for tc_reduce_kernel.
 // Precision: every f32 operand v is carried as two f16 values, hi = f16(v)
 // and lo = f16(v - hi), and each k16 slice is three MMAs, hi*hi + lo*hi +
 // hi*lo (the lo*lo term, ~2^-22 relative, is dropped): the products are
@@ -566,24 +566,55 @@ __global__ void tc_act_kernel(const float* __restrict__ x, int ldx, int m, int k
 // y[t][col0 + r] = epi(inv[t] * sum_s part[s][t][r]) for t < m, r < n;
 // partial rows have stride ldp.  EPI kEpiStore / kEpiAdd (y +=) /
 // kEpiSwiglu (part2 = up partials: silu(g) * u).
-template <int EPI>
+// Grid (column blocks, m tokens): token t = blockIdx.y; each thread takes V
+// consecutive columns (V = 4: 16-byte loads and stores, used when every row
+// start is 16-byte aligned).  Per element the splits are added in order s =
+// 0, 1, ..., as one thread per element would.
+template <int EPI, int V>
 __global__ void tc_reduce_kernel(const float* __restrict__ part, const float* __restrict__ part2, int splits,
                                  int mpad, int m, int n, int ldp, const float* __restrict__ inv,
                                  float* __restrict__ y, int ldy, int col0) {
   pdl_wait();
-  const int64_t total = (int64_t)m * n;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int t = (int)(i / n), r = (int)(i - (int64_t)t * n);
-    float g = 0.0f, u = 0.0f;
+  const int t = blockIdx.y;
+  const float it = inv[t];
+  float* yr = y + (size_t)t * ldy + col0;
+  for (int r = (blockIdx.x * blockDim.x + threadIdx.x) * V; r < n; r += gridDim.x * blockDim.x * V) {
+    float g[V], u[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) g[j] = u[j] = 0.0f;
     for (int s = 0; s < splits; ++s) {
-      g += part[((size_t)s * mpad + t) * ldp + r];
-      if (EPI == kEpiSwiglu) u += part2[((size_t)s * mpad + t) * ldp + r];
+      const size_t off = ((size_t)s * mpad + t) * ldp + r;
+      if (V == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(part + off);
+        g[0] += a.x; g[1] += a.y; g[2] += a.z; g[3] += a.w;
+        if (EPI == kEpiSwiglu) {
+          const float4 b = *reinterpret_cast<const float4*>(part2 + off);
+          u[0] += b.x; u[1] += b.y; u[2] += b.z; u[3] += b.w;
+        }
+      } else {
+        g[0] += part[off];
+        if (EPI == kEpiSwiglu) u[0] += part2[off];
+      }
     }
-    g *= inv[t];
-    float* yp = y + (size_t)t * ldy + col0 + r;
-    if (EPI == kEpiSwiglu) *yp = silu_f(g) * (u * inv[t]);
-    else if (EPI == kEpiAdd) *yp += g;
-    else *yp = g;
+    float o[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const float gg = g[j] * it;
+      if (EPI == kEpiSwiglu) o[j] = silu_f(gg) * (u[j] * it);
+      else o[j] = gg;
+    }
+    if (V == 4) {
+      float4* yp = reinterpret_cast<float4*>(yr + r);
+      if (EPI == kEpiAdd) {
+        const float4 prev = *yp;
+        *yp = make_float4(prev.x + o[0], prev.y + o[1], prev.z + o[2], prev.w + o[3]);
+      } else {
+        *yp = make_float4(o[0], o[1], o[2], o[3]);
+      }
+    } else {
+      if (EPI == kEpiAdd) yr[r] += o[0];
+      else yr[r] = o[0];
+    }
   }
   pdl_launch_dependents();
 }

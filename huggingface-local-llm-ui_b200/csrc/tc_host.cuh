@@ -87,11 +87,19 @@ static cudaError_t tc_launch_gemm(b2q_engine* e, const b2q_weight* const* ws, co
 template <int EPI>
 static cudaError_t tc_launch_reduce(b2q_engine* e, const TcPlan& p, int m, int n, int ldp, const float* part2,
                                     float* y, int ldy, int col0, cudaStream_t st) {
-  const int64_t total = (int64_t)m * n;
-  const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)e->num_sms * 8);
+  // 16-byte vectors when every row of the partials and of y starts aligned
+  const bool v4 = n % 4 == 0 && ldp % 4 == 0 && ldy % 4 == 0 && col0 % 4 == 0 &&
+                  ((reinterpret_cast<uintptr_t>(e->tc.part) | reinterpret_cast<uintptr_t>(part2) |
+                    reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  const int per = 256 * (v4 ? 4 : 1);
+  const dim3 grid((unsigned)std::min(64, (n + per - 1) / per), (unsigned)m);
   launch_counted(e, 1);
-  tc_reduce_kernel<EPI><<<blocks, 256, 0, st>>>(e->tc.part, part2, p.splits, p.mpad, m, n, ldp, e->tc.inv, y,
-                                                ldy, col0);
+  if (v4)
+    tc_reduce_kernel<EPI, 4><<<grid, 256, 0, st>>>(e->tc.part, part2, p.splits, p.mpad, m, n, ldp, e->tc.inv, y,
+                                                   ldy, col0);
+  else
+    tc_reduce_kernel<EPI, 1><<<grid, 256, 0, st>>>(e->tc.part, part2, p.splits, p.mpad, m, n, ldp, e->tc.inv, y,
+                                                   ldy, col0);
   return cudaGetLastError();
 }
 
