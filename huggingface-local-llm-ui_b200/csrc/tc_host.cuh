@@ -9,10 +9,11 @@ struct TcPlan {
 };
 
 // Token tiles of at most 256 (balanced), k-stages of 64, and a split-K
-// factor of one split per 16 stages (at most 8).  The split depends on k
-// only, so every output element is summed in the same order whatever the
-// number of rows (a tensor-parallel shard gives the same bits as the whole
-// weight) or tokens.
+// factor of about one split per 24 stages (at most 16): long enough k-ranges
+// to keep a CTA's pipeline full, few enough partial sums.  The split depends
+// on k only, so every output element is summed in the same order whatever
+// the number of rows (a tensor-parallel shard gives the same bits as the
+// whole weight) or tokens.
 static TcPlan tc_plan(int m, int64_t n, int64_t k, int num_sms) {
   (void)num_sms;
   TcPlan p;
@@ -21,7 +22,7 @@ static TcPlan tc_plan(int m, int64_t n, int64_t k, int num_sms) {
   p.mpad = p.tiles * p.N;
   p.KS = (int)((k + kTcK - 1) / kTcK);
   p.rowtiles = (int)((n + kTcM - 1) / kTcM);
-  p.splits = std::max(1, std::min(8, p.KS / 16));
+  p.splits = std::max(1, std::min(16, (p.KS + 12) / 24));
   return p;
 }
 
