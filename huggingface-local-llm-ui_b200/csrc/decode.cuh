@@ -111,6 +111,8 @@ struct DecodeArgs {
   int pos;                // its position
   float* part;            // [H][nsplit][kPartStride] attention split partials
   int nsplit;
+  unsigned long long* attnpll;  // [H][attn_ngmax][kPartStride] tagged group partials (G >= 8)
+  int attn_ngmax;               // groups per KV head at most: max(1, grid / KV)
   DecSync* sync;
   // [n_layers][KV] attention splits finished per layer and KV head (the
   // last split to finish merges and returns the word to zero; the next use
@@ -1054,93 +1056,148 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
                               [&](int r, int, int, float mt, float lt, float ot) { run.fold(r, mt, lt, ot); });
   }
   B2Q_FTRACE(tl, 11);
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int i = gt + kAttnThreads * r;
-    if (i < G * HD) attn_store_partial(a.part, g, G, j, a.nsplit, i / HD, i % HD, run.m[r], run.l[r], run.o[r]);
-  }
-  // the last group of this KV head to finish merges all of them
-  consumer_sync();
-  B2Q_FTRACE(tl, 12);
-  if (gt == 0) {
-    __threadfence();
-    const unsigned int old = atomicAdd(&a.attn_cnt[tl * KV + g], 1u);
-    *s_last = old == (unsigned int)(ng - 1);
-  }
-  consumer_sync();
-  B2Q_FTRACE(tl, 13);
-  if (*s_last) {
-    // merge (attn_combine_kernel's arithmetic, same order): the partials of
-    // up to kZc groups per head are brought into the idle tile with bulk
-    // copies (one round trip), then reduced in group order
-    __threadfence();
-    const int nsplit = a.nsplit;
-    constexpr int kZc = (2 * kAttnTile * HD / 2) / (G * kPartStride);  // splits per chunk (T.k + T.v)
-    float* pb = reinterpret_cast<float*>(T.k);                          // [G][zc][kPartStride]
-    float M[R], Ls[R], O[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      M[r] = -INFINITY;
-      Ls[r] = 0.0f;
-      O[r] = 0.0f;
-    }
-    if (ng > kZc) {  // many groups: the maxima of every partial first, 8 loads in flight
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int i = gt + kAttnThreads * r;
-        if (i >= G * HD) continue;
-        const float* ph = a.part + (int64_t)(g * G + i / HD) * nsplit * kPartStride;
-        for (int zz0 = 0; zz0 < ng; zz0 += 8) {
-          float mv[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) mv[u] = zz0 + u < ng ? __ldcg(ph + (zz0 + u) * kPartStride) : -INFINITY;
-#pragma unroll
-          for (int u = 0; u < 8; ++u) M[r] = fmaxf(M[r], mv[u]);
-        }
-      }
-    }
-    for (int z0 = 0; z0 < ng; z0 += kZc) {
-      const int zn = min(kZc, ng - z0);
-      if (gt == 0) {
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-        fence_proxy_async_smem();
-        const uint32_t bytes = (uint32_t)zn * kPartStride * 4;
-        mbar_arrive_expect_tx(bar, bytes * G);
-        for (int h = 0; h < G; ++h)
-          bulk_g2s(pb + h * zn * kPartStride, a.part + ((int64_t)(g * G + h) * nsplit + z0) * kPartStride, bytes, bar);
-      }
-      mbar_wait_bounded(bar, (uint32_t)(uses & 1));
-      ++uses;
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int i = gt + kAttnThreads * r;
-        if (i >= G * HD) continue;
-        const int h = i / HD, d = i % HD;
-        const float* ph = pb + h * zn * kPartStride;
-        if (ng <= kZc)  // one chunk holds every partial: maxima from shared memory
-          for (int zz = 0; zz < zn; ++zz) M[r] = fmaxf(M[r], ph[zz * kPartStride]);
-        for (int zz = 0; zz < zn; ++zz) {
-          const float m = ph[zz * kPartStride];
-          const float f = m == -INFINITY ? 0.0f : expf(m - M[r]);
-          Ls[r] = fmaf(f, ph[zz * kPartStride + 1], Ls[r]);
-          O[r] = fmaf(f, ph[zz * kPartStride + 2 + d], O[r]);
-        }
-      }
-      consumer_sync();  // chunk consumed before the next copy lands
-    }
+  if constexpr (G >= 8) {
+    // long-context widths (eight query heads per KV head, many groups per
+    // head): the group partials {max, sum, O[128]} are stored tagged, and
+    // the ng groups of the head each finalise a slice of its G*128 outputs
+    // from every group's partial (polled, bounded) -- no counter, no fence,
+    // no serial merge.  attn_combine_kernel's arithmetic, same group order.
+    const uint32_t tp = a.tag0 + (uint32_t)(5 * tl + 2);
+    const int ngm = a.attn_ngmax;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int i = gt + kAttnThreads * r;
-      if (i < G * HD) {
-        const float v = O[r] * (1.0f / fmaxf(Ls[r], 1e-12f));
-        const int oi = (g * G + i / HD) * HD + i % HD;  // this rank's heads, local
-        if (b2q_check(oi < a.H * HD, kChkTag)) ll_store(a.attnll + oi, v, a.tag0 + (uint32_t)(5 * tl + 2));
+      if (i < G * HD && b2q_check(j < ngm, kChkPart)) {
+        const int h = i / HD, d = i % HD;
+        unsigned long long* pp = a.attnpll + ((int64_t)(g * G + h) * ngm + j) * kPartStride;
+        if (d == 0) {
+          ll_store(pp, run.m[r], tp);
+          ll_store(pp + 1, run.l[r], tp);
+        }
+        ll_store(pp + 2 + d, run.o[r], tp);
       }
     }
-    if (gt == 0) a.attn_cnt[tl * KV + g] = 0u;
+    B2Q_FTRACE(tl, 12);
+    consumer_sync();  // the tile buffers are free for the gathered partials
+    const int n = G * HD;
+    const int e0 = n * j / ng, ne = n * (j + 1) / ng - e0, np = ne * ng;
+    float* sm_m = reinterpret_cast<float*>(T.k);
+    float* sm_l = sm_m + np;
+    float* sm_o = sm_l + np;
+    for (int i = gt; i < np; i += kAttnThreads) {
+      const int el = i / ng, z = i - el * ng, e = e0 + el;
+      const unsigned long long* pw = a.attnpll + ((int64_t)(g * G + e / HD) * ngm + z) * kPartStride;
+      const unsigned long long u0 = ld_relaxed_u64(pw), u1 = ld_relaxed_u64(pw + 1),
+                               u2 = ld_relaxed_u64(pw + 2 + e % HD);
+      sm_m[i] = ll_value(pw, u0, tp, s_ok);
+      sm_l[i] = ll_value(pw + 1, u1, tp, s_ok);
+      sm_o[i] = ll_value(pw + 2 + e % HD, u2, tp, s_ok);
+    }
+    consumer_sync();
+    B2Q_FTRACE(tl, 13);
+    for (int el = gt; el < ne; el += kAttnThreads) {
+      const float* m = sm_m + el * ng;
+      float M = -INFINITY;
+      for (int z = 0; z < ng; ++z) M = fmaxf(M, m[z]);
+      float L = 0.0f, O = 0.0f;
+      for (int z = 0; z < ng; ++z) {
+        const float f = m[z] == -INFINITY ? 0.0f : expf(m[z] - M);
+        L = fmaf(f, sm_l[el * ng + z], L);
+        O = fmaf(f, sm_o[el * ng + z], O);
+      }
+      const int oi = g * n + e0 + el;  // this rank's heads, local
+      if (b2q_check(oi < a.H * HD, kChkTag)) ll_store(a.attnll + oi, O * (1.0f / fmaxf(L, 1e-12f)), tp);
+    }
     B2Q_FTRACE(tl, 14);
+  } else {
+  #pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int i = gt + kAttnThreads * r;
+      if (i < G * HD) attn_store_partial(a.part, g, G, j, a.nsplit, i / HD, i % HD, run.m[r], run.l[r], run.o[r]);
+    }
+    // the last group of this KV head to finish merges all of them
+    consumer_sync();
+    B2Q_FTRACE(tl, 12);
+    if (gt == 0) {
+      __threadfence();
+      const unsigned int old = atomicAdd(&a.attn_cnt[tl * KV + g], 1u);
+      *s_last = old == (unsigned int)(ng - 1);
+    }
+    consumer_sync();
+    B2Q_FTRACE(tl, 13);
+    if (*s_last) {
+      // merge (attn_combine_kernel's arithmetic, same order): the partials of
+      // up to kZc groups per head are brought into the idle tile with bulk
+      // copies (one round trip), then reduced in group order
+      __threadfence();
+      const int nsplit = a.nsplit;
+      constexpr int kZc = (2 * kAttnTile * HD / 2) / (G * kPartStride);  // splits per chunk (T.k + T.v)
+      float* pb = reinterpret_cast<float*>(T.k);                          // [G][zc][kPartStride]
+      float M[R], Ls[R], O[R];
+  #pragma unroll
+      for (int r = 0; r < R; ++r) {
+        M[r] = -INFINITY;
+        Ls[r] = 0.0f;
+        O[r] = 0.0f;
+      }
+      if (ng > kZc) {  // many groups: the maxima of every partial first, 8 loads in flight
+  #pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int i = gt + kAttnThreads * r;
+          if (i >= G * HD) continue;
+          const float* ph = a.part + (int64_t)(g * G + i / HD) * nsplit * kPartStride;
+          for (int zz0 = 0; zz0 < ng; zz0 += 8) {
+            float mv[8];
+  #pragma unroll
+            for (int u = 0; u < 8; ++u) mv[u] = zz0 + u < ng ? __ldcg(ph + (zz0 + u) * kPartStride) : -INFINITY;
+  #pragma unroll
+            for (int u = 0; u < 8; ++u) M[r] = fmaxf(M[r], mv[u]);
+          }
+        }
+      }
+      for (int z0 = 0; z0 < ng; z0 += kZc) {
+        const int zn = min(kZc, ng - z0);
+        if (gt == 0) {
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          fence_proxy_async_smem();
+          const uint32_t bytes = (uint32_t)zn * kPartStride * 4;
+          mbar_arrive_expect_tx(bar, bytes * G);
+          for (int h = 0; h < G; ++h)
+            bulk_g2s(pb + h * zn * kPartStride, a.part + ((int64_t)(g * G + h) * nsplit + z0) * kPartStride, bytes, bar);
+        }
+        mbar_wait_bounded(bar, (uint32_t)(uses & 1));
+        ++uses;
+  #pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int i = gt + kAttnThreads * r;
+          if (i >= G * HD) continue;
+          const int h = i / HD, d = i % HD;
+          const float* ph = pb + h * zn * kPartStride;
+          if (ng <= kZc)  // one chunk holds every partial: maxima from shared memory
+            for (int zz = 0; zz < zn; ++zz) M[r] = fmaxf(M[r], ph[zz * kPartStride]);
+          for (int zz = 0; zz < zn; ++zz) {
+            const float m = ph[zz * kPartStride];
+            const float f = m == -INFINITY ? 0.0f : expf(m - M[r]);
+            Ls[r] = fmaf(f, ph[zz * kPartStride + 1], Ls[r]);
+            O[r] = fmaf(f, ph[zz * kPartStride + 2 + d], O[r]);
+          }
+        }
+        consumer_sync();  // chunk consumed before the next copy lands
+      }
+  #pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int i = gt + kAttnThreads * r;
+        if (i < G * HD) {
+          const float v = O[r] * (1.0f / fmaxf(Ls[r], 1e-12f));
+          const int oi = (g * G + i / HD) * HD + i % HD;  // this rank's heads, local
+          if (b2q_check(oi < a.H * HD, kChkTag)) ll_store(a.attnll + oi, v, a.tag0 + (uint32_t)(5 * tl + 2));
+        }
+      }
+      if (gt == 0) a.attn_cnt[tl * KV + g] = 0u;
+      B2Q_FTRACE(tl, 14);
+    }
   }
-  consumer_sync();  // the tile and s_last are reused by the next item
+  consumer_sync();  // the tile (and s_last) are reused by the next item
 }
 
 // ---------------------------------------------------------------------------

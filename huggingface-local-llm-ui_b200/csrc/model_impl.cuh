@@ -724,10 +724,14 @@ static cudaError_t setup_decode(b2q_model* M) {
   if (err == cudaSuccess) err = dalloc(&M->dec_sync, 1);
   if (err == cudaSuccess) err = dalloc(&M->dec_attn_cnt, (size_t)c.n_layers * KV);
   // tagged vectors: x (rounded up to even: the residual copy reads pairs),
-  // q|k|v and the attention output of this rank's heads
+  // q|k|v and the attention output of this rank's heads, and (eight query
+  // heads per KV head) the attention group partials of its heads, at most
+  // max(1, grid / KV) groups per head
+  const int ngmax = std::max(1, grid / KV);
   const size_t ll_x = (size_t)round_up_int(c.n_embd, 2), ll_qkv = (size_t)(H + 2 * KV) * hd, ll_attn = (size_t)H * hd;
-  if (err == cudaSuccess) err = dalloc(&M->dec_ll, ll_x + ll_qkv + ll_attn);
-  M->dec_ll_words = ll_x + ll_qkv + ll_attn;
+  const size_t ll_part = G >= 8 ? (size_t)H * ngmax * kPartStride : 0;
+  if (err == cudaSuccess) err = dalloc(&M->dec_ll, ll_x + ll_qkv + ll_attn + ll_part);
+  M->dec_ll_words = ll_x + ll_qkv + ll_attn + ll_part;
   const XBlock xl = xblock_layout(c.n_embd, c.n_heads * hd, c.n_ff, c.n_vocab, P, grid);
   if (err == cudaSuccess) err = dalloc(reinterpret_cast<uint8_t**>(&M->dec_xblock), xl.total);
   if (err != cudaSuccess) return err;
@@ -774,6 +778,8 @@ static cudaError_t setup_decode(b2q_model* M) {
   a.xll = M->dec_ll;
   a.qkvll = M->dec_ll + ll_x;
   a.attnll = M->dec_ll + ll_x + ll_qkv;
+  a.attnpll = M->dec_ll + ll_x + ll_qkv + ll_attn;
+  a.attn_ngmax = ngmax;
   a.argmax = M->argmax;
   a.tp = P;
   a.rank = rk;
