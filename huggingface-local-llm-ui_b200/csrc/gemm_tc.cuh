@@ -48,7 +48,7 @@ constexpr int kTcThreads = (kTcDequantWarps + 2) * 32;
 constexpr int kTcABytes = kTcM * kTcK * 2;  // one f16 image of the weight tile: 16 KB
 constexpr int kTcMinTokens = 16;   // below this the GEMV path is used
 constexpr int kTcSmemBudget = 200 * 1024;
-constexpr int kTcPrefetch = 4;     // stages of raw weight bytes loaded ahead (registers)
+constexpr int kTcPrefetch = 3;     // stages of raw weight bytes loaded ahead (registers)
 
 // Bytes of the activation stage (hi and lo images of N tokens x 64 k).
 __host__ __device__ inline int tc_b_bytes(int N) { return 2 * N * kTcK * 2; }
