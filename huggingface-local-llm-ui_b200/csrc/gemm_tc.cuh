@@ -313,9 +313,11 @@ template <int DT>
 __device__ __forceinline__ void tc_produce(const WeightDev& w, int row0, int ks0, int nst, int S, uint8_t* As,
                                            uint64_t* empty, uint64_t* a_full, volatile int* s_ok) {
   const int d = threadIdx.x, lane = threadIdx.x & 31;
-  // lanes 4i..4i+3 take the four quarters of one tile row, so a warp's raw
-  // loads cover eight rows with whole 32-byte sectors
-  const int qq = d & 3, r = d >> 2;
+  // a warp takes eight tile rows and all four quarters of each, so its raw
+  // loads cover eight rows with whole 32-byte sectors; lanes 8q..8q+7 take
+  // quarter q of the eight rows, so each 8-lane phase of an image store
+  // writes one 128-byte core matrix (eight rows, distinct banks)
+  const int qq = (d >> 3) & 3, r = ((d >> 5) << 3) | (d & 7);
   const int64_t R = (int64_t)row0 + r;
   TcRaw raw[kTcPrefetch];
 #pragma unroll
