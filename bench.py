@@ -19,8 +19,9 @@ prompt is prefilled, then one step = one greedy decode token at batch 1.
               host start skew stays out of every rank's events.  4.9 GB of
               weights are read per step, far above L2 (126 MB).
 * e2e      -- the same through the host API b2q_forward: the token id copied
-              in from pinned host memory and the logits [128256] f32 copied
-              back every step; host wall clock, max over ranks.
+              in from host memory and the logits [128256] f32 copied back into
+              a page-locked array every step, with the greedy next token that
+              b2q_forward returns beside them; host wall clock, max over ranks.
 * roofline -- the dominant kernel, decode_kernel (the only kernel of a step):
               algorithmic bytes of one step on this rank (the weight rows or
               columns it owns, one token_embd row, the norms and the f16 K/V
@@ -467,16 +468,18 @@ def timed_decode(m, tok, pos, steps, sp, stream, dist, dev, clk_dev):
 
 
 def timed_e2e(m, tok0, pos, steps, dist, dev):
-    """b2q_forward with host token ids and host logits every step; host wall
-    clock, max over ranks."""
+    """b2q_forward with host token ids and host logits every step (into a
+    page-locked array; the next token is the library's greedy argmax, which
+    b2q_forward returns beside the logits); host wall clock, max over
+    ranks."""
     import torch
     nxt = tok0
+    logits = torch.empty(m.cfg["n_vocab"], dtype=torch.float32, pin_memory=True).numpy()
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(steps):
-        logits = m.forward([nxt], pos)
-        nxt = int(np.argmax(logits))
+        nxt = m.forward_into([nxt], pos, logits)
         pos += 1
     s = time.perf_counter() - t0
     if dist:
@@ -569,8 +572,9 @@ def run_model(args, name, engine, rank, world, local, dist, dev, stream, orc):
     value = steps / (ms / 1000.0)
     e2e_s, pos = timed_e2e(m, int(tok[0].item()), pos, e2e_steps, dist, dev)
     e2e = {"value": e2e_steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4,
-           "d2h_bytes_per_step": 4 * cfg["n_vocab"],
-           "note": "b2q_forward with host token ids and host logits; host wall clock, max over ranks"}
+           "d2h_bytes_per_step": 4 * cfg["n_vocab"] + 4,
+           "note": "b2q_forward with host token ids and host logits (a page-locked array) and the greedy "
+                   "argmax it returns; host wall clock, max over ranks"}
     peak, peak_kind = measured_peaks()
     ctx = pos_t0 + steps // 2
     step_bytes = step_algorithmic_bytes(cfg, rank, world, ctx)

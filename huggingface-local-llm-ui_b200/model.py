@@ -145,6 +145,19 @@ class StandardNativeEngine:
                                 logits.ctypes.data_as(C.POINTER(C.c_float)), None))
         return logits
 
+    def forward_into(self, tokens, start_pos: int, logits: np.ndarray) -> int:
+        """forward with the logits written into the caller's float32 array
+        (page-locked host memory makes the copy a direct DMA) and the greedy
+        next token (the library's device argmax, first index of the maximum)
+        returned."""
+        if logits.dtype != np.float32 or logits.size < self.cfg["n_vocab"] or not logits.flags.c_contiguous:
+            raise ValueError("logits must be a contiguous float32 array of n_vocab elements")
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = C.c_uint32()
+        check(lib().b2q_forward(self._h, t.ctypes.data_as(C.POINTER(C.c_uint32)), t.size, start_pos,
+                                logits.ctypes.data_as(C.POINTER(C.c_float)), C.byref(out)))
+        return int(out.value)
+
     def forward_argmax(self, tokens, start_pos: int) -> int:
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
         out = C.c_uint32()
