@@ -52,6 +52,29 @@ def test_gqa_ratios(engine, orc, pkg, gqa):
     assert rel_l2(dev.forward([35], 5), ref.forward_f64([35], 5, kv_f16=True)) <= TOL
 
 
+@pytest.mark.parametrize("gqa", [1, 2, 4, 8])
+def test_prompt_attention_rows_and_chunks(engine, orc, pkg, gqa):
+    """The prompt-pass attention (16 or more tokens: 64 query rows per CTA,
+    64 / G tokens): prompts that fill no CTA exactly (16, 47 and 130 tokens)
+    and a two-chunk prompt whose second chunk starts at position 256, for
+    every GQA ratio, against the fp64 forward."""
+    cfg = dict(TOY, n_heads=8, n_kv_heads=8 // gqa, n_layers=2)
+    dev, ref = _pair(engine, orc, pkg, cfg, seed=40 + gqa, max_seq=512)
+    rng = np.random.default_rng(gqa)
+    pos = 0
+    for n in (16, 47, 130):
+        toks = rng.integers(0, cfg["n_vocab"], n).tolist()
+        a = dev.forward(toks, pos)
+        b = ref.forward_f64(toks, pos, kv_f16=True)
+        assert rel_l2(a, b) <= TOL, f"G={gqa} {n} tokens at {pos}: {rel_l2(a, b)}"
+        pos += n
+    toks = rng.integers(0, cfg["n_vocab"], 300).tolist()
+    dev2, ref2 = _pair(engine, orc, pkg, cfg, seed=40 + gqa, max_seq=512)
+    a = dev2.forward(toks, 0)
+    b = ref2.forward_f64(toks, 0, kv_f16=True)
+    assert rel_l2(a, b) <= TOL, f"G={gqa} 300 tokens: {rel_l2(a, b)}"
+
+
 def test_long_prompt_chunks_and_splits(engine, orc, pkg):
     """A prompt longer than one forward chunk (256 tokens; the second one
     ragged) and than one attention split (64 keys) exercises the chunked
