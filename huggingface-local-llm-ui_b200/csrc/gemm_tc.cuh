@@ -567,6 +567,72 @@ __global__ void tc_act_kernel(const float* __restrict__ x, int ldx, int m, int k
   pdl_launch_dependents();
 }
 
+// RMSNorm of x's rows (rms_norm_rows, inference.rs:1501-1512) written
+// straight into the activation images: rmsnorm_quant_kernel's f32 values
+// (the same reduction order, (x * inv) * w with two roundings), then
+// tc_act_kernel's per-token power-of-two scaling and hi/lo split, so the
+// images hold the bits the two kernels in sequence give, without the f32 row
+// going through global memory.  One block of 1024 threads per token
+// (padding tokens write zeros); k floats of dynamic shared memory.
+__global__ void __launch_bounds__(1024) tc_rmsnorm_act_kernel(const float* __restrict__ x, int ldx,
+                                                              const float* __restrict__ w, float eps, int m, int k,
+                                                              int KS, int N, __half* __restrict__ img,
+                                                              float* __restrict__ inv) {
+  pdl_wait();
+  extern __shared__ float vrow[];
+  __shared__ float part[32];
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  const bool live = t < m;
+  const float* xr = x + (size_t)(live ? t : 0) * ldx;
+  float ss = 0.0f;
+  if (live)
+    for (int e = threadIdx.x; e < k; e += blockDim.x) ss = fmaf(xr[e], xr[e], ss);
+  ss = warp_sum(ss);
+  if (lane == 0) part[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    float v = lane < nw ? part[lane] : 0.0f;
+    v = warp_sum(v);
+    if (lane == 0) part[0] = v;
+  }
+  __syncthreads();
+  const float rinv = 1.0f / sqrtf(part[0] / (float)k + eps);
+  float mx = 0.0f;  // fmaxf leaves NaN out
+  for (int e = threadIdx.x; e < k; e += blockDim.x) {
+    const float v = live ? __fmul_rn(__fmul_rn(xr[e], rinv), w[e]) : 0.0f;
+    vrow[e] = v;
+    mx = fmaxf(mx, fabsf(v));
+  }
+  mx = warp_max(mx);
+  __syncthreads();  // part[0] read by every thread above
+  if (lane == 0) part[warp] = mx;
+  __syncthreads();
+  mx = lane < nw ? part[lane] : 0.0f;
+  mx = warp_max(mx);
+  float sc = 1.0f, iv = 1.0f;
+  if (mx > 0.0f && mx <= 3.0e38f) {
+    int e;
+    frexpf(mx, &e);
+    sc = ldexpf(1.0f, 14 - e);
+    iv = ldexpf(1.0f, e - 14);
+  }
+  if (threadIdx.x == 0 && live) inv[t] = iv;
+  const int tile = t / N, tt = t - tile * N;
+  for (int ch = threadIdx.x; ch < KS * 8; ch += blockDim.x) {
+    const int ks = ch >> 3, kk = (ch & 7) * 8, k0 = ks * kTcK + kk;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float u = k0 + e < k ? vrow[k0 + e] * sc : 0.0f;
+      v[e] = u != u ? 0.0f : u;  // a NaN element contributes nothing
+    }
+    uint8_t* stage = reinterpret_cast<uint8_t*>(img) + ((size_t)tile * KS + ks) * (size_t)tc_b_bytes(N);
+    st_img8(stage, N * kTcK * 2, tt, kk, N, v);
+  }
+  pdl_launch_dependents();
+}
+
 // y[t][col0 + r] = epi(inv[t] * sum_s part[s][t][r]) for t < m, r < n;
 // partial rows have stride ldp.  EPI kEpiStore / kEpiAdd (y +=) /
 // kEpiSwiglu (part2 = up partials: silu(g) * u).

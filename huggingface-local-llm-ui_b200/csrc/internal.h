@@ -83,9 +83,12 @@ cudaError_t launch_quantize(b2q_engine* e, const float* x, int m, int k, XQBuf& 
 // Multi-token matmul on the tensor cores (gemm_tc.cuh): for weight i of
 // `ws`, y[t][col0[i] + r] = (X W_i^T)[t][r] (epi kEpiStore / kEpiAdd), or
 // with ws = {gate, up} and epi kEpiSwiglu, y[t][col0[0] + r] =
-// silu(g) * u.  x is [m][ldx] f32 on the device, m >= kTcMinTokens.
+// silu(g) * u.  x is [m][ldx] f32 on the device, m >= kTcMinTokens.  With
+// norm_w, x is taken through RMSNorm (weights norm_w, epsilon eps) first,
+// fused into the activation images.
 cudaError_t tc_matmul(b2q_engine* e, const float* x, int ldx, int m, int k, const b2q_weight* const* ws,
-                      int nw, int epi, float* y, int ldy, const int* col0, cudaStream_t st, bool pdl);
+                      int nw, int epi, float* y, int ldy, const int* col0, cudaStream_t st, bool pdl,
+                      const float* norm_w = nullptr, float eps = 0.0f);
 void tc_free(b2q_engine* e);
 // Next token from logits_dev [n] (SelfMadeSampler::sample); *rng_state is
 // advanced when the sampler draws.  Synchronous on `st`.

@@ -298,7 +298,6 @@ b2q_status b2q_model_finalize(b2q_model* M) {
     }
   }
   if (err == cudaSuccess) err = dalloc(&M->x, (size_t)mm * E);
-  if (err == cudaSuccess && mm >= kTcMinTokens) err = dalloc(&M->xn, (size_t)mm * E);
   if (err == cudaSuccess) err = dalloc(&M->qkv, (size_t)mm * (M->H_loc + 2 * M->KV_loc) * hd);
   if (err == cudaSuccess) err = dalloc(&M->attn, (size_t)mm * H * hd);
   if (err == cudaSuccess) err = dalloc(&M->attn_loc, (size_t)mm * M->H_loc * hd);
@@ -584,7 +583,7 @@ b2q_status b2q_model_destroy(b2q_model* M) {
   }
   b2q_weight_free(M->output);
   void* ps[] = {M->tok_raw, M->output_norm, M->x, M->qkv, M->attn, M->attn_loc, M->hbuf, M->h_loc,
-                M->y_loc, M->logits, M->logits_loc, M->part, M->tokens, M->argmax, M->pos, M->xn,
+                M->y_loc, M->logits, M->logits_loc, M->part, M->tokens, M->argmax, M->pos,
                 M->rope_cos, M->rope_sin, M->dec_layers, M->dec_tab, M->dec_sync, M->dec_xblock,
                 M->dec_attn_cnt, M->dec_ll, M->kv_maps};
   for (int p = 0; p < b2q::kMaxTp; ++p)

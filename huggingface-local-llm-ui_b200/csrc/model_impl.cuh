@@ -81,7 +81,6 @@ struct b2q_model {
   b2q::TpComm tp;
   // activations
   float* x = nullptr;       // [mmax][E] residual stream
-  float* xn = nullptr;      // [mmax][E] normalised rows (tensor-core prompt pass)
   float* qkv = nullptr;     // [mmax][(H_loc + 2 KV_loc) hd]
   float* attn = nullptr;    // [mmax][H hd] (gathered under TP)
   float* attn_loc = nullptr;
@@ -253,22 +252,24 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
   // prompt passes of kTcMinTokens or more tokens run their projections on
   // the tensor cores (gemm_tc.cuh); shorter passes and single-token steps
   // stream the weights through the GEMV
-  const bool tc = m >= kTcMinTokens && M->xn != nullptr;
+  const bool tc = m >= kTcMinTokens;
   for (int l = 0; l < c.n_layers; ++l) {
     LayerW& Lw = M->L[l];
-    // attention norm + quantise
-    {
+    // attention norm + quantise (on the tensor-core path the norm is fused
+    // into the projection's activation images)
+    if (!tc) {
       cudaLaunchConfig_t cfg = lcfg(dim3(m), dim3(1024), 0, st, attr, pdl);
       launch_counted(e, 1);
       err = cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, (const float*)M->x, E, 0,
-                               (const float*)Lw.attn_norm, E, c.rms_eps, M->xq_e.x, tc ? M->xn : (float*)nullptr);
+                               (const float*)Lw.attn_norm, E, c.rms_eps, M->xq_e.x, (float*)nullptr);
       if (err != cudaSuccess) return err;
     }
     // q, k, v projections (one launch, outputs interleaved per token)
     if (tc) {
       const b2q_weight* ws[3] = {Lw.q, Lw.k, Lw.v};
       const int col0[3] = {0, (int)Lw.q->n, (int)(Lw.q->n + Lw.k->n)};
-      err = tc_matmul(e, M->xn, E, m, E, ws, 3, kEpiStore, M->qkv, width_loc, col0, st, pdl);
+      err = tc_matmul(e, M->x, E, m, E, ws, 3, kEpiStore, M->qkv, width_loc, col0, st, pdl, Lw.attn_norm,
+                      c.rms_eps);
       if (err != cudaSuccess) return err;
     } else {
       GemvSeg segs[3];
@@ -371,12 +372,12 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
       }
       if (err != cudaSuccess) return err;
     }
-    // FFN norm + quantise
-    {
+    // FFN norm + quantise (fused into the images on the tensor-core path)
+    if (!tc) {
       cudaLaunchConfig_t cfg = lcfg(dim3(m), dim3(1024), 0, st, attr, pdl);
       launch_counted(e, 1);
       err = cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, (const float*)M->x, E, 0,
-                               (const float*)Lw.ffn_norm, E, c.rms_eps, M->xq_e.x, tc ? M->xn : (float*)nullptr);
+                               (const float*)Lw.ffn_norm, E, c.rms_eps, M->xq_e.x, (float*)nullptr);
       if (err != cudaSuccess) return err;
     }
     // gate/up with fused SwiGLU, per token
@@ -385,7 +386,7 @@ static cudaError_t forward_pass(b2q_model* M, int m, bool pdl, cudaStream_t st) 
       if (tc) {
         const b2q_weight* ws[2] = {Lw.gate, Lw.up};
         const int col0 = 0;
-        err = tc_matmul(e, M->xn, E, m, E, ws, 2, kEpiSwiglu, hout, Fl, &col0, st, pdl);
+        err = tc_matmul(e, M->x, E, m, E, ws, 2, kEpiSwiglu, hout, Fl, &col0, st, pdl, Lw.ffn_norm, c.rms_eps);
         if (err != cudaSuccess) return err;
       }
       for (int t = 0; t < (tc ? 0 : m); ++t) {

@@ -105,7 +105,8 @@ static cudaError_t tc_launch_reduce(b2q_engine* e, const TcPlan& p, int m, int n
 }
 
 cudaError_t tc_matmul(b2q_engine* e, const float* x, int ldx, int m, int k, const b2q_weight* const* ws, int nw,
-                      int epi, float* y, int ldy, const int* col0, cudaStream_t st, bool pdl) {
+                      int epi, float* y, int ldy, const int* col0, cudaStream_t st, bool pdl, const float* norm_w,
+                      float eps) {
   if (m < 1 || nw < 1 || (epi == kEpiSwiglu && nw != 2)) return cudaErrorInvalidValue;
   for (int i = 0; i < nw; ++i)
     if (ws[i]->k != k || !gemv_supported(ws[i]->dtype)) return cudaErrorInvalidValue;
@@ -139,7 +140,13 @@ cudaError_t tc_matmul(b2q_engine* e, const float* x, int ldx, int m, int k, cons
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    err = cudaLaunchKernelEx(&cfg, tc_act_kernel, x, ldx, m, k, p.KS, p.N, t.img, t.inv);
+    if (norm_w != nullptr) {  // x is the residual: RMSNorm fused into the images
+      cfg.blockDim = dim3(1024);
+      cfg.dynamicSmemBytes = (size_t)k * sizeof(float);
+      err = cudaLaunchKernelEx(&cfg, tc_rmsnorm_act_kernel, x, ldx, norm_w, eps, m, k, p.KS, p.N, t.img, t.inv);
+    } else {
+      err = cudaLaunchKernelEx(&cfg, tc_act_kernel, x, ldx, m, k, p.KS, p.N, t.img, t.inv);
+    }
     if (err != cudaSuccess) return err;
   }
   if (fused) {
