@@ -1119,8 +1119,14 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
     consumer_sync();
     B2Q_FTRACE(tl, 12);
     if (gt == 0) {
-      __threadfence();
-      const unsigned int old = atomicAdd(&a.attn_cnt[tl * KV + g], 1u);
+      // one acquire-release arrival: it releases this CTA's partials (the
+      // stores of every thread, ordered before it by the CTA barrier) and,
+      // for the last arrival, acquires every other group's
+      unsigned int old;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                   : "=r"(old)
+                   : "l"(&a.attn_cnt[tl * KV + g])
+                   : "memory");
       *s_last = old == (unsigned int)(ng - 1);
     }
     consumer_sync();
@@ -1129,7 +1135,6 @@ __device__ __forceinline__ void attn_item(const DecodeArgs& a, const DecLayer& L
       // merge (attn_combine_kernel's arithmetic, same order): the partials of
       // up to kZc groups per head are brought into the idle tile with bulk
       // copies (one round trip), then reduced in group order
-      __threadfence();
       const int nsplit = a.nsplit;
       constexpr int kZc = (2 * kAttnTile * HD / 2) / (G * kPartStride);  // splits per chunk (T.k + T.v)
       float* pb = reinterpret_cast<float*>(T.k);                          // [G][zc][kPartStride]
