@@ -9,8 +9,8 @@
 
 // Device error word: set by a kernel whose bounded wait gave up
 // (B2Q_ETIMEOUT = 5), or by the persistent decode kernel when its shared
-// memory is not laid out as planned (B2Q_ECUDA = 3).  Read and cleared by b2q_check_device_error() and by
-// the blocking forward entry points.
+// memory is not laid out as planned (B2Q_ECUDA = 3).  Read and cleared by
+// b2q_check_device_error() and by the blocking forward entry points.
 // libb2q is a single translation unit (b2q_api.cu includes the rest).
 __device__ int g_b2q_device_error = 0;
 
@@ -18,7 +18,7 @@ __device__ int g_b2q_device_error = 0;
 // libb2q_checks.so): index and layout checks in front of the accesses that
 // a wrong plan, layout or argument could send astray -- ring offsets, staged
 // input sizes, attention tile rows, tagged-vector and partial-sum indices,
-// tensor-core stage offsets, GEMV row groups, embedding rows.  A failed check
+// tensor-core stage offsets, GEMV row groups.  A failed check
 // records its site (the first one wins) in g_b2q_check_site, sets the device
 // error word to B2Q_ECUDA (3) and skips the access it guards; the host reads
 // the site with b2q_debug_check_site().  Without the flag every check is the
@@ -161,7 +161,8 @@ __device__ __forceinline__ float f16_bits_fast(uint32_t h) {
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier + 1-D bulk async copy (TMA engine, no tensor map, no multicast).
+// mbarrier, 1-D bulk async copies and 2-D tiled tensor copies (TMA engine, no
+// multicast).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
