@@ -107,7 +107,8 @@ struct DecodeArgs {
   int64_t tok_row_bytes;
   const float* rope_cos;
   const float* rope_sin;
-  const uint32_t* token;  // this step's token id (device)
+  const uint32_t* token;  // this step's token id (device), or nullptr: token_imm
+  uint32_t token_imm;     // the token id by value (a host caller's token)
   int pos;                // its position
   float* part;            // [H][nsplit][kPartStride] attention split partials
   int nsplit;
@@ -1294,7 +1295,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_kernel(const __grid_co
     const int4* src = reinterpret_cast<const int4*>(a.ctab + (size_t)blockIdx.x * a.nph);
     int4* dst = reinterpret_cast<int4*>(tab);
     for (int i = threadIdx.x; i < a.nph * 2; i += kGemvConsumerWarps * 32) dst[i] = __ldcg(src + i);
-    uint32_t tok = a.token[0];
+    uint32_t tok = a.token != nullptr ? a.token[0] : a.token_imm;
     if (tok >= (uint32_t)a.V) tok = 0;
     const uint8_t* rowp = a.tok_raw + (int64_t)tok * a.tok_row_bytes;
     const int64_t slots = dequant_slots(a.tok_dtype, a.E);

@@ -371,20 +371,20 @@ static b2q_status forward_impl(b2q_model* M, const uint32_t* tokens, bool tok_on
   for (int off = 0; off < n && err == cudaSuccess; off += M->mmax) {
     const int m = std::min(M->mmax, n - off);
     const uint32_t* src = tokens + off;
+    if (m == 1 && M->dec_on && !capturing) {
+      // one persistent kernel for the whole step (validates the id itself); a
+      // host token goes by value in the launch arguments
+      err = launch_decode(M, tok_on_dev ? src : nullptr, tok_on_dev ? 0u : tokens[off], start + off, argmax_dev, st);
+      M->last_logits = M->dec_logits;
+      if (err == cudaSuccess && argmax_done) *argmax_done = argmax_dev != nullptr;
+      continue;
+    }
     if (!tok_on_dev) {
       // host tokens: stage through the pinned buffer (synchronous callers only)
       memcpy(M->h_tok, tokens + off, sizeof(uint32_t) * m);
       err = cudaMemcpyAsync(M->tokens + M->mmax, M->h_tok, sizeof(uint32_t) * m, cudaMemcpyHostToDevice, st);
       if (err != cudaSuccess) break;
       src = M->tokens + M->mmax;
-    }
-    if (m == 1 && M->dec_on && !capturing) {
-      // one persistent kernel for the whole step (validates the id itself)
-      err = launch_decode(M, src, start + off, argmax_dev, st);
-      M->last_logits = M->dec_logits;
-      if (err == cudaSuccess && argmax_done) *argmax_done = argmax_dev != nullptr;
-      if (err == cudaSuccess && !tok_on_dev && off + m < n) err = cudaStreamSynchronize(st);
-      continue;
     }
     launch_counted(M->eng, 1);
     set_step_kernel<<<1, 64, 0, st>>>(M->pos, start + off, M->tokens, src, m, c.n_vocab);

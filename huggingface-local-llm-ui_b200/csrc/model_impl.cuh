@@ -832,9 +832,13 @@ static cudaError_t setup_decode(b2q_model* M) {
 }
 
 // One single-token step: token id at `tok` (device), position `pos`.
-static cudaError_t launch_decode(b2q_model* M, const uint32_t* tok, int pos, uint32_t* argmax2, cudaStream_t st) {
+// `tok`: the token id in device memory, or nullptr and the id `tok_imm` by
+// value in the launch arguments (a host caller's token: no copy).
+static cudaError_t launch_decode(b2q_model* M, const uint32_t* tok, uint32_t tok_imm, int pos, uint32_t* argmax2,
+                                 cudaStream_t st) {
   DecodeArgs a = M->dec;
   a.token = tok;
+  a.token_imm = tok_imm;
   a.pos = pos;
   a.argmax2 = argmax2;
   // every earlier launch passed 5L + 2 grid barriers (the last one the

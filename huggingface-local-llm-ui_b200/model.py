@@ -77,6 +77,7 @@ class StandardNativeEngine:
         idbuf = (C.c_ubyte * 128).from_buffer_copy(tp_id) if tp_id else None
         check(lib().b2q_model_create(engine.handle, C.byref(c), idbuf, C.byref(h)))
         self._h = h
+        self._logits_ptr = None  # (address, ctypes pointer) of forward_into's last logits buffer
         self.tp_rank, self.tp_size = tp_rank, tp_size
         self.current_pos = 0
 
@@ -152,10 +153,19 @@ class StandardNativeEngine:
         returned."""
         if logits.dtype != np.float32 or logits.size < self.cfg["n_vocab"] or not logits.flags.c_contiguous:
             raise ValueError("logits must be a contiguous float32 array of n_vocab elements")
-        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        # a decode loop calls this once per token: one id goes in a ctypes
+        # array, and the logits pointer is converted once per buffer address
+        if type(tokens) is list and len(tokens) == 1 and type(tokens[0]) is int and 0 <= tokens[0] < 1 << 32:
+            tp, nt = (C.c_uint32 * 1)(tokens[0]), 1
+        else:
+            t = np.ascontiguousarray(tokens, dtype=np.uint32)
+            tp, nt = t.ctypes.data_as(C.POINTER(C.c_uint32)), t.size
+        addr = logits.ctypes.data
+        lp = self._logits_ptr
+        if lp is None or lp[0] != addr:
+            lp = self._logits_ptr = (addr, C.cast(addr, C.POINTER(C.c_float)))
         out = C.c_uint32()
-        check(lib().b2q_forward(self._h, t.ctypes.data_as(C.POINTER(C.c_uint32)), t.size, start_pos,
-                                logits.ctypes.data_as(C.POINTER(C.c_float)), C.byref(out)))
+        check(lib().b2q_forward(self._h, tp, nt, start_pos, lp[1], C.byref(out)))
         return int(out.value)
 
     def forward_argmax(self, tokens, start_pos: int) -> int:
