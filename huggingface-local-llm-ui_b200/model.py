@@ -59,10 +59,11 @@ class StandardNativeEngine:
                  tp_size: int = 1, tp_id: bytes | None = None, use_graph: bool = True,
                  decode: str | None = None):
         """`decode` picks how single-token steps run: "persistent" (default:
-        one persistent kernel per token on one GPU; the captured graph under
-        tensor parallelism), "graph" (the captured graph of the per-layer
-        kernels) or "eager" (the same kernels launched one by one; also
-        use_graph=False).  All three give the same logits bit for bit."""
+        one persistent kernel per token, on one GPU or across the
+        tensor-parallel ranks; the captured graph where the model does not
+        fit it), "graph" (the captured graph of the per-layer kernels) or
+        "eager" (the same kernels launched one by one; also use_graph=False).
+        All three give the same logits bit for bit."""
         self.engine = engine
         self.cfg = dict(cfg)
         self.max_seq = max_seq
