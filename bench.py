@@ -41,7 +41,9 @@ prompt is prefilled, then one step = one greedy decode token at batch 1.
 * cpu_baseline -- the reference's CPU path (the oracle's restatement of the
               AVX2/FMA Rayon matvec and the Llama forward), rank 0 at N = 1:
               all host cores, and the reference governor's thread count
-              min(3/4 cores, cores - 2) (hardware.rs:157-166).
+              min(3/4 cores, cores - 2) (hardware.rs:157-166); `matvec_shapes`:
+              the same CPU matvec per gemv_shapes config shape, weight copies
+              rotated past 256 MB.
 * model_70b -- the Llama-3-70B-shaped decoder (80 layers, hidden 8192, 64/8
               heads, FFN 28672, same quant mix, 44 GB): the f16 KV cache is
               filled with seeded synthetic rows (b2q_model_fill_kv) up to the
@@ -344,6 +346,37 @@ def time_gemv_shape(engine, synth, key, seed, dev, sp, copies=None, reps=None, c
     for b in bufs:
         b.free()
     return ms_l, alg
+
+
+CPU_ROTATE_BYTES = 256 << 20  # weight copies rotated by the CPU matvec timing (past the host's LLC)
+
+
+def cpu_matvec_shape(orc, synth, key, seed, threads: list[int], min_s: float = 0.25, max_reps: int = 64) -> dict:
+    """The reference CPU matvec (matmul_batched, inference.rs:589-760: x
+    quantised to Q8_K / Q8_0, then the AVX2/FMA row dots over the threads) on
+    one config shape, per thread count: wall time per call, rotating weight
+    copies that together exceed the host's last-level cache, so the rows come
+    from DRAM as they do on the GPU side."""
+    t, n, k, _ = GEMV_SHAPES[key]
+    raw = synth.tensor_rows(t, n, k, seed, 900)
+    copies = [raw] + [raw.copy() for _ in range(max(0, -(-CPU_ROTATE_BYTES // raw.nbytes) - 1))]
+    x = np.random.default_rng(seed).standard_normal(k).astype(np.float32)
+    alg = n * raw.shape[1] + 4 * k + 4 * n
+    out = {"bytes": alg, "copies": len(copies)}
+    for th in threads:
+        orc.set_threads(th)
+        orc.matmul_batched(raw, t, n, k, x)  # warm-up
+        reps = 0
+        t0 = time.perf_counter()
+        while True:
+            orc.matmul_batched(copies[reps % len(copies)], t, n, k, x)
+            reps += 1
+            dt = time.perf_counter() - t0
+            if (dt >= min_s and reps >= len(copies)) or reps >= max_reps:
+                break
+        us = dt / reps * 1e6
+        out[f"threads_{th}"] = {"us": round(us, 1), "GBps": round(alg / (us * 1e-6) / 1e9, 2), "reps": reps}
+    return out
 
 
 def time_head_shard(engine, synth, world, rank, seed, dev, sp, dist, peak, peak_kind):
@@ -735,6 +768,16 @@ def main():
                                        "rule": "min(3/4 cores, cores - 2), hardware.rs:157-166"}
         except Exception as ex:  # the baseline is reported, never required
             cpu = {"value": None, "error": str(ex)}
+        try:  # the matvec config shapes on the same CPU path, beside gemv_shapes
+            cores = os.cpu_count() or 1
+            keys = ["q4k_14336x4096"] if args.no_gemv_shapes else list(GEMV_SHAPES)
+            cpu["matvec_shapes"] = {key: cpu_matvec_shape(orc, synth, key, args.seed,
+                                                          sorted({governor_threads(cores), cores}))
+                                    for key in keys}
+            cpu["matvec_note"] = ("oracle matmul_batched (x quantised, AVX2/FMA row dots) per call, weight copies "
+                                  "rotated past 256 MB; GBps = the GPU side's algorithmic bytes / call time")
+        except Exception as ex:
+            cpu["matvec_shapes"] = {"error": str(ex)}
     host = None
 
     parity = None
