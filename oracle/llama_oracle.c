@@ -12,6 +12,10 @@
  *                       bit-exact dequantised weights; the KV cache can be
  *                       rounded to f16 on store, as the device cache is.
  *                       This is the tolerance oracle (rel-L2 <= 1e-3).
+ * Parity unpinned: the reference cannot run here and ships no golden
+ * logits, so neither forward is checked against reference outputs; the f32
+ * path follows the cited lines operation by operation, and the fp64 path is
+ * the gate.
  * The RoPE cos/sin tables follow the reference's f32 recipe
  * (inference.rs:2538-2549) in both paths: they are part of the model
  * definition, like the weights.
