@@ -11,7 +11,8 @@
 //    per stage.  Weight copies are issued before the kernel waits for its
 //    predecessor (programmatic dependent launch): weights never depend on an
 //    earlier kernel, so the first stages stream while the previous kernel
-//    drains.
+//    drains; the kernel lets its own dependent launch at its start, so the
+//    next launch's CTAs take each SM as soon as this grid's CTA there exits.
 //  * The CTA walks its tiles chunk-major: for each k-chunk c, every 8-row
 //    group it owns.  A stage holds NR = 2 tiles when they fit (two groups, or
 //    the gate and up tiles of the fused SwiGLU), else one.
@@ -577,6 +578,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     }
     mbar_init(&x_bar, 1);
     fence_mbar_init();
+    // let the next kernel launch now: its CTAs take each SM as soon as this
+    // grid's CTA there exits, and stream their weights while the rest of this
+    // grid finishes.  Its reads of this kernel's outputs still wait for the
+    // whole grid (griddepcontrol.wait in every kernel launched dependent).
+    pdl_launch_dependents();
   }
   __syncthreads();
   Ring rg;
@@ -610,7 +616,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
   else if (sg.nr == 2) consume_gemv<MT, 2, false>(rg, L, gb, ge, a.rows_cap, sx, ok, racc);
   else consume_gemv<MT, 1, false>(rg, L, gb, ge, a.rows_cap, sx, ok, racc);
   gemv_epilogue<MT, EPI>(racc, a.rows_cap, gb, ge, L.n, sg.y, sg.ldy, ok);
-  if (threadIdx.x == 0) pdl_launch_dependents();
 }
 
 }  // namespace b2q
