@@ -234,7 +234,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch: wait for the producer grid's memory, and
 // let the next grid start its prologue early.  No-ops without the launch
-// attribute.
+// attribute.  Every kernel launched with the attribute calls pdl_wait()
+// before it touches memory an earlier kernel writes, so a kernel may fire
+// pdl_launch_dependents() as early as it likes: the kernels here fire it
+// right after their own wait (the GEMV at its start), and the next grid's
+// CTAs take SMs, and its weight streams start, while this grid still runs.
+// griddepcontrol.wait returns only once the whole producer grid has
+// completed and its memory is visible.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {

@@ -404,6 +404,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   } else if (warp == kTcDequantWarps) {
     // ---- activation producer ----
     if (lane == 0) {
+      pdl_wait();  // the activation images come from the previous kernel
       const uint8_t* xt = reinterpret_cast<const uint8_t*>(a.xh) + (size_t)tile * a.KS * bb;
       int issued = 0;
       for (int i = 0; i < nst; ++i) {
@@ -469,6 +470,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 
   // ---- epilogue: warps 0-3 read rows 32w..32w+31 of the accumulator ----
   if (warp < 4) {
+    pdl_wait();  // the partial-sum buffer is read by an earlier kernel's reduce
     const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&done_bar, 0)) && *s_ok;
     tc_fence_after();
     if (ok && nst > 0) {
@@ -515,6 +517,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 __global__ void tc_act_kernel(const float* __restrict__ x, int ldx, int m, int k, int KS, int N,
                               __half* __restrict__ img, float* __restrict__ inv) {
   pdl_wait();
+  pdl_launch_dependents();
   __shared__ float red[32];
   const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool live = t < m;
@@ -564,7 +567,6 @@ __global__ void tc_act_kernel(const float* __restrict__ x, int ldx, int m, int k
     uint8_t* stage = reinterpret_cast<uint8_t*>(img) + ((size_t)tile * KS + ks) * (size_t)tc_b_bytes(N);
     st_img8(stage, N * kTcK * 2, tt, kk, N, v);
   }
-  pdl_launch_dependents();
 }
 
 // RMSNorm of x's rows (rms_norm_rows, inference.rs:1501-1512) written
@@ -579,6 +581,7 @@ __global__ void __launch_bounds__(1024) tc_rmsnorm_act_kernel(const float* __res
                                                               int KS, int N, __half* __restrict__ img,
                                                               float* __restrict__ inv) {
   pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ float vrow[];
   __shared__ float part[32];
   const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -630,7 +633,6 @@ __global__ void __launch_bounds__(1024) tc_rmsnorm_act_kernel(const float* __res
     uint8_t* stage = reinterpret_cast<uint8_t*>(img) + ((size_t)tile * KS + ks) * (size_t)tc_b_bytes(N);
     st_img8(stage, N * kTcK * 2, tt, kk, N, v);
   }
-  pdl_launch_dependents();
 }
 
 // y[t][col0 + r] = epi(inv[t] * sum_s part[s][t][r]) for t < m, r < n;
@@ -645,6 +647,7 @@ __global__ void tc_reduce_kernel(const float* __restrict__ part, const float* __
                                  int mpad, int m, int n, int ldp, const float* __restrict__ inv,
                                  float* __restrict__ y, int ldy, int col0) {
   pdl_wait();
+  pdl_launch_dependents();
   const int t = blockIdx.y;
   const float it = inv[t];
   float* yr = y + (size_t)t * ldy + col0;
@@ -686,7 +689,6 @@ __global__ void tc_reduce_kernel(const float* __restrict__ part, const float* __
       else yr[r] = o[0];
     }
   }
-  pdl_launch_dependents();
 }
 
 }  // namespace b2q

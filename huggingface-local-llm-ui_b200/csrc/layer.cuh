@@ -21,6 +21,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_quant_kernel(
     const float* __restrict__ x, int row_stride, int row0, const float* __restrict__ w, int dim,
     float eps, XQ xq, float* __restrict__ y) {
   pdl_wait();
+  pdl_launch_dependents();
   __shared__ float part[32];
   const int t = blockIdx.x;
   const float* xr = x + (int64_t)(row0 + t) * row_stride;
@@ -49,7 +50,6 @@ __global__ void __launch_bounds__(1024) rmsnorm_quant_kernel(
     }
     xq_store_block(va, vb, lane, t, e0 >> 6, xq);
   }
-  pdl_launch_dependents();
 }
 
 // NeoX half-split RoPE on q (in place) and k, plus the f16 KV-cache append
@@ -62,6 +62,7 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int m, int H, int KV, in
                                __half* __restrict__ vc, const float* __restrict__ q_bias,
                                const float* __restrict__ k_bias, const float* __restrict__ v_bias) {
   pdl_wait();
+  pdl_launch_dependents();
   const int s = blockIdx.x;
   const int start = *pos_dev;
   const int p_abs = start + s;
@@ -99,7 +100,6 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int m, int H, int KV, in
     if (v_bias != nullptr) v += v_bias[idx];
     if (p_abs < cap) vc[((int64_t)kh * cap + p_abs) * hd + d] = __float2half_rn(v);
   }
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -383,6 +383,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
   __shared__ uint64_t bar;
   AttnTile<G>& T = *reinterpret_cast<AttnTile<G>*>(smem_align1024(attn_smem));
   pdl_wait();
+  pdl_launch_dependents();
   constexpr int HD = kHeadDim;
   constexpr int R = (G * HD + kAttnThreads - 1) / kAttnThreads;
   const int g = blockIdx.x, s = blockIdx.y, j = blockIdx.z;
@@ -429,7 +430,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
     const int i = threadIdx.x + kAttnThreads * r;
     if (i < G * HD) attn_store_partial(ps, g, G, j, nsplit, i / HD, i % HD, run.m[r], run.l[r], run.o[r]);
   }
-  pdl_launch_dependents();
 }
 
 // Merge the split partials of every head, normalise (inv_sum =
@@ -439,6 +439,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int m, int H
                                     const int* __restrict__ pos_dev, int cap, int nsplit,
                                     float* __restrict__ out, XQ xq, int grid) {
   pdl_wait();
+  pdl_launch_dependents();
   constexpr int HD = kHeadDim;
   __shared__ float vals[8 * HD];
   const int g = blockIdx.x, s = blockIdx.y;
@@ -467,7 +468,6 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int m, int H
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp < 2 * G)
     xq_store_block(vals[64 * warp + lane], vals[64 * warp + 32 + lane], lane, s, (col0 >> 6) + warp, xq);
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -505,6 +505,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const float* __restri
   __shared__ uint64_t bars[2];
   constexpr int HD = kHeadDim, QT = 64 / G;  // tokens per CTA
   pdl_wait();
+  pdl_launch_dependents();
   const int g = blockIdx.x, s0 = blockIdx.y * QT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, t = lane & 3;
   const int start = *pos_dev;
@@ -652,7 +653,6 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const float* __restri
     if (tok0 < m) *reinterpret_cast<float2*>(o0 + d) = make_float2(o[n][0] * i0, o[n][1] * i0);
     if (tok1 < m) *reinterpret_cast<float2*>(o1 + d) = make_float2(o[n][2] * i1, o[n][3] * i1);
   }
-  pdl_launch_dependents();
 }
 
 // Seeded synthetic KV rows (benchmark set-up: a long context without a
@@ -693,6 +693,7 @@ __global__ void set_step_kernel(int* __restrict__ pos_dev, int pos, uint32_t* __
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ v, int n,
                                                       uint32_t* __restrict__ out) {
   pdl_wait();
+  pdl_launch_dependents();
   __shared__ float bv[32];
   __shared__ int bi[32];
   float best = -INFINITY;
@@ -722,7 +723,6 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     }
     if (lane == 0) *out = idx == 0x7fffffff ? 0u : (uint32_t)idx;
   }
-  pdl_launch_dependents();
 }
 
 }  // namespace b2q

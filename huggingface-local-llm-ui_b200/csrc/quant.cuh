@@ -134,6 +134,7 @@ __device__ __forceinline__ void xq_store_chunk8(const float (&v)[8], int lane, i
 // x [m][k] f32 -> XQ (all kpad/64 blocks of every row, zero tail).
 __global__ void quantize_x_kernel(const float* __restrict__ x, int m, int k, XQ xq) {
   pdl_wait();
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int nblk = xq.kpad / 64;
   const int warps = (gridDim.x * blockDim.x) >> 5;
@@ -143,7 +144,6 @@ __global__ void quantize_x_kernel(const float* __restrict__ x, int m, int k, XQ 
     const float* xr = x + (size_t)t * k;
     xq_store_block(p0 < k ? xr[p0] : 0.0f, p1 < k ? xr[p1] : 0.0f, lane, t, j, xq);
   }
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -272,6 +272,7 @@ __global__ void embed_rows_kernel(const uint8_t* __restrict__ raw, int dtype, in
                                   int k, int vocab, const uint32_t* __restrict__ tokens,
                                   float* __restrict__ x) {
   pdl_wait();
+  pdl_launch_dependents();
   const int t = blockIdx.y;
   uint32_t tok = tokens[t];
   if (tok >= (uint32_t)vocab) tok = 0;  // out-of-range ids are rejected on the host
@@ -281,7 +282,6 @@ __global__ void embed_rows_kernel(const uint8_t* __restrict__ raw, int dtype, in
   for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < slots;
        s += (int64_t)gridDim.x * blockDim.x)
     dequant_slot(row, dtype, s, out);
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------

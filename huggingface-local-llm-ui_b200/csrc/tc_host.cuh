@@ -50,7 +50,7 @@ void tc_free(b2q_engine* e) {
 // One launch over the weights ws[0..nw) (same k): weight i's rows go to
 // columns c0[i].. of partial sums with ncol columns.
 static cudaError_t tc_launch_gemm(b2q_engine* e, const b2q_weight* const* ws, const int* c0, int nw,
-                                  const TcPlan& p, int m, float* part, int ncol, cudaStream_t st) {
+                                  const TcPlan& p, int m, float* part, int ncol, cudaStream_t st, bool pdl) {
   if (p.N < 16 || p.N > kTcNMax || p.N % 16 != 0 || nw < 1 || nw > kTcMaxSegs) return cudaErrorInvalidValue;
   TcArgs a;
   memset(&a, 0, sizeof a);
@@ -81,6 +81,15 @@ static cudaError_t tc_launch_gemm(b2q_engine* e, const b2q_weight* const* ws, co
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
+  // dependent launch: the weight-dequantising warps and the TMEM allocation
+  // start while the previous kernel runs; the activation copies and the
+  // partial-sum stores wait for it (griddepcontrol.wait).  Two GEMM grids
+  // never overlap: the split-K reduce between them is a plain launch.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
   launch_counted(e, 1);
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, a);
 }
@@ -156,7 +165,7 @@ cudaError_t tc_matmul(b2q_engine* e, const float* x, int ldx, int m, int k, cons
       c[i] = (int)o;
       o += ws[i]->n;
     }
-    err = tc_launch_gemm(e, ws, c, nw, p, m, t.part, (int)ncol, st);
+    err = tc_launch_gemm(e, ws, c, nw, p, m, t.part, (int)ncol, st, pdl);
     if (err != cudaSuccess) return err;
     if (epi == kEpiSwiglu)
       return tc_launch_reduce<kEpiSwiglu>(e, p, m, (int)ws[0]->n, (int)ncol, t.part + ws[0]->n, y, ldy, col0[0], st);
@@ -165,7 +174,7 @@ cudaError_t tc_matmul(b2q_engine* e, const float* x, int ldx, int m, int k, cons
   }
   for (int i = 0; i < nw && err == cudaSuccess; ++i) {
     const int z0 = 0, n = (int)ws[i]->n;
-    err = tc_launch_gemm(e, &ws[i], &z0, 1, p, m, t.part, n, st);
+    err = tc_launch_gemm(e, &ws[i], &z0, 1, p, m, t.part, n, st, pdl);
     if (err != cudaSuccess) break;
     err = epi == kEpiAdd ? tc_launch_reduce<kEpiAdd>(e, p, m, n, n, nullptr, y, ldy, col0[i], st)
                          : tc_launch_reduce<kEpiStore>(e, p, m, n, n, nullptr, y, ldy, col0[i], st);
