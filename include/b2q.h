@@ -20,6 +20,12 @@
  *    and return after the result is on the host, as the reference's
  *    synchronous memcpy path did.  `_dev` entry points take DEVICE pointers
  *    and a cudaStream_t (passed as void*) and are asynchronous.
+ *  - The library's kernels let the next launch on their stream start early
+ *    (programmatic dependent launch).  A caller's kernel launched right
+ *    after a `_dev` call WITHOUT the programmatic-serialisation attribute
+ *    waits for it as usual; one launched WITH it must call
+ *    cudaGridDependencySynchronize() (griddepcontrol.wait) before it reads
+ *    the call's outputs or writes its inputs.
  *  - One engine per CUDA device; handles are internally locked.
  */
 #ifndef B2Q_H
