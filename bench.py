@@ -121,19 +121,33 @@ def load_peaks() -> dict:
     return {"hbm_gbs": HBM_FALLBACK_GBS, "bf16_tflops": 1590.0}
 
 
-def profile_traffic(name: str = "gemv_q4k_14336x4096.md") -> float | None:
+def profile_traffic(name: str = "gemv_q4k_14336x4096.md",
+                    key: str = "traffic_bytes_per_launch") -> float | None:
     """DRAM bytes per launch from a committed ncu summary under profiles/
-    (its "traffic_bytes_per_launch:" line), if one has been captured."""
+    (its "traffic_bytes_per_launch:" line, or another `key:` line), if one
+    has been captured."""
     p = REPO / "profiles" / name
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
+        if line.strip().startswith(key + ":"):
             try:
                 return float(line.split(":", 1)[1].strip())
             except ValueError:
                 return None
     return None
+
+
+def scaled_profile_traffic(name: str, step_bytes: int) -> float | None:
+    """DRAM bytes of a full launch from a capture of a smaller case of the
+    same kernel: the capture's traffic / algorithmic-bytes ratio times this
+    launch's algorithmic bytes (traffic grows with the layers and keys in
+    proportion; the summary under profiles/ records both figures)."""
+    t = profile_traffic(name)
+    a = profile_traffic(name, "algorithmic_bytes_per_launch")
+    if not t or not a:
+        return None
+    return round(t / a * step_bytes)
 
 
 def governor_threads(cores: int) -> int:
@@ -617,8 +631,14 @@ def run_model(args, name, engine, rank, world, local, dist, dev, stream, orc):
         traffic = None
         if world == 1 and not is70 and cfg["n_layers"] == 32:
             traffic = profile_traffic("decode_kernel_llama3_8b.md")
+        elif world == 1 and is70 and cfg["n_layers"] == 80:
+            traffic = scaled_profile_traffic("decode_kernel_llama3_70b_2layers_8192ctx.md", step_bytes)
+        traffic_source = (None if traffic is None else
+                          "ncu capture of this launch" if not is70 else
+                          "ncu capture of the 2-layer 8192-key case, its traffic/algorithmic ratio (1.0025) "
+                          "times this launch's algorithmic bytes")
         roof = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(step_gbs / peak, 4), "traffic": traffic,
+                "frac": round(step_gbs / peak, 4), "traffic": traffic, "traffic_source": traffic_source,
                 "kernel": "decode_kernel (persistent single-token step)",
                 "algorithmic_bytes_per_launch": int(step_bytes), "peak_kind": peak_kind,
                 "launch_us": round(ms_step * 1000, 2), "context": ctx}

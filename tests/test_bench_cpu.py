@@ -31,3 +31,12 @@ def test_cpu_matvec_shape_reports_every_thread_count(pkg, orc):
     for th in (1, 2):
         e = r[f"threads_{th}"]
         assert e["reps"] == 2 and e["us"] > 0 and e["GBps"] > 0
+
+
+def test_traffic_figures_from_the_committed_captures():
+    b = _bench()
+    assert b.profile_traffic("decode_kernel_llama3_8b.md") > 4.9e9
+    # the 70B launch's traffic scales the 2-layer capture by its algorithmic bytes
+    t = b.scaled_profile_traffic("decode_kernel_llama3_70b_2layers_8192ctx.md", 47_046_119_936)
+    assert 1.0 < t / 47_046_119_936 < 1.01
+    assert b.scaled_profile_traffic("no_such_capture.md", 1) is None
