@@ -27,6 +27,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <cstdint>
 #include <cstring>
 #include <string>
 #include <unordered_map>
@@ -250,9 +251,13 @@ inline std::string parse(File* f, std::vector<std::string>* keys) {
   for (Raw& r : raw) {
     int bs, ts;
     type_geometry((uint32_t)r.t.ggml_type, &bs, &ts);
-    unsigned __int128 elems = 1;
-    for (int j = 0; j < r.t.n_dims; ++j) elems *= (uint64_t)r.t.dims[j];
-    const unsigned __int128 blen = elems / (unsigned)bs * (unsigned)ts;
+    // element count in 64 bits, overflow rejected: a product that wrapped
+    // would give a small byte length for dims that describe a huge tensor
+    uint64_t elems = 1;
+    for (int j = 0; j < r.t.n_dims; ++j)
+      if (__builtin_mul_overflow(elems, (uint64_t)r.t.dims[j], &elems))
+        return "tensor '" + r.t.name + "': element count overflows 64 bits";
+    const unsigned __int128 blen = (unsigned __int128)(elems / (unsigned)bs) * (unsigned)ts;
     const unsigned __int128 end = (unsigned __int128)f->data_offset + r.rel + blen;
     if (end > f->size)
       return "tensor '" + r.t.name + "' extends past the end of the GGUF file (" +

@@ -32,11 +32,16 @@ b2q_status gguf_int(const b2q_gguf* g, const std::string& key, int* out) {
 // host, as tensor_f32_1d dequantises them (src/inference.rs:494-500).
 b2q_status load_tensor(b2q_model* M, const b2q_gguf* g, const gguf::Tensor& t, const char* as_name) {
   const uint8_t* src = g->data + t.abs_offset;
-  int64_t n = 1;
-  for (int j = 0; j + 1 < t.n_dims; ++j) n *= t.dims[j];
   if (t.n_dims < 1) return set_error(B2Q_EINVAL, "tensor %s: no dims", t.name.c_str());
+  uint64_t n = 1;  // outer rows (the parser has checked that all dims multiply within 64 bits)
+  for (int j = 0; j + 1 < t.n_dims; ++j)
+    if (__builtin_mul_overflow(n, (uint64_t)t.dims[j], &n))
+      return set_error(B2Q_EINVAL, "tensor %s: dims overflow", t.name.c_str());
   if (t.n_dims == 1 || n == 1) {
     const int64_t k = t.dims[t.n_dims - 1];
+    if ((t.ggml_type == kF16 || t.ggml_type == kBF16) && (uint64_t)k * 2 > t.byte_len)
+      return set_error(B2Q_EINVAL, "tensor %s: %lld elements in %llu bytes", t.name.c_str(), (long long)k,
+                       (unsigned long long)t.byte_len);
     if (t.ggml_type == kF32)
       return set_tensor_impl(M, as_name, kF32, t.dims, t.n_dims, 0, 1, src, (size_t)t.byte_len);
     if (t.ggml_type != kF16 && t.ggml_type != kBF16)
