@@ -335,7 +335,8 @@ b2q_status b2q_model_debug_desync(b2q_model* m);
  * A read-only POSIX mapping of the file, parsed as GgufModelFile::open
  * does (inference.rs:343-446): versions 1..3, metadata types 0..12, dims
  * reversed to [outer.., inner], data section aligned to general.alignment
- * (default 32), every tensor checked to end inside the file.  Names and
+ * (default 32), every tensor checked to end inside the file; a tensor
+ * whose element count overflows 64 bits is rejected.  Names and
  * string values returned below point into the handle and stay valid until
  * b2q_gguf_close.  Errors are B2Q_EINVAL with the reason in
  * b2q_last_error() (the reference's anyhow messages). */
